@@ -1,0 +1,163 @@
+/*
+ * mimo_moe.h — C ABI of the B200 (sm_100a) MiMo MoE block:
+ *   router -> dispatch -> MXFP4 expert products -> fixed-order combine.
+ *
+ * Every pointer argument is a DEVICE pointer except `pools`, which is a host pointer to a struct of
+ * device pointers; `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * The entry points below do not allocate memory, synchronise the host or change the current device:
+ * outputs and workspaces are caller-owned, and every launch is stream-ordered.  Return value: MIMO_OK
+ * or an error code below (host-side argument checks and launch errors).  Errors found while the kernels
+ * run (a route table that overflows R, an activation outside the f16 range, a bounded device wait that
+ * expired) are written to the optional device word `status` (caller-zeroed int32; first error wins) and
+ * are visible after the stream is synchronised.
+ *
+ * Tensor contract (the reference's expert pool layout, engine/mimo_stream/model.py:28-45 and
+ * scripts/convert-mimo-v26-mlx.py:8-12): per MoE layer and slot s,
+ *   gate_w, up_w  uint32 [S, I, H/8]   e2m1 nibbles, 8 per word, element k = nibble k%8 of word k/8
+ *   gate_s, up_s  uint8  [S, I, H/32]  e8m0 scale per 32 consecutive K elements (s=0 -> 2^-127, 255 -> NaN)
+ *   down_w        uint32 [S, H, I/8]
+ *   down_s        uint8  [S, H, I/32]
+ * Activations are bf16 (passed as uint16_t bit patterns); router logits and weights are float32.
+ */
+#ifndef MIMO_MOE_H
+#define MIMO_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MIMO_MOE_VERSION 1
+
+enum mimo_moe_error {
+  MIMO_OK = 0,
+  MIMO_EINVAL = 1,    /* bad shape, null pointer, unsupported size, workspace too small */
+  MIMO_ERANGE = 2,    /* expert id outside [0,E), more than R rows on one expert, activation overflow */
+  MIMO_ETIMEOUT = 3,  /* a bounded device-side wait expired; the kernel returned without the result */
+  MIMO_ECUDA = 4,     /* CUDA launch / runtime error (see mimo_moe_last_cuda_error) */
+};
+
+/* Expert pool of one MoE layer (device pointers, reference layout above). */
+typedef struct mimo_moe_pools {
+  const uint32_t* gate_w;
+  const uint8_t* gate_s;
+  const uint32_t* up_w;
+  const uint8_t* up_s;
+  const uint32_t* down_w;
+  const uint8_t* down_s;
+  int32_t num_slots; /* S */
+  int32_t hidden;    /* H, multiple of 2048 (4096 for MiMo) */
+  int32_t inter;     /* I, multiple of 2048 (2048 for MiMo) */
+} mimo_moe_pools;
+
+/* Library version and error text. */
+int mimo_moe_version(void);
+const char* mimo_moe_strerror(int code);
+/* Last CUDA error code seen by a failing call on this host thread (0 if none). */
+int mimo_moe_last_cuda_error(void);
+
+/*
+ * Router — replaces Router.__call__ (engine/mimo_stream/model.py:58-65).
+ *   logits[T,E] = fp32(x[T,H]) . fp32(w[E,H])^T         (float32 accumulation)
+ *   s = sigmoid(logits); sel = s + bias; idx = top-k of sel (descending sel, ties by ascending id)
+ *   weight[t,j] = s[t,idx[t,j]] / (sum_j s[t,idx[t,j]] + 1e-20)   (float32 sum in j order)
+ * E multiple of 32 and <= 256; 1 <= topk <= 8; H multiple of 256.  `logits` is a caller buffer [T,E].
+ */
+int mimo_moe_router(const uint16_t* x, const uint16_t* w, const float* bias, int32_t T, int32_t H,
+                    int32_t E, int32_t topk, float* logits, int32_t* idx, float* weight, void* stream);
+
+/* The selection half of the router, from given logits — model.py:60-64.  bias may be NULL (zeros). */
+int mimo_moe_topk(const float* logits, const float* bias, int32_t T, int32_t E, int32_t topk,
+                  int32_t* idx, float* weight, void* stream);
+
+/*
+ * Decode route grouping — replaces group_routes (engine/mimo_stream/kernels.py:149-173).
+ * idx/weight [M,topk] (expert or slot ids in [0,E)) -> per distinct id u (ascending):
+ *   uids[u], urows[u,R] (row per route, 0-padded), ucnt[u], uw[u,R] (weight, 0-padded),
+ *   gather_idx[M*topk] = u*R + c, num_unique[0] = U.
+ * Output arrays are sized for U_max = min(E, M*topk).  M*topk <= 1024.  More than R routes on one id
+ * sets MIMO_ERANGE in `status` (the reference raises ValueError, kernels.py:167-168).
+ */
+int mimo_moe_group_routes(const int32_t* idx, const float* weight, int32_t M, int32_t topk, int32_t R,
+                          int32_t E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                          int32_t* gather_idx, int32_t* num_unique, int32_t* status, void* stream);
+
+/*
+ * Prefill dispatch — replaces the pair permutation of Engine._moe_prefill
+ * (engine/mimo_stream/model.py:235-244, 266-268): pairs p = t*topk + j in flat order, stable-sorted by
+ * idx; order[i] = pair at sorted position i, inv[p] = sorted position of pair p, offsets[E+1] = bucket
+ * starts.  Workspace: mimo_moe_dispatch_workspace_bytes(T, topk, E).
+ */
+size_t mimo_moe_dispatch_workspace_bytes(int32_t T, int32_t topk, int32_t E);
+int mimo_moe_dispatch(const int32_t* idx, int32_t T, int32_t topk, int32_t E, int32_t* offsets,
+                      int32_t* order, int32_t* inv, void* workspace, size_t workspace_bytes,
+                      int32_t* status, void* stream);
+
+/*
+ * Small-batch expert products over distinct experts — replaces moe_experts
+ * (engine/mimo_stream/kernels.py:176-199: kernel A gate/up+SwiGLU, kernel B down*weight, combine).
+ *   x [M,H] bf16; uslot/urows/ucnt/uw/gather_idx from mimo_moe_group_routes (uslot = pool slot per
+ *   distinct expert); U = capacity of those arrays; num_unique (device, may be NULL -> U) = live count;
+ *   topk = routes per row in gather_idx [M*topk].
+ *   y [M,H] bf16 = sum over each row's routes, in gather_idx order, of w * expert(x_row)   (float32 sum)
+ *   gather_idx NULL -> per-row sum in (u, r) order (the reference's scatter-add, kernels.py:196-197).
+ *   pairs_rounding != 0 rounds each expert's down output to bf16 before weighting, as the reference's
+ *   stock gather_qmm path does at M == 1 (model.py:173-182).
+ * 1 <= R <= 8, M <= 128.  Workspace: mimo_moe_experts_workspace_bytes(M, U, R, H, I).
+ */
+size_t mimo_moe_experts_workspace_bytes(int32_t M, int32_t U, int32_t R, int32_t H, int32_t I);
+int mimo_moe_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,
+                     const int32_t* urows, const int32_t* ucnt, const float* uw,
+                     const int32_t* num_unique, int32_t U, int32_t R, const int32_t* gather_idx,
+                     int32_t topk, int32_t M, int32_t pairs_rounding, uint16_t* y, void* workspace,
+                     size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Prefill expert products — replaces Engine._pair_outputs + the combine of Engine._moe_prefill
+ * (engine/mimo_stream/model.py:221-271): per (token, k) pair, bf16 gate/up, bf16 SwiGLU, bf16 down
+ * output; y[t] = bf16(sum_k fp32(out[t,k]) * w[t,k]) in k order.
+ *   idx/weight [T,topk] expert ids in [0,E); slot_of [E] (may be NULL: slot = expert id, E = S) maps
+ *   expert id -> pool slot.  Workspace: mimo_moe_prefill_workspace_bytes(T, topk, H, I, E).
+ */
+size_t mimo_moe_prefill_workspace_bytes(int32_t T, int32_t topk, int32_t H, int32_t I, int32_t E);
+int mimo_moe_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* slot_of, int32_t E,
+                     const int32_t* idx, const float* weight, int32_t T, int32_t topk, uint16_t* y,
+                     void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * The whole block — replaces one MoE layer of Engine.forward (engine/mimo_stream/model.py:303-336)
+ * with all experts resident (E = S): router, then the reference's dispatch rule (T == 1: stock-path
+ * rounding; 2 <= T <= 8: distinct-expert kernels; T > 8: prefill path).  idx_out/w_out (may be NULL)
+ * receive the routes.  Workspace: mimo_moe_block_workspace_bytes(T, H, I, E, topk).
+ */
+size_t mimo_moe_block_workspace_bytes(int32_t T, int32_t H, int32_t I, int32_t E, int32_t topk);
+int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bias,
+                   const mimo_moe_pools* pools, int32_t T, int32_t topk, uint16_t* y, int32_t* idx_out,
+                   float* w_out, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Synthetic pool fill (benchmarks and tests): counter-based splitmix64 stream per (seed, layer, tensor);
+ * experts [first_expert, first_expert + S) of the layer are written to slots [0, S).  Nibbles uniform
+ * over the 16 e2m1 codes; scale bytes 120 with p = 0.6875, else 119.
+ */
+int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up_w, uint8_t* up_s,
+                                 uint32_t* down_w, uint8_t* down_s, int32_t S, int32_t H, int32_t I,
+                                 uint64_t seed, int32_t layer, int32_t first_expert, void* stream);
+
+/*
+ * Benchmark support (no counterpart in the reference).  mimo_moe_profile_enable(n) with n > 0 makes
+ * the library record a CUDA event pair around each of the next n expert-tile kernel launches on the
+ * launching stream (the events are created here, once); n = 0 turns it off.  mimo_moe_profile_read()
+ * synchronises those events and returns, per kernel kind (0 decode gate/up, 1 decode down, 2 prefill
+ * gate/up, 3 prefill down), the launch count and the summed device milliseconds, then resets.
+ * Off by default; do not enable it while a stream is being captured.
+ */
+int mimo_moe_profile_enable(int32_t capacity);
+int mimo_moe_profile_read(int32_t* launches, float* milliseconds);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MIMO_MOE_H */

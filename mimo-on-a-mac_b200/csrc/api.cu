@@ -1,0 +1,428 @@
+// C ABI of the MoE block (include/mimo_moe.h): argument checks, workspace carving, launches.
+// No allocation, no host synchronisation, no device selection: everything is stream-ordered.
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace mimo;
+
+namespace {
+
+thread_local int g_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+  g_last_cuda_error = (int)e;
+  return MIMO_ECUDA;
+}
+#define MIMO_TRY(expr)                           \
+  do {                                           \
+    const cudaError_t _e = (expr);               \
+    if (_e != cudaSuccess) return cuda_fail(_e); \
+  } while (0)
+
+int num_sms_current() {
+  static int cache[128] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// ----------------------------------------------------------------- optional launch profiling
+struct ProfRec {
+  int kind;
+  cudaEvent_t a, b;
+};
+std::mutex g_prof_mu;
+std::vector<ProfRec> g_prof_pool;  // created once, reused
+size_t g_prof_used = 0;
+int g_prof_cap = 0;
+
+cudaError_t tiles(const ExpertParams& p, int kind, int sms, cudaStream_t st) {
+  ProfRec* rec = nullptr;
+  if (g_prof_cap > 0) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (g_prof_used < (size_t)g_prof_cap && g_prof_used < g_prof_pool.size()) rec = &g_prof_pool[g_prof_used++];
+  }
+  if (rec) {
+    rec->kind = kind;
+    cudaEventRecord(rec->a, st);
+  }
+  const cudaError_t e = launch_expert_tiles(p, kind, sms, st);
+  if (rec) cudaEventRecord(rec->b, st);
+  return e;
+}
+
+// Bump allocator over the caller's workspace; with base == nullptr it only measures.
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) & ~size_t(255);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+bool dims_ok(int H, int I) { return H > 0 && I > 0 && H % 2048 == 0 && I % 2048 == 0; }
+
+bool pools_ok(const mimo_moe_pools* p) {
+  return p && p->gate_w && p->gate_s && p->up_w && p->up_s && p->down_w && p->down_s &&
+         p->num_slots > 0 && dims_ok(p->hidden, p->inter);
+}
+
+// ------------------------------------------------------------------- workspace layouts
+struct DecodeWs {
+  __half* x16;
+  __half* h16;
+  float* part;
+};
+DecodeWs carve_decode(Carver& c, int M, int U, int R, int H, int I) {
+  DecodeWs w;
+  w.x16 = c.take<__half>((size_t)M * H);
+  w.h16 = c.take<__half>((size_t)U * R * I);
+  w.part = c.take<float>((size_t)U * R * H);
+  return w;
+}
+
+struct PrefillWs {
+  __half* x16;
+  int32_t *offsets, *order, *inv, *unit_slot, *unit_p0, *unit_cnt, *num_units, *rtok;
+  float* rw;
+  void* dws;
+  __half* h16;
+  uint16_t* ypair;
+  int ucap;
+};
+PrefillWs carve_prefill(Carver& c, int T, int topk, int H, int I, int E) {
+  PrefillWs w;
+  const int P = T * topk;
+  w.ucap = P / kPrefillUnit + E;
+  w.x16 = c.take<__half>((size_t)T * H);
+  w.offsets = c.take<int32_t>(E + 1);
+  w.order = c.take<int32_t>(P);
+  w.inv = c.take<int32_t>(P);
+  w.dws = c.take<uint8_t>(dispatch_workspace_bytes(P, E));
+  w.unit_slot = c.take<int32_t>(w.ucap);
+  w.unit_p0 = c.take<int32_t>(w.ucap);
+  w.unit_cnt = c.take<int32_t>(w.ucap);
+  w.num_units = c.take<int32_t>(1);
+  w.rtok = c.take<int32_t>(P);
+  w.rw = c.take<float>(P);
+  w.h16 = c.take<__half>((size_t)P * I);
+  w.ypair = c.take<uint16_t>((size_t)P * H);
+  return w;
+}
+
+struct GroupWs {
+  int32_t *uids, *urows, *ucnt, *gidx, *nu;
+  float* uw;
+  int ucap;
+};
+GroupWs carve_group(Carver& c, int M, int topk, int R, int E) {
+  GroupWs g;
+  g.ucap = std::min(E, M * topk);
+  g.uids = c.take<int32_t>(g.ucap);
+  g.urows = c.take<int32_t>((size_t)g.ucap * R);
+  g.ucnt = c.take<int32_t>(g.ucap);
+  g.uw = c.take<float>((size_t)g.ucap * R);
+  g.gidx = c.take<int32_t>((size_t)M * topk);
+  g.nu = c.take<int32_t>(1);
+  return g;
+}
+
+ExpertParams gateup_params(const mimo_moe_pools* pools, int32_t* status) {
+  ExpertParams p{};
+  p.w[0] = reinterpret_cast<const uint8_t*>(pools->gate_w);
+  p.s[0] = pools->gate_s;
+  p.w[1] = reinterpret_cast<const uint8_t*>(pools->up_w);
+  p.s[1] = pools->up_s;
+  p.S = pools->num_slots;
+  p.N = pools->inter;
+  p.K = pools->hidden;
+  p.tiles = pools->inter / 16;
+  p.status = status;
+  return p;
+}
+
+ExpertParams down_params(const ExpertParams& gu, const mimo_moe_pools* pools) {
+  ExpertParams q = gu;
+  q.w[0] = reinterpret_cast<const uint8_t*>(pools->down_w);
+  q.s[0] = pools->down_s;
+  q.w[1] = nullptr;
+  q.s[1] = nullptr;
+  q.N = pools->hidden;
+  q.K = pools->inter;
+  q.tiles = pools->hidden / 16;
+  q.rtok = nullptr;
+  q.bsrc = gu.h_out;
+  q.h_out = nullptr;
+  return q;
+}
+
+int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,
+                const int32_t* urows, const int32_t* ucnt, const float* uw, const int32_t* num_unique,
+                int U, int R, const int32_t* gidx, int topk, int M, int pairs_rounding, uint16_t* y,
+                const DecodeWs& w, int32_t* status, cudaStream_t st) {
+  const int H = pools->hidden;
+  const int sms = num_sms_current();
+  MIMO_TRY(launch_to_f16(x, w.x16, (size_t)M * H, status, st));
+  ExpertParams p = gateup_params(pools, status);
+  p.unit_slot = uslot;
+  p.unit_p0 = nullptr;
+  p.p0_stride = R;
+  p.unit_cnt = ucnt;
+  p.num_units = num_unique;
+  p.units_cap = U;
+  p.rtok = urows;
+  p.bsrc = w.x16;
+  p.h_out = w.h16;
+  MIMO_TRY(tiles(p, 0, sms, st));
+  ExpertParams q = down_params(p, pools);
+  q.rw = uw;
+  q.part_out = w.part;
+  q.pairs_rounding = pairs_rounding;
+  MIMO_TRY(tiles(q, 1, sms, st));
+  MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
+  return MIMO_OK;
+}
+
+int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* slot_of,
+                const int32_t* idx, const float* weight, int T, int topk, int E, uint16_t* y,
+                const PrefillWs& w, int32_t* status, cudaStream_t st) {
+  const int H = pools->hidden;
+  const int P = T * topk;
+  const int sms = num_sms_current();
+  MIMO_TRY(launch_to_f16(x, w.x16, (size_t)T * H, status, st));
+  MIMO_TRY(launch_dispatch(idx, P, E, w.offsets, w.order, w.inv, w.dws, status, st));
+  MIMO_TRY(launch_build_units(w.offsets, slot_of, E, pools->num_slots, kPrefillUnit, w.ucap,
+                              w.unit_slot, w.unit_p0, w.unit_cnt, w.num_units, w.order, weight, P,
+                              topk, w.rtok, w.rw, status, st));
+  ExpertParams p = gateup_params(pools, status);
+  p.unit_slot = w.unit_slot;
+  p.unit_p0 = w.unit_p0;
+  p.unit_cnt = w.unit_cnt;
+  p.num_units = w.num_units;
+  p.units_cap = w.ucap;
+  p.rtok = w.rtok;
+  p.bsrc = w.x16;
+  p.h_out = w.h16;
+  MIMO_TRY(tiles(p, 2, sms, st));
+  ExpertParams q = down_params(p, pools);
+  q.ypair_out = w.ypair;
+  MIMO_TRY(tiles(q, 3, sms, st));
+  MIMO_TRY(launch_combine_prefill(w.ypair, w.inv, weight, T, topk, H, y, st));
+  return MIMO_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mimo_moe_version(void) { return MIMO_MOE_VERSION; }
+
+const char* mimo_moe_strerror(int code) {
+  switch (code) {
+    case MIMO_OK: return "ok";
+    case MIMO_EINVAL: return "invalid argument (shape, null pointer or workspace too small)";
+    case MIMO_ERANGE: return "value out of range (expert id, rows per expert, or activation beyond f16)";
+    case MIMO_ETIMEOUT: return "bounded device wait expired";
+    case MIMO_ECUDA: return "CUDA error";
+    default: return "unknown error";
+  }
+}
+
+int mimo_moe_last_cuda_error(void) { return g_last_cuda_error; }
+
+int mimo_moe_router(const uint16_t* x, const uint16_t* w, const float* bias, int32_t T, int32_t H,
+                    int32_t E, int32_t topk, float* logits, int32_t* idx, float* weight, void* stream) {
+  if (!x || !w || !logits || !idx || !weight || T < 1 || H < 256 || H % 256 || E < 32 || E > 256 ||
+      E % 32 || topk < 1 || topk > 8 || topk > E)
+    return MIMO_EINVAL;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MIMO_TRY(launch_router_logits(x, w, logits, T, H, E, st));
+  MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, weight, st));
+  return MIMO_OK;
+}
+
+int mimo_moe_topk(const float* logits, const float* bias, int32_t T, int32_t E, int32_t topk,
+                  int32_t* idx, float* weight, void* stream) {
+  if (!logits || !idx || !weight || T < 1 || E < 32 || E > 256 || E % 32 || topk < 1 || topk > 8 ||
+      topk > E)
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, weight, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_group_routes(const int32_t* idx, const float* weight, int32_t M, int32_t topk, int32_t R,
+                          int32_t E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                          int32_t* gather_idx, int32_t* num_unique, int32_t* status, void* stream) {
+  if (!idx || !weight || !uids || !urows || !ucnt || !uw || !gather_idx || !num_unique || M < 1 ||
+      topk < 1 || R < 1 || E < 1 || E > 1024 || (int64_t)M * topk > 1024)
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_group_routes(idx, weight, M, topk, R, E, uids, urows, ucnt, uw, gather_idx, num_unique,
+                               status, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+size_t mimo_moe_dispatch_workspace_bytes(int32_t T, int32_t topk, int32_t E) {
+  if (T < 1 || topk < 1 || E < 1) return 0;
+  return dispatch_workspace_bytes(T * topk, E);
+}
+
+int mimo_moe_dispatch(const int32_t* idx, int32_t T, int32_t topk, int32_t E, int32_t* offsets,
+                      int32_t* order, int32_t* inv, void* workspace, size_t workspace_bytes,
+                      int32_t* status, void* stream) {
+  if (!idx || !offsets || !order || !inv || !workspace || T < 1 || topk < 1 || E < 1 || E > 1024 ||
+      (int64_t)T * topk > (1 << 30))
+    return MIMO_EINVAL;
+  if (workspace_bytes < dispatch_workspace_bytes(T * topk, E)) return MIMO_EINVAL;
+  MIMO_TRY(launch_dispatch(idx, T * topk, E, offsets, order, inv, workspace, status,
+                           static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+size_t mimo_moe_experts_workspace_bytes(int32_t M, int32_t U, int32_t R, int32_t H, int32_t I) {
+  if (M < 1 || U < 1 || R < 1) return 0;
+  Carver c(nullptr);
+  carve_decode(c, M, U, R, H, I);
+  return c.off;
+}
+
+int mimo_moe_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,
+                     const int32_t* urows, const int32_t* ucnt, const float* uw,
+                     const int32_t* num_unique, int32_t U, int32_t R, const int32_t* gather_idx,
+                     int32_t topk, int32_t M, int32_t pairs_rounding, uint16_t* y, void* workspace,
+                     size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!x || !pools_ok(pools) || !uslot || !urows || !ucnt || !uw || !y || !workspace || U < 1 ||
+      R < 1 || R > 8 || M < 1 || M > 128 || (gather_idx && (topk < 1 || topk > 64)))
+    return MIMO_EINVAL;
+  Carver c(workspace);
+  const DecodeWs w = carve_decode(c, M, U, R, pools->hidden, pools->inter);
+  if (c.off > workspace_bytes) return MIMO_EINVAL;
+  return run_experts(x, pools, uslot, urows, ucnt, uw, num_unique, U, R, gather_idx, topk, M,
+                     pairs_rounding, y, w, status, static_cast<cudaStream_t>(stream));
+}
+
+size_t mimo_moe_prefill_workspace_bytes(int32_t T, int32_t topk, int32_t H, int32_t I, int32_t E) {
+  if (T < 1 || topk < 1 || E < 1) return 0;
+  Carver c(nullptr);
+  carve_prefill(c, T, topk, H, I, E);
+  return c.off;
+}
+
+int mimo_moe_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* slot_of, int32_t E,
+                     const int32_t* idx, const float* weight, int32_t T, int32_t topk, uint16_t* y,
+                     void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!x || !pools_ok(pools) || !idx || !weight || !y || !workspace || T < 1 || topk < 1 || topk > 64 ||
+      (int64_t)T * topk > (1 << 26) || E < 1 || E > 1024 || (!slot_of && E != pools->num_slots))
+    return MIMO_EINVAL;
+  Carver c(workspace);
+  const PrefillWs w = carve_prefill(c, T, topk, pools->hidden, pools->inter, E);
+  if (c.off > workspace_bytes) return MIMO_EINVAL;
+  return run_prefill(x, pools, slot_of, idx, weight, T, topk, E, y, w, status,
+                     static_cast<cudaStream_t>(stream));
+}
+
+size_t mimo_moe_block_workspace_bytes(int32_t T, int32_t H, int32_t I, int32_t E, int32_t topk) {
+  if (T < 1 || topk < 1 || E < 1) return 0;
+  Carver c(nullptr);
+  c.take<float>((size_t)T * E);
+  c.take<int32_t>((size_t)T * topk);
+  c.take<float>((size_t)T * topk);
+  if (T <= 8) {
+    const GroupWs g = carve_group(c, T, topk, 8, E);
+    carve_decode(c, T, g.ucap, 8, H, I);
+  } else {
+    carve_prefill(c, T, topk, H, I, E);
+  }
+  return c.off;
+}
+
+int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bias,
+                   const mimo_moe_pools* pools, int32_t T, int32_t topk, uint16_t* y, int32_t* idx_out,
+                   float* w_out, void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!x || !router_w || !pools_ok(pools) || !y || !workspace || T < 1 || topk < 1 || topk > 8 ||
+      (int64_t)T * topk > (1 << 26))
+    return MIMO_EINVAL;
+  const int E = pools->num_slots, H = pools->hidden, I = pools->inter;
+  if (E < 32 || E > 256 || E % 32 || topk > E) return MIMO_EINVAL;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  float* logits = c.take<float>((size_t)T * E);
+  int32_t* idx = c.take<int32_t>((size_t)T * topk);
+  float* wts = c.take<float>((size_t)T * topk);
+  if (idx_out) idx = idx_out;
+  if (w_out) wts = w_out;
+  if (T <= 8) {
+    const GroupWs g = carve_group(c, T, topk, 8, E);
+    const DecodeWs dw = carve_decode(c, T, g.ucap, 8, H, I);
+    if (c.off > workspace_bytes) return MIMO_EINVAL;
+    MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st));
+    MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, wts, st));
+    MIMO_TRY(launch_group_routes(idx, wts, T, topk, 8, E, g.uids, g.urows, g.ucnt, g.uw, g.gidx, g.nu,
+                                 status, st));
+    return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
+                       T == 1 ? 1 : 0, y, dw, status, st);
+  }
+  const PrefillWs pw = carve_prefill(c, T, topk, H, I, E);
+  if (c.off > workspace_bytes) return MIMO_EINVAL;
+  MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st));
+  MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, wts, st));
+  return run_prefill(x, pools, nullptr, idx, wts, T, topk, E, y, pw, status, st);
+}
+
+int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up_w, uint8_t* up_s,
+                                 uint32_t* down_w, uint8_t* down_s, int32_t S, int32_t H, int32_t I,
+                                 uint64_t seed, int32_t layer, int32_t first_expert, void* stream) {
+  if (!gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || S < 1 || H < 256 || I < 256 ||
+      H % 256 || I % 256 || layer < 0 || first_expert < 0)
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_fill_synthetic(gate_w, gate_s, up_w, up_s, down_w, down_s, S, H, I, seed, layer,
+                                 first_expert, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_profile_enable(int32_t capacity) {
+  if (capacity < 0) return MIMO_EINVAL;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  while (g_prof_pool.size() < (size_t)capacity) {
+    ProfRec r{0, nullptr, nullptr};
+    MIMO_TRY(cudaEventCreate(&r.a));
+    MIMO_TRY(cudaEventCreate(&r.b));
+    g_prof_pool.push_back(r);
+  }
+  g_prof_cap = capacity;
+  g_prof_used = 0;
+  return MIMO_OK;
+}
+
+int mimo_moe_profile_read(int32_t* launches, float* milliseconds) {
+  if (!launches || !milliseconds) return MIMO_EINVAL;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (int k = 0; k < 4; ++k) {
+    launches[k] = 0;
+    milliseconds[k] = 0.f;
+  }
+  for (size_t i = 0; i < g_prof_used; ++i) {
+    const ProfRec& r = g_prof_pool[i];
+    MIMO_TRY(cudaEventSynchronize(r.b));
+    float ms = 0.f;
+    MIMO_TRY(cudaEventElapsedTime(&ms, r.a, r.b));
+    launches[r.kind] += 1;
+    milliseconds[r.kind] += ms;
+  }
+  g_prof_used = 0;
+  return MIMO_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,65 @@
+// Internal launch interface between the C ABI (api.cu) and the kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstddef>
+#include <cstdint>
+
+namespace mimo {
+
+// Parameters of the expert tile kernel (see experts.cu).
+struct ExpertParams {
+  const uint8_t* w[2];  // packed e2m1 bytes of matrix m: [S][N][K/2]
+  const uint8_t* s[2];  // e8m0 scales of matrix m: [S][N][K/32]
+  int S, N, K, tiles;   // tiles = N / 16
+  // work units: (pool slot, first route position p0, route count)
+  const int32_t* unit_slot;
+  const int32_t* unit_p0;  // null: p0 = unit * p0_stride
+  const int32_t* unit_cnt;
+  int p0_stride;
+  const int32_t* num_units;  // device count, null: units_cap
+  int units_cap;
+  // B operand: row(route p) = rtok ? rtok[p] : p; values bsrc[row * K + k] (f16)
+  const int32_t* rtok;
+  const __half* bsrc;
+  const float* rw;  // route weights (down, decode)
+  // outputs (one per mode)
+  __half* h_out;        // gate/up: SwiGLU output [P][N] (f16 copy of the bf16 value)
+  float* part_out;      // down, decode: [P][N] float32 = dot * weight
+  uint16_t* ypair_out;  // down, prefill: [P][N] bf16(dot)
+  int pairs_rounding;
+  int32_t* status;
+};
+
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* logits, int T, int H,
+                                 int E, cudaStream_t st);
+cudaError_t launch_router_topk(const float* logits, const float* bias, int T, int E, int topk,
+                               int32_t* idx, float* weight, cudaStream_t st);
+cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,
+                                int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                                int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);
+size_t dispatch_workspace_bytes(int P, int E);
+cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* order,
+                            int32_t* inv, void* ws, int32_t* status, cudaStream_t st);
+cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, int E, int S,
+                               int unit_max, int ucap, int32_t* unit_slot, int32_t* unit_p0,
+                               int32_t* unit_cnt, int32_t* num_units, const int32_t* order,
+                               const float* weight, int P, int topk, int32_t* rtok, float* rw,
+                               int32_t* status, cudaStream_t st);
+cudaError_t launch_to_f16(const uint16_t* x, __half* y, size_t n, int32_t* status, cudaStream_t st);
+// kind: 0 decode gate/up, 1 decode down, 2 prefill gate/up, 3 prefill down
+cudaError_t launch_expert_tiles(const ExpertParams& p, int kind, int num_sms, cudaStream_t st);
+cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const int32_t* urows,
+                                  const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
+                                  int M, int topk, int H, uint16_t* y, cudaStream_t st);
+cudaError_t launch_combine_prefill(const uint16_t* ypair, const int32_t* inv, const float* w, int T,
+                                   int topk, int H, uint16_t* y, cudaStream_t st);
+cudaError_t launch_fill_synthetic(uint32_t* gw, uint8_t* gs, uint32_t* uw, uint8_t* us, uint32_t* dw,
+                                  uint8_t* ds, int S, int H, int I, uint64_t seed, int layer,
+                                  int first_expert, cudaStream_t st);
+
+constexpr int kPrefillUnit = 64;  // routes per prefill work unit (8 token blocks of 8)
+
+}  // namespace mimo

@@ -1,0 +1,12 @@
+"""B200-native (sm_100a) MiMo MoE block: router -> dispatch -> MXFP4 expert products -> combine.
+
+Drop-in for the expert path of cialanjcampbell-coder/mimo-on-a-mac's engine/mimo_stream
+(Router, group_routes, moe_experts, the gather_qmm pair path).  All compute runs in hand-written CUDA
+(libmimo_moe.so, C ABI in include/mimo_moe.h); there is no CPU fallback."""
+from ._lib import LIB_PATH, MimoError, lib
+from .ops import (ExpertPools, Groups, MoEBlock, MoEConfig, Router, dispatch, group_routes, moe_block,
+                  moe_experts, moe_prefill, read_status, router, topk)
+
+__all__ = ["LIB_PATH", "MimoError", "lib", "ExpertPools", "Groups", "MoEBlock", "MoEConfig", "Router",
+           "dispatch", "group_routes", "moe_block", "moe_experts", "moe_prefill", "read_status", "router",
+           "topk"]

@@ -1,0 +1,88 @@
+"""ctypes binding of libmimo_moe.so (the C ABI in include/mimo_moe.h).
+
+There is no CPU fallback: if the library is missing or cannot be loaded, every op raises."""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_int32, c_size_t, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libmimo_moe.so")
+
+MIMO_OK, MIMO_EINVAL, MIMO_ERANGE, MIMO_ETIMEOUT, MIMO_ECUDA = 0, 1, 2, 3, 4
+
+
+class Pools(ctypes.Structure):
+    """struct mimo_moe_pools."""
+    _fields_ = [("gate_w", c_void_p), ("gate_s", c_void_p), ("up_w", c_void_p), ("up_s", c_void_p),
+                ("down_w", c_void_p), ("down_s", c_void_p), ("num_slots", c_int32),
+                ("hidden", c_int32), ("inter", c_int32)]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "mimo_moe_version": (c_int32, []),
+    "mimo_moe_strerror": (ctypes.c_char_p, [c_int32]),
+    "mimo_moe_last_cuda_error": (c_int32, []),
+    "mimo_moe_router": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                  c_void_p, c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_topk": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                c_void_p]),
+    "mimo_moe_group_routes": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_void_p]),
+    "mimo_moe_dispatch_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "mimo_moe_dispatch": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_experts_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "mimo_moe_experts": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_void_p, c_void_p, c_void_p,
+                                   c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_int32,
+                                   c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "mimo_moe_prefill": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_int32, c_void_p, c_void_p,
+                                   c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_block_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "mimo_moe_block": (c_int32, [c_void_p, c_void_p, c_void_p, POINTER(Pools), c_int32, c_int32,
+                                 c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_profile_enable": (c_int32, [c_int32]),
+    "mimo_moe_profile_read": (c_int32, [c_void_p, c_void_p]),
+    "mimo_moe_fill_synthetic_pool": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                               c_void_p, c_int32, c_int32, c_int32, c_uint64, c_int32,
+                                               c_int32, c_void_p]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the CUDA library (raises RuntimeError when it is absent: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"mimo_moe: CUDA library not built ({LIB_PATH}); run "
+                               "`python mimo-on-a-mac_b200/mimo_moe/build.py` or __graft_entry__.build()")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+class MimoError(RuntimeError):
+    def __init__(self, code: int, where: str):
+        L = lib()
+        msg = L.mimo_moe_strerror(code).decode()
+        if code == MIMO_ECUDA:
+            msg += f" (cudaError {L.mimo_moe_last_cuda_error()})"
+        super().__init__(f"{where}: {msg}")
+        self.code = code
+
+
+def check(code: int, where: str) -> None:
+    if code == MIMO_OK:
+        return
+    if code == MIMO_EINVAL:
+        raise ValueError(f"{where}: {lib().mimo_moe_strerror(code).decode()}")
+    raise MimoError(code, where)
