@@ -249,3 +249,20 @@ def test_moe_block_end_to_end(gpu, T):
     _, ri, _ = O.router(x.float().numpy(), W.float().numpy(), bias.numpy())
     assert (np.sort(idx_np, 1) == np.sort(ri, 1)).mean() > 0.99
     assert O.rel_err(f32(y), O.moe_layer(x.float().numpy(), opool, idx_np, w_np)) <= TOL_ORACLE
+
+
+def test_matches_reference_kernel_golden_outputs(gpu):
+    """The CUDA path against outputs of the reference's own kernels A/B (tests/golden/kernels_full.npz,
+    made by tests/golden/make_golden.py from engine/mimo_stream/kernels.py:33-123 run on the CPU)."""
+    import mimo_moe
+    from pathlib import Path
+    g = np.load(Path(__file__).resolve().parent / "golden" / "kernels_full.npz")
+    pool = mimo_moe.ExpertPools.synthetic(int(g["S"]), seed=int(g["seed"]), layer=int(g["layer"]), device=gpu)
+    for M in g["Ms"]:
+        x = torch.from_numpy(g[f"M{M}_x"].view(np.int16)).view(torch.bfloat16).to(gpu)
+        inds, sc = g[f"M{M}_inds"], g[f"M{M}_scores"]
+        gr = mimo_moe.group_routes(torch.from_numpy(inds).to(gpu), torch.from_numpy(sc).to(gpu), check_rows=True)
+        y = mimo_moe.moe_experts(x, pool, gr.uids, gr.urows, gr.ucnt, gr.uw, gather_idx=gr.gather_idx,
+                                 num_unique=gr.num_unique)
+        want = O.bf16_bits_to_f32(g[f"M{M}_y"])
+        assert O.rel_err(f32(y), want) <= TOL_ORACLE, M
