@@ -157,6 +157,8 @@ def main():
     ap.add_argument("--workload", default="decode8", choices=list(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--pool-experts", type=int, default=E,
+                    help="experts in the pool and router (small cases for profiling; default 256)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -177,9 +179,11 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     B = WORKLOADS[args.workload]
-    pool = mimo_moe.ExpertPools.synthetic(E, seed=0, layer=0, device=dev)
+    NE = args.pool_experts
+    pool = mimo_moe.ExpertPools.synthetic(NE, seed=0, layer=0, device=dev)
     xs, W = make_inputs(B, dev, torch)
-    bias = torch.zeros(E, device=dev)
+    W = W[:NE].contiguous()
+    bias = torch.zeros(NE, device=dev)
     y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     L = mimo_moe.lib()
@@ -264,10 +268,10 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "mxfp4 x f16 -> f32",
             "data": "synthetic (seeded MXFP4 pool, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
-            "config": {"workload": args.workload, "B": B, "experts": E, "hidden": H, "inter": I,
+            "config": {"workload": args.workload, "B": B, "experts": NE, "hidden": H, "inter": I,
                        "topk": K_TOP, "routing": "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
                        "parallelism": "replicas" if world > 1 else "single",
-                       "l2": "inputs > L2: routes rotate over 16 batches of a 3.42 GB pool"},
+                       "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
             "expert_gbs": expert_gbs,
             "expert_frac_of_measured_hbm": expert_gbs / hbm,
             "roofline": {"kernel": "expert_tiles_kernel<2,1,5,0> (gate/up+SwiGLU)" if B <= 8 else
