@@ -147,6 +147,24 @@ int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up
                                  uint64_t seed, int32_t layer, int32_t first_expert, void* stream);
 
 /*
+ * mimo_moe_experts with no workspace argument (no counterpart in the reference).  For callers that
+ * cannot allocate device memory when they run the block - a runtime that passes only activations and
+ * weights, a fixed preallocated arena, a process barred from cudaMalloc - the scratch lives in a
+ * fixed device array inside the library, held on every GPU that loads it until exit
+ * (mimo_moe_experts_static_scratch_bytes(), about 10 MiB).  Limits: M <= 8, U*R <= 512, H <= 4096,
+ * I <= 2048; larger sizes return MIMO_ERANGE without launching.  The first call on a device looks up
+ * the array's device address, so make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race, so issue them on one stream.  Arguments and results otherwise
+ * as mimo_moe_experts.
+ */
+size_t mimo_moe_experts_static_scratch_bytes(void);
+int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,
+                            const int32_t* urows, const int32_t* ucnt, const float* uw,
+                            const int32_t* num_unique, int32_t U, int32_t R, const int32_t* gather_idx,
+                            int32_t topk, int32_t M, int32_t pairs_rounding, uint16_t* y, int32_t* status,
+                            void* stream);
+
+/*
  * Benchmark support (no counterpart in the reference).  mimo_moe_profile_enable(n) with n > 0 makes
  * the library record a CUDA event pair around each of the next n expert-tile kernel launches on the
  * launching stream (the events are created here, once); n = 0 turns it off.  mimo_moe_profile_read()

@@ -44,6 +44,10 @@ SIGNATURES = {
     "mimo_moe_block_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "mimo_moe_block": (c_int32, [c_void_p, c_void_p, c_void_p, POINTER(Pools), c_int32, c_int32,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_experts_static_scratch_bytes": (c_size_t, []),
+    "mimo_moe_experts_static": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32,
+                                          c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "mimo_moe_profile_enable": (c_int32, [c_int32]),
     "mimo_moe_profile_read": (c_int32, [c_void_p, c_void_p]),
     "mimo_moe_fill_synthetic_pool": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
