@@ -274,7 +274,7 @@ def main():
                        "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
             "expert_gbs": expert_gbs,
             "expert_frac_of_measured_hbm": expert_gbs / hbm,
-            "roofline": {"kernel": "expert_tiles_kernel<2,1,5,0> (gate/up+SwiGLU)" if B <= 8 else
+            "roofline": {"kernel": "expert_decode_tma_kernel<2,4,0,4096> (gate/up+SwiGLU)" if B <= 8 else
                          "expert_tiles_kernel<2,8,4,0> (prefill gate/up)", "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_kind": peak_kind, "traffic": None,

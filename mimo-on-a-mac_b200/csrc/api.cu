@@ -44,7 +44,9 @@ std::vector<ProfRec> g_prof_pool;  // created once, reused
 size_t g_prof_used = 0;
 int g_prof_cap = 0;
 
-cudaError_t tiles(const ExpertParams& p, int kind, int sms, cudaStream_t st) {
+// Runs `launch` between an event pair of the profiling pool when profiling is enabled.
+template <class F>
+cudaError_t profiled(int kind, cudaStream_t st, F&& launch) {
   ProfRec* rec = nullptr;
   if (g_prof_cap > 0) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -54,9 +56,13 @@ cudaError_t tiles(const ExpertParams& p, int kind, int sms, cudaStream_t st) {
     rec->kind = kind;
     cudaEventRecord(rec->a, st);
   }
-  const cudaError_t e = launch_expert_tiles(p, kind, sms, st);
+  const cudaError_t e = launch();
   if (rec) cudaEventRecord(rec->b, st);
   return e;
+}
+
+cudaError_t tiles(const ExpertParams& p, int kind, int sms, cudaStream_t st) {
+  return profiled(kind, st, [&] { return launch_expert_tiles(p, kind, sms, st); });
 }
 
 // Bump allocator over the caller's workspace; with base == nullptr it only measures.
@@ -169,13 +175,84 @@ ExpertParams down_params(const ExpertParams& gu, const mimo_moe_pools* pools) {
   return q;
 }
 
+// Decode expert products through the TMA-fed kernels (H <= 4096, I <= 2048).
+int run_experts_tma(const mimo_moe_pools* pools, const int32_t* uslot, const int32_t* urows,
+                    const int32_t* ucnt, const float* uw, const int32_t* num_unique, int U, int R,
+                    int pairs_rounding, const DecodeWs& w, int32_t* status, cudaStream_t st) {
+  const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
+  const int sms = num_sms_current();
+  DecodeParams p{};
+  WeightMap wm;
+  MIMO_TRY(weight_map(&wm, pools->gate_w, (uint64_t)S * I, H / 2, 8));
+  p.wmap[0] = wm.map;
+  int per_panel = wm.per_panel;
+  MIMO_TRY(weight_map(&wm, pools->up_w, (uint64_t)S * I, H / 2, 8));
+  p.wmap[1] = wm.map;
+  per_panel |= wm.per_panel;
+  MIMO_TRY(scale_map(&p.smap[0], pools->gate_s, (uint64_t)S * I, H / 32, 64));
+  MIMO_TRY(scale_map(&p.smap[1], pools->up_s, (uint64_t)S * I, H / 32, 64));
+  if (per_panel) {  // keep both maps in the same (2-D) form
+    MIMO_TRY(weight_map(&wm, pools->gate_w, (uint64_t)S * I, H / 2, 1));
+    p.wmap[0] = wm.map;
+    MIMO_TRY(weight_map(&wm, pools->up_w, (uint64_t)S * I, H / 2, 1));
+    p.wmap[1] = wm.map;
+  }
+  p.per_panel = per_panel;
+  p.S = S;
+  p.N = I;
+  p.K = H;
+  p.tiles = I / 16;
+  p.unit_slot = uslot;
+  p.unit_cnt = ucnt;
+  p.p0_stride = R;
+  p.num_units = num_unique;
+  p.units_cap = U;
+  p.rtok = urows;
+  p.bsrc = w.x16;
+  p.h_out = w.h16;
+  p.status = status;
+  MIMO_TRY(profiled(0, st, [&] { return launch_decode_tma(p, 0, sms, st); }));
+  DecodeParams q{};
+  MIMO_TRY(weight_map(&wm, pools->down_w, (uint64_t)S * H, I / 2, 8));
+  q.wmap[0] = wm.map;
+  if (wm.per_panel) {
+    MIMO_TRY(weight_map(&wm, pools->down_w, (uint64_t)S * H, I / 2, 1));
+    q.wmap[0] = wm.map;
+  }
+  q.per_panel = wm.per_panel;
+  MIMO_TRY(scale_map(&q.smap[0], pools->down_s, (uint64_t)S * H, I / 32, 64));
+  q.S = S;
+  q.N = H;
+  q.K = I;
+  q.tiles = H / 16;
+  q.unit_slot = uslot;
+  q.unit_cnt = ucnt;
+  q.p0_stride = R;
+  q.num_units = num_unique;
+  q.units_cap = U;
+  q.rtok = nullptr;
+  q.bsrc = w.h16;
+  q.rw = uw;
+  q.part_out = w.part;
+  q.pairs_rounding = pairs_rounding;
+  q.status = status;
+  MIMO_TRY(profiled(1, st, [&] { return launch_decode_tma(q, 1, sms, st); }));
+  return MIMO_OK;
+}
+
 int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,
                 const int32_t* urows, const int32_t* ucnt, const float* uw, const int32_t* num_unique,
                 int U, int R, const int32_t* gidx, int topk, int M, int pairs_rounding, uint16_t* y,
-                const DecodeWs& w, int32_t* status, cudaStream_t st) {
+                const DecodeWs& w, int32_t* status, cudaStream_t st, bool x16_ready = false) {
   const int H = pools->hidden;
   const int sms = num_sms_current();
-  MIMO_TRY(launch_to_f16(x, w.x16, (size_t)M * H, status, st));
+  if (!x16_ready) MIMO_TRY(launch_to_f16(x, w.x16, (size_t)M * H, status, st));
+  if (pools->hidden <= 4096 && pools->inter <= 2048) {
+    const int rc = run_experts_tma(pools, uslot, urows, ucnt, uw, num_unique, U, R, pairs_rounding, w, status, st);
+    if (rc != MIMO_OK) return rc;
+    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
+    return MIMO_OK;
+  }
   ExpertParams p = gateup_params(pools, status);
   p.unit_slot = uslot;
   p.unit_p0 = nullptr;
@@ -339,7 +416,9 @@ size_t mimo_moe_block_workspace_bytes(int32_t T, int32_t H, int32_t I, int32_t E
   c.take<float>((size_t)T * E);
   c.take<int32_t>((size_t)T * topk);
   c.take<float>((size_t)T * topk);
+  c.take<int32_t>(1);
   if (T <= 8) {
+    c.take<float>((size_t)(H / 256) * T * E);
     const GroupWs g = carve_group(c, T, topk, 8, E);
     carve_decode(c, T, g.ucap, 8, H, I);
   } else {
@@ -361,18 +440,19 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
   float* logits = c.take<float>((size_t)T * E);
   int32_t* idx = c.take<int32_t>((size_t)T * topk);
   float* wts = c.take<float>((size_t)T * topk);
+  int32_t* counter = c.take<int32_t>(1);
   if (idx_out) idx = idx_out;
   if (w_out) wts = w_out;
   if (T <= 8) {
+    c.take<float>((size_t)(H / 256) * T * E);  // (kept: layout shared with the size query)
     const GroupWs g = carve_group(c, T, topk, 8, E);
     const DecodeWs dw = carve_decode(c, T, g.ucap, 8, H, I);
     if (c.off > workspace_bytes) return MIMO_EINVAL;
-    MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st));
-    MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, wts, st));
-    MIMO_TRY(launch_group_routes(idx, wts, T, topk, 8, E, g.uids, g.urows, g.ucnt, g.uw, g.gidx, g.nu,
-                                 status, st));
+    // one launch: logits, top-k, grouping and the f16 copy of x
+    MIMO_TRY(launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, counter, g.uids,
+                                 g.urows, g.ucnt, g.uw, g.gidx, g.nu, dw.x16, status, st));
     return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
-                       T == 1 ? 1 : 0, y, dw, status, st);
+                       T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/true);
   }
   const PrefillWs pw = carve_prefill(c, T, topk, H, I, E);
   if (c.off > workspace_bytes) return MIMO_EINVAL;

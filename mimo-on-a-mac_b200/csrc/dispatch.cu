@@ -2,12 +2,12 @@
 // prefill stable token->expert permutation (engine/mimo_stream/model.py:235-244, 266-268).
 #include "common.cuh"
 #include "kernels.h"
+#include "route_dev.cuh"
 
 namespace mimo {
 
 // ------------------------------------------------------------------------------ decode grouping
-// One CTA, one thread per route t (P = M*topk <= 1024).  Distinct ids come out ascending (an E-bit
-// occupancy bitmap and popcounts give each id its rank); the routes of one id keep flat (row, k) order.
+// One CTA, one thread per route t (P = M*topk <= 1024); see group_routes_cta.
 __global__ void __launch_bounds__(1024) group_routes_kernel(
     const int32_t* __restrict__ idx, const float* __restrict__ weight, int P, int topk, int R, int E,
     int ucap, int32_t* __restrict__ uids, int32_t* __restrict__ urows, int32_t* __restrict__ ucnt,
@@ -15,63 +15,8 @@ __global__ void __launch_bounds__(1024) group_routes_kernel(
     int32_t* status) {
   __shared__ uint32_t bitmap[32];  // E <= 1024
   __shared__ int32_t sid[1024];
-  const int t = threadIdx.x;
-  const int nwords = (E + 31) >> 5;
-  if (t < 32) bitmap[t] = 0u;
-  // zero-pad the outputs (the reference pads urows/uw with 0)
-  for (int i = t; i < ucap * R; i += blockDim.x) {
-    urows[i] = 0;
-    uw[i] = 0.f;
-  }
-  for (int i = t; i < ucap; i += blockDim.x) {
-    ucnt[i] = 0;
-    uids[i] = 0;
-  }
-  __syncthreads();
-  int id = -1;
-  if (t < P) {
-    id = idx[t];
-    if (id < 0 || id >= E) {
-      set_status(status, MIMO_ERANGE);
-      id = -1;
-    } else {
-      atomicOr(&bitmap[id >> 5], 1u << (id & 31));
-    }
-    sid[t] = id;
-  }
-  __syncthreads();
-  if (t < P) {
-    if (id >= 0) {
-      int u = 0;
-      for (int wv = 0; wv < (id >> 5); ++wv) u += __popc(bitmap[wv]);
-      u += __popc(bitmap[id >> 5] & ((1u << (id & 31)) - 1u));
-      int c = 0, n = 0;
-      for (int q = 0; q < P; ++q) {
-        const int same = (sid[q] == id);
-        c += (q < t) & same;
-        n += same;
-      }
-      if (c == 0) {
-        uids[u] = id;
-        ucnt[u] = min(n, R);
-      }
-      if (c >= R) {
-        set_status(status, MIMO_ERANGE);
-        gidx[t] = -1;
-      } else {
-        urows[u * R + c] = t / topk;
-        uw[u * R + c] = weight[t];
-        gidx[t] = u * R + c;
-      }
-    } else {
-      gidx[t] = -1;
-    }
-  }
-  if (t == 0) {
-    int U = 0;
-    for (int wv = 0; wv < nwords; ++wv) U += __popc(bitmap[wv]);
-    num_unique[0] = U;
-  }
+  group_routes_cta(idx, weight, P, topk, R, E, ucap, uids, urows, ucnt, uw, gidx, num_unique, status, sid,
+                   bitmap);
 }
 
 cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,

@@ -7,6 +7,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "tma.h"
+
 namespace mimo {
 
 // Parameters of the expert tile kernel (see experts.cu).
@@ -33,10 +35,38 @@ struct ExpertParams {
   int32_t* status;
 };
 
+// Parameters of the TMA-fed decode kernel (see experts.cu).  Passed as a __grid_constant__ so the
+// tensor maps stay in parameter space.
+struct DecodeParams {
+  CUtensorMap wmap[2];  // weight maps of matrix m (gate/up or down), see tma.h
+  CUtensorMap smap[2];  // scale maps
+  int per_panel;        // weight maps are 2-D (one TMA box per 128-byte panel)
+  int S, N, K, tiles;
+  const int32_t* unit_slot;
+  const int32_t* unit_cnt;
+  int p0_stride;             // unit u's routes start at u * p0_stride
+  const int32_t* num_units;  // device count, null: units_cap
+  int units_cap;
+  const int32_t* rtok;  // B row of route p (null: row p)
+  const __half* bsrc;   // B rows [*, K] f16
+  const float* rw;
+  __half* h_out;
+  float* part_out;
+  int pairs_rounding;
+  int32_t* status;
+};
+// kind 0: gate/up + SwiGLU (K <= 4096); kind 1: down x weight (K <= 2048)
+cudaError_t launch_decode_tma(const DecodeParams& p, int kind, int num_sms, cudaStream_t st);
+
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* logits, int T, int H,
                                  int E, cudaStream_t st);
 cudaError_t launch_router_topk(const float* logits, const float* bias, int T, int E, int topk,
                                int32_t* idx, float* weight, cudaStream_t st);
+cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
+                                int E, int topk, int R, float* logits, int32_t* idx, float* wts,
+                                int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                                int32_t* gidx, int32_t* num_unique, __half* x16, int32_t* status,
+                                cudaStream_t st);
 cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);

@@ -2,46 +2,48 @@
 // weights.  Follows Router.__call__ of the reference (engine/mimo_stream/model.py:58-65).
 #include "common.cuh"
 #include "kernels.h"
+#include "route_dev.cuh"
 
 namespace mimo {
 
-// logits[t, e] = sum_k f32(x[t,k]) * f32(w[e,k]).  One warp per expert row, 8 tokens per block row.
-// Each lane accumulates its 8-element chunks in order (float32 FMA), then a fixed xor-tree reduces the
-// lanes, so the result is deterministic for a given (T, H).
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
-                                                            const uint16_t* __restrict__ w,
-                                                            float* __restrict__ logits, int T, int H,
-                                                            int E) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 8 + warp;
-  const int t0 = blockIdx.y * 8;
-  if (e >= E) return;
-  const int nt = min(8, T - t0);
+// One warp: logits of expert row e for tokens [t0, t0+nt) (nt <= 8).  Lane l takes the 8-element
+// chunks c = l + 32 i in ascending i; each chunk is 8 float32 FMAs in element order; lanes are then
+// combined by a fixed xor tree.  The whole row (up to 4096 elements per pass) is loaded before use.
+__device__ __forceinline__ void logits_warp(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                            float* __restrict__ logits, int t0, int nt, int H, int E, int e) {
+  const int lane = threadIdx.x & 31;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)e * H);
   const int nchunk = H >> 3;
-  for (int c = lane; c < nchunk; c += 32) {
-    const uint4 wv = __ldg(wr + c);
-    float wf[8];
-    wf[0] = __uint_as_float(wv.x << 16); wf[1] = __uint_as_float(wv.x & 0xFFFF0000u);
-    wf[2] = __uint_as_float(wv.y << 16); wf[3] = __uint_as_float(wv.y & 0xFFFF0000u);
-    wf[4] = __uint_as_float(wv.z << 16); wf[5] = __uint_as_float(wv.z & 0xFFFF0000u);
-    wf[6] = __uint_as_float(wv.w << 16); wf[7] = __uint_as_float(wv.w & 0xFFFF0000u);
+  for (int base = 0; base < nchunk; base += 32 * 16) {
+    uint4 wv[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int c = base + lane + 32 * i;
+      wv[i] = (c < nchunk) ? __ldg(wr + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
 #pragma unroll
     for (int tt = 0; tt < 8; ++tt) {
       if (tt < nt) {
-        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H) + c);
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H);
         float a = acc[tt];
-        a = fmaf(__uint_as_float(xv.x << 16), wf[0], a);
-        a = fmaf(__uint_as_float(xv.x & 0xFFFF0000u), wf[1], a);
-        a = fmaf(__uint_as_float(xv.y << 16), wf[2], a);
-        a = fmaf(__uint_as_float(xv.y & 0xFFFF0000u), wf[3], a);
-        a = fmaf(__uint_as_float(xv.z << 16), wf[4], a);
-        a = fmaf(__uint_as_float(xv.z & 0xFFFF0000u), wf[5], a);
-        a = fmaf(__uint_as_float(xv.w << 16), wf[6], a);
-        a = fmaf(__uint_as_float(xv.w & 0xFFFF0000u), wf[7], a);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = base + lane + 32 * i;
+          if (c < nchunk) {
+            const uint4 xv = __ldg(xr + c);
+            a = fmaf(__uint_as_float(xv.x << 16), __uint_as_float(wv[i].x << 16), a);
+            a = fmaf(__uint_as_float(xv.x & 0xFFFF0000u), __uint_as_float(wv[i].x & 0xFFFF0000u), a);
+            a = fmaf(__uint_as_float(xv.y << 16), __uint_as_float(wv[i].y << 16), a);
+            a = fmaf(__uint_as_float(xv.y & 0xFFFF0000u), __uint_as_float(wv[i].y & 0xFFFF0000u), a);
+            a = fmaf(__uint_as_float(xv.z << 16), __uint_as_float(wv[i].z << 16), a);
+            a = fmaf(__uint_as_float(xv.z & 0xFFFF0000u), __uint_as_float(wv[i].z & 0xFFFF0000u), a);
+            a = fmaf(__uint_as_float(xv.w << 16), __uint_as_float(wv[i].w << 16), a);
+            a = fmaf(__uint_as_float(xv.w & 0xFFFF0000u), __uint_as_float(wv[i].w & 0xFFFF0000u), a);
+          }
+        }
         acc[tt] = a;
       }
     }
@@ -58,80 +60,105 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
     if (lane == tt && tt < nt) logits[(size_t)(t0 + tt) * E + e] = acc[tt];
 }
 
-// Selection key order: larger sel first, ties -> smaller expert id first (NaN was mapped to -inf).
-__device__ __forceinline__ bool key_better(float a, int ia, float b, int ib) {
-  if (a != b) return a > b;
-  return ia < ib;
+// logits[t, e] = sum_k f32(x[t,k]) * f32(w[e,k]): one warp per expert row, 8 tokens per block row.
+__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __restrict__ x,
+                                                            const uint16_t* __restrict__ w,
+                                                            float* __restrict__ logits, int T, int H,
+                                                            int E) {
+  const int warp = threadIdx.x >> 5;
+  const int e = blockIdx.x * 8 + warp;
+  const int t0 = blockIdx.y * 8;
+  if (e >= E) return;
+  logits_warp(x, w, logits, t0, min(8, T - t0), H, E, e);
 }
 
-// One warp per token.  s = sigmoid(logit) evaluated in double and rounded once to float32;
-// sel = s + bias (float32); top-k by the total order; w_j = s_j / (sum_j s_j + 1e-20) with the sum
-// taken in float32 in output order.
+// One warp per token (see topk_warp).
 __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits,
                                                           const float* __restrict__ bias, int T,
                                                           int E, int topk, int32_t* __restrict__ idx,
                                                           float* __restrict__ weight) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
-  constexpr int kMaxPer = 8;  // E <= 256
-  const int per = E >> 5;
-  float sv[kMaxPer], key[kMaxPer];
+  topk_warp(logits + (size_t)t * E, bias, E, topk, idx + (size_t)t * topk, weight + (size_t)t * topk);
+}
+
+// Decode (T <= 8) routing in one launch.  Logits on the tensor cores: CTA c owns router rows
+// [16c, 16c+16); its warp w multiplies them by the T tokens over the K slices w, w+16, ... (256 elements
+// each) with bf16 MMAs (exact products, float32 accumulation); the warps' partial sums are added in
+// warp order in shared memory.  The last CTA to finish (atomic ticket, no waiting) selects the top-k of
+// every token, groups the routes by distinct expert (group_routes, engine/mimo_stream/kernels.py:149-173)
+// and writes the f16 copy of x that the expert kernels read.  `counter` must be zero at launch; the
+// last CTA resets it.
+constexpr int kRouteWarps = 16;
+__global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const float* __restrict__ bias, int T,
+    int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
+    float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, int32_t* status) {
+  __shared__ float red[kRouteWarps][128];
+  __shared__ int32_t sid[64];
+  __shared__ uint32_t bitmap[32];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int e0 = blockIdx.x * 16;
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int ks = warp; ks < H / 256; ks += kRouteWarps) {
+    const int k0 = ks * 256;
+    const uint16_t* wa = w + (size_t)(e0 + g) * H + k0 + t * 8;
+    const uint16_t* wb = w + (size_t)(e0 + g + 8) * H + k0 + t * 8;
+    const uint16_t* xr = x + (size_t)(g < T ? g : 0) * H + k0 + t * 8;
+    uint4 A[8], Bm[8], X[8];
 #pragma unroll
-  for (int j = 0; j < kMaxPer; ++j) {
-    sv[j] = 0.f;
-    key[j] = -INFINITY;
-    if (j < per) {
-      const int e = lane + 32 * j;
-      const double l = (double)logits[(size_t)t * E + e];
-      const float s = (float)(1.0 / (1.0 + exp(-l)));
-      const float sel = s + (bias ? bias[e] : 0.f);
-      sv[j] = s;
-      key[j] = isnan(sel) ? -INFINITY : sel;
+    for (int kk = 0; kk < 8; ++kk) {
+      A[kk] = __ldg(reinterpret_cast<const uint4*>(wa + kk * 32));
+      Bm[kk] = __ldg(reinterpret_cast<const uint4*>(wb + kk * 32));
+      X[kk] = (g < T) ? __ldg(reinterpret_cast<const uint4*>(xr + kk * 32)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      mma_16816_bf16(d, A[kk].x, Bm[kk].x, A[kk].y, Bm[kk].y, X[kk].x, X[kk].y, d);
+      mma_16816_bf16(d, A[kk].z, Bm[kk].z, A[kk].w, Bm[kk].w, X[kk].z, X[kk].w, d);
     }
   }
-  unsigned taken = 0u;
-  float chosen_s[8];
-  int chosen_id[8];
-  for (int r = 0; r < topk; ++r) {
-    float bk = -INFINITY;
-    int bid = 0x7FFFFFFF;
-    float bs = 0.f;
+  // red[w][row*8 + tok]: row = expert within the tile, tok = token
+  red[warp][g * 8 + 2 * t] = d[0];
+  red[warp][g * 8 + 2 * t + 1] = d[1];
+  red[warp][(g + 8) * 8 + 2 * t] = d[2];
+  red[warp][(g + 8) * 8 + 2 * t + 1] = d[3];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int row = threadIdx.x >> 3, tok = threadIdx.x & 7;
+    if (tok < T) {
+      float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxPer; ++j) {
-      if (j < per && !(taken & (1u << j))) {
-        const int e = lane + 32 * j;
-        if (bid == 0x7FFFFFFF || key_better(key[j], e, bk, bid)) {
-          bk = key[j];
-          bid = e;
-          bs = sv[j];
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ok = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
-      const int oid = __shfl_xor_sync(0xFFFFFFFFu, bid, o);
-      const float os = __shfl_xor_sync(0xFFFFFFFFu, bs, o);
-      if (oid != 0x7FFFFFFF && (bid == 0x7FFFFFFF || key_better(ok, oid, bk, bid))) {
-        bk = ok;
-        bid = oid;
-        bs = os;
-      }
-    }
-    if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
-    chosen_s[r] = bs;
-    chosen_id[r] = bid;
-  }
-  float tot = 0.f;
-  for (int r = 0; r < topk; ++r) tot = __fadd_rn(tot, chosen_s[r]);
-  tot = __fadd_rn(tot, 1e-20f);
-  for (int r = 0; r < topk; ++r) {
-    if (lane == r) {
-      idx[(size_t)t * topk + r] = chosen_id[r];
-      weight[(size_t)t * topk + r] = __fdiv_rn(chosen_s[r], tot);
+      for (int ww = 0; ww < kRouteWarps; ++ww) sum += red[ww][threadIdx.x];
+      logits[(size_t)tok * E + e0 + row] = sum;
     }
   }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (warp < T) topk_warp(logits + (size_t)warp * E, bias, E, topk, idx + warp * topk, wts + warp * topk);
+  __syncthreads();
+  const int P = T * topk;
+  group_routes_cta(idx, wts, P, topk, R, E, min(E, P), uids, urows, ucnt, uw, gidx, num_unique, status,
+                   sid, bitmap);
+  for (int i = threadIdx.x * 2; i < T * H; i += blockDim.x * 2) {
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(x + i);
+    float lo = __uint_as_float(v << 16), hi = __uint_as_float(v & 0xFFFF0000u);
+    if ((fabsf(lo) > 65504.f && !isnan(lo)) || (fabsf(hi) > 65504.f && !isnan(hi))) {
+      set_status(status, MIMO_ERANGE);
+      lo = fminf(fmaxf(lo, -65504.f), 65504.f);
+      hi = fminf(fmaxf(hi, -65504.f), 65504.f);
+    }
+    *reinterpret_cast<__half2*>(x16 + i) = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
+  }
+  if (threadIdx.x == 0) *counter = 0;
 }
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* logits, int T, int H,
@@ -144,6 +171,20 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* lo
 cudaError_t launch_router_topk(const float* logits, const float* bias, int T, int E, int topk,
                                int32_t* idx, float* weight, cudaStream_t st) {
   router_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, E, topk, idx, weight);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
+                                int E, int topk, int R, float* logits, int32_t* idx, float* wts,
+                                int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                                int32_t* gidx, int32_t* num_unique, __half* x16, int32_t* status,
+                                cudaStream_t st) {
+  if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  route_decode_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, bias, T, H, E, topk, R, logits, idx, wts,
+                                                           counter, uids, urows, ucnt, uw, gidx, num_unique,
+                                                           x16, status);
   return cudaGetLastError();
 }
 
