@@ -1,6 +1,8 @@
 // C ABI of the MoE block (include/mimo_moe.h): argument checks, workspace carving, launches.
 // No allocation, no host synchronisation, no device selection: everything is stream-ordered.
+#include <cstdlib>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -87,32 +89,49 @@ bool pools_ok(const mimo_moe_pools* p) {
 }
 
 // ------------------------------------------------------------------- workspace layouts
+// Term matrices of the tcgen05 path: per unit 2 * routes rows of e4m3 terms + ue8m0 block scales.
+struct TermWs {
+  uint8_t *bq, *bs, *hq, *hs;
+};
+TermWs carve_terms(Carver& c, int units, int routes, int H, int I) {
+  const size_t rows = (size_t)units * 2 * routes;
+  TermWs t;
+  t.bq = c.take<uint8_t>(rows * H);
+  t.bs = c.take<uint8_t>(rows * (H / 32));
+  t.hq = c.take<uint8_t>(rows * I);
+  t.hs = c.take<uint8_t>(rows * (I / 32));
+  return t;
+}
+
 struct DecodeWs {
   __half* x16;
   __half* h16;
   float* part;
+  TermWs t;
 };
 DecodeWs carve_decode(Carver& c, int M, int U, int R, int H, int I) {
   DecodeWs w;
   w.x16 = c.take<__half>((size_t)M * H);
   w.h16 = c.take<__half>((size_t)U * R * I);
   w.part = c.take<float>((size_t)U * R * H);
+  w.t = carve_terms(c, U, kTcDecodeRoutes, H, I);
   return w;
 }
 
 struct PrefillWs {
   __half* x16;
-  int32_t *offsets, *order, *inv, *unit_slot, *unit_p0, *unit_cnt, *num_units, *rtok;
+  int32_t *offsets, *order, *inv, *unit_slot, *unit_p0, *unit_cnt, *unit_first, *unit_nsub, *num_units, *rtok;
   float* rw;
   void* dws;
   __half* h16;
   uint16_t* ypair;
   int ucap;
+  TermWs t;
 };
 PrefillWs carve_prefill(Carver& c, int T, int topk, int H, int I, int E) {
   PrefillWs w;
   const int P = T * topk;
-  w.ucap = P / kPrefillUnit + E;
+  w.ucap = P / std::min(kPrefillUnit, kTcPrefillRoutes) + E;
   w.x16 = c.take<__half>((size_t)T * H);
   w.offsets = c.take<int32_t>(E + 1);
   w.order = c.take<int32_t>(P);
@@ -121,11 +140,14 @@ PrefillWs carve_prefill(Carver& c, int T, int topk, int H, int I, int E) {
   w.unit_slot = c.take<int32_t>(w.ucap);
   w.unit_p0 = c.take<int32_t>(w.ucap);
   w.unit_cnt = c.take<int32_t>(w.ucap);
+  w.unit_first = c.take<int32_t>(w.ucap);
+  w.unit_nsub = c.take<int32_t>(w.ucap);
   w.num_units = c.take<int32_t>(1);
   w.rtok = c.take<int32_t>(P);
   w.rw = c.take<float>(P);
   w.h16 = c.take<__half>((size_t)P * I);
   w.ypair = c.take<uint16_t>((size_t)P * H);
+  w.t = carve_terms(c, w.ucap, kTcPrefillRoutes, H, I);
   return w;
 }
 
@@ -173,6 +195,87 @@ ExpertParams down_params(const ExpertParams& gu, const mimo_moe_pools* pools) {
   q.bsrc = gu.h_out;
   q.h_out = nullptr;
   return q;
+}
+
+// The tcgen05 block-scaled path needs 32-byte aligned weight pools (TMA 16U4_ALIGN16B rule) and
+// 16-byte aligned scale pools (TMA base rule); MIMO_MOE_EXPERT_PATH=cuda-core selects the mma.sync kernels instead
+// (a comparison knob: both are complete CUDA implementations of the same products).
+bool tc_path(const mimo_moe_pools* pools) {
+  static const bool forced_off = [] {
+    const char* e = getenv("MIMO_MOE_EXPERT_PATH");
+    return e && std::string(e) == "cuda-core";
+  }();
+  auto al = [](const void* q, uintptr_t a) { return ((uintptr_t)q & (a - 1)) == 0; };
+  return !forced_off && al(pools->gate_w, 32) && al(pools->up_w, 32) && al(pools->down_w, 32) &&
+         al(pools->gate_s, 16) && al(pools->up_s, 16) && al(pools->down_s, 16);
+}
+
+// Gate/up + SwiGLU and down over units of up to `routes` routes, on the tensor cores.
+// Decode (routes 8): unit u's routes start at u * R, B rows come from rtok = urows, the down pass
+// writes part = dot * weight.  Prefill (routes 32): units from build_units, down writes ypair.
+int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int32_t* uslot,
+           const int32_t* ucnt, const int32_t* up0, int p0_stride, const int32_t* ufirst,
+           const int32_t* unsub, const int32_t* rtok, const float* rw,
+           const int32_t* num_units, int ucap, int pairs_rounding, const TermWs& t, float* part,
+           uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false) {
+  const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
+  const int sms = num_sms_current();
+  const int N = 2 * routes;
+  const bool decode = routes == kTcDecodeRoutes;
+  // by_token_rows = M > 0: B holds the M (<= 8) token rows once, shared by every unit (decode).
+  if (!terms_ready) {
+    if (by_token_rows) MIMO_TRY(launch_tc_split_tokens(x, by_token_rows, H, t.bq, t.bs, status, st));
+    else MIMO_TRY(launch_tc_split(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, routes, t.bq, t.bs, status, st));
+  }
+  const uint64_t brows = by_token_rows ? (uint64_t)N : (uint64_t)ucap * N;
+  TcParams p{};
+  MIMO_TRY(fp4_weight_map(&p.amap[0], pools->gate_w, (uint64_t)S * I, H));
+  MIMO_TRY(fp4_weight_map(&p.amap[1], pools->up_w, (uint64_t)S * I, H));
+  MIMO_TRY(fp4_prefetch_map(&p.pmap[0], pools->gate_w, (uint64_t)S * I, H));
+  MIMO_TRY(fp4_prefetch_map(&p.pmap[1], pools->up_w, (uint64_t)S * I, H));
+  MIMO_TRY(sf_map(&p.smap[0], pools->gate_s, (uint64_t)S * I, H / 32, 128));
+  MIMO_TRY(sf_map(&p.smap[1], pools->up_s, (uint64_t)S * I, H / 32, 128));
+  MIMO_TRY(rows_map(&p.bmap, t.bq, brows, H, N));
+  MIMO_TRY(sf_map(&p.bsmap, t.bs, brows, H / 32, N));
+  p.btok = by_token_rows ? rtok : nullptr;
+  p.S = S;
+  p.Nw = I;
+  p.K = H;
+  p.tiles = I / 128;
+  p.unit_slot = uslot;
+  p.unit_cnt = ucnt;
+  p.unit_p0 = up0;
+  p.p0_stride = p0_stride;
+  p.unit_first = ufirst;
+  p.unit_nsub = unsub;
+  p.num_units = num_units;
+  p.units_cap = ucap;
+  p.weights_once = decode ? 1 : 0;
+  p.hq = t.hq;
+  p.hs = t.hs;
+  p.status = status;
+  MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
+  TcParams q = p;
+  MIMO_TRY(fp4_weight_map(&q.amap[0], pools->down_w, (uint64_t)S * H, I));
+  q.amap[1] = q.amap[0];
+  MIMO_TRY(fp4_prefetch_map(&q.pmap[0], pools->down_w, (uint64_t)S * H, I));
+  q.pmap[1] = q.pmap[0];
+  MIMO_TRY(sf_map(&q.smap[0], pools->down_s, (uint64_t)S * H, I / 32, 128));
+  q.smap[1] = q.smap[0];
+  MIMO_TRY(rows_map(&q.bmap, t.hq, (uint64_t)ucap * N, I, N));
+  MIMO_TRY(sf_map(&q.bsmap, t.hs, (uint64_t)ucap * N, I / 32, N));
+  q.Nw = H;
+  q.K = I;
+  q.tiles = H / 128;
+  q.btok = nullptr;
+  q.hq = nullptr;
+  q.hs = nullptr;
+  q.rw = rw;
+  q.part = part;
+  q.ypair = ypair;
+  q.pairs_rounding = pairs_rounding;
+  MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
+  return MIMO_OK;
 }
 
 // Decode expert products through the TMA-fed kernels (H <= 4096, I <= 2048).
@@ -243,9 +346,18 @@ int run_experts_tma(const mimo_moe_pools* pools, const int32_t* uslot, const int
 int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,
                 const int32_t* urows, const int32_t* ucnt, const float* uw, const int32_t* num_unique,
                 int U, int R, const int32_t* gidx, int topk, int M, int pairs_rounding, uint16_t* y,
-                const DecodeWs& w, int32_t* status, cudaStream_t st, bool x16_ready = false) {
+                const DecodeWs& w, int32_t* status, cudaStream_t st, bool x16_ready = false,
+                bool terms_ready = false) {
   const int H = pools->hidden;
   const int sms = num_sms_current();
+  if (R <= kTcDecodeRoutes && tc_path(pools)) {
+    const int rc = run_tc(x, pools, kTcDecodeRoutes, uslot, ucnt, nullptr, R, nullptr, nullptr, urows, uw,
+                          num_unique, U, pairs_rounding, w.t, w.part, nullptr, status, st,
+                          M <= kTcDecodeRoutes ? M : 0, terms_ready && M <= kTcDecodeRoutes);
+    if (rc != MIMO_OK) return rc;
+    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
+    return MIMO_OK;
+  }
   if (!x16_ready) MIMO_TRY(launch_to_f16(x, w.x16, (size_t)M * H, status, st));
   if (pools->hidden <= 4096 && pools->inter <= 2048) {
     const int rc = run_experts_tma(pools, uslot, urows, ucnt, uw, num_unique, U, R, pairs_rounding, w, status, st);
@@ -279,11 +391,22 @@ int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* s
   const int H = pools->hidden;
   const int P = T * topk;
   const int sms = num_sms_current();
+  if (tc_path(pools)) {
+    MIMO_TRY(launch_dispatch(idx, P, E, w.offsets, w.order, w.inv, w.dws, status, st));
+    MIMO_TRY(launch_build_units(w.offsets, slot_of, E, pools->num_slots, kTcPrefillRoutes, w.ucap,
+                                w.unit_slot, w.unit_p0, w.unit_cnt, w.unit_first, w.unit_nsub, w.num_units,
+                                w.order, weight, P, topk, w.rtok, w.rw, status, st));
+    const int rc = run_tc(x, pools, kTcPrefillRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, w.unit_first,
+                          w.unit_nsub, w.rtok, nullptr, w.num_units, w.ucap, 0, w.t, nullptr, w.ypair, status, st);
+    if (rc != MIMO_OK) return rc;
+    MIMO_TRY(launch_combine_prefill(w.ypair, w.inv, weight, T, topk, H, y, st));
+    return MIMO_OK;
+  }
   MIMO_TRY(launch_to_f16(x, w.x16, (size_t)T * H, status, st));
   MIMO_TRY(launch_dispatch(idx, P, E, w.offsets, w.order, w.inv, w.dws, status, st));
   MIMO_TRY(launch_build_units(w.offsets, slot_of, E, pools->num_slots, kPrefillUnit, w.ucap,
-                              w.unit_slot, w.unit_p0, w.unit_cnt, w.num_units, w.order, weight, P,
-                              topk, w.rtok, w.rw, status, st));
+                              w.unit_slot, w.unit_p0, w.unit_cnt, nullptr, nullptr, w.num_units, w.order,
+                              weight, P, topk, w.rtok, w.rw, status, st));
   ExpertParams p = gateup_params(pools, status);
   p.unit_slot = w.unit_slot;
   p.unit_p0 = w.unit_p0;
@@ -448,15 +571,18 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
     const GroupWs g = carve_group(c, T, topk, 8, E);
     const DecodeWs dw = carve_decode(c, T, g.ucap, 8, H, I);
     if (c.off > workspace_bytes) return MIMO_EINVAL;
-    // one launch: logits, top-k, grouping and the f16 copy of x
+    // one launch: logits, top-k, grouping and the expert kernels' copy of x (e4m3 terms for the
+    // tensor-core path, f16 for the mma.sync path)
+    const bool tc = tc_path(pools);
     MIMO_TRY(launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, counter, g.uids,
-                                 g.urows, g.ucnt, g.uw, g.gidx, g.nu, dw.x16, status, st));
+                                 g.urows, g.ucnt, g.uw, g.gidx, g.nu, tc ? nullptr : dw.x16,
+                                 tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, status, st));
     return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
-                       T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/true);
+                       T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/!tc, /*terms_ready=*/tc);
   }
   const PrefillWs pw = carve_prefill(c, T, topk, H, I, E);
   if (c.off > workspace_bytes) return MIMO_EINVAL;
-  MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st));
+  MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st, status));
   MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, wts, st));
   return run_prefill(x, pools, nullptr, idx, wts, T, topk, E, y, pw, status, st);
 }

@@ -171,6 +171,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, 
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// L2 prefetch of a 3-D tensor-map box (no shared memory involved).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n" ::"l"(map), "r"(c0),
+               "r"(c1), "r"(c2)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_map(const void* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
 }
@@ -185,6 +191,25 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
+}
+
+// Correctly rounded bf16 sigmoid of a bf16 value (the reference's 64K-entry sigmoid table,
+// kernels.py:138-146, defined as bf16(float32(sigmoid)) of the exact sigmoid).  Fast float path;
+// when the float result sits within a few ulp of a bf16 rounding tie, recompute in double.
+__device__ __forceinline__ float sigmoid_bf16(float xb) {
+  const float s = 1.0f / (1.0f + expf(-xb));
+  const uint32_t lo = __float_as_uint(s) & 0xFFFFu;
+  float sr = s;
+  if (lo > 0x7FF0u && lo < 0x8010u) sr = (float)(1.0 / (1.0 + exp(-(double)xb)));
+  return bf16_round(sr);
+}
+
+// Kernel A epilogue: gt = bf16(g), ut = bf16(u), h = bf16(bf16(gt * sig(gt)) * ut)  (kernels.py:79-82)
+__device__ __forceinline__ float swiglu_ref(float g, float u) {
+  const float gt = bf16_round(g);
+  const float ut = bf16_round(u);
+  const float gs = bf16_round(gt * sigmoid_bf16(gt));
+  return bf16_round(gs * ut);
 }
 
 }  // namespace mimo

@@ -159,7 +159,8 @@ cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, 
 __global__ void __launch_bounds__(1024) build_units_kernel(
     const int32_t* __restrict__ offsets, const int32_t* __restrict__ slot_of, int E, int S,
     int unit_max, int ucap, int32_t* __restrict__ unit_slot, int32_t* __restrict__ unit_p0,
-    int32_t* __restrict__ unit_cnt, int32_t* __restrict__ num_units, int32_t* status) {
+    int32_t* __restrict__ unit_cnt, int32_t* __restrict__ unit_first, int32_t* __restrict__ unit_nsub,
+    int32_t* __restrict__ num_units, int32_t* status) {
   __shared__ int32_t nu[1024];
   const int e = threadIdx.x;
   int n = 0, c = 0, o0 = 0;
@@ -187,6 +188,10 @@ __global__ void __launch_bounds__(1024) build_units_kernel(
       unit_slot[first + g] = slot;
       unit_p0[first + g] = o0 + g * unit_max;
       unit_cnt[first + g] = min(unit_max, c - g * unit_max);
+      if (unit_first) {  // groups cut by ucap keep only their stored units
+        unit_first[first + g] = first;
+        unit_nsub[first + g] = min(n, ucap - first);
+      }
     }
   }
   if (e == 1023) num_units[0] = min(nu[1023], ucap);
@@ -206,11 +211,12 @@ __global__ void route_rows_kernel(const int32_t* __restrict__ order, const float
 
 cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, int E, int S,
                                int unit_max, int ucap, int32_t* unit_slot, int32_t* unit_p0,
-                               int32_t* unit_cnt, int32_t* num_units, const int32_t* order,
+                               int32_t* unit_cnt, int32_t* unit_first, int32_t* unit_nsub,
+                               int32_t* num_units, const int32_t* order,
                                const float* weight, int P, int topk, int32_t* rtok, float* rw,
                                int32_t* status, cudaStream_t st) {
   build_units_kernel<<<1, 1024, 0, st>>>(offsets, slot_of, E, S, unit_max, ucap, unit_slot, unit_p0,
-                                         unit_cnt, num_units, status);
+                                         unit_cnt, unit_first, unit_nsub, num_units, status);
   route_rows_kernel<<<(P + 255) / 256, 256, 0, st>>>(order, weight, offsets, E, P, topk, rtok, rw);
   return cudaGetLastError();
 }

@@ -49,25 +49,6 @@ constexpr int smem_bytes() {
   return kBarBytes + NSTAGE * stage_bytes<NM, TB, KC>() + kCW * NM * TB * 128 * 4;
 }
 
-// Correctly rounded bf16 sigmoid of a bf16 value (the reference's 64K-entry sigmoid table,
-// kernels.py:138-146, defined as bf16(float32(sigmoid)) of the exact sigmoid).  Fast float path;
-// when the float result sits within a few ulp of a bf16 rounding tie, recompute in double.
-__device__ __forceinline__ float sigmoid_bf16(float xb) {
-  const float s = 1.0f / (1.0f + expf(-xb));
-  const uint32_t lo = __float_as_uint(s) & 0xFFFFu;
-  float sr = s;
-  if (lo > 0x7FF0u && lo < 0x8010u) sr = (float)(1.0 / (1.0 + exp(-(double)xb)));
-  return bf16_round(sr);
-}
-
-// Kernel A epilogue: gt = bf16(g), ut = bf16(u), h = bf16(bf16(gt * sig(gt)) * ut)  (kernels.py:79-82)
-__device__ __forceinline__ float swiglu_ref(float g, float u) {
-  const float gt = bf16_round(g);
-  const float ut = bf16_round(u);
-  const float gs = bf16_round(gt * sigmoid_bf16(gt));
-  return bf16_round(gs * ut);
-}
-
 __device__ __forceinline__ __half to_f16_checked(float v, int32_t* status) {
   if (fabsf(v) > 65504.f && !isnan(v)) {
     set_status(status, MIMO_ERANGE);

@@ -58,15 +58,59 @@ struct DecodeParams {
 // kind 0: gate/up + SwiGLU (K <= 4096); kind 1: down x weight (K <= 2048)
 cudaError_t launch_decode_tma(const DecodeParams& p, int kind, int num_sms, cudaStream_t st);
 
+// Parameters of the tcgen05 block-scaled expert kernel (see tc_experts.cu).  Unit u's activation
+// terms are rows [u * 2 * ntok, (u + 1) * 2 * ntok) of the term matrix: rows q < ntok hold the first
+// e4m3 term of route q, rows ntok + q the second.
+struct TcParams {
+  CUtensorMap amap[2];   // weights of matrix m, 16U4_ALIGN16B, box [128 values, 128 rows], 128B swizzle
+  CUtensorMap smap[2];   // e8m0 scales of matrix m [S * Nw][K / 32], box [16 B, 128 rows]
+  CUtensorMap bmap;      // activation terms [units * 2 * ntok][K] e4m3, box [128 B, 2 * ntok rows]
+  CUtensorMap bsmap;     // their ue8m0 scales [units * 2 * ntok][K / 32], box [16 B, 2 * ntok rows]
+  CUtensorMap pmap[2];   // L2 prefetch view of the weights: [K / 128 chunks][rows][128 values], box 8 chunks
+  int S, Nw, K, tiles;   // Nw: weight rows (output features) per expert; tiles = Nw / 128
+  const int32_t* unit_slot;
+  const int32_t* unit_cnt;
+  const int32_t* unit_p0;     // null: p0 = unit * p0_stride
+  int p0_stride;
+  const int32_t* btok;        // non-null: B rows are token rows (hi t, lo ntok + t) shared by every unit,
+                              // and route q of a unit reads column btok[p0 + q]; null: B rows per route
+  const int32_t* unit_first;  // first unit of the unit's expert group (null: one unit per group)
+  const int32_t* unit_nsub;   // units in that group
+  const int32_t* num_units;   // device count, null: units_cap
+  int units_cap;
+  int weights_once;           // weights are read once per call: stream them with L2 evict-first
+  const float* rw;            // route weights (down, decode)
+  uint8_t* hq;                // gate/up: h terms [units * 2 * ntok][Nw] e4m3
+  uint8_t* hs;                // gate/up: h term scales [units * 2 * ntok][Nw / 32]
+  float* part;                // down, decode: [P][Nw] = dot * weight
+  uint16_t* ypair;            // down, prefill: [P][Nw] bf16(dot)
+  int pairs_rounding;
+  int32_t* status;
+};
+// kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (32 routes per
+// unit), 3: prefill down.
+cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
+// Splits bf16 activation rows into the two e4m3 terms + ue8m0 scales of each unit's routes.
+cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
+                            int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
+                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st);
+// Splits token rows x[t] (t < T <= 8) into terms at rows t (hi) and 8 + t (lo) of bq/bs.
+cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
+                                   cudaStream_t st);
+constexpr int kTcDecodeRoutes = 8;   // routes per decode unit on the tcgen05 path
+constexpr int kTcPrefillRoutes = 32; // routes per prefill unit on the tcgen05 path
+
+// T > 8: tcgen05 GEMM (128 x 64 tiles; an expired wait sets MIMO_ETIMEOUT in `status` when given);
+// T <= 8 or unaligned operands: one warp per expert row.
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* logits, int T, int H,
-                                 int E, cudaStream_t st);
+                                 int E, cudaStream_t st, int32_t* status = nullptr);
 cudaError_t launch_router_topk(const float* logits, const float* bias, int T, int E, int topk,
                                int32_t* idx, float* weight, cudaStream_t st);
 cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
-                                int32_t* gidx, int32_t* num_unique, __half* x16, int32_t* status,
-                                cudaStream_t st);
+                                int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
+                                int32_t* status, cudaStream_t st);
 cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);
@@ -75,7 +119,8 @@ cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, 
                             int32_t* inv, void* ws, int32_t* status, cudaStream_t st);
 cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, int E, int S,
                                int unit_max, int ucap, int32_t* unit_slot, int32_t* unit_p0,
-                               int32_t* unit_cnt, int32_t* num_units, const int32_t* order,
+                               int32_t* unit_cnt, int32_t* unit_first, int32_t* unit_nsub,
+                               int32_t* num_units, const int32_t* order,
                                const float* weight, int P, int topk, int32_t* rtok, float* rw,
                                int32_t* status, cudaStream_t st);
 cudaError_t launch_to_f16(const uint16_t* x, __half* y, size_t n, int32_t* status, cudaStream_t st);

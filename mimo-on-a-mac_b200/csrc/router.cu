@@ -1,8 +1,11 @@
 // Router: FP32 logits GEMV/GEMM, sigmoid + noaux bias, warp top-k with a total order, normalised
 // weights.  Follows Router.__call__ of the reference (engine/mimo_stream/model.py:58-65).
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "route_dev.cuh"
+#include "tcgen05.cuh"
 
 namespace mimo {
 
@@ -88,15 +91,26 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // each) with bf16 MMAs (exact products, float32 accumulation); the warps' partial sums are added in
 // warp order in shared memory.  The last CTA to finish (atomic ticket, no waiting) selects the top-k of
 // every token, groups the routes by distinct expert (group_routes, engine/mimo_stream/kernels.py:149-173)
-// and writes the f16 copy of x that the expert kernels read.  `counter` must be zero at launch; the
-// last CTA resets it.
+// and (x16 non-null) writes the f16 copy of x that the mma.sync expert kernels read.  With xq non-null,
+// every CTA also splits its share of x into the e4m3 terms the tensor-core expert kernels read.
+// `counter` must be zero at launch; the last CTA resets it.
 constexpr int kRouteWarps = 16;
 __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const float* __restrict__ bias, int T,
     int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
     float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
-    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, int32_t* status) {
+    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
+    uint8_t* __restrict__ xs, int32_t* status) {
   __shared__ float red[kRouteWarps][128];
+  if (xq) {  // e4m3 terms of x for the tensor-core expert path: token t -> rows t (hi) and 8 + t (lo)
+    const int nb = H / 32;
+    for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < T * nb; b += gridDim.x * blockDim.x) {
+      const int t = b / nb, blk = b - t * nb;
+      tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
+                        xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
+                        xs + (size_t)(8 + t) * nb + blk, status);
+    }
+  }
   __shared__ int32_t sid[64];
   __shared__ uint32_t bitmap[32];
   __shared__ int is_last;
@@ -148,7 +162,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
   const int P = T * topk;
   group_routes_cta(idx, wts, P, topk, R, E, min(E, P), uids, urows, ucnt, uw, gidx, num_unique, status,
                    sid, bitmap);
-  for (int i = threadIdx.x * 2; i < T * H; i += blockDim.x * 2) {
+  for (int i = threadIdx.x * 2; x16 && i < T * H; i += blockDim.x * 2) {
     const uint32_t v = *reinterpret_cast<const uint32_t*>(x + i);
     float lo = __uint_as_float(v << 16), hi = __uint_as_float(v & 0xFFFF0000u);
     if ((fabsf(lo) > 65504.f && !isnan(lo)) || (fabsf(hi) > 65504.f && !isnan(hi))) {
@@ -161,8 +175,132 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
   if (threadIdx.x == 0) *counter = 0;
 }
 
+// Prefill router logits on the tensor cores: one CTA per 128-token x 64-expert tile, K = H in
+// 64-value chunks through a TMA ring; tcgen05.mma.kind::f16 multiplies bf16 x by bf16 W exactly and
+// accumulates in float32 in TMEM.  Warp 0 lane 0 issues the copies, warp 1 lane 0 the MMAs; all four
+// warps then read their 32 token rows back (tcgen05.ld) and store 64 logits per row.
+constexpr int kRtM = 128, kRtN = 64, kRtKC = 64, kRtStages = 6;
+constexpr int kRtStageBytes = (kRtM + kRtN) * kRtKC * 2;  // 24 KiB
+constexpr int kRtSmem = 1024 + 1024 + kRtStages * kRtStageBytes;
+
+struct RouterTcParams {
+  CUtensorMap xmap;  // x bf16 [T][H], box [64, 128], 128B swizzle (rows past T read as zero)
+  CUtensorMap wmap;  // W bf16 [E][H], box [64, 64], 128B swizzle
+  float* logits;
+  int T, H, E;
+  int32_t* status;  // may be null (the stand-alone router entry has no status word)
+};
+
+__global__ void __launch_bounds__(128, 1) router_tc_kernel(const __grid_constant__ RouterTcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kRtStages;
+  uint64_t* acc = empty + kRtStages;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc + 1);
+  uint8_t* stages = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + 1024) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kRtM, e0 = blockIdx.y * kRtN;
+  const int nk = p.H / kRtKC;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRtStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc, 1);
+    mbar_fence_init();
+  }
+  if (warp == 2) {
+    tc::tmem_alloc(tslot, kRtN);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tslot;
+  bool ok = true;
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&p.xmap);
+    tma_prefetch_map(&p.wmap);
+    const uint64_t pol = tc::l2_evict_normal_policy();
+    int issued = 0;
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % kRtStages;
+      if (!mbar_wait(&empty[s], (uint32_t)(((k / kRtStages) & 1) ^ 1))) {
+        ok = false;
+        break;
+      }
+      uint8_t* sb = stages + s * kRtStageBytes;
+      mbar_arrive_expect_tx(&full[s], kRtStageBytes);
+      tma_load_2d(sb, &p.xmap, k * kRtKC, m0, &full[s], pol);
+      tma_load_2d(sb + kRtM * kRtKC * 2, &p.wmap, k * kRtKC, e0, &full[s], pol);
+      ++issued;
+    }
+    for (int k = issued - 1; k >= 0 && k >= issued - kRtStages; --k)  // copies landed before exit
+      if (!mbar_wait(&full[k % kRtStages], (uint32_t)((k / kRtStages) & 1))) ok = false;
+  } else if (warp == 1 && lane == 0) {
+    const uint32_t idesc = tc::idesc_bf16(kRtM, kRtN);
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % kRtStages;
+      if (!mbar_wait(&full[s], (uint32_t)((k / kRtStages) & 1))) {
+        ok = false;
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t sa = smem_u32(stages + s * kRtStageBytes), sb = sa + kRtM * kRtKC * 2;
+#pragma unroll
+      for (int kk = 0; kk < kRtKC / 16; ++kk)
+        tc::tc_mma_f16(tbase, tc::desc_sw128(sa + kk * 32), tc::desc_sw128(sb + kk * 32), idesc, (k | kk) != 0);
+      tc::tc_commit(&empty[s]);
+    }
+    tc::tc_commit(acc);  // also drains every MMA issued before
+  }
+  if (!ok && p.status) set_status(p.status, MIMO_ETIMEOUT);
+  __syncwarp();
+  if (!mbar_wait(acc, 0)) {
+    if (lane == 0 && p.status) set_status(p.status, MIMO_ETIMEOUT);
+  } else {
+    tc::tc_fence_after();
+    const int row = m0 + warp * 32 + lane;
+#pragma unroll
+    for (int c = 0; c < kRtN; c += 16) {
+      float v[16];
+      tc::tmem_ld<16>(tbase + ((uint32_t)(warp * 32) << 16) + c, v);
+      tc::tmem_wait_ld();
+      if (row < p.T) {
+        float4* dst = reinterpret_cast<float4*>(p.logits + (size_t)row * p.E + e0 + c);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, kRtN);
+  }
+}
+
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* logits, int T, int H,
-                                 int E, cudaStream_t st) {
+                                 int E, cudaStream_t st, int32_t* status) {
+  if (T > 8 && E % kRtN == 0 && H % kRtKC == 0 && ((uintptr_t)x & 15) == 0 &&
+      ((uintptr_t)w & 15) == 0 && ((uintptr_t)logits & 15) == 0) {
+    RouterTcParams p;
+    std::memset(&p, 0, sizeof(p));
+    cudaError_t e = bf16_rows_map(&p.xmap, x, (uint64_t)T, (uint64_t)H, kRtM);
+    if (e == cudaSuccess) e = bf16_rows_map(&p.wmap, w, (uint64_t)E, (uint64_t)H, kRtN);
+    if (e == cudaSuccess) {
+      p.logits = logits;
+      p.T = T;
+      p.H = H;
+      p.E = E;
+      p.status = status;
+      e = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmem);
+      if (e != cudaSuccess) return e;
+      router_tc_kernel<<<dim3((T + kRtM - 1) / kRtM, E / kRtN), 128, kRtSmem, st>>>(p);
+      return cudaGetLastError();
+    }
+  }
   dim3 grid((E + 7) / 8, (T + 7) / 8);
   router_logits_kernel<<<grid, 256, 0, st>>>(x, w, logits, T, H, E);
   return cudaGetLastError();
@@ -177,14 +315,14 @@ cudaError_t launch_router_topk(const float* logits, const float* bias, int T, in
 cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
-                                int32_t* gidx, int32_t* num_unique, __half* x16, int32_t* status,
-                                cudaStream_t st) {
+                                int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
+                                int32_t* status, cudaStream_t st) {
   if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
   route_decode_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, bias, T, H, E, topk, R, logits, idx, wts,
                                                            counter, uids, urows, ucnt, uw, gidx, num_unique,
-                                                           x16, status);
+                                                           x16, xq, xs, status);
   return cudaGetLastError();
 }
 

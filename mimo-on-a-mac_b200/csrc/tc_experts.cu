@@ -1,0 +1,592 @@
+// MXFP4 expert products on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Weights stay in their MXFP4 form end to end: TMA copies the packed e2m1 bytes of a 128-row x
+// 128-value tile into shared memory in the padded layout the block-scaled MMA reads
+// (CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B: 8 data bytes + 8 gap bytes per 16 values, 128B swizzle),
+// and tcgen05.mma.kind::mxf8f6f4.block_scale applies the pool's e8m0 scales in hardware.
+// Activations are split into two e4m3 terms, each with one ue8m0 scale per 32 values
+// (x = hi * s1 + lo * s2; two 4-bit-significand terms carry all 8 significant bits of a bf16 value
+// unless a value is 2^9 or more below its block's largest), and enter the MMA as 2 * NTOK columns;
+// the epilogue adds the two columns of each route.
+//
+// Roles (one CTA per SM, persistent over work items = (unit, 128-row weight tile)):
+//   warp 0      TMA producer: per 128-value K chunk, the weight tiles of NM matrices and the unit's
+//               activation-term tile into a ring of NSTAGE stages; per group of 4 chunks, 16-byte
+//               wide boxes of the weight and activation scale rows into a 2-entry scale ring;
+//   warp 1      scale-factor builder: per stage, rearranges the chunk's 4 e8m0 bytes of each of the
+//               128 weight rows and of the (padded to 128) activation rows into the 512-byte block
+//               that tcgen05.cp.32x128b.warpx4 turns into the TMEM scale layout (block byte
+//               (m % 32) * 16 + (m / 32) * 4 + kb for row m, K block kb); its arrival is the second
+//               of the stage's `full` barrier, so the MMA issuer waits on one barrier per stage;
+//   warp 2      MMA issuer (one lane): tcgen05.cp of the scale blocks, 4 MMAs of K = 32 per matrix
+//               per stage into a double-buffered TMEM accumulator, one tcgen05.commit to free the stage;
+//   warp 3      TMEM allocator;
+//   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 * (w % 4) + 0..31,
+//               i.e. weight rows), then
+//               MODE 0  SwiGLU with the reference's roundings (engine/mimo_stream/kernels.py:79-82)
+//                       and the split of h into two e4m3 terms for the down pass;
+//               MODE 1  down x route weight (kernels.py:120), fp32 partials for the fixed-order
+//                       combine;
+//               MODE 2  bf16 pair outputs (engine/mimo_stream/model.py:228).
+// The producer does its per-item work (coordinates, slot, row base) once per item: at decode sizes a
+// stage lasts ~600 cycles and the single issuing threads are the critical path.
+// Every wait is bounded; an expired wait sets MIMO_ETIMEOUT and the CTA drains and returns.
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace mimo {
+namespace tc {
+
+constexpr int kM = 128;           // weight rows per tile (MMA M)
+constexpr int kKC = 128;          // K values per stage
+constexpr int kATile = kM * kKC;  // shared bytes of one padded e2m1 tile (16 KiB)
+constexpr int kAGlobal = kATile / 2;  // global (packed) bytes of one tile: the TMA transaction count
+constexpr int kThreads = 256;
+constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment slack
+
+// Ring depths of kinds 0..3 (decode gate/up, decode down, prefill gate/up, prefill down).
+#ifndef MIMO_TC_ST0
+#define MIMO_TC_ST0 6
+#endif
+#ifndef MIMO_TC_ST1
+#define MIMO_TC_ST1 11
+#endif
+#ifndef MIMO_TC_ST2
+#define MIMO_TC_ST2 5
+#endif
+#ifndef MIMO_TC_ST3
+#define MIMO_TC_ST3 8
+#endif
+#ifndef MIMO_TC_PREFETCH
+#define MIMO_TC_PREFETCH 0  // 1: L2 prefetch of the next 8 K chunks of every weight row (measured slower)
+#endif
+#ifndef MIMO_TC_WEIGHT_EVICT_FIRST
+#define MIMO_TC_WEIGHT_EVICT_FIRST 1  // decode streams each weight once: L2 evict-first
+#endif
+#ifndef MIMO_TC_SCALE_EVICT_FIRST
+#define MIMO_TC_SCALE_EVICT_FIRST 0
+#endif
+constexpr int kStages[4] = {MIMO_TC_ST0, MIMO_TC_ST1, MIMO_TC_ST2, MIMO_TC_ST3};
+
+template <int NM, int N>
+constexpr int stage_bytes() { return (NM * kATile + N * kKC + 1023) / 1024 * 1024; }
+template <int NM, int N>
+constexpr int scale_box_bytes() { return NM * kM * 16 + N * 16; }  // one 4-stage group's scale boxes
+template <int NM, int N, int NSTAGE>
+constexpr int smem_bytes() {
+  return kBarBytes + 1024 + NSTAGE * stage_bytes<NM, N>() + 2 * scale_box_bytes<NM, N>() + NSTAGE * (NM + 1) * 512;
+}
+template <int NM, int N, int NSTAGE>
+constexpr int tmem_cols_needed() { return 2 * NM * N + NSTAGE * (NM + 1) * 4; }
+template <int NM, int N, int NSTAGE>
+constexpr uint32_t tmem_cols() {
+  constexpr int n = tmem_cols_needed<NM, N, NSTAGE>();
+  return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
+}
+
+// Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (5), B e4m3 (0), ue8m0 scales,
+// both K-major, M = 128, N = n, dense K = 32; the sf ids pick the byte (K block) of each 32-bit
+// TMEM scale cell and equal the top two bits of the scale addresses.
+__device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t kb) {
+  uint32_t d = 0;
+  d |= (kb & 3u) << 4;   // B scale id
+  d |= 5u << 7;          // A format E2M1
+  d |= 0u << 10;         // B format E4M3
+  d |= (uint32_t)(n >> 3) << 17;
+  d |= 1u << 23;         // scale format UE8M0
+  d |= (uint32_t)(kM >> 4) << 24;
+  d |= (kb & 3u) << 29;  // A scale id
+  return d;
+}
+
+// Splits v into hi/lo e4m3 bytes and their block scale bytes; the 32 lanes form one block.
+__device__ __forceinline__ void split_warp_block(float v, uint32_t& hi, uint32_t& lo, uint32_t& b1, uint32_t& b2) {
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  b1 = block_scale_byte(amax);
+  hi = f32_to_e4m3(v * inv_exp2_byte(b1));
+  const float r = v - e4m3_to_f32(hi) * exp2_byte(b1);
+  float rmax = fabsf(r);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xFFFFFFFFu, rmax, o));
+  b2 = block_scale_byte(rmax);
+  lo = f32_to_e4m3(r * inv_exp2_byte(b2));
+}
+
+// ------------------------------------------------------------------------------------ kernel
+// Work item i -> (unit, weight tile).  Without groups, unit-major.  With groups (prefill: the units
+// of one expert are consecutive), the items of a group are taken tile-major, so the units of one
+// expert read each weight tile back to back and all but the first find it in L2.
+__device__ __forceinline__ void item_coords(const TcParams& p, long long i, int& unit, int& tile) {
+  const int ur = (int)(i / p.tiles);
+  if (p.unit_first) {
+    const int u0 = __ldg(p.unit_first + ur);
+    const int n = __ldg(p.unit_nsub + ur);
+    const long long j = i - (long long)u0 * p.tiles;
+    tile = (int)(j / n);
+    unit = u0 + (int)(j % n);
+  } else {
+    unit = ur;
+    tile = (int)(i % p.tiles);
+  }
+}
+
+template <int NM, int NTOK, int NSTAGE, int MODE>
+__global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_constant__ TcParams p) {
+  constexpr int N = 2 * NTOK;
+  constexpr int SB = stage_bytes<NM, N>();
+  constexpr int SCB = scale_box_bytes<NM, N>();
+  constexpr uint32_t TCOLS = tmem_cols<NM, N, NSTAGE>();
+  constexpr int QC = NTOK < 16 ? NTOK : 16;  // routes per TMEM load in the epilogue
+  static_assert(N % 16 == 0 && N <= 256 && NTOK % QC == 0, "MMA N");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NSTAGE] tiles landed + scale block written
+  uint64_t* empty = full + NSTAGE;                     // [NSTAGE] MMAs (and scale copies) of the stage done
+  uint64_t* sc_full = empty + NSTAGE;                  // [2] scale boxes of a 4-stage group landed
+  uint64_t* sc_empty = sc_full + 2;                    // [2] scale boxes read
+  uint64_t* acc_full = sc_empty + 2;                   // [2]
+  uint64_t* acc_empty = acc_full + 2;                  // [2]
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + kBarBytes) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stages = base;                                 // NSTAGE x [A tiles | B tile]
+  uint8_t* scbox = stages + NSTAGE * SB;                  // 2 x [A scale boxes | B scale box]
+  uint8_t* sfblk = scbox + 2 * SCB;                       // NSTAGE x (NM + 1) x 512 B
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
+  const long long items = (long long)units * p.tiles;
+  const long long it0 = items * blockIdx.x / gridDim.x;
+  const long long it1 = items * (blockIdx.x + 1) / gridDim.x;
+  const int nk = p.K / kKC;  // a multiple of 4: scale groups never straddle items
+  const long long nsteps = (it1 - it0) * nk;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 2);  // the producer's expect-tx arrival + the scale builder's arrival
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sc_full[b], 1);
+      mbar_init(&sc_empty[b], 1);
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 3) {
+    tmem_alloc(tmem_slot, TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  constexpr uint32_t kSfCol0 = 2 * NM * N;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a =
+          (p.weights_once && MIMO_TC_WEIGHT_EVICT_FIRST) ? l2_evict_first_policy() : l2_evict_normal_policy();
+      const uint64_t pol_b = l2_evict_normal_policy();
+      for (int m = 0; m < NM; ++m) {
+        tma_prefetch_map(&p.amap[m]);
+        tma_prefetch_map(&p.smap[m]);
+        tma_prefetch_map(&p.pmap[m]);
+      }
+      tma_prefetch_map(&p.bmap);
+      tma_prefetch_map(&p.bsmap);
+      int stage = 0;
+      uint32_t ph = 0;
+      long long issued = 0, groups = 0;
+      bool stop = false;
+      // Per item: coordinates, slot and row base once; per step only the ring bookkeeping.
+      for (long long it = it0; it < it1 && !stop; ++it) {
+        int unit, tile;
+        item_coords(p, it, unit, tile);
+        int slot = __ldg(p.unit_slot + unit);
+        if (slot < 0 || slot >= p.S) {
+          set_status(p.status, MIMO_ERANGE);
+          slot = 0;
+        }
+        const int row0 = slot * p.Nw + tile * kM;
+        const int brow = p.btok ? 0 : unit * N;
+#if MIMO_TC_PREFETCH
+        int nrow = -1;  // first weight row of the next item (for the L2 prefetch)
+        if (it + 1 < it1) {
+          int nu, nt;
+          item_coords(p, it + 1, nu, nt);
+          const int ns = __ldg(p.unit_slot + nu);
+          if (ns >= 0 && ns < p.S) nrow = ns * p.Nw + nt * kM;
+        }
+#endif
+        for (int kc = 0; kc < nk; ++kc) {
+          if (*s_abort) {
+            stop = true;
+            break;
+          }
+#if MIMO_TC_PREFETCH
+          if ((kc & 7) == 0) {
+            // Next 8 chunks of this item's rows, or the first 8 of the next item's: 512 contiguous
+            // bytes per row in one request.
+            const bool same = kc + 8 < nk;
+            if (same || nrow >= 0)
+              for (int m = 0; m < NM; ++m) tma_prefetch_l2_3d(&p.pmap[m], 0, same ? row0 : nrow, same ? kc + 8 : 0);
+          }
+#endif
+          if ((kc & 3) == 0) {  // scale boxes for chunks kc..kc+3: 16 bytes of each row
+            const int e = (int)(groups & 1);
+            if (!mbar_wait(&sc_empty[e], (uint32_t)(((groups >> 1) & 1) ^ 1))) {
+              set_status(p.status, MIMO_ETIMEOUT);
+              *s_abort = 1;
+              stop = true;
+              break;
+            }
+            uint8_t* sc = scbox + e * SCB;
+            mbar_arrive_expect_tx(&sc_full[e], NM * kM * 16 + N * 16);
+            for (int m = 0; m < NM; ++m)
+              tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0, &sc_full[e],
+                          MIMO_TC_SCALE_EVICT_FIRST ? pol_a : pol_b);
+            tma_load_2d(sc + NM * kM * 16, &p.bsmap, kc * 4, brow, &sc_full[e], pol_b);
+            ++groups;
+          }
+          if (!mbar_wait(&empty[stage], ph ^ 1u)) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            stop = true;
+            break;
+          }
+          uint8_t* sb = stages + stage * SB;
+          mbar_arrive_expect_tx(&full[stage], NM * kAGlobal + N * kKC);
+          for (int m = 0; m < NM; ++m)
+            tma_load_2d(sb + m * kATile, &p.amap[m], kc * kKC, row0, &full[stage], pol_a);
+          tma_load_2d(sb + NM * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+          ++issued;
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Shared memory must not be released with copies still landing.
+      bool ok = true;
+      for (long long k = 0; ok && k < (issued < NSTAGE ? issued : NSTAGE); ++k) {
+        const long long f = issued - 1 - k;
+        ok = mbar_wait(&full[(int)(f % NSTAGE)], (uint32_t)((f / NSTAGE) & 1));
+      }
+      for (long long k = 0; ok && k < (groups < 2 ? groups : 2); ++k) {
+        const long long g = groups - 1 - k;
+        ok = mbar_wait(&sc_full[(int)(g & 1)], (uint32_t)((g >> 1) & 1));
+      }
+      if (!ok) set_status(p.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------ scale-factor builder
+    // From the landed boxes ([row][16 B], chunk c at bytes 4c..4c+3), lane l writes 16-byte row l of
+    // each 512-byte block: the chunk's 4 bytes for rows l, l+32, l+64, l+96.
+    int stage = 0;
+    uint32_t ph = 0;
+    for (long long s = 0; s < nsteps; ++s) {
+      if (*s_abort) break;
+      const int c = (int)(s & 3);
+      const uint32_t g = (uint32_t)(s >> 2);
+      const int e = (int)(g & 1);
+      if (c == 0 && !mbar_wait(&sc_full[e], (g >> 1) & 1)) {
+        if (lane == 0) set_status(p.status, MIMO_ETIMEOUT);
+        *s_abort = 1;
+        break;
+      }
+      if (!mbar_wait(&empty[stage], ph ^ 1u)) {
+        if (lane == 0) set_status(p.status, MIMO_ETIMEOUT);
+        *s_abort = 1;
+        break;
+      }
+      const uint8_t* sc = scbox + e * SCB;
+      uint8_t* blk = sfblk + stage * (NM + 1) * 512;
+#pragma unroll
+      for (int m = 0; m < NM; ++m) {
+        const uint8_t* box = sc + m * kM * 16 + c * 4;
+        uint4 v;
+        v.x = *reinterpret_cast<const uint32_t*>(box + (lane + 0) * 16);
+        v.y = *reinterpret_cast<const uint32_t*>(box + (lane + 32) * 16);
+        v.z = *reinterpret_cast<const uint32_t*>(box + (lane + 64) * 16);
+        v.w = *reinterpret_cast<const uint32_t*>(box + (lane + 96) * 16);
+        *reinterpret_cast<uint4*>(blk + m * 512 + lane * 16) = v;
+      }
+      {
+        const uint8_t* box = sc + NM * kM * 16 + c * 4;
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int n = lane + 32 * q;
+          w[q] = n < N ? *reinterpret_cast<const uint32_t*>(box + n * 16) : 0x7F7F7F7Fu;
+        }
+        *reinterpret_cast<uint4*>(blk + NM * 512 + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&full[stage]);
+        if (c == 3) mbar_arrive(&sc_empty[e]);
+      }
+      if (++stage == NSTAGE) {
+        stage = 0;
+        ph ^= 1u;
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      bool aborted = false;
+      for (long long it = it0; it < it1 && !aborted; ++it) {
+        const int buf = (int)((it - it0) & 1);
+        const uint32_t use = (uint32_t)(((it - it0) >> 1) & 1);
+        if (!mbar_wait(&acc_empty[buf], use ^ 1u)) {
+          set_status(p.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&full[stage], ph)) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sb = smem_u32(stages + stage * SB);
+          const uint32_t blk = smem_u32(sfblk + stage * (NM + 1) * 512);
+          const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * (NM + 1) * 4;
+          for (int m = 0; m <= NM; ++m) tc_cp_sf(sf_col + m * 4, desc_sf(blk + m * 512));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bdesc = desc_sw128(sb + NM * kATile + kk * 32);
+            const uint32_t sfb_t = (sf_col + NM * 4) | ((uint32_t)kk << 30);
+#pragma unroll
+            for (int m = 0; m < NM; ++m) {
+              const uint64_t adesc = desc_sw128(sb + m * kATile + kk * 32);
+              const uint32_t d = tbase + (uint32_t)(buf * NM + m) * N;
+              const uint32_t sfa_t = (sf_col + m * 4) | ((uint32_t)kk << 30);
+              tc_mma_mx(d, adesc, bdesc, idesc_mx(N, kk), sfa_t, sfb_t, (kc | kk) != 0);
+            }
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!aborted) tc_commit(&acc_full[buf]);
+      }
+      // Nothing may still read shared memory or TMEM when the CTA releases them.
+      tc_commit(drain);
+      if (!mbar_wait(drain, 0)) set_status(p.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    bool aborted = false;
+    for (long long it = it0; it < it1; ++it) {
+      const int buf = (int)((it - it0) & 1);
+      const uint32_t use = (uint32_t)(((it - it0) >> 1) & 1);
+      int unit, tile;
+      item_coords(p, it, unit, tile);
+      const int slot = __ldg(p.unit_slot + unit);
+      const int cnt = min(__ldg(p.unit_cnt + unit), NTOK);
+      const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
+      if (!aborted && !mbar_wait(&acc_full[buf], use)) {
+        set_status(p.status, MIMO_ETIMEOUT);
+        aborted = true;
+      }
+      tc_fence_after();
+      const bool live = !aborted && slot >= 0 && slot < p.S;
+      const int row = tile * kM + quad * 32 + lane;  // output feature of this lane
+      if (MODE == 0 && live && p.btok) {
+        // Columns are tokens: route q reads its token's hi/lo columns.
+#pragma unroll 1
+        for (int q = 0; q < NTOK; ++q) {
+          float h = 0.f;
+          if (q < cnt) {
+            const int t = __ldg(p.btok + p0 + q);
+            if (t >= 0 && t < NTOK) {
+              float gh[1], gl[1], uh[1], ul[1];
+              const uint32_t c0 = tbase + lane_base + (uint32_t)(buf * NM) * N + t;
+              tmem_ld<1>(c0, gh);
+              tmem_ld<1>(c0 + NTOK, gl);
+              tmem_ld<1>(c0 + (NM - 1) * N, uh);
+              tmem_ld<1>(c0 + (NM - 1) * N + NTOK, ul);
+              tmem_wait_ld();
+              h = swiglu_ref(gh[0] + gl[0], uh[0] + ul[0]);
+              if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
+            } else if (lane == 0) {
+              set_status(p.status, MIMO_ERANGE);
+            }
+          }
+          uint32_t th, tl, b1, b2;
+          split_warp_block(h, th, tl, b1, b2);
+          const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
+          p.hq[rh * p.Nw + row] = (uint8_t)th;
+          p.hq[rl * p.Nw + row] = (uint8_t)tl;
+          if (lane == 0) {
+            p.hs[rh * (p.Nw / 32) + row / 32] = (uint8_t)b1;
+            p.hs[rl * (p.Nw / 32) + row / 32] = (uint8_t)b2;
+          }
+        }
+      }
+#pragma unroll 1
+      for (int q0 = 0; q0 < NTOK && live && !(MODE == 0 && p.btok); q0 += QC) {
+        float hi[NM][QC], lo[NM][QC];
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+          const uint32_t c = tbase + lane_base + (uint32_t)(buf * NM + m) * N + q0;
+          tmem_ld<QC>(c, hi[m]);
+          tmem_ld<QC>(c + NTOK, lo[m]);
+        }
+        tmem_wait_ld();
+        if constexpr (MODE == 0) {
+#pragma unroll
+          for (int i = 0; i < QC; ++i) {
+            const int q = q0 + i;
+            float h = 0.f;
+            if (q < cnt) {
+              h = swiglu_ref(hi[0][i] + lo[0][i], hi[NM - 1][i] + lo[NM - 1][i]);
+              if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
+            }
+            uint32_t th, tl, b1, b2;
+            split_warp_block(h, th, tl, b1, b2);
+            const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
+            p.hq[rh * p.Nw + row] = (uint8_t)th;
+            p.hq[rl * p.Nw + row] = (uint8_t)tl;
+            if (lane == 0) {
+              p.hs[rh * (p.Nw / 32) + row / 32] = (uint8_t)b1;
+              p.hs[rl * (p.Nw / 32) + row / 32] = (uint8_t)b2;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < QC; ++i) {
+            const int q = q0 + i;
+            if (q < cnt) {
+              const float d = hi[0][i] + lo[0][i];
+              const size_t op = (size_t)(p0 + q) * p.Nw + row;
+              if constexpr (MODE == 1) {
+                p.part[op] = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
+              } else {
+                p.ypair[op] = (uint16_t)f32_to_bf16(d);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 3) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TCOLS);
+  }
+}
+
+template <int NM, int NTOK, int NSTAGE, int MODE>
+static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
+  auto kfn = tc_expert_kernel<NM, NTOK, NSTAGE, MODE>;
+  constexpr int smem = smem_bytes<NM, 2 * NTOK, NSTAGE>();
+  static_assert(smem <= 232448, "shared memory budget");
+  static_assert(tmem_cols_needed<NM, 2 * NTOK, NSTAGE>() <= 512, "TMEM budget");
+  static_assert((2 * NSTAGE + 4 + 4 + 1) * 8 + 8 <= kBarBytes, "barrier area");
+  if (p.K % (4 * kKC) != 0 || p.Nw % kM != 0 || p.tiles != p.Nw / kM) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kfn<<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------- activation term split
+// Block (unit, q): route q of the unit.  Thread t splits 32-value block t of the route's token row;
+// routes q >= cnt are left unwritten (their MMA columns are never read).
+template <int NTOK>
+__global__ void __launch_bounds__(128) split_rows_kernel(const uint16_t* __restrict__ x, int K,
+                                                         const int32_t* __restrict__ unit_cnt,
+                                                         const int32_t* __restrict__ unit_p0, int p0_stride,
+                                                         const int32_t* __restrict__ rtok,
+                                                         const int32_t* __restrict__ num_units, int units_cap,
+                                                         uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
+                                                         int32_t* status) {
+  constexpr int N = 2 * NTOK;
+  const int unit = blockIdx.x / NTOK, q = blockIdx.x % NTOK;
+  const int units = num_units ? min(*num_units, units_cap) : units_cap;
+  if (unit >= units) return;
+  const int cnt = min(unit_cnt[unit], NTOK);
+  if (q >= cnt) return;
+  const int p0 = unit_p0 ? unit_p0[unit] : unit * p0_stride;
+  const int tok = rtok ? rtok[p0 + q] : p0 + q;
+  const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
+  const int nb = K / 32;
+  for (int blk = threadIdx.x; blk < nb; blk += blockDim.x) {
+    split_block32(x + (size_t)tok * K + blk * 32, bq + rh * K + blk * 32, bq + rl * K + blk * 32,
+                  bs + rh * nb + blk, bs + rl * nb + blk, status);
+  }
+}
+
+// Block t: token row t -> term rows t (hi) and 8 + t (lo).
+__global__ void __launch_bounds__(128) split_tokens_kernel(const uint16_t* __restrict__ x, int K,
+                                                           uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
+                                                           int32_t* status) {
+  const int t = blockIdx.x, nb = K / 32;
+  for (int blk = threadIdx.x; blk < nb; blk += blockDim.x)
+    split_block32(x + (size_t)t * K + blk * 32, bq + (size_t)t * K + blk * 32,
+                  bq + (size_t)(kTcDecodeRoutes + t) * K + blk * 32, bs + (size_t)t * nb + blk,
+                  bs + (size_t)(kTcDecodeRoutes + t) * nb + blk, status);
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------------------ host entry
+cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
+                                   cudaStream_t st) {
+  if (T < 1 || T > kTcDecodeRoutes || K % 128 != 0) return cudaErrorInvalidValue;
+  tc::split_tokens_kernel<<<T, 128, 0, st>>>(x, K, bq, bs, status);
+  return cudaGetLastError();
+}
+cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
+                            int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
+                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st) {
+  if (K % 128 != 0 || units_cap < 1) return cudaErrorInvalidValue;
+  if (ntok == kTcDecodeRoutes)
+    tc::split_rows_kernel<kTcDecodeRoutes><<<units_cap * kTcDecodeRoutes, 128, 0, st>>>(
+        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status);
+  else if (ntok == kTcPrefillRoutes)
+    tc::split_rows_kernel<kTcPrefillRoutes><<<units_cap * kTcPrefillRoutes, 128, 0, st>>>(
+        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st) {
+  switch (kind) {
+    case 0: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 0>(p, num_sms, st);
+    case 1: return tc::launch<1, kTcDecodeRoutes, tc::kStages[1], 1>(p, num_sms, st);
+    case 2: return tc::launch<2, kTcPrefillRoutes, tc::kStages[2], 0>(p, num_sms, st);
+    case 3: return tc::launch<1, kTcPrefillRoutes, tc::kStages[3], 2>(p, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace mimo

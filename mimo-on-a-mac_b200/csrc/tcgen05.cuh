@@ -1,0 +1,195 @@
+// tcgen05 (5th-generation tensor core) building blocks for sm_100a: TMEM allocation, fences,
+// commits, scale-factor copies, MMAs, TMEM loads and shared-memory matrix descriptors.  Forms follow
+// the PTX ISA for tcgen05; descriptor bit positions are documented next to each builder.
+#pragma once
+#include "common.cuh"
+
+namespace mimo {
+namespace tc {
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+// Arrives on `bar` once every tcgen05 operation this thread issued before has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void tc_mma_mx(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t sfa_taddr, uint32_t sfb_taddr, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(
+          d_taddr),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_taddr), "r"(sfb_taddr)
+      : "memory");
+}
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[NC]);
+template <>
+__device__ __forceinline__ void tmem_ld<1>(uint32_t taddr, float (&v)[1]) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n" : "=r"(r) : "r"(taddr));
+  v[0] = __uint_as_float(r);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+      "[%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_normal_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+
+// Shared-memory matrix descriptors (sm_100 format: version 1 in bits 46-47).
+//   K-major, 128B swizzle: 128-byte rows, 8-row groups 1024 B apart (stride byte offset); the
+//   leading byte offset is unused for this layout.  Tiles start 1024-byte aligned (base offset 0).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+//   K-major, no swizzle: 8-row core matrices of 16-byte rows, 128 B apart (the scale blocks).
+__device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(128 >> 4) << 16;
+  d |= (uint64_t)(128 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+// kind::f16 MMA (bf16/f16 operands from shared memory, f32 accumulate), no disabled lanes.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_taddr),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+// Instruction descriptor of kind::f16: f32 accumulator (bits 4-5 = 1), A and B bf16 (bits 7-9 and
+// 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__device__ __forceinline__ uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// e4m3 two-term split helpers.
+__device__ __forceinline__ uint32_t f32_to_e4m3(float v) {  // RNE, saturating
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(0.f), "f"(v));
+  return (uint32_t)r & 0xFFu;
+}
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {  // exact (every e4m3 value is an f16)
+  uint32_t h2;
+  const uint16_t in = (uint16_t)b;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(h2) : "h"(in));
+  return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+// ue8m0 byte of a block whose largest magnitude is amax: 2^(e(amax) - 7), so |v| / s < 256 <= 448.
+__device__ __forceinline__ uint32_t block_scale_byte(float amax) {
+  if (!(amax > 0.f)) return 127u;
+  const int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+  const int b = e - 7;
+  return (uint32_t)(b < 1 ? 1 : (b > 254 ? 254 : b));
+}
+__device__ __forceinline__ float exp2_byte(uint32_t b) { return __uint_as_float(b << 23); }  // 2^(b - 127)
+__device__ __forceinline__ float inv_exp2_byte(uint32_t b) {                                  // 2^(127 - b)
+  return __uint_as_float((254u - b) << 23);
+}
+// Splits 32 bf16 values (64 bytes at src, 16-byte aligned) into two e4m3 terms with one ue8m0 scale
+// each: hi = e4m3(v / s1) with s1 = 2^(e(max|v|) - 7), lo = e4m3((v - hi * s1) / s2) with s2 from the
+// residual's maximum.  Non-finite inputs set MIMO_ERANGE.
+__device__ __forceinline__ void split_block32(const uint16_t* src, uint8_t* dh, uint8_t* dl, uint8_t* sh,
+                                              uint8_t* sl, int32_t* status) {
+  float v[32];
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 w = s4[i];
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[i * 8 + 2 * j] = __uint_as_float(ww[j] << 16);
+      v[i * 8 + 2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+    }
+  }
+  float amax = 0.f;
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    amax = fmaxf(amax, fabsf(v[i]));
+    bad |= !isfinite(v[i]);
+  }
+  if (bad) set_status(status, MIMO_ERANGE);
+  const uint32_t b1 = block_scale_byte(amax);
+  uint32_t hw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, lw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float r[32], rmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint32_t e = f32_to_e4m3(v[i] * inv_exp2_byte(b1));
+    r[i] = v[i] - e4m3_to_f32(e) * exp2_byte(b1);
+    rmax = fmaxf(rmax, fabsf(r[i]));
+    hw[i >> 2] |= e << (8 * (i & 3));
+  }
+  const uint32_t b2 = block_scale_byte(rmax);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) lw[i >> 2] |= f32_to_e4m3(r[i] * inv_exp2_byte(b2)) << (8 * (i & 3));
+  uint4* h4 = reinterpret_cast<uint4*>(dh);
+  uint4* l4 = reinterpret_cast<uint4*>(dl);
+  h4[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  h4[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+  l4[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  l4[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+  *sh = (uint8_t)b1;
+  *sl = (uint8_t)b2;
+}
+
+}  // namespace tc
+}  // namespace mimo

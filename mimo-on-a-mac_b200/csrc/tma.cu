@@ -123,4 +123,119 @@ cudaError_t scale_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_
   return cudaSuccess;
 }
 
+namespace {
+bool cached(const Key& key, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = cache().find(key);
+  if (it == cache().end()) return false;
+  *out = it->second.map;
+  return true;
+}
+void remember(const Key& key, const CUtensorMap& m) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (cache().size() > 4096) cache().clear();
+  WeightMap wm{};
+  wm.map = m;
+  cache()[key] = wm;
+}
+}  // namespace
+
+cudaError_t fp4_weight_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K) {
+  const Key key{(uint64_t)base, rows, K, 2, 0};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || K % 128 != 0 || ((uint64_t)base & 31) != 0 || (K / 2) % 32 != 0) return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {K, rows};
+  const cuuint64_t strides[1] = {K / 2};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), dims, strides,
+                        box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
+cudaError_t fp4_prefetch_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K) {
+  const Key key{(uint64_t)base, rows, K, 6, 0};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || K % 1024 != 0 || ((uint64_t)base & 31) != 0) return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {128, rows, K / 128};
+  const cuuint64_t strides[2] = {K / 2, 64};
+  const cuuint32_t box[3] = {128, 128, 8};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims, strides, box,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
+cudaError_t sf_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows) {
+  const Key key{(uint64_t)base, rows, row_bytes, 4, box_rows};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || row_bytes % 16 != 0 || box_rows < 1 || box_rows > 256 || ((uint64_t)base & 15) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {16, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
+cudaError_t bf16_rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, int box_rows) {
+  const Key key{(uint64_t)base, rows, cols, 5, box_rows};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || (cols * 2) % 16 != 0 || box_rows < 1 || box_rows > 256 || ((uint64_t)base & 15) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
+cudaError_t rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows) {
+  const Key key{(uint64_t)base, rows, row_bytes, 3, box_rows};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || row_bytes % 128 != 0 || box_rows < 1 || box_rows > 256 || ((uint64_t)base & 15) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
 }  // namespace mimo

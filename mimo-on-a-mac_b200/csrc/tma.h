@@ -21,4 +21,18 @@ cudaError_t weight_map(WeightMap* out, const void* base, uint64_t rows, uint64_t
 // Scale map [rows, K/32 bytes]: boxes of 16 rows x box_bytes, no swizzle.
 cudaError_t scale_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_bytes);
 
+// MXFP4 weight map for the block-scaled tensor cores: [rows][K] e2m1 values (K / 2 bytes a row),
+// 16U4_ALIGN16B (each 16 values land as 8 data bytes + 8 gap bytes), box [128 values, 128 rows],
+// 128B swizzle.  K must be a multiple of 128 and the rows 32-byte aligned.
+cudaError_t fp4_weight_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K);
+// L2-prefetch view of the same weights: dims [128 values, rows, K / 128 chunks] (chunk stride 64 B),
+// box [128, 128, 8]: one prefetch covers 512 contiguous bytes of each of 128 rows.
+cudaError_t fp4_prefetch_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K);
+// Scale-matrix map [rows][row_bytes], box [16 bytes, box_rows], no swizzle.
+cudaError_t sf_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
+// bf16 matrix map [rows][cols], box [64 values, box_rows], 128B swizzle; rows past the end read 0.
+cudaError_t bf16_rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, int box_rows);
+// Byte-matrix map [rows][row_bytes], box [128 bytes, box_rows], 128B swizzle.
+cudaError_t rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
+
 }  // namespace mimo

@@ -4,10 +4,11 @@ There is no CPU fallback: if the library is missing or cannot be loaded, every o
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, c_int32, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().with_name("libmimo_moe.so")
+LIB_PATH = Path(os.environ.get("MIMO_MOE_LIBRARY") or Path(__file__).resolve().with_name("libmimo_moe.so"))
 
 MIMO_OK, MIMO_EINVAL, MIMO_ERANGE, MIMO_ETIMEOUT, MIMO_ECUDA = 0, 1, 2, 3, 4
 
