@@ -18,9 +18,9 @@
 //               that tcgen05.cp.32x128b.warpx4 turns into the TMEM scale layout (block byte
 //               (m % 32) * 16 + (m / 32) * 4 + kb for row m, K block kb); its arrival is the second
 //               of the stage's `full` barrier, so the MMA issuer waits on one barrier per stage;
-//   warp 2      MMA issuer (one lane): tcgen05.cp of the scale blocks, 4 MMAs of K = 32 per matrix
-//               per stage into a double-buffered TMEM accumulator, one tcgen05.commit to free the stage;
-//   warp 3      TMEM allocator;
+//   warps 2-3   MMA issuers (one lane each, warp 3 also allocates TMEM): tcgen05.cp of the scale
+//               blocks and 4 MMAs of K = 32 per stage into the issuer's own accumulator of a double
+//               buffer (gate / up, or even / odd stages of down), tcgen05.commit to free the stage;
 //   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 * (w % 4) + 0..31,
 //               i.e. weight rows), then
 //               MODE 0  SwiGLU with the reference's roundings (engine/mimo_stream/kernels.py:79-82)
@@ -80,7 +80,7 @@ constexpr int smem_bytes() {
   return kBarBytes + 1024 + NSTAGE * stage_bytes<NM, N>() + 2 * scale_box_bytes<NM, N>() + NSTAGE * (NM + 1) * 512;
 }
 template <int NM, int N, int NSTAGE>
-constexpr int tmem_cols_needed() { return 2 * NM * N + NSTAGE * (NM + 1) * 4; }
+constexpr int tmem_cols_needed() { return 4 * N + NSTAGE * NM * 8; }  // 2 buffers x 2 accumulators + scales
 template <int NM, int N, int NSTAGE>
 constexpr uint32_t tmem_cols() {
   constexpr int n = tmem_cols_needed<NM, N, NSTAGE>();
@@ -169,15 +169,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
       mbar_init(&full[i], 2);  // the producer's expect-tx arrival + the scale builder's arrival
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], NM);  // one commit per issuer that reads the stage
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sc_full[b], 1);
       mbar_init(&sc_empty[b], 1);
-      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_full[b], 2);
       mbar_init(&acc_empty[b], 4);
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     *s_abort = 0;
     mbar_fence_init();
   }
@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  constexpr uint32_t kSfCol0 = 2 * NM * N;
+  constexpr uint32_t kSfCol0 = 4 * N;  // accumulator (buf, j) at columns (2 * buf + j) * N
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------ TMA producer
@@ -342,12 +342,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
         ph ^= 1u;
       }
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------------------- MMA issuer
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------------------ MMA issuers
+    // Two issuing threads (one MMA stream per thread runs at ~77 cycles per MMA at small N; two
+    // overlap).  Issuer j owns accumulator j of each buffer: with NM == 2 the matrix j (gate / up)
+    // of every stage, with NM == 1 the stages of parity j (the epilogue adds the two partial sums).
+    // Each copies the scales its own MMAs read, so no ordering is needed between the two threads.
+    const int j = warp - 2;
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0;
       bool aborted = false;
+      const int m = NM == 2 ? j : 0;
       for (long long it = it0; it < it1 && !aborted; ++it) {
         const int buf = (int)((it - it0) & 1);
         const uint32_t use = (uint32_t)(((it - it0) >> 1) & 1);
@@ -357,31 +363,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
           break;
         }
         tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)(2 * buf + j) * N;
         for (int kc = 0; kc < nk; ++kc) {
-          if (!mbar_wait(&full[stage], ph)) {
-            set_status(p.status, MIMO_ETIMEOUT);
-            *s_abort = 1;
-            aborted = true;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sb = smem_u32(stages + stage * SB);
-          const uint32_t blk = smem_u32(sfblk + stage * (NM + 1) * 512);
-          const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * (NM + 1) * 4;
-          for (int m = 0; m <= NM; ++m) tc_cp_sf(sf_col + m * 4, desc_sf(blk + m * 512));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bdesc = desc_sw128(sb + NM * kATile + kk * 32);
-            const uint32_t sfb_t = (sf_col + NM * 4) | ((uint32_t)kk << 30);
-#pragma unroll
-            for (int m = 0; m < NM; ++m) {
-              const uint64_t adesc = desc_sw128(sb + m * kATile + kk * 32);
-              const uint32_t d = tbase + (uint32_t)(buf * NM + m) * N;
-              const uint32_t sfa_t = (sf_col + m * 4) | ((uint32_t)kk << 30);
-              tc_mma_mx(d, adesc, bdesc, idesc_mx(N, kk), sfa_t, sfb_t, (kc | kk) != 0);
+          if (NM == 2 || (kc & 1) == j) {
+            if (!mbar_wait(&full[stage], ph)) {
+              set_status(p.status, MIMO_ETIMEOUT);
+              *s_abort = 1;
+              aborted = true;
+              break;
             }
+            tc_fence_after();
+            const uint32_t sb = smem_u32(stages + stage * SB);
+            const uint32_t blk = smem_u32(sfblk + stage * (NM + 1) * 512);
+            const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * NM * 8 + (NM == 2 ? 8 * j : 0);
+            tc_cp_sf(sf_col, desc_sf(blk + m * 512));       // this matrix's weight scales
+            tc_cp_sf(sf_col + 4, desc_sf(blk + NM * 512));  // activation scales
+            const int first = NM == 2 ? kc : (kc >> 1);     // 0 on this accumulator's first stage
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_mx(d, desc_sw128(sb + m * kATile + kk * 32), desc_sw128(sb + NM * kATile + kk * 32),
+                        idesc_mx(N, kk), sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30),
+                        (first | kk) != 0);
+            tc_commit(&empty[stage]);
           }
-          tc_commit(&empty[stage]);
           if (++stage == NSTAGE) {
             stage = 0;
             ph ^= 1u;
@@ -422,11 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
             const int t = __ldg(p.btok + p0 + q);
             if (t >= 0 && t < NTOK) {
               float gh[1], gl[1], uh[1], ul[1];
-              const uint32_t c0 = tbase + lane_base + (uint32_t)(buf * NM) * N + t;
+              const uint32_t c0 = tbase + lane_base + (uint32_t)(2 * buf) * N + t;
               tmem_ld<1>(c0, gh);
               tmem_ld<1>(c0 + NTOK, gl);
-              tmem_ld<1>(c0 + (NM - 1) * N, uh);
-              tmem_ld<1>(c0 + (NM - 1) * N + NTOK, ul);
+              tmem_ld<1>(c0 + N, uh);
+              tmem_ld<1>(c0 + N + NTOK, ul);
               tmem_wait_ld();
               h = swiglu_ref(gh[0] + gl[0], uh[0] + ul[0]);
               if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
@@ -447,12 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       }
 #pragma unroll 1
       for (int q0 = 0; q0 < NTOK && live && !(MODE == 0 && p.btok); q0 += QC) {
-        float hi[NM][QC], lo[NM][QC];
+        float hi[2][QC], lo[2][QC];  // accumulators 0 and 1 of the buffer
 #pragma unroll
-        for (int m = 0; m < NM; ++m) {
-          const uint32_t c = tbase + lane_base + (uint32_t)(buf * NM + m) * N + q0;
-          tmem_ld<QC>(c, hi[m]);
-          tmem_ld<QC>(c + NTOK, lo[m]);
+        for (int a = 0; a < 2; ++a) {
+          const uint32_t c = tbase + lane_base + (uint32_t)(2 * buf + a) * N + q0;
+          tmem_ld<QC>(c, hi[a]);
+          tmem_ld<QC>(c + NTOK, lo[a]);
         }
         tmem_wait_ld();
         if constexpr (MODE == 0) {
@@ -461,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
             const int q = q0 + i;
             float h = 0.f;
             if (q < cnt) {
-              h = swiglu_ref(hi[0][i] + lo[0][i], hi[NM - 1][i] + lo[NM - 1][i]);
+              h = swiglu_ref(hi[0][i] + lo[0][i], hi[1][i] + lo[1][i]);
               if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
             }
             uint32_t th, tl, b1, b2;
@@ -479,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
           for (int i = 0; i < QC; ++i) {
             const int q = q0 + i;
             if (q < cnt) {
-              const float d = hi[0][i] + lo[0][i];
+              const float d = (hi[0][i] + hi[1][i]) + (lo[0][i] + lo[1][i]);
               const size_t op = (size_t)(p0 + q) * p.Nw + row;
               if constexpr (MODE == 1) {
                 p.part[op] = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
