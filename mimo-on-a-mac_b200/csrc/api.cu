@@ -231,8 +231,6 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   TcParams p{};
   MIMO_TRY(fp4_weight_map(&p.amap[0], pools->gate_w, (uint64_t)S * I, H));
   MIMO_TRY(fp4_weight_map(&p.amap[1], pools->up_w, (uint64_t)S * I, H));
-  MIMO_TRY(fp4_prefetch_map(&p.pmap[0], pools->gate_w, (uint64_t)S * I, H));
-  MIMO_TRY(fp4_prefetch_map(&p.pmap[1], pools->up_w, (uint64_t)S * I, H));
   MIMO_TRY(sf_map(&p.smap[0], pools->gate_s, (uint64_t)S * I, H / 32, 128));
   MIMO_TRY(sf_map(&p.smap[1], pools->up_s, (uint64_t)S * I, H / 32, 128));
   MIMO_TRY(rows_map(&p.bmap, t.bq, brows, H, N));
@@ -255,14 +253,12 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.hs = t.hs;
   p.status = status;
   MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
-  TcParams q = p;
-  MIMO_TRY(fp4_weight_map(&q.amap[0], pools->down_w, (uint64_t)S * H, I));
+  TcParams q = p;  // down: two K chunks per stage through 3-D boxes
+  MIMO_TRY(fp4_weight_map3(&q.amap[0], pools->down_w, (uint64_t)S * H, I, 2));
   q.amap[1] = q.amap[0];
-  MIMO_TRY(fp4_prefetch_map(&q.pmap[0], pools->down_w, (uint64_t)S * H, I));
-  q.pmap[1] = q.pmap[0];
   MIMO_TRY(sf_map(&q.smap[0], pools->down_s, (uint64_t)S * H, I / 32, 128));
   q.smap[1] = q.smap[0];
-  MIMO_TRY(rows_map(&q.bmap, t.hq, (uint64_t)ucap * N, I, N));
+  MIMO_TRY(rows_map3(&q.bmap, t.hq, (uint64_t)ucap * N, I, N, 2));
   MIMO_TRY(sf_map(&q.bsmap, t.hs, (uint64_t)ucap * N, I / 32, N));
   q.Nw = H;
   q.K = I;

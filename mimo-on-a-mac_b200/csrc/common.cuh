@@ -171,12 +171,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, 
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
-// L2 prefetch of a 3-D tensor-map box (no shared memory involved).
-__device__ __forceinline__ void tma_prefetch_l2_3d(const void* map, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n" ::"l"(map), "r"(c0),
-               "r"(c1), "r"(c2)
-               : "memory");
-}
 __device__ __forceinline__ void tma_prefetch_map(const void* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
 }

@@ -62,11 +62,12 @@ cudaError_t launch_decode_tma(const DecodeParams& p, int kind, int num_sms, cuda
 // terms are rows [u * 2 * ntok, (u + 1) * 2 * ntok) of the term matrix: rows q < ntok hold the first
 // e4m3 term of route q, rows ntok + q the second.
 struct TcParams {
-  CUtensorMap amap[2];   // weights of matrix m, 16U4_ALIGN16B, box [128 values, 128 rows], 128B swizzle
+  CUtensorMap amap[2];   // weights of matrix m, 16U4_ALIGN16B, 128B swizzle: gate/up 2-D boxes
+                         // [128 values, 128 rows]; down one 3-D view [chunk][row][128 values], box 2 chunks
   CUtensorMap smap[2];   // e8m0 scales of matrix m [S * Nw][K / 32], box [16 B, 128 rows]
-  CUtensorMap bmap;      // activation terms [units * 2 * ntok][K] e4m3, box [128 B, 2 * ntok rows]
+  CUtensorMap bmap;      // activation terms [units * 2 * ntok][K] e4m3: box [128 B, 2 * ntok rows]
+                         // (gate/up), or the 3-D view [chunk][row][128 B] with 2 chunks per box (down)
   CUtensorMap bsmap;     // their ue8m0 scales [units * 2 * ntok][K / 32], box [16 B, 2 * ntok rows]
-  CUtensorMap pmap[2];   // L2 prefetch view of the weights: [K / 128 chunks][rows][128 values], box 8 chunks
   int S, Nw, K, tiles;   // Nw: weight rows (output features) per expert; tiles = Nw / 128
   const int32_t* unit_slot;
   const int32_t* unit_cnt;

@@ -21,8 +21,8 @@
 //   warps 2-3   MMA issuers (one lane each, warp 3 also allocates TMEM): tcgen05.cp of the scale
 //               blocks and 4 MMAs of K = 32 per stage into the issuer's own accumulator of a double
 //               buffer (gate / up, or even / odd stages of down), tcgen05.commit to free the stage;
-//   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 * (w % 4) + 0..31,
-//               i.e. weight rows), then
+//   warps 4-11  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes 32 * (w % 4) + 0..31,
+//               i.e. weight rows, for half of the routes), then
 //               MODE 0  SwiGLU with the reference's roundings (engine/mimo_stream/kernels.py:79-82)
 //                       and the split of h into two e4m3 terms for the down pass;
 //               MODE 1  down x route weight (kernels.py:120), fp32 partials for the fixed-order
@@ -44,7 +44,8 @@ constexpr int kM = 128;           // weight rows per tile (MMA M)
 constexpr int kKC = 128;          // K values per stage
 constexpr int kATile = kM * kKC;  // shared bytes of one padded e2m1 tile (16 KiB)
 constexpr int kAGlobal = kATile / 2;  // global (packed) bytes of one tile: the TMA transaction count
-constexpr int kThreads = 256;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quadrant, each taking half of the routes
+constexpr int kThreads = (4 + kEpiWarps) * 32;
 constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment slack
 
 // Ring depths of kinds 0..3 (decode gate/up, decode down, prefill gate/up, prefill down).
@@ -52,38 +53,40 @@ constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment 
 #define MIMO_TC_ST0 6
 #endif
 #ifndef MIMO_TC_ST1
-#define MIMO_TC_ST1 11
+#define MIMO_TC_ST1 5
 #endif
 #ifndef MIMO_TC_ST2
 #define MIMO_TC_ST2 5
 #endif
 #ifndef MIMO_TC_ST3
-#define MIMO_TC_ST3 8
-#endif
-#ifndef MIMO_TC_PREFETCH
-#define MIMO_TC_PREFETCH 0  // 1: L2 prefetch of the next 8 K chunks of every weight row (measured slower)
+#define MIMO_TC_ST3 4
 #endif
 #ifndef MIMO_TC_WEIGHT_EVICT_FIRST
 #define MIMO_TC_WEIGHT_EVICT_FIRST 1  // decode streams each weight once: L2 evict-first
 #endif
-#ifndef MIMO_TC_SCALE_EVICT_FIRST
-#define MIMO_TC_SCALE_EVICT_FIRST 0
-#endif
 constexpr int kStages[4] = {MIMO_TC_ST0, MIMO_TC_ST1, MIMO_TC_ST2, MIMO_TC_ST3};
 
+// A stage holds two "slots", one per MMA issuer: (matrix j, chunk c) for gate/up (NM = 2, one K
+// chunk per stage) or (matrix 0, chunk c + j) for down (NM = 1, two K chunks per stage).
+// Stage layout: [A tile slot 0 | A tile slot 1 | KPS activation tiles], 1024-byte aligned tiles.
+template <int NM>
+constexpr int kps() { return 2 / NM; }  // K chunks per stage
 template <int NM, int N>
-constexpr int stage_bytes() { return (NM * kATile + N * kKC + 1023) / 1024 * 1024; }
+constexpr int stage_bytes() { return 2 * kATile + kps<NM>() * N * kKC; }
 template <int NM, int N>
-constexpr int scale_box_bytes() { return NM * kM * 16 + N * 16; }  // one 4-stage group's scale boxes
+constexpr int scale_box_bytes() { return NM * kM * 16 + N * 16; }  // one 4-chunk group's scale boxes
+template <int NM>
+constexpr int sf_block_bytes() { return (2 + kps<NM>()) * 512; }  // per stage: 2 weight + KPS act. blocks
 template <int NM, int N, int NSTAGE>
 constexpr int smem_bytes() {
-  return kBarBytes + 1024 + NSTAGE * stage_bytes<NM, N>() + 2 * scale_box_bytes<NM, N>() + NSTAGE * (NM + 1) * 512;
+  return kBarBytes + 1024 + NSTAGE * stage_bytes<NM, N>() + 2 * scale_box_bytes<NM, N>() +
+         NSTAGE * sf_block_bytes<NM>();
 }
-template <int NM, int N, int NSTAGE>
-constexpr int tmem_cols_needed() { return 4 * N + NSTAGE * NM * 8; }  // 2 buffers x 2 accumulators + scales
-template <int NM, int N, int NSTAGE>
+template <int N, int NSTAGE>
+constexpr int tmem_cols_needed() { return 4 * N + NSTAGE * 16; }  // 2 buffers x 2 accumulators + scales
+template <int N, int NSTAGE>
 constexpr uint32_t tmem_cols() {
-  constexpr int n = tmem_cols_needed<NM, N, NSTAGE>();
+  constexpr int n = tmem_cols_needed<N, NSTAGE>();
   return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
 }
 
@@ -104,15 +107,12 @@ __device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t kb) {
 
 // Splits v into hi/lo e4m3 bytes and their block scale bytes; the 32 lanes form one block.
 __device__ __forceinline__ void split_warp_block(float v, uint32_t& hi, uint32_t& lo, uint32_t& b1, uint32_t& b2) {
-  float amax = fabsf(v);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  // Non-negative floats order like their bit patterns: one redux.sync gives the block maximum.
+  const float amax = __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, __float_as_uint(fabsf(v))));
   b1 = block_scale_byte(amax);
   hi = f32_to_e4m3(v * inv_exp2_byte(b1));
   const float r = v - e4m3_to_f32(hi) * exp2_byte(b1);
-  float rmax = fabsf(r);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xFFFFFFFFu, rmax, o));
+  const float rmax = __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, __float_as_uint(fabsf(r))));
   b2 = block_scale_byte(rmax);
   lo = f32_to_e4m3(r * inv_exp2_byte(b2));
 }
@@ -138,15 +138,19 @@ __device__ __forceinline__ void item_coords(const TcParams& p, long long i, int&
 template <int NM, int NTOK, int NSTAGE, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_constant__ TcParams p) {
   constexpr int N = 2 * NTOK;
+  constexpr int KPS = kps<NM>();
   constexpr int SB = stage_bytes<NM, N>();
   constexpr int SCB = scale_box_bytes<NM, N>();
-  constexpr uint32_t TCOLS = tmem_cols<NM, N, NSTAGE>();
-  constexpr int QC = NTOK < 16 ? NTOK : 16;  // routes per TMEM load in the epilogue
-  static_assert(N % 16 == 0 && N <= 256 && NTOK % QC == 0, "MMA N");
+  constexpr int SFB = sf_block_bytes<NM>();
+  constexpr uint32_t TCOLS = tmem_cols<N, NSTAGE>();
+  constexpr int QH = NTOK / 2;               // routes per epilogue warp
+  constexpr int QC = QH < 16 ? QH : 16;      // routes per TMEM load in the epilogue
+  static_assert(NM * KPS == 2, "two slots per stage");
+  static_assert(N % 16 == 0 && N <= 256 && QH % QC == 0, "MMA N");
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NSTAGE] tiles landed + scale block written
-  uint64_t* empty = full + NSTAGE;                     // [NSTAGE] MMAs (and scale copies) of the stage done
-  uint64_t* sc_full = empty + NSTAGE;                  // [2] scale boxes of a 4-stage group landed
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NSTAGE] tiles landed + scale blocks written
+  uint64_t* empty = full + NSTAGE;                     // [NSTAGE] both issuers' MMAs of the stage done
+  uint64_t* sc_full = empty + NSTAGE;                  // [2] scale boxes of a 4-chunk group landed
   uint64_t* sc_empty = sc_full + 2;                    // [2] scale boxes read
   uint64_t* acc_full = sc_empty + 2;                   // [2]
   uint64_t* acc_empty = acc_full + 2;                  // [2]
@@ -154,28 +158,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + kBarBytes) + 1023) & ~(uintptr_t)1023);
-  uint8_t* stages = base;                                 // NSTAGE x [A tiles | B tile]
-  uint8_t* scbox = stages + NSTAGE * SB;                  // 2 x [A scale boxes | B scale box]
-  uint8_t* sfblk = scbox + 2 * SCB;                       // NSTAGE x (NM + 1) x 512 B
+  uint8_t* stages = base;                   // NSTAGE x [2 A tiles | KPS B tiles]
+  uint8_t* scbox = stages + NSTAGE * SB;    // 2 x [NM x A scale box | B scale box]
+  uint8_t* sfblk = scbox + 2 * SCB;         // NSTAGE x [2 weight scale blocks | KPS activation blocks]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
   const long long items = (long long)units * p.tiles;
   const long long it0 = items * blockIdx.x / gridDim.x;
   const long long it1 = items * (blockIdx.x + 1) / gridDim.x;
-  const int nk = p.K / kKC;  // a multiple of 4: scale groups never straddle items
-  const long long nsteps = (it1 - it0) * nk;
+  const int ns = p.K / (kKC * KPS);  // stages per item; K chunks per item are a multiple of 4
+  const long long nsteps = (it1 - it0) * ns;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
-      mbar_init(&full[i], 2);  // the producer's expect-tx arrival + the scale builder's arrival
-      mbar_init(&empty[i], NM);  // one commit per issuer that reads the stage
+      mbar_init(&full[i], 2);   // the producer's expect-tx arrival + the scale builder's arrival
+      mbar_init(&empty[i], 2);  // one commit per issuer
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sc_full[b], 1);
       mbar_init(&sc_empty[b], 1);
       mbar_init(&acc_full[b], 2);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpiWarps);
     }
     mbar_init(drain, 2);
     *s_abort = 0;
@@ -200,7 +204,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       for (int m = 0; m < NM; ++m) {
         tma_prefetch_map(&p.amap[m]);
         tma_prefetch_map(&p.smap[m]);
-        tma_prefetch_map(&p.pmap[m]);
       }
       tma_prefetch_map(&p.bmap);
       tma_prefetch_map(&p.bsmap);
@@ -208,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       uint32_t ph = 0;
       long long issued = 0, groups = 0;
       bool stop = false;
-      // Per item: coordinates, slot and row base once; per step only the ring bookkeeping.
+      // Per item: coordinates, slot and row base once; per stage only the ring bookkeeping.
       for (long long it = it0; it < it1 && !stop; ++it) {
         int unit, tile;
         item_coords(p, it, unit, tile);
@@ -219,30 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
         }
         const int row0 = slot * p.Nw + tile * kM;
         const int brow = p.btok ? 0 : unit * N;
-#if MIMO_TC_PREFETCH
-        int nrow = -1;  // first weight row of the next item (for the L2 prefetch)
-        if (it + 1 < it1) {
-          int nu, nt;
-          item_coords(p, it + 1, nu, nt);
-          const int ns = __ldg(p.unit_slot + nu);
-          if (ns >= 0 && ns < p.S) nrow = ns * p.Nw + nt * kM;
-        }
-#endif
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int ks = 0; ks < ns; ++ks) {
           if (*s_abort) {
             stop = true;
             break;
           }
-#if MIMO_TC_PREFETCH
-          if ((kc & 7) == 0) {
-            // Next 8 chunks of this item's rows, or the first 8 of the next item's: 512 contiguous
-            // bytes per row in one request.
-            const bool same = kc + 8 < nk;
-            if (same || nrow >= 0)
-              for (int m = 0; m < NM; ++m) tma_prefetch_l2_3d(&p.pmap[m], 0, same ? row0 : nrow, same ? kc + 8 : 0);
-          }
-#endif
-          if ((kc & 3) == 0) {  // scale boxes for chunks kc..kc+3: 16 bytes of each row
+          const int kc = ks * KPS;  // first K chunk of the stage
+          if ((kc & 3) == 0) {      // scale boxes for chunks kc..kc+3: 16 bytes of each row
             const int e = (int)(groups & 1);
             if (!mbar_wait(&sc_empty[e], (uint32_t)(((groups >> 1) & 1) ^ 1))) {
               set_status(p.status, MIMO_ETIMEOUT);
@@ -252,9 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
             }
             uint8_t* sc = scbox + e * SCB;
             mbar_arrive_expect_tx(&sc_full[e], NM * kM * 16 + N * 16);
-            for (int m = 0; m < NM; ++m)
-              tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0, &sc_full[e],
-                          MIMO_TC_SCALE_EVICT_FIRST ? pol_a : pol_b);
+            for (int m = 0; m < NM; ++m) tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0, &sc_full[e], pol_b);
             tma_load_2d(sc + NM * kM * 16, &p.bsmap, kc * 4, brow, &sc_full[e], pol_b);
             ++groups;
           }
@@ -265,10 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
             break;
           }
           uint8_t* sb = stages + stage * SB;
-          mbar_arrive_expect_tx(&full[stage], NM * kAGlobal + N * kKC);
-          for (int m = 0; m < NM; ++m)
-            tma_load_2d(sb + m * kATile, &p.amap[m], kc * kKC, row0, &full[stage], pol_a);
-          tma_load_2d(sb + NM * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+          mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * N * kKC);
+          if constexpr (KPS == 1) {
+            tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol_a);
+            tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol_a);
+            tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+          } else {  // 3-D boxes [2 chunks][rows][128 B]: both chunks' tiles in one copy each
+            tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol_a);
+            tma_load_3d(sb + 2 * kATile, &p.bmap, 0, brow, kc, &full[stage], pol_b);
+          }
           ++issued;
           if (++stage == NSTAGE) {
             stage = 0;
@@ -291,13 +280,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   } else if (warp == 1) {
     // ------------------------------------------------------------------------ scale-factor builder
     // From the landed boxes ([row][16 B], chunk c at bytes 4c..4c+3), lane l writes 16-byte row l of
-    // each 512-byte block: the chunk's 4 bytes for rows l, l+32, l+64, l+96.
+    // each 512-byte block: the chunk's 4 bytes for rows l, l+32, l+64, l+96.  Blocks of a stage:
+    // [weight scales of slot 0 | slot 1 | activation scales of chunk 0 (| chunk 1)].
     int stage = 0;
     uint32_t ph = 0;
     for (long long s = 0; s < nsteps; ++s) {
       if (*s_abort) break;
-      const int c = (int)(s & 3);
-      const uint32_t g = (uint32_t)(s >> 2);
+      const uint32_t kc = (uint32_t)(s * KPS);  // running chunk index; groups of 4 align with items
+      const int c = (int)(kc & 3);
+      const uint32_t g = kc >> 2;
       const int e = (int)(g & 1);
       if (c == 0 && !mbar_wait(&sc_full[e], (g >> 1) & 1)) {
         if (lane == 0) set_status(p.status, MIMO_ETIMEOUT);
@@ -310,32 +301,34 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
         break;
       }
       const uint8_t* sc = scbox + e * SCB;
-      uint8_t* blk = sfblk + stage * (NM + 1) * 512;
+      uint8_t* blk = sfblk + stage * SFB;
 #pragma unroll
-      for (int m = 0; m < NM; ++m) {
-        const uint8_t* box = sc + m * kM * 16 + c * 4;
+      for (int j = 0; j < 2; ++j) {
+        const int m = NM == 2 ? j : 0, cj = c + (KPS == 2 ? j : 0);
+        const uint8_t* box = sc + m * kM * 16 + cj * 4;
         uint4 v;
         v.x = *reinterpret_cast<const uint32_t*>(box + (lane + 0) * 16);
         v.y = *reinterpret_cast<const uint32_t*>(box + (lane + 32) * 16);
         v.z = *reinterpret_cast<const uint32_t*>(box + (lane + 64) * 16);
         v.w = *reinterpret_cast<const uint32_t*>(box + (lane + 96) * 16);
-        *reinterpret_cast<uint4*>(blk + m * 512 + lane * 16) = v;
+        *reinterpret_cast<uint4*>(blk + j * 512 + lane * 16) = v;
       }
-      {
-        const uint8_t* box = sc + NM * kM * 16 + c * 4;
+#pragma unroll
+      for (int j = 0; j < KPS; ++j) {
+        const uint8_t* box = sc + NM * kM * 16 + (c + j) * 4;
         uint32_t w[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int n = lane + 32 * q;
           w[q] = n < N ? *reinterpret_cast<const uint32_t*>(box + n * 16) : 0x7F7F7F7Fu;
         }
-        *reinterpret_cast<uint4*>(blk + NM * 512 + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(blk + (2 + j) * 512 + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&full[stage]);
-        if (c == 3) mbar_arrive(&sc_empty[e]);
+        if (c + KPS == 4) mbar_arrive(&sc_empty[e]);
       }
       if (++stage == NSTAGE) {
         stage = 0;
@@ -344,16 +337,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
     }
   } else if (warp == 2 || warp == 3) {
     // ------------------------------------------------------------------------------ MMA issuers
-    // Two issuing threads (one MMA stream per thread runs at ~77 cycles per MMA at small N; two
-    // overlap).  Issuer j owns accumulator j of each buffer: with NM == 2 the matrix j (gate / up)
-    // of every stage, with NM == 1 the stages of parity j (the epilogue adds the two partial sums).
+    // One issuing thread runs tcgen05.mma at ~77 cycles per instruction at small N; two overlap.
+    // Issuer j owns slot j of every stage (gate / up matrix, or the stage's first / second K chunk
+    // of down) and accumulator j of each buffer (the epilogue adds the two partial sums for down).
     // Each copies the scales its own MMAs read, so no ordering is needed between the two threads.
     const int j = warp - 2;
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0;
       bool aborted = false;
-      const int m = NM == 2 ? j : 0;
       for (long long it = it0; it < it1 && !aborted; ++it) {
         const int buf = (int)((it - it0) & 1);
         const uint32_t use = (uint32_t)(((it - it0) >> 1) & 1);
@@ -364,28 +356,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
         }
         tc_fence_after();
         const uint32_t d = tbase + (uint32_t)(2 * buf + j) * N;
-        for (int kc = 0; kc < nk; ++kc) {
-          if (NM == 2 || (kc & 1) == j) {
-            if (!mbar_wait(&full[stage], ph)) {
-              set_status(p.status, MIMO_ETIMEOUT);
-              *s_abort = 1;
-              aborted = true;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t sb = smem_u32(stages + stage * SB);
-            const uint32_t blk = smem_u32(sfblk + stage * (NM + 1) * 512);
-            const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * NM * 8 + (NM == 2 ? 8 * j : 0);
-            tc_cp_sf(sf_col, desc_sf(blk + m * 512));       // this matrix's weight scales
-            tc_cp_sf(sf_col + 4, desc_sf(blk + NM * 512));  // activation scales
-            const int first = NM == 2 ? kc : (kc >> 1);     // 0 on this accumulator's first stage
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc_mma_mx(d, desc_sw128(sb + m * kATile + kk * 32), desc_sw128(sb + NM * kATile + kk * 32),
-                        idesc_mx(N, kk), sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30),
-                        (first | kk) != 0);
-            tc_commit(&empty[stage]);
+        for (int ks = 0; ks < ns; ++ks) {
+          if (!mbar_wait(&full[stage], ph)) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            aborted = true;
+            break;
           }
+          tc_fence_after();
+          const uint32_t sb = smem_u32(stages + stage * SB);
+          const uint32_t blk = smem_u32(sfblk + stage * SFB);
+          const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * 16 + 8 * j;
+          const int bj = KPS == 2 ? j : 0;  // activation tile / scale block of this slot's chunk
+          tc_cp_sf(sf_col, desc_sf(blk + j * 512));             // weight scales of the slot
+          tc_cp_sf(sf_col + 4, desc_sf(blk + (2 + bj) * 512));  // activation scales of its chunk
+          const uint32_t a0 = sb + j * kATile, b0 = sb + 2 * kATile + bj * N * kKC;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_mx(d, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc_mx(N, kk),
+                      sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30), (ks | kk) != 0);
+          tc_commit(&empty[stage]);
           if (++stage == NSTAGE) {
             stage = 0;
             ph ^= 1u;
@@ -399,7 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
     }
   } else if (warp >= 4) {
     // --------------------------------------------------------------------------------- epilogue
-    const int quad = warp & 3;
+    const int quad = warp & 3;                     // TMEM lanes this warp may read
+    const int qlo = ((warp - 4) >> 2) * QH;        // its half of the routes: [qlo, qlo + QH)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     bool aborted = false;
     for (long long it = it0; it < it1; ++it) {
@@ -420,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       if (MODE == 0 && live && p.btok) {
         // Columns are tokens: route q reads its token's hi/lo columns.
 #pragma unroll 1
-        for (int q = 0; q < NTOK; ++q) {
+        for (int q = qlo; q < qlo + QH; ++q) {
           float h = 0.f;
           if (q < cnt) {
             const int t = __ldg(p.btok + p0 + q);
@@ -450,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
         }
       }
 #pragma unroll 1
-      for (int q0 = 0; q0 < NTOK && live && !(MODE == 0 && p.btok); q0 += QC) {
+      for (int q0 = qlo; q0 < qlo + QH && live && !(MODE == 0 && p.btok); q0 += QC) {
         float hi[2][QC], lo[2][QC];  // accumulators 0 and 1 of the buffer
 #pragma unroll
         for (int a = 0; a < 2; ++a) {
@@ -512,7 +503,7 @@ static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   auto kfn = tc_expert_kernel<NM, NTOK, NSTAGE, MODE>;
   constexpr int smem = smem_bytes<NM, 2 * NTOK, NSTAGE>();
   static_assert(smem <= 232448, "shared memory budget");
-  static_assert(tmem_cols_needed<NM, 2 * NTOK, NSTAGE>() <= 512, "TMEM budget");
+  static_assert(tmem_cols_needed<2 * NTOK, NSTAGE>() <= 512, "TMEM budget");
   static_assert((2 * NSTAGE + 4 + 4 + 1) * 8 + 8 <= kBarBytes, "barrier area");
   if (p.K % (4 * kKC) != 0 || p.Nw % kM != 0 || p.tiles != p.Nw / kM) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -159,18 +159,41 @@ cudaError_t fp4_weight_map(CUtensorMap* out, const void* base, uint64_t rows, ui
   return cudaSuccess;
 }
 
-cudaError_t fp4_prefetch_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K) {
-  const Key key{(uint64_t)base, rows, K, 6, 0};
+cudaError_t fp4_weight_map3(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K, int chunks) {
+  const Key key{(uint64_t)base, rows, K, 6, chunks};
   if (cached(key, out)) return cudaSuccess;
   auto fn = encode_fn();
-  if (!fn || K % 1024 != 0 || ((uint64_t)base & 31) != 0) return cudaErrorInvalidValue;
+  if (!fn || K % 128 != 0 || ((uint64_t)base & 31) != 0 || (K / 2) % 32 != 0 || chunks < 1 || chunks > 8)
+    return cudaErrorInvalidValue;
   CUtensorMap m;
   const cuuint64_t dims[3] = {128, rows, K / 128};
   const cuuint64_t strides[2] = {K / 2, 64};
-  const cuuint32_t box[3] = {128, 128, 8};
+  const cuuint32_t box[3] = {128, 128, (cuuint32_t)chunks};
   const cuuint32_t es[3] = {1, 1, 1};
   const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, const_cast<void*>(base), dims, strides, box,
-                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
+cudaError_t rows_map3(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows,
+                      int chunks) {
+  const Key key{(uint64_t)base, rows, row_bytes, 7, box_rows * 16 + chunks};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || row_bytes % 128 != 0 || box_rows < 1 || box_rows > 256 || chunks < 1 || chunks > 8 ||
+      ((uint64_t)base & 15) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {128, rows, row_bytes / 128};
+  const cuuint64_t strides[2] = {row_bytes, 128};
+  const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)chunks};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   remember(key, m);

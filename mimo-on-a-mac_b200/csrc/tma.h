@@ -25,9 +25,13 @@ cudaError_t scale_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_
 // 16U4_ALIGN16B (each 16 values land as 8 data bytes + 8 gap bytes), box [128 values, 128 rows],
 // 128B swizzle.  K must be a multiple of 128 and the rows 32-byte aligned.
 cudaError_t fp4_weight_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K);
-// L2-prefetch view of the same weights: dims [128 values, rows, K / 128 chunks] (chunk stride 64 B),
-// box [128, 128, 8]: one prefetch covers 512 contiguous bytes of each of 128 rows.
-cudaError_t fp4_prefetch_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K);
+// 3-D view of the same weights: dims [128 values, rows, K / 128 chunks] (chunk stride 64 B), box
+// [128, 128, chunks], 128B swizzle: lands as `chunks` consecutive 16 KiB tiles [row][128 B].
+cudaError_t fp4_weight_map3(CUtensorMap* out, const void* base, uint64_t rows, uint64_t K, int chunks);
+// 3-D view of a byte matrix [rows][row_bytes]: dims [128, rows, row_bytes / 128], box
+// [128, box_rows, chunks], 128B swizzle: lands as `chunks` consecutive [box_rows][128 B] tiles.
+cudaError_t rows_map3(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows,
+                      int chunks);
 // Scale-matrix map [rows][row_bytes], box [16 bytes, box_rows], no swizzle.
 cudaError_t sf_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
 // bf16 matrix map [rows][cols], box [64 values, box_rows], 128B swizzle; rows past the end read 0.
