@@ -537,7 +537,7 @@ size_t mimo_moe_block_workspace_bytes(int32_t T, int32_t H, int32_t I, int32_t E
   c.take<float>((size_t)T * topk);
   c.take<int32_t>(1);
   if (T <= 8) {
-    c.take<float>((size_t)(H / 256) * T * E);
+    c.take<float>((size_t)T * E);  // router scores
     const GroupWs g = carve_group(c, T, topk, 8, E);
     carve_decode(c, T, g.ucap, 8, H, I);
   } else {
@@ -563,7 +563,7 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
   if (idx_out) idx = idx_out;
   if (w_out) wts = w_out;
   if (T <= 8) {
-    c.take<float>((size_t)(H / 256) * T * E);  // (kept: layout shared with the size query)
+    float* score = c.take<float>((size_t)T * E);  // router scores (sigmoid of the logits)
     const GroupWs g = carve_group(c, T, topk, 8, E);
     const DecodeWs dw = carve_decode(c, T, g.ucap, 8, H, I);
     if (c.off > workspace_bytes) return MIMO_EINVAL;
@@ -572,7 +572,7 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
     const bool tc = tc_path(pools);
     MIMO_TRY(launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, counter, g.uids,
                                  g.urows, g.ucnt, g.uw, g.gidx, g.nu, tc ? nullptr : dw.x16,
-                                 tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, status, st));
+                                 tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, score, status, st));
     return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
                        T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/!tc, /*terms_ready=*/tc);
   }

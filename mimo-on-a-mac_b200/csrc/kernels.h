@@ -111,7 +111,7 @@ cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const floa
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
-                                int32_t* status, cudaStream_t st);
+                                float* score, int32_t* status, cudaStream_t st);
 cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);

@@ -7,64 +7,77 @@
 namespace mimo {
 
 // Selection key order: larger sel first, ties -> smaller expert id first (NaN mapped to -inf).
-__device__ __forceinline__ bool key_better(float a, int ia, float b, int ib) {
-  if (a != b) return a > b;
-  return ia < ib;
+
+// s = sigmoid(logit) evaluated in double and rounded once to float32 (the router's score).
+__device__ __forceinline__ float sigmoid_score(float logit) {
+  return (float)(1.0 / (1.0 + exp(-(double)logit)));
 }
 
-// One warp selects the top-k of one token's E <= 256 logits.  s = sigmoid(logit) in double, rounded
-// once to float32; sel = s + bias in float32; weights s / (sum + 1e-20) with the float32 sum taken in
-// output order.  Logits are read through L2 (they may come from other CTAs of the same kernel).
-__device__ __forceinline__ void topk_warp(const float* logits_row, const float* bias, int E, int topk,
-                                          int32_t* idx_row, float* w_row) {
+// One warp selects the top-k of one token's E <= 256 experts.  s = sigmoid_score(logit);
+// sel = s + bias in float32; weights s / (sum + 1e-20) with the float32 sum taken in output order.
+// PRE: `row` already holds the scores s (computed by the CTAs that produced the logits); otherwise it
+// holds logits.  Rows are read through L2 (they may come from other CTAs of the same kernel).
+// idx_s / w_s (optional, e.g. shared memory) receive a copy of the selection.
+template <bool PRE>
+__device__ __forceinline__ void topk_warp_impl(const float* row, const float* bias, int E, int topk,
+                                               int32_t* idx_row, float* w_row, int32_t* idx_s, float* w_s) {
   const int lane = threadIdx.x & 31;
   constexpr int kMaxPer = 8;
   const int per = E >> 5;
-  float sv[kMaxPer], key[kMaxPer];
+  float sv[kMaxPer], key[kMaxPer], bz[kMaxPer];
+  // All loads first (independent, so their L2 latencies overlap), then the arithmetic.
 #pragma unroll
   for (int j = 0; j < kMaxPer; ++j) {
-    sv[j] = 0.f;
+    const int e = lane + 32 * j;
+    sv[j] = j < per ? __ldcg(row + e) : 0.f;
+    bz[j] = (bias && j < per) ? __ldg(bias + e) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
     key[j] = -INFINITY;
     if (j < per) {
-      const int e = lane + 32 * j;
-      const double l = (double)__ldcg(logits_row + e);
-      const float s = (float)(1.0 / (1.0 + exp(-l)));
-      const float sel = s + (bias ? bias[e] : 0.f);
+      const float s = PRE ? sv[j] : sigmoid_score(sv[j]);
+      const float sel = s + bz[j];
       sv[j] = s;
       key[j] = isnan(sel) ? -INFINITY : sel;
+    } else {
+      sv[j] = 0.f;
     }
   }
-  unsigned taken = 0u;
+  // Branch-free selection: candidate keys as (order-preserving bits of sel, ~id) pairs, so "larger
+  // sel, then smaller id" is a lexicographic maximum; each round takes two warp max-reductions.
+  uint32_t kh[kMaxPer], kl[kMaxPer];
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    const uint32_t u = __float_as_uint(key[j] + 0.0f);  // -0 -> +0: equal keys compare equal
+    kh[j] = j < per ? ((u >> 31) ? ~u : (u | 0x80000000u)) : 0u;  // valid keys are > 0 (-inf -> 0x007FFFFF)
+    kl[j] = j < per ? ~(uint32_t)(lane + 32 * j) : 0u;
+  }
   float tot = 0.f, my_s = 0.f;
   int my_id = 0;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     if (r < topk) {
-      float bk = -INFINITY, bs = 0.f;
-      int bid = 0x7FFFFFFF;
+      uint32_t bh = 0u, bl = 0u;
 #pragma unroll
       for (int j = 0; j < kMaxPer; ++j) {
-        if (j < per && !(taken & (1u << j))) {
-          const int e = lane + 32 * j;
-          if (bid == 0x7FFFFFFF || key_better(key[j], e, bk, bid)) {
-            bk = key[j];
-            bid = e;
-            bs = sv[j];
-          }
-        }
+        const bool better = kh[j] > bh || (kh[j] == bh && kl[j] > bl);
+        bh = better ? kh[j] : bh;
+        bl = better ? kl[j] : bl;
       }
+      const uint32_t wh = __reduce_max_sync(0xFFFFFFFFu, bh);
+      const uint32_t wl = __reduce_max_sync(0xFFFFFFFFu, bh == wh ? bl : 0u);
+      const int bid = (int)~wl;
+      const int owner = bid & 31, jw = bid >> 5;
+      float s_own = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ok = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
-        const int oid = __shfl_xor_sync(0xFFFFFFFFu, bid, o);
-        const float os = __shfl_xor_sync(0xFFFFFFFFu, bs, o);
-        if (oid != 0x7FFFFFFF && (bid == 0x7FFFFFFF || key_better(ok, oid, bk, bid))) {
-          bk = ok;
-          bid = oid;
-          bs = os;
-        }
+      for (int j = 0; j < kMaxPer; ++j) {
+        const bool hit = (j == jw) && (lane == owner);
+        s_own = hit ? sv[j] : s_own;
+        kh[j] = hit ? 0u : kh[j];
+        kl[j] = hit ? 0u : kl[j];
       }
-      if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
+      const float bs = __shfl_sync(0xFFFFFFFFu, s_own, owner);
       tot = __fadd_rn(tot, bs);
       if (lane == r) {
         my_s = bs;
@@ -74,12 +87,23 @@ __device__ __forceinline__ void topk_warp(const float* logits_row, const float* 
   }
   tot = __fadd_rn(tot, 1e-20f);
   if (lane < topk) {
+    const float wv = __fdiv_rn(my_s, tot);
     idx_row[lane] = my_id;
-    w_row[lane] = __fdiv_rn(my_s, tot);
+    w_row[lane] = wv;
+    if (idx_s) {
+      idx_s[lane] = my_id;
+      w_s[lane] = wv;
+    }
   }
 }
+__device__ __forceinline__ void topk_warp(const float* logits_row, const float* bias, int E, int topk,
+                                          int32_t* idx_row, float* w_row) {
+  topk_warp_impl<false>(logits_row, bias, E, topk, idx_row, w_row, nullptr, nullptr);
+}
 
-// CTA-wide grouping of P <= blockDim.x routes.  sid/bitmap are shared scratch (sid[P], bitmap[32]).
+// CTA-wide grouping of P <= blockDim.x routes (idx / weight: global or shared memory, written before
+// the call's first barrier by this CTA or by an earlier kernel).  sid/bitmap are shared scratch
+// (sid[P], bitmap[32]).
 // Distinct ids ascending (bitmap popcount rank); routes of one id in flat (row, k) order.  Pads
 // urows/uw of the first ucap ids with zeros like the reference.  Ends with a __syncthreads().
 __device__ __forceinline__ void group_routes_cta(const int32_t* idx, const float* weight, int P, int topk,
@@ -101,7 +125,7 @@ __device__ __forceinline__ void group_routes_cta(const int32_t* idx, const float
   __syncthreads();
   int id = -1;
   if (t < P) {
-    id = __ldcg(idx + t);
+    id = idx[t];
     if (id < 0 || id >= E) {
       set_status(status, MIMO_ERANGE);
       id = -1;
@@ -131,7 +155,7 @@ __device__ __forceinline__ void group_routes_cta(const int32_t* idx, const float
         gidx[t] = -1;
       } else {
         urows[u * R + c] = t / topk;
-        uw[u * R + c] = __ldcg(weight + t);
+        uw[u * R + c] = weight[t];
         gidx[t] = u * R + c;
       }
     } else {

@@ -89,7 +89,8 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // Decode (T <= 8) routing in one launch.  Logits on the tensor cores: CTA c owns router rows
 // [16c, 16c+16); its warp w multiplies them by the T tokens over the K slices w, w+16, ... (256 elements
 // each) with bf16 MMAs (exact products, float32 accumulation); the warps' partial sums are added in
-// warp order in shared memory.  The last CTA to finish (atomic ticket, no waiting) selects the top-k of
+// warp order in shared memory, and each CTA turns its logits into scores (the exact sigmoid) at once.
+// The last CTA to finish (atomic ticket, no waiting) selects the top-k of
 // every token, groups the routes by distinct expert (group_routes, engine/mimo_stream/kernels.py:149-173)
 // and (x16 non-null) writes the f16 copy of x that the mma.sync expert kernels read.  With xq non-null,
 // every CTA also splits its share of x into the e4m3 terms the tensor-core expert kernels read.
@@ -100,18 +101,23 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
     float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
     int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
-    uint8_t* __restrict__ xs, int32_t* status) {
+    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status) {
   __shared__ float red[kRouteWarps][128];
-  if (xq) {  // e4m3 terms of x for the tensor-core expert path: token t -> rows t (hi) and 8 + t (lo)
+  // e4m3 terms of x for the tensor-core expert path (token t -> rows t (hi) and 8 + t (lo)): 32-value
+  // blocks spread evenly over the CTAs, split after the logits (off the critical path; in the last
+  // CTA by the warps that do not select).  first_thread: the CTA thread taking its first block.
+  auto split_share = [&](int first_thread) {
     const int nb = H / 32;
-    for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < T * nb; b += gridDim.x * blockDim.x) {
+    for (int b = (threadIdx.x - first_thread) * gridDim.x + blockIdx.x; b < T * nb;
+         b += gridDim.x * (blockDim.x - first_thread)) {
       const int t = b / nb, blk = b - t * nb;
       tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
                         xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
                         xs + (size_t)(8 + t) * nb + blk, status);
     }
-  }
-  __shared__ int32_t sid[64];
+  };
+  __shared__ int32_t sid[64], s_idx[64];
+  __shared__ float s_w[64];
   __shared__ uint32_t bitmap[32];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -149,18 +155,26 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
 #pragma unroll
       for (int ww = 0; ww < kRouteWarps; ++ww) sum += red[ww][threadIdx.x];
       logits[(size_t)tok * E + e0 + row] = sum;
+      score[(size_t)tok * E + e0 + row] = sigmoid_score(sum);  // off the last CTA's serial path
     }
   }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
   __syncthreads();
-  if (!is_last) return;
+  if (!is_last) {
+    if (xq) split_share(0);
+    return;
+  }
   __threadfence();
-  if (warp < T) topk_warp(logits + (size_t)warp * E, bias, E, topk, idx + warp * topk, wts + warp * topk);
+  if (warp < T)
+    topk_warp_impl<true>(score + (size_t)warp * E, bias, E, topk, idx + warp * topk, wts + warp * topk,
+                         s_idx + warp * topk, s_w + warp * topk);
+  else if (xq && threadIdx.x >= 256)
+    split_share(256);
   __syncthreads();
   const int P = T * topk;
-  group_routes_cta(idx, wts, P, topk, R, E, min(E, P), uids, urows, ucnt, uw, gidx, num_unique, status,
+  group_routes_cta(s_idx, s_w, P, topk, R, E, min(E, P), uids, urows, ucnt, uw, gidx, num_unique, status,
                    sid, bitmap);
   for (int i = threadIdx.x * 2; x16 && i < T * H; i += blockDim.x * 2) {
     const uint32_t v = *reinterpret_cast<const uint32_t*>(x + i);
@@ -316,13 +330,13 @@ cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const floa
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
-                                int32_t* status, cudaStream_t st) {
+                                float* score, int32_t* status, cudaStream_t st) {
   if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
   route_decode_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, bias, T, H, E, topk, R, logits, idx, wts,
                                                            counter, uids, urows, ucnt, uw, gidx, num_unique,
-                                                           x16, xq, xs, status);
+                                                           x16, xq, xs, score, status);
   return cudaGetLastError();
 }
 
