@@ -86,9 +86,9 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-def make_inputs(B, dev, torch):
+def make_inputs(B, dev, torch, rank=0):
     from oracle import synth  # seeded generators only (no oracle math on this path)
-    xs = [synth.hidden(B, seed=2 + 1000 * i).to(dev) for i in range(NBATCH)]
+    xs = [synth.hidden(B, seed=2 + 1000 * i + 100000 * rank).to(dev) for i in range(NBATCH)]
     W = synth.router_weight().to(dev)
     return xs, W
 
@@ -181,16 +181,35 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     B = WORKLOADS[args.workload]
     NE = args.pool_experts
-    pool = mimo_moe.ExpertPools.synthetic(NE, seed=0, layer=0, device=dev)
-    xs, W = make_inputs(B, dev, torch)
+    ep = world > 1  # expert parallelism: rank r holds experts [r*NE/N, (r+1)*NE/N), routes its own B tokens
+    if ep:
+        from mimo_moe.ep import ExpertParallelMoE, expert_range
+        lo, hi = expert_range(rank, world, NE)
+        pool = mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=0, first_expert=lo, device=dev)
+    else:
+        lo, hi = 0, NE
+        pool = mimo_moe.ExpertPools.synthetic(NE, seed=0, layer=0, device=dev)
+    xs, W = make_inputs(B, dev, torch, rank)
     W = W[:NE].contiguous()
     bias = torch.zeros(NE, device=dev)
     y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     L = mimo_moe.lib()
+    blk = ExpertParallelMoE(pool, W, bias, num_experts=NE) if ep else None
+    # expert parallelism replays one CUDA graph per step (router, collectives, expert kernels, combine):
+    # the step issues ~10 kernels and 2 collectives, whose host-side launch cost would otherwise set
+    # the pace.  The x copy into the graph's input is inside the step.
+    from mimo_moe.ep import GraphedStep
+    gstep = GraphedStep(blk, B, H, dev) if ep else None
+
+    def block(x):
+        return gstep(x) if ep else mimo_moe.moe_block(x, W, bias, pool, status=status)
 
     def step(i):
-        mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
+        if ep:
+            gstep(xs[i % NBATCH])
+        else:
+            mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
 
     for i in range(max(3, args.warmup)):
         step(i)
@@ -212,8 +231,15 @@ def main():
         dist.barrier()
     ms = ev0.elapsed_time(ev1)
     clk = clocks.stop()
-    launches = (ctypes_arr := (np.zeros(4, np.int32), np.zeros(4, np.float32)))
+    launches = (np.zeros(4, np.int32), np.zeros(4, np.float32))
     _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
+    if ep:  # graph replays carry no profiling events: time the expert kernels in an eager pass
+        nprof = min(args.steps, 50)
+        _lib.check(L.mimo_moe_profile_enable(4 * nprof + 8), "profile_enable")
+        for i in range(nprof):
+            blk(xs[i % NBATCH])
+        torch.cuda.synchronize()
+        _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
     _lib.check(L.mimo_moe_profile_enable(0), "profile_disable")
     if int(status.item()) != 0:
         raise RuntimeError(f"device status {int(status.item())} during the bench")
@@ -222,17 +248,27 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
 
-    # distinct experts per batch (deterministic routes) -> algorithmic bytes
-    U = []
+    # distinct experts per batch (deterministic routes) -> algorithmic bytes; with expert parallelism
+    # U counts the distinct experts over all ranks' tokens (each lives on one rank) and U_local this
+    # rank's share, which its kernels stream
+    U, U_local = [], []
     for i in range(NBATCH):
         idx, _ = mimo_moe.router(xs[i], W, bias)
-        U.append(int(torch.unique(idx).numel()))
+        idx = idx.to(torch.int32).contiguous()
+        if ep:
+            allidx = torch.empty(world * idx.shape[0], idx.shape[1], dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(allidx, idx)
+            idx = allidx
+        u = torch.unique(idx)
+        U.append(int(u.numel()))
+        U_local.append(int(((u >= lo) & (u < hi)).sum().item()))
     steps_U = [U[i % NBATCH] for i in range(args.steps)]
+    steps_Ul = [U_local[i % NBATCH] for i in range(args.steps)]
     hbm, tflops_peak, peak_kind = peaks()
     kind_gu, kind_dn = (0, 1) if B <= 8 else (2, 3)
     gu_ms = float(launches[1][kind_gu]) / max(1, int(launches[0][kind_gu]))
     dn_ms = float(launches[1][kind_dn]) / max(1, int(launches[0][kind_dn]))
-    gu_bytes = statistics.mean(steps_U) * GATEUP_BYTES
+    gu_bytes = statistics.mean(steps_Ul) * GATEUP_BYTES
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
     if B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
         roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
@@ -261,7 +297,7 @@ def main():
     e0.record()
     for i in range(args.steps):
         xd = xh[i % NBATCH].to(dev, non_blocking=True)
-        yd = mimo_moe.moe_block(xd, W, bias, pool, status=status)
+        yd = block(xd)
         yh.copy_(yd, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -281,16 +317,22 @@ def main():
         # our kernels per step: decode = route (+ its counter memset, not counted), gate/up, down,
         # combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
         # down, combine
-        launches_per_step = 4 if B <= 8 else 11
+        # expert parallelism: router logits + top-k, 3 dispatch, 2 unit builders, term split, gate/up,
+        # down, combine (the NCCL collectives are library kernels and not counted)
+        launches_per_step = 10 if ep else (4 if B <= 8 else 11)
         out = {
             "metric": f"MoE-layer tok/s ({args.workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "e2m1 x e4m3 (two-term activations) -> f32, tcgen05 block-scaled",
             "data": "synthetic (seeded MXFP4 pool, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
-            "config": {"workload": args.workload, "B": B, "experts": NE, "hidden": H, "inter": I,
+            "config": {"workload": args.workload, "B": B * world, "experts": NE, "hidden": H, "inter": I,
                        "topk": K_TOP, "routing": "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
-                       "parallelism": "replicas" if world > 1 else "single",
+                       "mean_distinct_experts_this_gpu": statistics.mean(steps_Ul),
+                       "parallelism": f"ep{world} (experts sharded {NE // world} per GPU; all-gather "
+                                      "dispatch, exact reduce-scatter return, fixed-order combine)"
+                                      if ep else "single",
+                       "tokens_per_gpu": B,
                        "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
             "expert_gbs": expert_gbs,
             "expert_frac_of_measured_hbm": expert_gbs / hbm,
@@ -303,6 +345,8 @@ def main():
         }
         print(json.dumps(out))
     if world > 1:
+        del gstep  # a graph holding NCCL calls must be released before the process group
+        torch.cuda.synchronize()
         dist.destroy_process_group()
 
 

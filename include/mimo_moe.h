@@ -138,6 +138,30 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
                    float* w_out, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * Expert parallelism building blocks (the reference runs on one device; these follow the multi-GPU
+ * design of the B200 build: experts [expert_base, expert_base + S) live on this GPU).
+ *
+ * mimo_moe_experts_routes: per-route products of every route whose expert is local.  x holds `rows`
+ * token rows (bf16 [rows, H]); idx/weight are [rows, topk] global expert ids and router weights.
+ * part (float32 [rows * topk, H]) is zeroed, then row r * topk + k receives
+ * fp32(down . SwiGLU(gate . x_r, up . x_r)) * weight[r, k] for local routes (bf16-rounded before the
+ * weight when pairs_rounding != 0, the M = 1 stock path), exactly the per-route partial of
+ * mimo_moe_experts (kernels.py:120; model.py:173-182).  Non-local routes stay zero, so the partials
+ * of all ranks can be summed exactly (one nonzero term per element) before the fixed-order combine.
+ * Workspace: mimo_moe_experts_routes_workspace_bytes(rows, topk, H, I, S).
+ *
+ * mimo_moe_combine: y[m] = bf16(sum over k in order of part[gather_idx[m * topk + k]]) with
+ * gather_idx = NULL meaning row m * topk + k (kernels.py:194-199).
+ */
+size_t mimo_moe_experts_routes_workspace_bytes(int32_t rows, int32_t topk, int32_t H, int32_t I, int32_t S);
+int mimo_moe_experts_routes(const uint16_t* x, int32_t rows, const mimo_moe_pools* pools, int32_t expert_base,
+                            const int32_t* idx, const float* weight, int32_t topk, int32_t pairs_rounding,
+                            float* part, void* workspace, size_t workspace_bytes, int32_t* status,
+                            void* stream);
+int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,
+                     uint16_t* y, void* stream);
+
+/*
  * Synthetic pool fill (benchmarks and tests): counter-based splitmix64 stream per (seed, layer, tensor);
  * experts [first_expert, first_expert + S) of the layer are written to slots [0, S).  Nibbles uniform
  * over the 16 e2m1 codes; scale bytes 120 with p = 0.6875, else 119.

@@ -151,6 +151,31 @@ PrefillWs carve_prefill(Carver& c, int T, int topk, int H, int I, int E) {
   return w;
 }
 
+// Expert-parallel per-route products: dispatch tables + units of up to 8 routes + term matrices.
+struct RoutesWs {
+  int32_t *offsets, *order, *inv, *unit_slot, *unit_p0, *unit_cnt, *num_units, *rtok;
+  float* rw;
+  void* dws;
+  int ucap;
+  TermWs t;
+};
+RoutesWs carve_routes(Carver& c, int P, int H, int I, int S) {
+  RoutesWs w;
+  w.ucap = P / kTcDecodeRoutes + S;
+  w.offsets = c.take<int32_t>(S + 1);
+  w.order = c.take<int32_t>(P);
+  w.inv = c.take<int32_t>(P);
+  w.dws = c.take<uint8_t>(dispatch_workspace_bytes(P, S));
+  w.unit_slot = c.take<int32_t>(w.ucap);
+  w.unit_p0 = c.take<int32_t>(w.ucap);
+  w.unit_cnt = c.take<int32_t>(w.ucap);
+  w.num_units = c.take<int32_t>(1);
+  w.rtok = c.take<int32_t>(P);
+  w.rw = c.take<float>(P);
+  w.t = carve_terms(c, w.ucap, kTcDecodeRoutes, H, I);
+  return w;
+}
+
 struct GroupWs {
   int32_t *uids, *urows, *ucnt, *gidx, *nu;
   float* uw;
@@ -217,7 +242,8 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
            const int32_t* ucnt, const int32_t* up0, int p0_stride, const int32_t* ufirst,
            const int32_t* unsub, const int32_t* rtok, const float* rw,
            const int32_t* num_units, int ucap, int pairs_rounding, const TermWs& t, float* part,
-           uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false) {
+           uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false,
+           const int32_t* out_row = nullptr) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
   const int N = 2 * routes;
@@ -268,6 +294,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   q.hs = nullptr;
   q.rw = rw;
   q.part = part;
+  q.out_row = out_row;
   q.ypair = ypair;
   q.pairs_rounding = pairs_rounding;
   MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
@@ -581,6 +608,43 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
   MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st, status));
   MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, wts, st));
   return run_prefill(x, pools, nullptr, idx, wts, T, topk, E, y, pw, status, st);
+}
+
+size_t mimo_moe_experts_routes_workspace_bytes(int32_t rows, int32_t topk, int32_t H, int32_t I, int32_t S) {
+  if (rows < 1 || topk < 1 || S < 1 || !dims_ok(H, I)) return 0;
+  Carver c(nullptr);
+  carve_routes(c, rows * topk, H, I, S);
+  return c.off;
+}
+
+int mimo_moe_experts_routes(const uint16_t* x, int32_t rows, const mimo_moe_pools* pools, int32_t expert_base,
+                            const int32_t* idx, const float* weight, int32_t topk, int32_t pairs_rounding,
+                            float* part, void* workspace, size_t workspace_bytes, int32_t* status,
+                            void* stream) {
+  if (!x || !pools_ok(pools) || !idx || !weight || !part || !workspace || !status || rows < 1 || topk < 1 ||
+      topk > 8 || expert_base < 0 || (int64_t)rows * topk > (1 << 24) || pools->num_slots > 1024)
+    return MIMO_EINVAL;
+  const int P = rows * topk, S = pools->num_slots, H = pools->hidden, I = pools->inter;
+  Carver c(workspace);
+  const RoutesWs w = carve_routes(c, P, H, I, S);
+  if (c.off > workspace_bytes) return MIMO_EINVAL;
+  if (!tc_path(pools)) return MIMO_EINVAL;  // needs the TMA alignment of the tensor-core path
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MIMO_TRY(cudaMemsetAsync(part, 0, (size_t)P * H * sizeof(float), st));
+  MIMO_TRY(launch_dispatch(idx, P, S, w.offsets, w.order, w.inv, w.dws, status, st, expert_base, 1));
+  MIMO_TRY(launch_build_units(w.offsets, nullptr, S, S, kTcDecodeRoutes, w.ucap, w.unit_slot, w.unit_p0,
+                              w.unit_cnt, nullptr, nullptr, w.num_units, w.order, weight, P, topk, w.rtok,
+                              w.rw, status, st));
+  return run_tc(x, pools, kTcDecodeRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, nullptr, nullptr, w.rtok,
+                w.rw, w.num_units, w.ucap, pairs_rounding, w.t, part, nullptr, status, st, 0, false, w.order);
+}
+
+int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,
+                     uint16_t* y, void* stream) {
+  if (!part || !y || M < 1 || topk < 1 || topk > 8 || H < 4 || H % 4) return MIMO_EINVAL;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MIMO_TRY(launch_combine_rows(part, gather_idx, M, topk, H, y, st));
+  return MIMO_OK;
 }
 
 int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up_w, uint8_t* up_s,

@@ -38,6 +38,7 @@ constexpr int kDispThreads = 256;
 __global__ void __launch_bounds__(kDispThreads) dispatch_count_kernel(const int32_t* __restrict__ idx,
                                                                       int P, int E,
                                                                       int32_t* __restrict__ chunk_counts,
+                                                                      int id_base, int skip_outside,
                                                                       int32_t* status) {
   extern __shared__ int32_t hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
@@ -46,10 +47,10 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_count_kernel(const int3
   for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
     const int p = base + i;
     if (p < P) {
-      const int id = idx[p];
+      const int id = idx[p] - id_base;
       if (id >= 0 && id < E)
         atomicAdd(&hist[id], 1);
-      else
+      else if (!skip_outside)
         set_status(status, MIMO_ERANGE);
     }
   }
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(1024) dispatch_scan_kernel(int32_t* __restrict
 // count table.
 __global__ void __launch_bounds__(kDispThreads) dispatch_scatter_kernel(
     const int32_t* __restrict__ idx, int P, int E, const int32_t* __restrict__ chunk_base,
-    int32_t* __restrict__ order, int32_t* __restrict__ inv) {
+    int32_t* __restrict__ order, int32_t* __restrict__ inv, int id_base) {
   extern __shared__ int32_t sm[];
   constexpr int kWarps = kDispThreads / 32;
   constexpr int kPerWarp = kChunk / kWarps;  // 256
@@ -104,7 +105,7 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_scatter_kernel(
   const unsigned lt = (1u << lane) - 1u;
   for (int b = 0; b < kPerWarp; b += 32) {
     const int p = wbase + b + lane;
-    int id = (p < P) ? idx[p] : -1;
+    int id = (p < P) ? idx[p] - id_base : -1;
     if (id >= E || id < 0) id = -1;
     const unsigned peers = __match_any_sync(0xFFFFFFFFu, id);
     if (id >= 0 && (peers & lt) == 0u) wcnt[warp * E + id] += __popc(peers);
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_scatter_kernel(
   __syncthreads();
   for (int b = 0; b < kPerWarp; b += 32) {
     const int p = wbase + b + lane;
-    int id = (p < P) ? idx[p] : -1;
+    int id = (p < P) ? idx[p] - id_base : -1;
     if (id >= E || id < 0) id = -1;
     const unsigned peers = __match_any_sync(0xFFFFFFFFu, id);
     int pos = -1;
@@ -143,13 +144,15 @@ size_t dispatch_workspace_bytes(int P, int E) {
 }
 
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* order,
-                            int32_t* inv, void* ws, int32_t* status, cudaStream_t st) {
+                            int32_t* inv, void* ws, int32_t* status, cudaStream_t st, int id_base,
+                            int skip_outside) {
   const int nchunks = std::max(1, (P + kChunk - 1) / kChunk);
   int32_t* cc = static_cast<int32_t*>(ws);
-  dispatch_count_kernel<<<nchunks, kDispThreads, E * sizeof(int32_t), st>>>(idx, P, E, cc, status);
+  dispatch_count_kernel<<<nchunks, kDispThreads, E * sizeof(int32_t), st>>>(idx, P, E, cc, id_base,
+                                                                             skip_outside, status);
   dispatch_scan_kernel<<<1, 1024, 0, st>>>(cc, nchunks, E, offsets);
   dispatch_scatter_kernel<<<nchunks, kDispThreads, (kDispThreads / 32) * E * sizeof(int32_t), st>>>(
-      idx, P, E, cc, order, inv);
+      idx, P, E, cc, order, inv, id_base);
   return cudaGetLastError();
 }
 

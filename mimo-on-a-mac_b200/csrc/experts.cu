@@ -730,6 +730,35 @@ cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const 
   return cudaGetLastError();
 }
 
+// y[m] = bf16(sum over k in order of part[row]) with row = gidx[m * topk + k] (skipped when < 0), or
+// m * topk + k without gidx (kernels.py:194-199).
+__global__ void combine_rows_kernel(const float* __restrict__ part, const int32_t* __restrict__ gidx, int M,
+                                    int topk, int H, uint16_t* __restrict__ y) {
+  const int t = blockIdx.y;
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (t >= M || m >= H) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < topk; ++k) {
+    const int sl = gidx ? gidx[t * topk + k] : t * topk + k;
+    if (sl < 0) continue;
+    const float4 v = *reinterpret_cast<const float4*>(part + (size_t)sl * H + m);
+    acc.x = __fadd_rn(acc.x, v.x);
+    acc.y = __fadd_rn(acc.y, v.y);
+    acc.z = __fadd_rn(acc.z, v.z);
+    acc.w = __fadd_rn(acc.w, v.w);
+  }
+  const uint32_t o0 = f32_to_bf16(acc.x) | (f32_to_bf16(acc.y) << 16);
+  const uint32_t o1 = f32_to_bf16(acc.z) | (f32_to_bf16(acc.w) << 16);
+  *reinterpret_cast<uint2*>(y + (size_t)t * H + m) = make_uint2(o0, o1);
+}
+
+cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H, uint16_t* y,
+                                cudaStream_t st) {
+  dim3 grid((H / 4 + 255) / 256, M);
+  combine_rows_kernel<<<grid, 256, 0, st>>>(part, gidx, M, topk, H, y);
+  return cudaGetLastError();
+}
+
 // Prefill (model.py:266-271): y[t, m] = bf16(sum_k fp32(ypair[inv[t, k], m]) * w[t, k]) in k order.
 __global__ void combine_prefill_kernel(const uint16_t* __restrict__ ypair, const int32_t* __restrict__ inv,
                                        const float* __restrict__ w, int T, int topk, int H,

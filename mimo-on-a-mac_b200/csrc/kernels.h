@@ -85,6 +85,7 @@ struct TcParams {
   uint8_t* hs;                // gate/up: h term scales [units * 2 * ntok][Nw / 32]
   float* part;                // down, decode: [P][Nw] = dot * weight
   uint16_t* ypair;            // down, prefill: [P][Nw] bf16(dot)
+  const int32_t* out_row;     // down, decode kinds: partial of sorted route i goes to row out_row[i]
   int pairs_rounding;
   int32_t* status;
 };
@@ -116,8 +117,11 @@ cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, 
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);
 size_t dispatch_workspace_bytes(int P, int E);
+// Routes with expert id - id_base outside [0, E) are dropped (inv = -1); they set MIMO_ERANGE unless
+// skip_outside (expert parallelism: routes to other ranks' experts).
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* order,
-                            int32_t* inv, void* ws, int32_t* status, cudaStream_t st);
+                            int32_t* inv, void* ws, int32_t* status, cudaStream_t st, int id_base = 0,
+                            int skip_outside = 0);
 cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, int E, int S,
                                int unit_max, int ucap, int32_t* unit_slot, int32_t* unit_p0,
                                int32_t* unit_cnt, int32_t* unit_first, int32_t* unit_nsub,
@@ -127,6 +131,8 @@ cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, i
 cudaError_t launch_to_f16(const uint16_t* x, __half* y, size_t n, int32_t* status, cudaStream_t st);
 // kind: 0 decode gate/up, 1 decode down, 2 prefill gate/up, 3 prefill down
 cudaError_t launch_expert_tiles(const ExpertParams& p, int kind, int num_sms, cudaStream_t st);
+cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H, uint16_t* y,
+                                cudaStream_t st);
 cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const int32_t* urows,
                                   const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
                                   int M, int topk, int H, uint16_t* y, cudaStream_t st);

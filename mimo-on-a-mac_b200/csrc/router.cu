@@ -96,30 +96,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // every CTA also splits its share of x into the e4m3 terms the tensor-core expert kernels read.
 // `counter` must be zero at launch; the last CTA resets it.
 constexpr int kRouteWarps = 16;
-__global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const float* __restrict__ bias, int T,
-    int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
-    float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
-    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
-    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status) {
-  __shared__ float red[kRouteWarps][128];
-  // e4m3 terms of x for the tensor-core expert path (token t -> rows t (hi) and 8 + t (lo)): 32-value
-  // blocks spread evenly over the CTAs, split after the logits (off the critical path; in the last
-  // CTA by the warps that do not select).  first_thread: the CTA thread taking its first block.
-  auto split_share = [&](int first_thread) {
-    const int nb = H / 32;
-    for (int b = (threadIdx.x - first_thread) * gridDim.x + blockIdx.x; b < T * nb;
-         b += gridDim.x * (blockDim.x - first_thread)) {
-      const int t = b / nb, blk = b - t * nb;
-      tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
-                        xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
-                        xs + (size_t)(8 + t) * nb + blk, status);
-    }
-  };
-  __shared__ int32_t sid[64], s_idx[64];
-  __shared__ float s_w[64];
-  __shared__ uint32_t bitmap[32];
-  __shared__ int is_last;
+// Logits of router rows [16c, 16c+16) (c = blockIdx.x) for T <= 8 tokens: warp w multiplies them by
+// the tokens over the K slices w, w+16, ... (256 elements each) with bf16 MMAs (exact products,
+// float32 accumulation); the warps' partial sums are added in warp order in shared memory (red).
+// score (optional) receives sigmoid_score of each logit.  kRouteWarps warps; ends after the stores.
+__device__ __forceinline__ void route_logits_cta(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                 int T, int H, int E, float* __restrict__ logits,
+                                                 float* __restrict__ score, float (*red)[128]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int e0 = blockIdx.x * 16;
@@ -155,9 +138,45 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
 #pragma unroll
       for (int ww = 0; ww < kRouteWarps; ++ww) sum += red[ww][threadIdx.x];
       logits[(size_t)tok * E + e0 + row] = sum;
-      score[(size_t)tok * E + e0 + row] = sigmoid_score(sum);  // off the last CTA's serial path
+      if (score) score[(size_t)tok * E + e0 + row] = sigmoid_score(sum);  // off the last CTA's serial path
     }
   }
+}
+
+// Stand-alone logits for T <= 8 (the router entry point): E / 16 CTAs.
+__global__ void __launch_bounds__(kRouteWarps * 32) router_logits_small_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H, int E,
+    float* __restrict__ logits) {
+  __shared__ float red[kRouteWarps][128];
+  route_logits_cta(x, w, T, H, E, logits, nullptr, red);
+}
+
+__global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const float* __restrict__ bias, int T,
+    int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
+    float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
+    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status) {
+  __shared__ float red[kRouteWarps][128];
+  // e4m3 terms of x for the tensor-core expert path (token t -> rows t (hi) and 8 + t (lo)): 32-value
+  // blocks spread evenly over the CTAs, split after the logits (off the critical path; in the last
+  // CTA by the warps that do not select).  first_thread: the CTA thread taking its first block.
+  auto split_share = [&](int first_thread) {
+    const int nb = H / 32;
+    for (int b = (threadIdx.x - first_thread) * gridDim.x + blockIdx.x; b < T * nb;
+         b += gridDim.x * (blockDim.x - first_thread)) {
+      const int t = b / nb, blk = b - t * nb;
+      tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
+                        xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
+                        xs + (size_t)(8 + t) * nb + blk, status);
+    }
+  };
+  __shared__ int32_t sid[64], s_idx[64];
+  __shared__ float s_w[64];
+  __shared__ uint32_t bitmap[32];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5;
+  route_logits_cta(x, w, T, H, E, logits, score, red);
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
@@ -314,6 +333,10 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* lo
       router_tc_kernel<<<dim3((T + kRtM - 1) / kRtM, E / kRtN), 128, kRtSmem, st>>>(p);
       return cudaGetLastError();
     }
+  }
+  if (T <= 8 && E % 16 == 0 && H % 256 == 0) {  // decode sizes: 16-row tiles on bf16 mma.sync
+    router_logits_small_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, T, H, E, logits);
+    return cudaGetLastError();
   }
   dim3 grid((E + 7) / 8, (T + 7) / 8);
   router_logits_kernel<<<grid, 256, 0, st>>>(x, w, logits, T, H, E);

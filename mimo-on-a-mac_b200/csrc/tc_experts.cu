@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
             const int q = q0 + i;
             if (q < cnt) {
               const float d = (hi[0][i] + hi[1][i]) + (lo[0][i] + lo[1][i]);
-              const size_t op = (size_t)(p0 + q) * p.Nw + row;
+              const size_t op = (size_t)(MODE == 1 && p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q) * p.Nw + row;
               if constexpr (MODE == 1) {
                 p.part[op] = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
               } else {

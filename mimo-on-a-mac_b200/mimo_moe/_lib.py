@@ -40,6 +40,11 @@ SIGNATURES = {
                                    c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_int32,
                                    c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "mimo_moe_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "mimo_moe_experts_routes_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "mimo_moe_experts_routes": (c_int32, [c_void_p, c_int32, POINTER(Pools), c_int32, c_void_p, c_void_p,
+                                          c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p,
+                                          c_void_p]),
+    "mimo_moe_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mimo_moe_prefill": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_int32, c_void_p, c_void_p,
                                    c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "mimo_moe_block_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),

@@ -1,0 +1,116 @@
+"""Expert parallelism for the MoE block: one process per GPU, experts sharded 256/N per rank.
+
+The reference runs the whole block on one device (engine/mimo_stream/model.py:303-336).  Here rank r
+holds experts [r*E/N, (r+1)*E/N) and routes only its own tokens; one step is
+
+  1. route: top-8 of the rank's own T tokens (model.py:58-65), replicated router weights;
+  2. dispatch: all-gather of the T token rows and their routes (every rank sees all N*T tokens);
+  3. local products: per-route float32 partials of the routes whose expert is local
+     (`moe_experts_routes`), zero for every other route;
+  4. return: reduce-scatter (sum) of the partials back to the token owners.  Each element has exactly
+     one nonzero term, so the sum is exact and does not depend on the collective's order;
+  5. combine: the owner adds its tokens' 8 partials in the reference's fixed route order
+     (kernels.py:194-199).
+
+Steps 3 and 5 are bit-identical to the single-GPU path, so the block output does not depend on N
+(the reference's dispatch rule picks the rounding: T == 1 and T > 8 round each expert's output to
+bf16 before the weight, 2 <= T <= 8 keep it in float32).  Every rank must call with the same T.
+
+The compute steps are pluggable (`router_fn`, `experts_fn`, `combine_fn`) so the exchange logic runs
+unchanged on CPU `gloo` ranks in the tests, with the CPU oracle as the compute.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+RouterFn = Callable[[torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
+ExpertsFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, bool], torch.Tensor]
+CombineFn = Callable[[torch.Tensor, int, int], torch.Tensor]
+
+
+def expert_range(rank: int, world: int, num_experts: int = 256) -> Tuple[int, int]:
+    """Experts owned by `rank`: the contiguous block [rank*E/N, (rank+1)*E/N)."""
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    n = num_experts // world
+    return rank * n, (rank + 1) * n
+
+
+def pairs_rounding_for(T: int) -> bool:
+    """The reference's dispatch rule (model.py:184-219, 324-336): bf16 expert outputs for T == 1
+    (stock gather_qmm path) and T > 8 (prefill pair path); float32 partials for 2 <= T <= 8."""
+    return T == 1 or T > 8
+
+
+class ExpertParallelMoE:
+    """One MoE layer over N ranks.  On GPUs the defaults call the CUDA library; `router_fn`,
+    `experts_fn`, `combine_fn` replace the compute steps (tests).
+
+    pools_local: this rank's expert shard (slot s = expert expert_base + s);
+    router_w / bias: the full router (replicated)."""
+
+    def __init__(self, pools_local, router_w: torch.Tensor, bias: Optional[torch.Tensor], *,
+                 num_experts: int = 256, topk: int = 8, group=None, router_fn: Optional[RouterFn] = None,
+                 experts_fn: Optional[ExpertsFn] = None, combine_fn: Optional[CombineFn] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.num_experts = num_experts
+        self.topk = topk
+        self.expert_base, hi = expert_range(self.rank, self.world, num_experts)
+        self.pools = pools_local
+        if pools_local is not None and getattr(pools_local, "S", hi - self.expert_base) != hi - self.expert_base:
+            raise ValueError("local pool does not hold this rank's expert range")
+        self.router_w, self.bias = router_w, bias
+        self.router_fn = router_fn or (lambda x: ops.router(x, self.router_w, self.bias, topk=self.topk))
+        self.experts_fn = experts_fn or (lambda X, I, W, rnd: ops.moe_experts_routes(
+            X, self.pools, I, W, expert_base=self.expert_base, pairs_rounding=rnd))
+        self.combine_fn = combine_fn or (lambda part, M, k: ops.combine(part, M, k))
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        N, k = self.world, self.topk
+        idx, w = self.router_fn(x)
+        idx = idx.to(torch.int32).contiguous()
+        w = w.to(torch.float32).contiguous()
+        # dispatch: every rank receives all tokens and routes (rank-major order), in one collective
+        # over rows packed as [x as int32 words | idx | w bits]
+        hw = H * x.element_size() // 4
+        row = torch.cat([x.contiguous().view(torch.int32).reshape(T, hw), idx, w.view(torch.int32)], dim=1)
+        rows = torch.empty(N * T, hw + 2 * k, dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(rows, row, group=self.group)
+        X = rows[:, :hw].contiguous().view(x.dtype).reshape(N * T, H)
+        IDX = rows[:, hw:hw + k].contiguous()
+        W = rows[:, hw + k:].contiguous().view(torch.float32)
+        # local per-route partials, zero for other ranks' experts: [N*T*k, H] float32
+        part = self.experts_fn(X, IDX, W, pairs_rounding_for(T))
+        # return: owner r receives rows [r*T*k, (r+1)*T*k) summed over ranks (one nonzero term each)
+        mine = torch.empty(T * k, H, dtype=torch.float32, device=x.device)
+        dist.reduce_scatter_tensor(mine, part.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
+        return self.combine_fn(mine, T, k)
+
+
+class GraphedStep:
+    """The block for a fixed T captured once as a CUDA graph (collectives included), replayed per step:
+    `run(x)` copies x into the graph's input and returns the graph's output tensor (overwritten by
+    the next replay).  Delete the object before destroy_process_group."""
+
+    def __init__(self, block: ExpertParallelMoE, T: int, H: int, device, dtype=torch.bfloat16, warmup: int = 2):
+        self.x = torch.zeros(T, H, dtype=dtype, device=device)
+        for _ in range(warmup):  # communicators, tensor maps, workspaces: created outside the capture
+            block(self.x)
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.y = block(self.x)
+        torch.cuda.synchronize(device)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        return self.y

@@ -114,6 +114,12 @@ class ExpertPools:
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self.t.values())
 
+    def slice(self, lo: int, hi: int) -> "ExpertPools":
+        """Experts [lo, hi) as a pool of hi - lo slots (views, no copy): one rank's shard."""
+        if not 0 <= lo < hi <= self.S:
+            raise ValueError(f"bad expert range [{lo}, {hi}) of {self.S}")
+        return ExpertPools({k: v[lo:hi] for k, v in self.t.items()})
+
     @staticmethod
     def empty(S: int, hidden: int = 4096, inter: int = 2048, device=None) -> "ExpertPools":
         device = torch.device(device or "cuda")
@@ -311,6 +317,45 @@ def moe_prefill(x: torch.Tensor, pools, inds: torch.Tensor, w: torch.Tensor,
     check(lib().mimo_moe_prefill(x.data_ptr(), pools.struct, _ptr(so), E, inds.data_ptr(), w.data_ptr(),
                                  T, k, y.data_ptr(), ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()),
           "moe_prefill")
+    return y
+
+
+def moe_experts_routes(x: torch.Tensor, pools, idx: torch.Tensor, w: torch.Tensor, expert_base: int = 0,
+                       pairs_rounding: bool = False, status: Optional[torch.Tensor] = None,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-route partials of the routes whose expert is in this pool (experts [expert_base,
+    expert_base + S)): float32 [rows * k, H], row r * k + j = fp32(expert products of x[r]) * w[r, j]
+    (bf16-rounded products when pairs_rounding), zero for routes to other experts.  The partials of
+    all expert shards add exactly (one nonzero term per element), then `combine` sums over k."""
+    _need_cuda(x, "x")
+    if not isinstance(pools, ExpertPools):
+        pools = ExpertPools(pools)
+    x = x.to(torch.bfloat16).contiguous()
+    rows, H = x.shape
+    dev = x.device
+    idx = idx.to(device=dev, dtype=torch.int32).contiguous()
+    w = w.to(device=dev, dtype=torch.float32).contiguous()
+    k = idx.shape[1]
+    part = out if out is not None else torch.empty(rows * k, H, dtype=torch.float32, device=dev)
+    nb = lib().mimo_moe_experts_routes_workspace_bytes(rows, k, pools.hidden, pools.inter, pools.S)
+    ws = workspace(nb, dev)
+    st = _status(dev) if status is None else status
+    check(lib().mimo_moe_experts_routes(x.data_ptr(), rows, pools.struct, expert_base, idx.data_ptr(),
+                                        w.data_ptr(), k, int(pairs_rounding), part.data_ptr(), ws.data_ptr(),
+                                        ws.numel(), st.data_ptr(), _stream()), "experts_routes")
+    return part
+
+
+def combine(part: torch.Tensor, M: int, k: int = TOPK, gather_idx: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """kernels.py:194-199: y[m] = bf16(sum over j in order of part[gather_idx[m*k + j]]) (rows m*k + j
+    without gather_idx)."""
+    _need_cuda(part, "part")
+    part = part.to(torch.float32).contiguous()
+    H = part.shape[1]
+    y = out if out is not None else torch.empty(M, H, dtype=torch.bfloat16, device=part.device)
+    gi = None if gather_idx is None else gather_idx.to(device=part.device, dtype=torch.int32).contiguous()
+    check(lib().mimo_moe_combine(part.data_ptr(), _ptr(gi), M, k, H, y.data_ptr(), _stream()), "combine")
     return y
 
 

@@ -1,0 +1,57 @@
+"""Multi-GPU expert-parallel check, one process per GPU (launched by tests/test_ep_multi_gpu.py):
+
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 tests/ep_worker.py
+
+Rank r holds experts [r*256/N, (r+1)*256/N) of a seeded synthetic layer, routes its own T tokens and
+runs the expert-parallel block (mimo_moe/ep.py, NCCL).  Each rank then runs the single-GPU block on
+the same tokens with the whole layer resident and the outputs must be identical bit for bit, for
+T = 1 (stock-path rounding), 8 (decode) and 12 (prefill rounding).  Prints one JSON line per rank."""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (ROOT, os.path.join(ROOT, "mimo-on-a-mac_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import mimo_moe  # noqa: E402
+from mimo_moe.ep import ExpertParallelMoE, expert_range  # noqa: E402
+from oracle import synth  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    ok = True
+    res = {"rank": rank, "world": world}
+    try:
+        lo, hi = expert_range(rank, world)
+        shard = mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=3, first_expert=lo, device=dev)
+        full = mimo_moe.ExpertPools.synthetic(256, seed=0, layer=3, device=dev)
+        W = synth.router_weight().to(dev)
+        bias = torch.zeros(256, device=dev)
+        blk = ExpertParallelMoE(shard, W, bias)
+        for T in (1, 8, 12):
+            x = synth.hidden(T, seed=500 + 17 * rank + T).to(dev)
+            y_ep = blk(x)
+            y_1 = mimo_moe.moe_block(x, W, bias, full)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(y_ep.view(torch.int16), y_1.view(torch.int16)))
+            res[f"T{T}_bit_identical"] = same
+            ok &= same
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    print(json.dumps(res), flush=True)
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

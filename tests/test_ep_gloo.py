@@ -1,0 +1,100 @@
+"""Expert-parallel exchange logic (mimo_moe/ep.py) on CPU gloo ranks, world_size 2.
+
+The compute steps are replaced by small deterministic CPU functions (router: top-k of x @ Wr with
+normalised sigmoid weights; expert e: tanh(x @ M_e) * w; combine: float32 sum over k in order ->
+bf16), so the test checks what the multi-GPU path adds: expert ownership, the all-gather dispatch,
+zero partials for other ranks' experts, the exact reduce-scatter return and the fixed-order combine.
+The EP output must equal the single-process output bit for bit."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+E, H, K, T = 8, 64, 3, 5
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _router(x: torch.Tensor):
+    wr = torch.from_numpy(np.random.default_rng(1).standard_normal((H, E)).astype(np.float32))
+    s = torch.sigmoid(x.float() @ wr)
+    w, idx = torch.topk(s, K, dim=1)
+    return idx.to(torch.int32), (w / w.sum(1, keepdim=True)).float()
+
+
+def _expert_mats():
+    rng = np.random.default_rng(2)
+    return [torch.from_numpy(rng.standard_normal((H, H)).astype(np.float32) / 8) for _ in range(E)]
+
+
+def _experts(lo: int, hi: int):
+    mats = _expert_mats()
+
+    def fn(X, IDX, W, rnd):
+        part = torch.zeros(X.shape[0] * K, H, dtype=torch.float32)
+        for r in range(X.shape[0]):
+            for j in range(K):
+                e = int(IDX[r, j])
+                if lo <= e < hi:
+                    v = torch.tanh(X[r].float() @ mats[e])
+                    if rnd:
+                        v = v.to(torch.bfloat16).float()
+                    part[r * K + j] = v * W[r, j]
+        return part
+    return fn
+
+
+def _combine(part, M, k):
+    y = torch.zeros(M, part.shape[1], dtype=torch.float32)
+    for m in range(M):
+        for j in range(k):
+            y[m] += part[m * k + j]
+    return y.to(torch.bfloat16)
+
+
+def _tokens(rank: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(100 + rank)
+    return torch.randn(T, H, generator=g).to(torch.bfloat16)
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mimo_moe.ep import ExpertParallelMoE, expert_range
+        lo, hi = expert_range(rank, world, E)
+        blk = ExpertParallelMoE(None, None, None, num_experts=E, topk=K, router_fn=_router,
+                                experts_fn=_experts(lo, hi), combine_fn=_combine)
+        y = blk(_tokens(rank))
+        out[rank] = y.float().numpy().tobytes()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_matches_single_process_bit_for_bit():
+    world = 2
+    port = _free_port()
+    out = mp.Manager().dict()
+    mp.start_processes(_worker, args=(world, port, out), nprocs=world, start_method="spawn")
+    for rank in range(world):
+        x = _tokens(rank)
+        idx, w = _router(x)
+        ref = _combine(_experts(0, E)(x, idx, w, False), T, K)
+        got = np.frombuffer(out[rank], dtype=np.float32).reshape(T, H)
+        assert np.array_equal(got, ref.float().numpy()), rank
+
+
+def test_expert_ranges_and_rounding_rule():
+    from mimo_moe.ep import expert_range, pairs_rounding_for
+    assert [expert_range(r, 8) for r in (0, 7)] == [(0, 32), (224, 256)]
+    with pytest.raises(ValueError):
+        expert_range(0, 3)
+    assert [pairs_rounding_for(t) for t in (1, 2, 8, 9, 2048)] == [True, False, False, True, True]

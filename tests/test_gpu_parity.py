@@ -266,3 +266,37 @@ def test_matches_reference_kernel_golden_outputs(gpu):
                                  num_unique=gr.num_unique)
         want = O.bf16_bits_to_f32(g[f"M{M}_y"])
         assert O.rel_err(f32(y), want) <= TOL_ORACLE, M
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_expert_shards_reproduce_the_single_gpu_output(gpu, pool24, M):
+    """Expert parallelism's arithmetic on one GPU: the per-route partials of two expert shards
+    (experts 0-11 and 12-23), added and combined in route order, equal mimo_moe_experts bit for bit."""
+    import mimo_moe
+    pool, opool = pool24
+    rng = np.random.default_rng(70 + M)
+    x = synth.hidden(M, seed=80 + M)
+    inds, sc = _routes(rng, M, 24)
+    idx_t, w_t = torch.from_numpy(inds).to(gpu), torch.from_numpy(sc).to(gpu)
+    g = mimo_moe.group_routes(idx_t, w_t, check_rows=True)
+    y_ref = mimo_moe.moe_experts(x.to(gpu), pool, g.uids, g.urows, g.ucnt, g.uw, gather_idx=g.gather_idx,
+                                 num_unique=g.num_unique, pairs_rounding=(M == 1))
+    part = torch.zeros(M * 8, 4096, dtype=torch.float32, device=gpu)
+    for lo, hi in ((0, 12), (12, 24)):
+        part += mimo_moe.moe_experts_routes(x.to(gpu), pool.slice(lo, hi), idx_t, w_t, expert_base=lo,
+                                            pairs_rounding=(M == 1))
+    y = mimo_moe.combine(part, M, 8)
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+    assert O.rel_err(f32(y), O.moe_layer(x.float().numpy(), opool, inds, sc)) <= TOL_ORACLE
+
+
+def test_routes_outside_the_shard_stay_zero(gpu, pool24):
+    import mimo_moe
+    pool, _ = pool24
+    x = synth.hidden(2, seed=3)
+    idx = torch.tensor([[0, 5, 13, 20, 1, 2, 3, 4], [23, 22, 21, 12, 6, 7, 8, 9]], dtype=torch.int32, device=gpu)
+    w = torch.full((2, 8), 0.125, device=gpu)
+    part = mimo_moe.moe_experts_routes(x.to(gpu), pool.slice(12, 24), idx, w, expert_base=12)
+    local = ((idx >= 12) & (idx < 24)).reshape(-1)
+    assert torch.all(part[~local] == 0)
+    assert torch.all(part[local].abs().sum(1) > 0)
