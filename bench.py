@@ -278,7 +278,7 @@ def main():
     else:        # prefill: algorithmic FLOPs 2 (gate, up) x 2 x I x H per routed pair
         flops = B * K_TOP * 2 * 2 * I * H
         tf = flops / (gu_ms * 1e-3) / 1e12
-        roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=32,MODE=0> (prefill gate/up + SwiGLU)", "bound": "tensor",
+        roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=64,MODE=0> (prefill gate/up + SwiGLU)", "bound": "tensor",
                     "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
                     "peak_kind": f"{peak_kind} bf16_tflops_sustained (dense bf16; the e2m1 x e4m3 MMAs "
                                  "run at the fp8 rate, nominally 2x)",

@@ -89,7 +89,7 @@ struct TcParams {
   int pairs_rounding;
   int32_t* status;
 };
-// kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (32 routes per
+// kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (64 routes per
 // unit), 3: prefill down.
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
 // Splits bf16 activation rows into the two e4m3 terms + ue8m0 scales of each unit's routes.
@@ -100,7 +100,7 @@ cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, c
 cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
                                    cudaStream_t st);
 constexpr int kTcDecodeRoutes = 8;   // routes per decode unit on the tcgen05 path
-constexpr int kTcPrefillRoutes = 32; // routes per prefill unit on the tcgen05 path
+constexpr int kTcPrefillRoutes = 64; // routes per prefill unit on the tcgen05 path
 
 // T > 8: tcgen05 GEMM (128 x 64 tiles; an expired wait sets MIMO_ETIMEOUT in `status` when given);
 // T <= 8 or unaligned operands: one warp per expert row.

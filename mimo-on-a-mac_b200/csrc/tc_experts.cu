@@ -56,10 +56,10 @@ constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment 
 #define MIMO_TC_ST1 5
 #endif
 #ifndef MIMO_TC_ST2
-#define MIMO_TC_ST2 5
+#define MIMO_TC_ST2 4
 #endif
 #ifndef MIMO_TC_ST3
-#define MIMO_TC_ST3 4
+#define MIMO_TC_ST3 3
 #endif
 #ifndef MIMO_TC_WEIGHT_EVICT_FIRST
 #define MIMO_TC_WEIGHT_EVICT_FIRST 1  // decode streams each weight once: L2 evict-first
@@ -82,8 +82,12 @@ constexpr int smem_bytes() {
   return kBarBytes + 1024 + NSTAGE * stage_bytes<NM, N>() + 2 * scale_box_bytes<NM, N>() +
          NSTAGE * sf_block_bytes<NM>();
 }
+// Accumulator buffers: two (the epilogue of one item overlaps the MMAs of the next) when TMEM has
+// room, else one (the epilogue copies its columns to registers and frees the buffer at once).
 template <int N, int NSTAGE>
-constexpr int tmem_cols_needed() { return 4 * N + NSTAGE * 16; }  // 2 buffers x 2 accumulators + scales
+constexpr int abuf() { return 4 * N + NSTAGE * 16 <= 512 ? 2 : 1; }
+template <int N, int NSTAGE>
+constexpr int tmem_cols_needed() { return abuf<N, NSTAGE>() * 2 * N + NSTAGE * 16; }  // accumulators + scales
 template <int N, int NSTAGE>
 constexpr uint32_t tmem_cols() {
   constexpr int n = tmem_cols_needed<N, NSTAGE>();
@@ -165,10 +169,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
   const long long items = (long long)units * p.tiles;
-  const long long it0 = items * blockIdx.x / gridDim.x;
-  const long long it1 = items * (blockIdx.x + 1) / gridDim.x;
+  // Items are dealt round-robin: at any time the CTAs work on consecutive items (the tiles and units
+  // of the same experts), so a weight tile shared by an expert's units and a unit's activation tile
+  // shared by its weight tiles are read from L2 by CTAs running side by side.  CTA-local item n is
+  // item blockIdx.x + n * gridDim.x.
+  const long long my_items = items > blockIdx.x ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   const int ns = p.K / (kKC * KPS);  // stages per item; K chunks per item are a multiple of 4
-  const long long nsteps = (it1 - it0) * ns;
+  const long long nsteps = my_items * ns;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
@@ -193,7 +200,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  constexpr uint32_t kSfCol0 = 4 * N;  // accumulator (buf, j) at columns (2 * buf + j) * N
+  constexpr int ABUF = abuf<N, NSTAGE>();
+  constexpr uint32_t kSfCol0 = ABUF * 2 * N;  // accumulator (buf, j) at columns (2 * buf + j) * N
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------ TMA producer
@@ -212,7 +220,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       long long issued = 0, groups = 0;
       bool stop = false;
       // Per item: coordinates, slot and row base once; per stage only the ring bookkeeping.
-      for (long long it = it0; it < it1 && !stop; ++it) {
+      for (long long n = 0; n < my_items && !stop; ++n) {
+        const long long it = blockIdx.x + n * gridDim.x;
         int unit, tile;
         item_coords(p, it, unit, tile);
         int slot = __ldg(p.unit_slot + unit);
@@ -346,9 +355,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       int stage = 0;
       uint32_t ph = 0;
       bool aborted = false;
-      for (long long it = it0; it < it1 && !aborted; ++it) {
-        const int buf = (int)((it - it0) & 1);
-        const uint32_t use = (uint32_t)(((it - it0) >> 1) & 1);
+      for (long long n = 0; n < my_items && !aborted; ++n) {
+        const int buf = ABUF == 2 ? (int)(n & 1) : 0;
+        const uint32_t use = ABUF == 2 ? (uint32_t)((n >> 1) & 1) : (uint32_t)(n & 1);
         if (!mbar_wait(&acc_empty[buf], use ^ 1u)) {
           set_status(p.status, MIMO_ETIMEOUT);
           *s_abort = 1;
@@ -393,9 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
     const int qlo = ((warp - 4) >> 2) * QH;        // its half of the routes: [qlo, qlo + QH)
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     bool aborted = false;
-    for (long long it = it0; it < it1; ++it) {
-      const int buf = (int)((it - it0) & 1);
-      const uint32_t use = (uint32_t)(((it - it0) >> 1) & 1);
+    for (long long n = 0; n < my_items; ++n) {
+      const long long it = blockIdx.x + n * gridDim.x;
+      const int buf = ABUF == 2 ? (int)(n & 1) : 0;
+      const uint32_t use = ABUF == 2 ? (uint32_t)((n >> 1) & 1) : (uint32_t)(n & 1);
       int unit, tile;
       item_coords(p, it, unit, tile);
       const int slot = __ldg(p.unit_slot + unit);
@@ -440,54 +450,83 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
           }
         }
       }
-#pragma unroll 1
-      for (int q0 = qlo; q0 < qlo + QH && live && !(MODE == 0 && p.btok); q0 += QC) {
-        float hi[2][QC], lo[2][QC];  // accumulators 0 and 1 of the buffer
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          const uint32_t c = tbase + lane_base + (uint32_t)(2 * buf + a) * N + q0;
-          tmem_ld<QC>(c, hi[a]);
-          tmem_ld<QC>(c + NTOK, lo[a]);
-        }
-        tmem_wait_ld();
+      // One route's outputs from accumulators 0 / 1 (gate / up, or the two K halves of down), each
+      // as its hi and lo term columns.  MODE 0 is warp-collective (block maxima over the lanes).
+      auto emit = [&](int q, float h0, float h1, float l0, float l1) {
         if constexpr (MODE == 0) {
-#pragma unroll
-          for (int i = 0; i < QC; ++i) {
-            const int q = q0 + i;
-            float h = 0.f;
-            if (q < cnt) {
-              h = swiglu_ref(hi[0][i] + lo[0][i], hi[1][i] + lo[1][i]);
-              if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
-            }
-            uint32_t th, tl, b1, b2;
-            split_warp_block(h, th, tl, b1, b2);
-            const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
-            p.hq[rh * p.Nw + row] = (uint8_t)th;
-            p.hq[rl * p.Nw + row] = (uint8_t)tl;
-            if (lane == 0) {
-              p.hs[rh * (p.Nw / 32) + row / 32] = (uint8_t)b1;
-              p.hs[rl * (p.Nw / 32) + row / 32] = (uint8_t)b2;
-            }
+          float h = 0.f;
+          if (q < cnt) {
+            h = swiglu_ref(h0 + l0, h1 + l1);
+            if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
+          }
+          uint32_t th, tl, b1, b2;
+          split_warp_block(h, th, tl, b1, b2);
+          const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
+          p.hq[rh * p.Nw + row] = (uint8_t)th;
+          p.hq[rl * p.Nw + row] = (uint8_t)tl;
+          if (lane == 0) {
+            p.hs[rh * (p.Nw / 32) + row / 32] = (uint8_t)b1;
+            p.hs[rl * (p.Nw / 32) + row / 32] = (uint8_t)b2;
           }
         } else {
+          if (q < cnt) {
+            const float d = (h0 + h1) + (l0 + l1);
+            const size_t op = (size_t)(MODE == 1 && p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q) * p.Nw + row;
+            if constexpr (MODE == 1) {
+              p.part[op] = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
+            } else {
+              p.ypair[op] = (uint16_t)f32_to_bf16(d);
+            }
+          }
+        }
+      };
+      const bool chunks = live && !(MODE == 0 && p.btok);
+      if constexpr (ABUF == 2) {
+#pragma unroll 1
+        for (int q0 = qlo; q0 < qlo + QH && chunks; q0 += QC) {
+          float hi[2][QC], lo[2][QC];  // accumulators 0 and 1 of the buffer
 #pragma unroll
-          for (int i = 0; i < QC; ++i) {
-            const int q = q0 + i;
-            if (q < cnt) {
-              const float d = (hi[0][i] + hi[1][i]) + (lo[0][i] + lo[1][i]);
-              const size_t op = (size_t)(MODE == 1 && p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q) * p.Nw + row;
-              if constexpr (MODE == 1) {
-                p.part[op] = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
-              } else {
-                p.ypair[op] = (uint16_t)f32_to_bf16(d);
+          for (int a = 0; a < 2; ++a) {
+            const uint32_t c = tbase + lane_base + (uint32_t)(2 * buf + a) * N + q0;
+            tmem_ld<QC>(c, hi[a]);
+            tmem_ld<QC>(c + NTOK, lo[a]);
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < QC; ++i) emit(q0 + i, hi[0][i], hi[1][i], lo[0][i], lo[1][i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      } else {
+        // Single buffer: copy all of this warp's columns out, free the accumulator, then compute.
+        float hv[2][QH], lv[2][QH];
+        if (chunks) {
+#pragma unroll
+          for (int q0 = 0; q0 < QH; q0 += QC) {
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+              float th[QC], tl[QC];
+              const uint32_t c = tbase + lane_base + (uint32_t)(2 * buf + a) * N + qlo + q0;
+              tmem_ld<QC>(c, th);
+              tmem_ld<QC>(c + NTOK, tl);
+#pragma unroll
+              for (int i = 0; i < QC; ++i) {
+                hv[a][q0 + i] = th[i];
+                lv[a][q0 + i] = tl[i];
               }
             }
           }
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        if (chunks) {
+#pragma unroll
+          for (int i = 0; i < QH; ++i) emit(qlo + i, hv[0][i], hv[1][i], lv[0][i], lv[1][i]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();

@@ -300,3 +300,49 @@ def test_routes_outside_the_shard_stay_zero(gpu, pool24):
     local = ((idx >= 12) & (idx < 24)).reshape(-1)
     assert torch.all(part[~local] == 0)
     assert torch.all(part[local].abs().sum(1) > 0)
+
+
+def test_negative_control_scale_off_by_one_is_detected(gpu, pool24):
+    """Second planted mistake (the survey's parity rule 5): every e8m0 scale byte one too large in the
+    oracle (each weight doubled) must fail the comparison."""
+    import mimo_moe
+    pool, _ = pool24
+    rng = np.random.default_rng(16)
+    x = synth.hidden(2, seed=16)
+    inds, sc = _routes(rng, 2, 24)
+    g = mimo_moe.group_routes(torch.from_numpy(inds).to(gpu), torch.from_numpy(sc).to(gpu))
+    y = f32(mimo_moe.moe_experts(x.to(gpu), pool, g.uids, g.urows, g.ucnt, g.uw, gather_idx=g.gather_idx,
+                                 num_unique=g.num_unique))
+
+    class OffByOne:
+        def __getitem__(self, name):
+            src = synth.SynthPool(0, 0)[name]
+
+            class T:
+                def __getitem__(self, e):
+                    a = src[e]
+                    return (a + 1).astype(a.dtype) if name.endswith("_s") else a
+            return T()
+    bad = O.moe_layer(x.float().numpy(), O.Pool(OffByOne()), inds, sc)
+    assert O.rel_err(y, bad) > 0.5
+
+
+def test_downstream_logit_kl_through_a_random_head(gpu):
+    """Parity reported as the mean KL of downstream logits (the real lm_head is not available): a
+    seeded random bf16 head [4096 -> 32768] applied to the GPU block output and to the oracle's."""
+    import mimo_moe
+    pool = mimo_moe.ExpertPools.synthetic(256, seed=0, layer=2, device=gpu)
+    opool = O.Pool(synth.SynthPool(0, 2))
+    T = 8
+    x = synth.hidden(T, seed=91)
+    W = synth.router_weight()
+    y, idx, w = mimo_moe.moe_block(x.to(gpu), W.to(gpu), torch.zeros(256, device=gpu), pool, return_routes=True)
+    ref = O.moe_layer(x.float().numpy(), opool, idx.cpu().numpy(), w.cpu().numpy())
+    g = torch.Generator().manual_seed(4)
+    head = (torch.randn(4096, 32768, generator=g) * 0.02).to(torch.bfloat16).float()
+    yg = y.float().cpu()
+    yr = torch.from_numpy(ref).to(torch.bfloat16).float()
+    lg, lr = torch.log_softmax(yg @ head * 3, -1), torch.log_softmax(yr @ head * 3, -1)
+    kl = float((lr.exp() * (lr - lg)).sum(-1).mean())
+    print(f"mean KL(oracle || gpu) of downstream logits: {kl:.3e}")
+    assert kl < 1e-3
