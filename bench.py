@@ -195,7 +195,14 @@ def main():
     y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     L = mimo_moe.lib()
-    blk = ExpertParallelMoE(pool, W, bias, num_experts=NE) if ep else None
+    # decode sizes exchange through NVLink peer memory inside the kernels; larger batches use NCCL
+    peer = ep and B <= 8
+    if ep:
+        from mimo_moe.ep import PeerExpertParallelMoE
+        blk = PeerExpertParallelMoE(pool, W, bias, B, num_experts=NE) if peer else \
+            ExpertParallelMoE(pool, W, bias, num_experts=NE)
+    else:
+        blk = None
     # expert parallelism replays one CUDA graph per step (router, collectives, expert kernels, combine):
     # the step issues ~10 kernels and 2 collectives, whose host-side launch cost would otherwise set
     # the pace.  The x copy into the graph's input is inside the step.
@@ -317,9 +324,10 @@ def main():
         # our kernels per step: decode = route (+ its counter memset, not counted), gate/up, down,
         # combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
         # down, combine
-        # expert parallelism: router logits + top-k, 3 dispatch, 2 unit builders, term split, gate/up,
-        # down, combine (the NCCL collectives are library kernels and not counted)
-        launches_per_step = 10 if ep else (4 if B <= 8 else 11)
+        # expert parallelism, peer exchange: router logits, route+scatter, 2 barriers, unit builder, term
+        # split, gate/up, down, combine; NCCL exchange: router logits + top-k, 3 dispatch, 2 unit
+        # builders, term split, gate/up, down, combine (the collectives are library kernels)
+        launches_per_step = (8 if peer else 10) if ep else (4 if B <= 8 else 11)
         out = {
             "metric": f"MoE-layer tok/s ({args.workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -329,9 +337,11 @@ def main():
             "config": {"workload": args.workload, "B": B * world, "experts": NE, "hidden": H, "inter": I,
                        "topk": K_TOP, "routing": "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
                        "mean_distinct_experts_this_gpu": statistics.mean(steps_Ul),
-                       "parallelism": f"ep{world} (experts sharded {NE // world} per GPU; all-gather "
-                                      "dispatch, exact reduce-scatter return, fixed-order combine)"
-                                      if ep else "single",
+                       "parallelism": (f"ep{world} (experts sharded {NE // world} per GPU; " +
+                                       ("dispatch and return as NVLink peer stores inside the route and "
+                                        "down kernels, flag barriers" if peer else
+                                        "NCCL all-gather dispatch, exact reduce-scatter return") +
+                                       "; fixed-order combine; one CUDA graph per step)") if ep else "single",
                        "tokens_per_gpu": B,
                        "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
             "expert_gbs": expert_gbs,
@@ -347,6 +357,8 @@ def main():
     if world > 1:
         del gstep  # a graph holding NCCL calls must be released before the process group
         torch.cuda.synchronize()
+        if peer:
+            blk.close()
         dist.destroy_process_group()
 
 

@@ -142,24 +142,47 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
  * design of the B200 build: experts [expert_base, expert_base + S) live on this GPU).
  *
  * mimo_moe_experts_routes: per-route products of every route whose expert is local.  x holds `rows`
- * token rows (bf16 [rows, H]); idx/weight are [rows, topk] global expert ids and router weights.
- * part (float32 [rows * topk, H]) is zeroed, then row r * topk + k receives
- * fp32(down . SwiGLU(gate . x_r, up . x_r)) * weight[r, k] for local routes (bf16-rounded before the
- * weight when pairs_rounding != 0, the M = 1 stock path), exactly the per-route partial of
- * mimo_moe_experts (kernels.py:120; model.py:173-182).  Non-local routes stay zero, so the partials
- * of all ranks can be summed exactly (one nonzero term per element) before the fixed-order combine.
- * Workspace: mimo_moe_experts_routes_workspace_bytes(rows, topk, H, I, S).
+ * token rows (bf16, row r at x + r * x_ld; x_ld = 0 means H); idx/weight hold row r's topk global
+ * expert ids and router weights at idx + r * route_ld (route_ld = 0 means topk).  Route
+ * p = r * topk + k gets fp32(down . SwiGLU(gate . x_r, up . x_r)) * weight[r, k] (bf16-rounded before
+ * the weight when pairs_rounding != 0, the M = 1 stock path), exactly the per-route partial of
+ * mimo_moe_experts (kernels.py:120; model.py:173-182).  Output: with part (float32 [rows * topk, H]),
+ * part is zeroed and row p receives the partials of local routes, so the partials of all ranks add
+ * exactly (one nonzero term per element); with peer_part (a device array of world pointers), row p
+ * is stored straight into peer_part[p / rows_per_rank] at row p % rows_per_rank (each route on
+ * exactly one rank: no zeroing, no reduction).  Workspace:
+ * mimo_moe_experts_routes_workspace_bytes(rows, topk, H, I, S).
  *
  * mimo_moe_combine: y[m] = bf16(sum over k in order of part[gather_idx[m * topk + k]]) with
  * gather_idx = NULL meaning row m * topk + k (kernels.py:194-199).
+ *
+ * Peer-memory exchange (one process per GPU on one node): mimo_moe_peer_alloc allocates `bytes` of
+ * zeroed device memory and writes its 64-byte CUDA IPC handle; mimo_moe_peer_open maps another
+ * process's handle (mimo_moe_peer_close unmaps, mimo_moe_peer_free frees).  mimo_moe_peer_barrier
+ * orders everything issued before it on every rank before everything issued after it on every rank:
+ * signals[r] points at rank r's int32[world] signal array, my_signals at this rank's, epoch at a
+ * device counter that starts at 0; a wait longer than ~2 s sets MIMO_ETIMEOUT in *status.
+ * mimo_moe_route_scatter routes T <= 8 tokens (router logits into `logits`, float32 [T, E]) and stores
+ * each token's packed row [x as H/2 int32 words | topk ids | topk weights] into rows[r] at row
+ * rank * T + t for every rank r (ld int32 words per row).
  */
 size_t mimo_moe_experts_routes_workspace_bytes(int32_t rows, int32_t topk, int32_t H, int32_t I, int32_t S);
-int mimo_moe_experts_routes(const uint16_t* x, int32_t rows, const mimo_moe_pools* pools, int32_t expert_base,
-                            const int32_t* idx, const float* weight, int32_t topk, int32_t pairs_rounding,
-                            float* part, void* workspace, size_t workspace_bytes, int32_t* status,
+int mimo_moe_experts_routes(const uint16_t* x, int32_t x_ld, int32_t rows, const mimo_moe_pools* pools,
+                            int32_t expert_base, const int32_t* idx, const float* weight, int32_t route_ld,
+                            int32_t topk, int32_t pairs_rounding, float* part, float* const* peer_part,
+                            int32_t rows_per_rank, void* workspace, size_t workspace_bytes, int32_t* status,
                             void* stream);
 int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,
                      uint16_t* y, void* stream);
+int mimo_moe_peer_alloc(size_t bytes, void** ptr, void* handle);
+int mimo_moe_peer_open(const void* handle, void** ptr);
+int mimo_moe_peer_close(void* ptr);
+int mimo_moe_peer_free(void* ptr);
+int mimo_moe_peer_barrier(int32_t* const* signals, int32_t* my_signals, int32_t rank, int32_t world,
+                          int32_t* epoch, int32_t* status, void* stream);
+int mimo_moe_route_scatter(const uint16_t* x, int32_t T, int32_t H, const uint16_t* router_w, const float* bias,
+                           int32_t E, int32_t topk, int32_t* const* rows, int32_t ld, int32_t rank, int32_t world,
+                           float* logits, void* stream);
 
 /*
  * Synthetic pool fill (benchmarks and tests): counter-based splitmix64 stream per (seed, layer, tensor);

@@ -1,6 +1,7 @@
 // C ABI of the MoE block (include/mimo_moe.h): argument checks, workspace carving, launches.
 // No allocation, no host synchronisation, no device selection: everything is stream-ordered.
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -243,7 +244,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
            const int32_t* unsub, const int32_t* rtok, const float* rw,
            const int32_t* num_units, int ucap, int pairs_rounding, const TermWs& t, float* part,
            uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false,
-           const int32_t* out_row = nullptr) {
+           const int32_t* out_row = nullptr, int x_ld = 0, float* const* peer_part = nullptr, int peer_rows = 0) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
   const int N = 2 * routes;
@@ -251,7 +252,8 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   // by_token_rows = M > 0: B holds the M (<= 8) token rows once, shared by every unit (decode).
   if (!terms_ready) {
     if (by_token_rows) MIMO_TRY(launch_tc_split_tokens(x, by_token_rows, H, t.bq, t.bs, status, st));
-    else MIMO_TRY(launch_tc_split(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, routes, t.bq, t.bs, status, st));
+    else MIMO_TRY(launch_tc_split(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, routes, t.bq, t.bs, status, st,
+                                  x_ld));
   }
   const uint64_t brows = by_token_rows ? (uint64_t)N : (uint64_t)ucap * N;
   TcParams p{};
@@ -295,6 +297,8 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   q.rw = rw;
   q.part = part;
   q.out_row = out_row;
+  q.peer_part = peer_part;
+  q.peer_rows = peer_rows;
   q.ypair = ypair;
   q.pairs_rounding = pairs_rounding;
   MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
@@ -617,26 +621,90 @@ size_t mimo_moe_experts_routes_workspace_bytes(int32_t rows, int32_t topk, int32
   return c.off;
 }
 
-int mimo_moe_experts_routes(const uint16_t* x, int32_t rows, const mimo_moe_pools* pools, int32_t expert_base,
-                            const int32_t* idx, const float* weight, int32_t topk, int32_t pairs_rounding,
-                            float* part, void* workspace, size_t workspace_bytes, int32_t* status,
+int mimo_moe_experts_routes(const uint16_t* x, int32_t x_ld, int32_t rows, const mimo_moe_pools* pools,
+                            int32_t expert_base, const int32_t* idx, const float* weight, int32_t route_ld,
+                            int32_t topk, int32_t pairs_rounding, float* part, float* const* peer_part,
+                            int32_t rows_per_rank, void* workspace, size_t workspace_bytes, int32_t* status,
                             void* stream) {
-  if (!x || !pools_ok(pools) || !idx || !weight || !part || !workspace || !status || rows < 1 || topk < 1 ||
-      topk > 8 || expert_base < 0 || (int64_t)rows * topk > (1 << 24) || pools->num_slots > 1024)
+  if (!x || !pools_ok(pools) || !idx || !weight || !workspace || !status || rows < 1 || topk < 1 ||
+      topk > 8 || expert_base < 0 || (int64_t)rows * topk > (1 << 24) || pools->num_slots > 1024 ||
+      (!part && !peer_part) || (peer_part && (rows_per_rank < 1 || (rows * topk) % rows_per_rank)))
     return MIMO_EINVAL;
   const int P = rows * topk, S = pools->num_slots, H = pools->hidden, I = pools->inter;
+  if (x_ld <= 0) x_ld = H;
+  if (route_ld <= 0) route_ld = topk;
+  if (x_ld < H || x_ld % 8 || route_ld < topk) return MIMO_EINVAL;
   Carver c(workspace);
   const RoutesWs w = carve_routes(c, P, H, I, S);
   if (c.off > workspace_bytes) return MIMO_EINVAL;
   if (!tc_path(pools)) return MIMO_EINVAL;  // needs the TMA alignment of the tensor-core path
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MIMO_TRY(cudaMemsetAsync(part, 0, (size_t)P * H * sizeof(float), st));
-  MIMO_TRY(launch_dispatch(idx, P, S, w.offsets, w.order, w.inv, w.dws, status, st, expert_base, 1));
-  MIMO_TRY(launch_build_units(w.offsets, nullptr, S, S, kTcDecodeRoutes, w.ucap, w.unit_slot, w.unit_p0,
-                              w.unit_cnt, nullptr, nullptr, w.num_units, w.order, weight, P, topk, w.rtok,
-                              w.rw, status, st));
+  if (!peer_part) MIMO_TRY(cudaMemsetAsync(part, 0, (size_t)P * H * sizeof(float), st));
+  if (P <= 1024 && S <= 256) {  // decode sizes: one CTA builds the units
+    MIMO_TRY(launch_routes_prep(idx, weight, route_ld, rows, topk, expert_base, S, kTcDecodeRoutes, w.ucap, w.order,
+                                w.rtok, w.rw, w.unit_slot, w.unit_p0, w.unit_cnt, w.num_units, st));
+  } else {
+    if (route_ld != topk) return MIMO_EINVAL;  // the general dispatch reads packed routes
+    MIMO_TRY(launch_dispatch(idx, P, S, w.offsets, w.order, w.inv, w.dws, status, st, expert_base, 1));
+    MIMO_TRY(launch_build_units(w.offsets, nullptr, S, S, kTcDecodeRoutes, w.ucap, w.unit_slot, w.unit_p0,
+                                w.unit_cnt, nullptr, nullptr, w.num_units, w.order, weight, P, topk, w.rtok,
+                                w.rw, status, st));
+  }
   return run_tc(x, pools, kTcDecodeRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, nullptr, nullptr, w.rtok,
-                w.rw, w.num_units, w.ucap, pairs_rounding, w.t, part, nullptr, status, st, 0, false, w.order);
+                w.rw, w.num_units, w.ucap, pairs_rounding, w.t, part, nullptr, status, st, 0, false, w.order, x_ld,
+                peer_part, rows_per_rank);
+}
+
+// ------------------------------------------------------------------- peer-memory exchange
+int mimo_moe_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return MIMO_EINVAL;
+  MIMO_TRY(cudaMalloc(ptr, bytes));
+  MIMO_TRY(cudaMemset(*ptr, 0, bytes));
+  cudaIpcMemHandle_t h;
+  MIMO_TRY(cudaIpcGetMemHandle(&h, *ptr));
+  std::memcpy(handle, &h, sizeof(h));
+  return MIMO_OK;
+}
+
+int mimo_moe_peer_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return MIMO_EINVAL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  MIMO_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MIMO_OK;
+}
+
+int mimo_moe_peer_close(void* ptr) {
+  if (!ptr) return MIMO_EINVAL;
+  MIMO_TRY(cudaIpcCloseMemHandle(ptr));
+  return MIMO_OK;
+}
+
+int mimo_moe_peer_free(void* ptr) {
+  if (!ptr) return MIMO_EINVAL;
+  MIMO_TRY(cudaFree(ptr));
+  return MIMO_OK;
+}
+
+int mimo_moe_peer_barrier(int32_t* const* signals, int32_t* my_signals, int32_t rank, int32_t world,
+                          int32_t* epoch, int32_t* status, void* stream) {
+  if (!signals || !my_signals || !epoch || !status || world < 1 || world > 32 || rank < 0 || rank >= world)
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_peer_barrier(signals, my_signals, rank, world, epoch, status, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_route_scatter(const uint16_t* x, int32_t T, int32_t H, const uint16_t* router_w, const float* bias,
+                           int32_t E, int32_t topk, int32_t* const* rows, int32_t ld, int32_t rank, int32_t world,
+                           float* logits, void* stream) {
+  if (!x || !router_w || !rows || !logits || T < 1 || T > 8 || H < 256 || H % 256 || E < 32 || E > 256 ||
+      E % 32 || topk < 1 || topk > 8 || topk > E || world < 1 || world > 16 || rank < 0 || rank >= world ||
+      ld < H / 2 + 2 * topk)
+    return MIMO_EINVAL;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st));
+  MIMO_TRY(launch_route_scatter(x, logits, bias, T, H, E, topk, rows, ld, rank, world, st));
+  return MIMO_OK;
 }
 
 int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,

@@ -86,6 +86,8 @@ struct TcParams {
   float* part;                // down, decode: [P][Nw] = dot * weight
   uint16_t* ypair;            // down, prefill: [P][Nw] bf16(dot)
   const int32_t* out_row;     // down, decode kinds: partial of sorted route i goes to row out_row[i]
+  float* const* peer_part;    // non-null: row r goes to rank r / peer_rows's buffer, row r % peer_rows
+  int peer_rows;
   int pairs_rounding;
   int32_t* status;
 };
@@ -93,9 +95,18 @@ struct TcParams {
 // unit), 3: prefill down.
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
 // Splits bf16 activation rows into the two e4m3 terms + ue8m0 scales of each unit's routes.
+// x rows are x_ld elements apart.
 cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
                             int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
-                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st);
+                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld = 0);
+// Expert-parallel exchange over peer memory (peer.cu).
+cudaError_t launch_peer_barrier(int32_t* const* signals, int32_t* my_signals, int rank, int world, int32_t* epoch,
+                                int32_t* status, cudaStream_t st);
+cudaError_t launch_route_scatter(const uint16_t* x, const float* logits, const float* bias, int T, int H, int E,
+                                 int topk, int32_t* const* rows, int ld, int rank, int world, cudaStream_t st);
+cudaError_t launch_routes_prep(const int32_t* idx, const float* w, int route_ld, int rows, int topk, int base, int S,
+                               int unit_max, int ucap, int32_t* order, int32_t* rtok, float* rw, int32_t* unit_slot,
+                               int32_t* unit_p0, int32_t* unit_cnt, int32_t* num_units, cudaStream_t st);
 // Splits token rows x[t] (t < T <= 8) into terms at rows t (hi) and 8 + t (lo) of bq/bs.
 cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
                                    cudaStream_t st);

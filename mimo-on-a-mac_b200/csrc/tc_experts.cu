@@ -471,10 +471,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
         } else {
           if (q < cnt) {
             const float d = (h0 + h1) + (l0 + l1);
-            const size_t op = (size_t)(MODE == 1 && p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q) * p.Nw + row;
+            const int orow = MODE == 1 && p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q;
             if constexpr (MODE == 1) {
-              p.part[op] = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
+              const float v = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
+              if (p.peer_part)  // straight into the owner rank's receive buffer (NVLink store)
+                p.peer_part[orow / p.peer_rows][(size_t)(orow % p.peer_rows) * p.Nw + row] = v;
+              else
+                p.part[(size_t)orow * p.Nw + row] = v;
             } else {
+              const size_t op = (size_t)orow * p.Nw + row;
               p.ypair[op] = (uint16_t)f32_to_bf16(d);
             }
           }
@@ -561,7 +566,7 @@ __global__ void __launch_bounds__(128) split_rows_kernel(const uint16_t* __restr
                                                          const int32_t* __restrict__ rtok,
                                                          const int32_t* __restrict__ num_units, int units_cap,
                                                          uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
-                                                         int32_t* status) {
+                                                         int32_t* status, int x_ld) {
   constexpr int N = 2 * NTOK;
   const int unit = blockIdx.x / NTOK, q = blockIdx.x % NTOK;
   const int units = num_units ? min(*num_units, units_cap) : units_cap;
@@ -573,7 +578,7 @@ __global__ void __launch_bounds__(128) split_rows_kernel(const uint16_t* __restr
   const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
   const int nb = K / 32;
   for (int blk = threadIdx.x; blk < nb; blk += blockDim.x) {
-    split_block32(x + (size_t)tok * K + blk * 32, bq + rh * K + blk * 32, bq + rl * K + blk * 32,
+    split_block32(x + (size_t)tok * x_ld + blk * 32, bq + rh * K + blk * 32, bq + rl * K + blk * 32,
                   bs + rh * nb + blk, bs + rl * nb + blk, status);
   }
 }
@@ -600,14 +605,16 @@ cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq,
 }
 cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
                             int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
-                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st) {
+                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld) {
   if (K % 128 != 0 || units_cap < 1) return cudaErrorInvalidValue;
+  if (x_ld <= 0) x_ld = K;
+  if (x_ld < K || x_ld % 8) return cudaErrorInvalidValue;  // 16-byte aligned rows
   if (ntok == kTcDecodeRoutes)
     tc::split_rows_kernel<kTcDecodeRoutes><<<units_cap * kTcDecodeRoutes, 128, 0, st>>>(
-        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status);
+        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld);
   else if (ntok == kTcPrefillRoutes)
     tc::split_rows_kernel<kTcPrefillRoutes><<<units_cap * kTcPrefillRoutes, 128, 0, st>>>(
-        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status);
+        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();

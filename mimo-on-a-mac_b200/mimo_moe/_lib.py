@@ -41,9 +41,16 @@ SIGNATURES = {
                                    c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "mimo_moe_prefill_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "mimo_moe_experts_routes_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
-    "mimo_moe_experts_routes": (c_int32, [c_void_p, c_int32, POINTER(Pools), c_int32, c_void_p, c_void_p,
-                                          c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p,
-                                          c_void_p]),
+    "mimo_moe_experts_routes": (c_int32, [c_void_p, c_int32, c_int32, POINTER(Pools), c_int32, c_void_p,
+                                          c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32,
+                                          c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_peer_alloc": (c_int32, [c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_peer_open": (c_int32, [c_void_p, c_void_p]),
+    "mimo_moe_peer_close": (c_int32, [c_void_p]),
+    "mimo_moe_peer_free": (c_int32, [c_void_p]),
+    "mimo_moe_peer_barrier": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_route_scatter": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
+                                         c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mimo_moe_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mimo_moe_prefill": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_int32, c_void_p, c_void_p,
                                    c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),

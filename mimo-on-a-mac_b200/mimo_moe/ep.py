@@ -21,6 +21,7 @@ unchanged on CPU `gloo` ranks in the tests, with the CPU oracle as the compute.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -114,3 +115,99 @@ class GraphedStep:
         self.x.copy_(x, non_blocking=True)
         self.graph.replay()
         return self.y
+
+
+class PeerExpertParallelMoE:
+    """Expert parallelism with the exchange inside the kernels, over NVLink peer memory.
+
+    Same steps and results as ExpertParallelMoE (bit-identical to one GPU), without collectives:
+      route   `mimo_moe_route_scatter` selects the rank's T tokens' routes and stores each token's
+              packed row [x | ids | weights] into every rank's gather buffer (row rank*T + t);
+      barrier every rank's rows have landed;
+      experts the local experts' products of all N*T tokens; the down kernel stores each route's
+              float32 partial straight into its owner's receive buffer (row t*k + j);
+      barrier every partial has landed;
+      combine fixed route order, from the local receive buffer.
+    Two barriers per step also keep a rank from overwriting buffers a peer is still reading.  Buffers
+    are plain device allocations shared through CUDA IPC (setup time only); call close() before the
+    process group is destroyed.  T is fixed at construction."""
+
+    def __init__(self, pools_local, router_w: torch.Tensor, bias: Optional[torch.Tensor], T: int, *,
+                 num_experts: int = 256, topk: int = 8, group=None):
+        from ._lib import check, lib
+        self.L, self.check = lib(), check
+        self.group = group
+        self.world = N = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.T, self.k, self.E = T, topk, num_experts
+        self.expert_base, hi = expert_range(self.rank, N, num_experts)
+        if pools_local.S != hi - self.expert_base:
+            raise ValueError("local pool does not hold this rank's expert range")
+        self.pools = pools_local
+        self.router_w = router_w.contiguous()
+        self.bias = None if bias is None else bias.to(torch.float32).contiguous()
+        self.dev = router_w.device
+        H = self.H = router_w.shape[1]
+        self.ld = H // 2 + 2 * topk  # int32 words per packed row (x rows stay 16-byte aligned)
+        sizes = {"rows": N * T * self.ld * 4, "recv": T * topk * H * 4, "sig": 64 * 4}
+        self.local, self.opened, ptrs = {}, [], {}
+        for name, nbytes in sizes.items():
+            p, h = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+            check(self.L.mimo_moe_peer_alloc(nbytes, ctypes.addressof(p), ctypes.addressof(h)), "peer_alloc")
+            self.local[name] = p.value
+            handles = [None] * N
+            dist.all_gather_object(handles, h.raw, group=group)
+            ptrs[name] = []
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    ptrs[name].append(p.value)
+                    continue
+                q, hbuf = ctypes.c_void_p(), ctypes.create_string_buffer(hb, 64)
+                check(self.L.mimo_moe_peer_open(ctypes.addressof(hbuf), ctypes.addressof(q)), "peer_open")
+                self.opened.append(q.value)
+                ptrs[name].append(q.value)
+        self.tab = {n: torch.tensor(v, dtype=torch.int64, device=self.dev) for n, v in ptrs.items()}
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.logits = torch.empty(T, num_experts, dtype=torch.float32, device=self.dev)
+        nb = self.L.mimo_moe_experts_routes_workspace_bytes(N * T, topk, H, pools_local.inter, pools_local.S)
+        self.ws = torch.empty(nb, dtype=torch.uint8, device=self.dev)
+        self.y = torch.empty(T, H, dtype=torch.bfloat16, device=self.dev)
+        dist.barrier(group=group)
+
+    def _barrier(self, st: int) -> None:
+        self.check(self.L.mimo_moe_peer_barrier(self.tab["sig"].data_ptr(), self.local["sig"], self.rank,
+                                                self.world, self.epoch.data_ptr(), self.status.data_ptr(), st),
+                   "peer_barrier")
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if tuple(x.shape) != (self.T, self.H):
+            raise ValueError(f"x must be [{self.T}, {self.H}]")
+        x = x.to(torch.bfloat16).contiguous()
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        T, k, H, N = self.T, self.k, self.H, self.world
+        self.check(self.L.mimo_moe_route_scatter(
+            x.data_ptr(), T, H, self.router_w.data_ptr(), None if self.bias is None else self.bias.data_ptr(),
+            self.E, k, self.tab["rows"].data_ptr(), self.ld, self.rank, N, self.logits.data_ptr(), st),
+            "route_scatter")
+        self._barrier(st)
+        rows = self.local["rows"]
+        self.check(self.L.mimo_moe_experts_routes(
+            rows, 2 * self.ld, N * T, self.pools.struct, self.expert_base, rows + 2 * H,
+            rows + 2 * H + 4 * k, self.ld, k, int(pairs_rounding_for(T)), None, self.tab["recv"].data_ptr(),
+            T * k, self.ws.data_ptr(), self.ws.numel(), self.status.data_ptr(), st), "experts_routes")
+        self._barrier(st)
+        self.check(self.L.mimo_moe_combine(self.local["recv"], None, T, k, H, self.y.data_ptr(), st), "combine")
+        return self.y
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after the device is idle)."""
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.L.mimo_moe_peer_close(ctypes.c_void_p(p))
+        self.opened = []
+        dist.barrier(group=self.group)
+        for p in self.local.values():
+            self.L.mimo_moe_peer_free(ctypes.c_void_p(p))
+        self.local = {}

@@ -340,9 +340,9 @@ def moe_experts_routes(x: torch.Tensor, pools, idx: torch.Tensor, w: torch.Tenso
     nb = lib().mimo_moe_experts_routes_workspace_bytes(rows, k, pools.hidden, pools.inter, pools.S)
     ws = workspace(nb, dev)
     st = _status(dev) if status is None else status
-    check(lib().mimo_moe_experts_routes(x.data_ptr(), rows, pools.struct, expert_base, idx.data_ptr(),
-                                        w.data_ptr(), k, int(pairs_rounding), part.data_ptr(), ws.data_ptr(),
-                                        ws.numel(), st.data_ptr(), _stream()), "experts_routes")
+    check(lib().mimo_moe_experts_routes(x.data_ptr(), H, rows, pools.struct, expert_base, idx.data_ptr(),
+                                        w.data_ptr(), k, k, int(pairs_rounding), part.data_ptr(), None, 0,
+                                        ws.data_ptr(), ws.numel(), st.data_ptr(), _stream()), "experts_routes")
     return part
 
 

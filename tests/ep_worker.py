@@ -20,7 +20,7 @@ for p in (ROOT, os.path.join(ROOT, "mimo-on-a-mac_b200")):
         sys.path.insert(0, p)
 
 import mimo_moe  # noqa: E402
-from mimo_moe.ep import ExpertParallelMoE, expert_range  # noqa: E402
+from mimo_moe.ep import ExpertParallelMoE, GraphedStep, PeerExpertParallelMoE, expert_range  # noqa: E402
 from oracle import synth  # noqa: E402
 
 
@@ -46,6 +46,24 @@ def main() -> int:
             same = bool(torch.equal(y_ep.view(torch.int16), y_1.view(torch.int16)))
             res[f"T{T}_bit_identical"] = same
             ok &= same
+        # the peer-memory exchange (decode sizes), eager and as a replayed CUDA graph
+        for T in (1, 8):
+            peer = PeerExpertParallelMoE(shard, W, bias, T)
+            g = GraphedStep(peer, T, 4096, dev)
+            for rep in range(3):
+                x = synth.hidden(T, seed=900 + 31 * rank + 7 * rep + T).to(dev)
+                y_1 = mimo_moe.moe_block(x, W, bias, full)
+                y_p = peer(x).clone()
+                y_g = g(x).clone()
+                torch.cuda.synchronize()
+                same = bool(torch.equal(y_p.view(torch.int16), y_1.view(torch.int16)) and
+                            torch.equal(y_g.view(torch.int16), y_1.view(torch.int16)))
+                res[f"peer_T{T}_rep{rep}_bit_identical"] = same
+                ok &= same
+            res[f"peer_T{T}_status"] = int(peer.status.item())
+            ok &= res[f"peer_T{T}_status"] == 0
+            del g
+            peer.close()
     finally:
         dist.barrier()
         dist.destroy_process_group()
