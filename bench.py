@@ -93,58 +93,86 @@ def make_inputs(B, dev, torch, rank=0):
     return xs, W
 
 
+def _host_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        return 1
+
+
 def cpu_reference_rate(B, budget_s, seed_batch=0):
-    """The reference path restated on the CPU (oracle), on a bounded sample of one batch: the distinct
-    experts of the batch are processed until `budget_s` is spent (at least one), and the time for the
-    whole batch is extrapolated by U / k.  Expert bytes are regenerated before the clock starts."""
+    """The reference path on the host cores, on a bounded sample of one decode batch of B <= 8 rows:
+    the reference's own kernels A/B (engine/mimo_stream/kernels.py:33-123, compiled for the CPU into
+    oracle/_ref with OpenMP) and its own group_routes; the router rule (model.py:58-65, MLX on the
+    reference's side) and the fixed-order combine restated in numpy.  The batch's distinct experts are
+    processed one at a time until `budget_s` is spent (at least one) and the batch time is
+    extrapolated by U / k.  Expert bytes are generated before each expert's clock starts.  Without
+    oracle/_ref the numpy restatement of the same path is timed instead (kind "port")."""
     import numpy as np
+    import torch
     from oracle import mimo_oracle as O
+    from oracle import ref_runner as RR
     from oracle import synth
-    x = synth.hidden(B, seed=2 + 1000 * seed_batch).float().numpy()
+    use_ref = RR.available()
+    xt = synth.hidden(B, seed=2 + 1000 * seed_batch)
+    x = xt.float().numpy()
     W = synth.router_weight().float().numpy()
+    t0 = time.perf_counter()
     _, inds, w = O.router(x, W, np.zeros(E, np.float32))
-    uids = np.unique(inds)
+    uids, urows, ucnt, uw, gidx = (RR.group_routes(inds, w) if use_ref else O.group_routes(inds, w))
+    t_fixed = time.perf_counter() - t0
     sp = synth.SynthPool(0, 0)
+    sig = O.sigmoid_table_bits() if use_ref else None
+    xb = xt.view(torch.int16).numpy().view(np.uint16)
     t_total, done = 0.0, 0
-    for e in uids:
+    for u, e in enumerate(uids):
         raw = {n: {int(e): sp[n][int(e)]} for n in ("gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s")}
-        pool = O.Pool(raw, cache=1)
-        rows = np.nonzero((inds == e).any(1))[0]
-        t0 = time.perf_counter()
-        d = pool.deq(int(e))
-        h = O.swiglu_bf16(O._dots32(d["gate"], x[rows]), O._dots32(d["up"], x[rows]))
-        O._dots32(d["down"], h)
-        t_total += time.perf_counter() - t0
+        if use_ref:
+            pool = {n: raw[n][int(e)][None] for n in raw}
+            one = dict(uslot=np.zeros(1, np.int32), urows=urows[u:u + 1], ucnt=ucnt[u:u + 1], uw=uw[u:u + 1])
+            t1 = time.perf_counter()
+            RR.moe_experts(xb, pool, one["uslot"], one["urows"], one["ucnt"], one["uw"],
+                           np.zeros(B * 8, np.int64), sig)
+        else:
+            pool = O.Pool(raw, cache=1)
+            rows = np.nonzero((inds == e).any(1))[0]
+            t1 = time.perf_counter()
+            d = pool.deq(int(e))
+            h = O.swiglu_bf16(O._dots32(d["gate"], x[rows]), O._dots32(d["up"], x[rows]))
+            O._dots32(d["down"], h)
+        t_total += time.perf_counter() - t1
         done += 1
         if t_total >= budget_s:
             break
-    per_batch = t_total / done * len(uids)
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        cores = 1
-    return B / per_batch, cores, f"{done} of {len(uids)} distinct experts of one B={B} decode batch, " \
-                                 f"extrapolated by U/k ({t_total:.1f} s of CPU work)"
+    per_batch = t_fixed + t_total / done * len(uids)
+    kind = "reference" if use_ref else "port"
+    what = ("the reference's kernels A/B and group_routes (oracle/_ref, OpenMP) + numpy router/combine"
+            if use_ref else "numpy restatement of the path")
+    return B / per_batch, _host_threads() if not use_ref else int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())), \
+        kind, f"{what}: {done} of {len(uids)} distinct experts of one B={B} decode batch, extrapolated by " \
+              f"U/k ({t_total:.1f} s of CPU work)"
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    # all host threads for the OpenMP reference kernels (torchrun sets 1 per process); before loading
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
     B = WORKLOADS[args.workload]
     budget = max(0.5, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
     rates = []
     for s in range(args.warmup + args.steps):
-        r, cores, sample = cpu_reference_rate(min(B, 8), budget, seed_batch=s % NBATCH)
+        r, cores, kind, sample = cpu_reference_rate(min(B, 8), budget, seed_batch=s % NBATCH)
         if s >= args.warmup:
             rates.append(r)
     v = statistics.median(rates)
     out = {"impl": "reference", "metric": f"MoE-layer tok/s ({args.workload})", "value": v,
            "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-           "higher_is_better": True, "dtype": "f32/f64 (numpy)", "data": "synthetic",
+           "higher_is_better": True, "dtype": "f32 (the reference's kernel code on the CPU)", "data": "synthetic",
            "config": {"workload": args.workload, "B": B, "experts": E, "hidden": H, "inter": I},
-           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
 
@@ -316,8 +344,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r, cores, sample = cpu_reference_rate(min(B, 8), args.cpu_budget)
-        cpu = {"value": r, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+        r, cores, kind, sample = cpu_reference_rate(min(B, 8), args.cpu_budget)
+        cpu = {"value": r, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample}
 
     if rank == 0:
         tok = B * args.steps * world
