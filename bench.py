@@ -234,14 +234,21 @@ def main():
     # expert parallelism replays one CUDA graph per step (router, collectives, expert kernels, combine):
     # the step issues ~10 kernels and 2 collectives, whose host-side launch cost would otherwise set
     # the pace.  The x copy into the graph's input is inside the step.
+    # The single-GPU decode step (4 kernels + a memset) is replayed as a graph too; prefill steps are
+    # long enough that launch gaps do not matter and run eagerly.
     from mimo_moe.ep import GraphedStep
-    gstep = GraphedStep(blk, B, H, dev) if ep else None
+    if ep:
+        gstep = GraphedStep(blk, B, H, dev)
+    elif B <= 8:
+        gstep = GraphedStep(lambda x: mimo_moe.moe_block(x, W, bias, pool, status=status, out=y), B, H, dev)
+    else:
+        gstep = None
 
     def block(x):
-        return gstep(x) if ep else mimo_moe.moe_block(x, W, bias, pool, status=status)
+        return gstep(x) if gstep is not None else mimo_moe.moe_block(x, W, bias, pool, status=status)
 
     def step(i):
-        if ep:
+        if gstep is not None:
             gstep(xs[i % NBATCH])
         else:
             mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
@@ -268,11 +275,14 @@ def main():
     clk = clocks.stop()
     launches = (np.zeros(4, np.int32), np.zeros(4, np.float32))
     _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
-    if ep:  # graph replays carry no profiling events: time the expert kernels in an eager pass
+    if gstep is not None:  # graph replays carry no profiling events: time the kernels in an eager pass
         nprof = min(args.steps, 50)
         _lib.check(L.mimo_moe_profile_enable(4 * nprof + 8), "profile_enable")
         for i in range(nprof):
-            blk(xs[i % NBATCH])
+            if ep:
+                blk(xs[i % NBATCH])
+            else:
+                mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
         torch.cuda.synchronize()
         _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
     _lib.check(L.mimo_moe_profile_enable(0), "profile_disable")

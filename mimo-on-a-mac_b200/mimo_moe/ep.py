@@ -97,11 +97,12 @@ class ExpertParallelMoE:
 
 
 class GraphedStep:
-    """The block for a fixed T captured once as a CUDA graph (collectives included), replayed per step:
+    """A block for a fixed T captured once as a CUDA graph (collectives included), replayed per step:
     `run(x)` copies x into the graph's input and returns the graph's output tensor (overwritten by
-    the next replay).  Delete the object before destroy_process_group."""
+    the next replay).  `block` is any callable x -> y (an expert-parallel block, or the single-GPU
+    block with its arguments bound).  Delete the object before destroy_process_group."""
 
-    def __init__(self, block: ExpertParallelMoE, T: int, H: int, device, dtype=torch.bfloat16, warmup: int = 2):
+    def __init__(self, block, T: int, H: int, device, dtype=torch.bfloat16, warmup: int = 2):
         self.x = torch.zeros(T, H, dtype=dtype, device=device)
         for _ in range(warmup):  # communicators, tensor maps, workspaces: created outside the capture
             block(self.x)

@@ -346,3 +346,25 @@ def test_downstream_logit_kl_through_a_random_head(gpu):
     kl = float((lr.exp() * (lr - lg)).sum(-1).mean())
     print(f"mean KL(oracle || gpu) of downstream logits: {kl:.3e}")
     assert kl < 1e-3
+
+
+def test_prefill_at_full_size_equals_the_per_route_path(gpu):
+    """Size-independent check at BASELINE scale (T = 2048, 256 experts): the prefill path (64-route
+    units, bf16 pair outputs, weighted fixed-order combine) equals, bit for bit, the per-route partials
+    of the expert-parallel building block with bf16 rounding (8-route units) followed by the route-order
+    combine — two different kernel configurations computing the same arithmetic."""
+    import mimo_moe
+    pool = mimo_moe.ExpertPools.synthetic(256, seed=0, layer=4, device=gpu)
+    T = 2048
+    x = synth.hidden(T, seed=77).to(gpu)
+    W = synth.router_weight().to(gpu)
+    idx, w = mimo_moe.router(x, W, torch.zeros(256, device=gpu))
+    y_pref = mimo_moe.moe_prefill(x, pool, idx, w)
+    part = mimo_moe.moe_experts_routes(x, pool, idx, w, expert_base=0, pairs_rounding=True)
+    y_route = mimo_moe.combine(part, T, 8)
+    assert torch.equal(y_pref.view(torch.int16), y_route.view(torch.int16))
+    # and a spot check of a few tokens against the oracle
+    opool = O.Pool(synth.SynthPool(0, 4))
+    rows = [0, 1000, 2047]
+    ref = O.moe_pairs(x[rows].float().cpu().numpy(), opool, idx[rows].cpu().numpy(), w[rows].cpu().numpy())
+    assert O.rel_err(f32(y_pref[rows]), ref) <= TOL_ORACLE
