@@ -1,6 +1,6 @@
 """Benchmark of the B200 MiMo MoE block (BASELINE.json metric: MoE-layer tok/s + expert HBM GB/s).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode8|decode4|decode2|decode1|prefill2048]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode8|decode4|decode2|decode1|prefill2048|prefill16384z]
   python bench.py --impl reference ...     # the reference path's CPU restatement on the host cores
 
 One step = one MoE layer (router -> dispatch -> MXFP4 experts -> combine) over one batch of synthetic
@@ -28,7 +28,10 @@ H, I, E, K_TOP = 4096, 2048, 256, 8
 EXPERT_BYTES = 3 * (I * H // 2 + I * H // 32)      # 13,369,344
 GATEUP_BYTES = 2 * (I * H // 2 + I * H // 32)      # per distinct expert, kernel A
 DOWN_BYTES = H * I // 2 + H * I // 32
-WORKLOADS = {"decode1": 1, "decode2": 2, "decode4": 4, "decode8": 8, "prefill2048": 2048}
+WORKLOADS = {"decode1": 1, "decode2": 2, "decode4": 4, "decode8": 8, "prefill2048": 2048, "prefill16384z": 16384}
+# config 4: Zipf(1.1)-biased routing, bias_e = c * log(p_e * E); c = 0.055 puts the most loaded
+# expert at ~10x the mean load on the seeded 16384-token batch (tuned once on the CPU router)
+ZIPF_C = 0.055
 NBATCH = 16
 
 
@@ -219,7 +222,12 @@ def main():
         pool = mimo_moe.ExpertPools.synthetic(NE, seed=0, layer=0, device=dev)
     xs, W = make_inputs(B, dev, torch, rank)
     W = W[:NE].contiguous()
-    bias = torch.zeros(NE, device=dev)
+    zipf = args.workload.endswith("z")
+    if zipf:
+        from oracle import synth as _synth  # seeded generator only
+        bias = _synth.zipf_bias(E=NE, c=ZIPF_C).to(dev)
+    else:
+        bias = torch.zeros(NE, device=dev)
     y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     L = mimo_moe.lib()
@@ -373,7 +381,7 @@ def main():
             "dtype": "e2m1 x e4m3 (two-term activations) -> f32, tcgen05 block-scaled",
             "data": "synthetic (seeded MXFP4 pool, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
             "config": {"workload": args.workload, "B": B * world, "experts": NE, "hidden": H, "inter": I,
-                       "topk": K_TOP, "routing": "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
+                       "topk": K_TOP, "routing": f"Zipf(1.1) bias, c={ZIPF_C}" if zipf else "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
                        "mean_distinct_experts_this_gpu": statistics.mean(steps_Ul),
                        "parallelism": (f"ep{world} (experts sharded {NE // world} per GPU; " +
                                        ("dispatch and return as NVLink peer stores inside the route and "
