@@ -214,7 +214,7 @@ def main():
     NE = args.pool_experts
     ep = world > 1  # expert parallelism: rank r holds experts [r*NE/N, (r+1)*NE/N), routes its own B tokens
     if ep:
-        from mimo_moe.ep import ExpertParallelMoE, expert_range
+        from mimo_moe.ep import expert_range
         lo, hi = expert_range(rank, world, NE)
         pool = mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=0, first_expert=lo, device=dev)
     else:
@@ -231,21 +231,22 @@ def main():
     y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     L = mimo_moe.lib()
-    # decode sizes exchange through NVLink peer memory inside the kernels; larger batches use NCCL
+    # decode sizes exchange through NVLink peer memory inside the kernels; prefill batches send each
+    # route to its expert's rank with NCCL all-to-alls
     peer = ep and B <= 8
     if ep:
-        from mimo_moe.ep import PeerExpertParallelMoE
+        from mimo_moe.ep import ExpertParallelPrefill, PeerExpertParallelMoE
         blk = PeerExpertParallelMoE(pool, W, bias, B, num_experts=NE) if peer else \
-            ExpertParallelMoE(pool, W, bias, num_experts=NE)
+            ExpertParallelPrefill(pool, W, bias, num_experts=NE)
     else:
         blk = None
-    # expert parallelism replays one CUDA graph per step (router, collectives, expert kernels, combine):
-    # the step issues ~10 kernels and 2 collectives, whose host-side launch cost would otherwise set
-    # the pace.  The x copy into the graph's input is inside the step.
-    # The single-GPU decode step (4 kernels + a memset) is replayed as a graph too; prefill steps are
-    # long enough that launch gaps do not matter and run eagerly.
+    # expert-parallel decode replays one CUDA graph per step (router, exchanges, expert kernels,
+    # combine): the step issues ~8 kernels, whose host-side launch cost would otherwise set the pace.
+    # The x copy into the graph's input is inside the step.  The single-GPU decode step (4 kernels + a
+    # memset) is replayed as a graph too; prefill steps (whose all-to-all splits are data-dependent)
+    # are long enough that launch gaps do not matter and run eagerly.
     from mimo_moe.ep import GraphedStep
-    if ep:
+    if peer:
         gstep = GraphedStep(blk, B, H, dev)
     elif B <= 8:
         gstep = GraphedStep(lambda x: mimo_moe.moe_block(x, W, bias, pool, status=status, out=y), B, H, dev)
@@ -253,11 +254,15 @@ def main():
         gstep = None
 
     def block(x):
-        return gstep(x) if gstep is not None else mimo_moe.moe_block(x, W, bias, pool, status=status)
+        if gstep is not None:
+            return gstep(x)
+        return blk(x) if ep else mimo_moe.moe_block(x, W, bias, pool, status=status)
 
     def step(i):
         if gstep is not None:
             gstep(xs[i % NBATCH])
+        elif ep:
+            blk(xs[i % NBATCH])
         else:
             mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
 
@@ -371,9 +376,10 @@ def main():
         # combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
         # down, combine
         # expert parallelism, peer exchange: router logits, route+scatter, 2 barriers, unit builder, term
-        # split, gate/up, down, combine; NCCL exchange: router logits + top-k, 3 dispatch, 2 unit
-        # builders, term split, gate/up, down, combine (the collectives are library kernels)
-        launches_per_step = (8 if peer else 10) if ep else (4 if B <= 8 else 11)
+        # split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch, 2 unit
+        # builders, term split, gate/up, down, per-route combine, weighted combine (the collectives and
+        # the route sort / gathers are library kernels)
+        launches_per_step = (8 if peer else 12) if ep else (4 if B <= 8 else 11)
         out = {
             "metric": f"MoE-layer tok/s ({args.workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -385,9 +391,9 @@ def main():
                        "mean_distinct_experts_this_gpu": statistics.mean(steps_Ul),
                        "parallelism": (f"ep{world} (experts sharded {NE // world} per GPU; " +
                                        ("dispatch and return as NVLink peer stores inside the route and "
-                                        "down kernels, flag barriers" if peer else
-                                        "NCCL all-gather dispatch, exact reduce-scatter return") +
-                                       "; fixed-order combine; one CUDA graph per step)") if ep else "single",
+                                        "down kernels, flag barriers; one CUDA graph per step" if peer else
+                                        "NCCL all-to-all of each route to its expert's rank and back") +
+                                       "; fixed-order combine)") if ep else "single",
                        "tokens_per_gpu": B,
                        "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
             "expert_gbs": expert_gbs,

@@ -174,6 +174,10 @@ int mimo_moe_experts_routes(const uint16_t* x, int32_t x_ld, int32_t rows, const
                             void* stream);
 int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,
                      uint16_t* y, void* stream);
+/* Prefill combine (model.py:266-271): y[t] = bf16(sum over k in order of fp32(ypair[inv[t*topk+k]]) *
+ * weight[t*topk+k]), skipping inv < 0.  ypair bf16 [*, H] (per-route expert outputs). */
+int mimo_moe_combine_pairs(const uint16_t* ypair, const int32_t* inv, const float* weight, int32_t T, int32_t topk,
+                           int32_t H, uint16_t* y, void* stream);
 int mimo_moe_peer_alloc(size_t bytes, void** ptr, void* handle);
 int mimo_moe_peer_open(const void* handle, void** ptr);
 int mimo_moe_peer_close(void* ptr);

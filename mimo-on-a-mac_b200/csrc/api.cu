@@ -715,6 +715,13 @@ int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, in
   return MIMO_OK;
 }
 
+int mimo_moe_combine_pairs(const uint16_t* ypair, const int32_t* inv, const float* weight, int32_t T, int32_t topk,
+                           int32_t H, uint16_t* y, void* stream) {
+  if (!ypair || !inv || !weight || !y || T < 1 || topk < 1 || topk > 8 || H < 8 || H % 8) return MIMO_EINVAL;
+  MIMO_TRY(launch_combine_prefill(ypair, inv, weight, T, topk, H, y, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
 int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up_w, uint8_t* up_s,
                                  uint32_t* down_w, uint8_t* down_s, int32_t S, int32_t H, int32_t I,
                                  uint64_t seed, int32_t layer, int32_t first_expert, void* stream) {

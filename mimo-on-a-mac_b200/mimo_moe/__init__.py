@@ -4,9 +4,9 @@ Drop-in for the expert path of cialanjcampbell-coder/mimo-on-a-mac's engine/mimo
 (Router, group_routes, moe_experts, the gather_qmm pair path).  All compute runs in hand-written CUDA
 (libmimo_moe.so, C ABI in include/mimo_moe.h); there is no CPU fallback."""
 from ._lib import LIB_PATH, MimoError, lib
-from .ops import (ExpertPools, Groups, MoEBlock, MoEConfig, Router, combine, dispatch, group_routes,
+from .ops import (ExpertPools, Groups, MoEBlock, MoEConfig, Router, combine, combine_pairs, dispatch, group_routes,
                   moe_block, moe_experts, moe_experts_routes, moe_prefill, read_status, router, topk)
 
 __all__ = ["LIB_PATH", "MimoError", "lib", "ExpertPools", "Groups", "MoEBlock", "MoEConfig", "Router",
-           "combine", "dispatch", "group_routes", "moe_block", "moe_experts", "moe_experts_routes",
+           "combine", "combine_pairs", "dispatch", "group_routes", "moe_block", "moe_experts", "moe_experts_routes",
            "moe_prefill", "read_status", "router", "topk"]

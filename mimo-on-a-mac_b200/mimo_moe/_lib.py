@@ -52,6 +52,8 @@ SIGNATURES = {
     "mimo_moe_route_scatter": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                          c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mimo_moe_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
+    "mimo_moe_combine_pairs": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
+                                         c_void_p]),
     "mimo_moe_prefill": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_int32, c_void_p, c_void_p,
                                    c_int32, c_int32, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "mimo_moe_block_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),

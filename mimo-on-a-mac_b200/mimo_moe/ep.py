@@ -212,3 +212,65 @@ class PeerExpertParallelMoE:
         for p in self.local.values():
             self.L.mimo_moe_peer_free(ctypes.c_void_p(p))
         self.local = {}
+
+
+PairsFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+CombinePairsFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, int, int], torch.Tensor]
+
+
+class ExpertParallelPrefill:
+    """Expert parallelism for prefill-size batches: routes travel to their expert, not tokens to
+    every rank.  One step:
+
+      1. route the rank's own T tokens (model.py:58-65);
+      2. dispatch: routes sorted by destination rank (stable), per-destination counts exchanged, then
+         one all-to-all of the routes' token rows and local expert ids (variable splits; the counts
+         cross to the host once per step, acceptable at prefill sizes);
+      3. expert side: per-route bf16 products of the received routes (`moe_prefill` with one route per
+         row and weight 1, which returns each route's bf16 pair output unchanged, model.py:221-228);
+      4. return: the inverse all-to-all;
+      5. combine: y[t] = bf16(sum over k in order of fp32(out[t, k]) * w[t, k]) (model.py:266-271).
+
+    Each route's bf16 output is computed by the same kernels as on one GPU, so the result equals the
+    single-GPU prefill path bit for bit.  Compute steps are pluggable for the CPU gloo tests."""
+
+    def __init__(self, pools_local, router_w: torch.Tensor, bias: Optional[torch.Tensor], *,
+                 num_experts: int = 256, topk: int = 8, group=None, router_fn: Optional[RouterFn] = None,
+                 pairs_fn: Optional[PairsFn] = None, combine_fn: Optional[CombinePairsFn] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.num_experts, self.topk = num_experts, topk
+        self.per_rank = num_experts // self.world
+        self.expert_base, _ = expert_range(self.rank, self.world, num_experts)
+        self.pools = pools_local
+        self.router_w, self.bias = router_w, bias
+        self.router_fn = router_fn or (lambda x: ops.router(x, self.router_w, self.bias, topk=self.topk))
+        self.pairs_fn = pairs_fn or (lambda X, e: ops.moe_prefill(
+            X, self.pools, e[:, None], torch.ones(e.shape[0], 1, device=X.device), E=self.per_rank))
+        self.combine_fn = combine_fn or (lambda yp, inv, w, T, k: ops.combine_pairs(yp, inv, w, T, k))
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        N, k, dev = self.world, self.topk, x.device
+        idx, w = self.router_fn(x)
+        idx = idx.to(torch.int32).reshape(-1)
+        w = w.to(torch.float32).contiguous()
+        dest = (idx // self.per_rank).to(torch.int64)
+        order = torch.sort(dest, stable=True).indices            # send position -> route t*k + j
+        inv = torch.empty_like(order)
+        inv[order] = torch.arange(order.numel(), device=dev)     # route -> send position
+        send_counts = torch.bincount(dest, minlength=N).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()      # the step's one host crossing
+        send_x = x[order // k].contiguous()
+        send_e = (idx[order] - dest[order].to(torch.int32) * self.per_rank).to(torch.int32).contiguous()
+        recv_x = torch.empty(sum(rc), H, dtype=x.dtype, device=dev)
+        recv_e = torch.empty(sum(rc), dtype=torch.int32, device=dev)
+        dist.all_to_all_single(recv_x, send_x, rc, sc, group=self.group)
+        dist.all_to_all_single(recv_e, send_e, rc, sc, group=self.group)
+        out = self.pairs_fn(recv_x, recv_e) if recv_x.shape[0] else torch.empty(0, H, dtype=x.dtype, device=dev)
+        back = torch.empty(sum(sc), H, dtype=out.dtype, device=dev)
+        dist.all_to_all_single(back, out.contiguous(), sc, rc, group=self.group)
+        return self.combine_fn(back, inv.to(torch.int32), w, T, k)

@@ -359,6 +359,20 @@ def combine(part: torch.Tensor, M: int, k: int = TOPK, gather_idx: Optional[torc
     return y
 
 
+def combine_pairs(ypair: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, T: int, k: int = TOPK,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """model.py:266-271: y[t] = bf16(sum over j in order of fp32(ypair[inv[t*k + j]]) * w[t, j])."""
+    _need_cuda(ypair, "ypair")
+    ypair = ypair.to(torch.bfloat16).contiguous()
+    inv = inv.to(device=ypair.device, dtype=torch.int32).contiguous()
+    w = w.to(device=ypair.device, dtype=torch.float32).contiguous()
+    H = ypair.shape[1]
+    y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=ypair.device)
+    check(lib().mimo_moe_combine_pairs(ypair.data_ptr(), inv.data_ptr(), w.data_ptr(), T, k, H, y.data_ptr(),
+                                       _stream()), "combine_pairs")
+    return y
+
+
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, bias: Optional[torch.Tensor], pools,
               topk: int = TOPK, status: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
               return_routes: bool = False):

@@ -5,7 +5,9 @@
 Rank r holds experts [r*256/N, (r+1)*256/N) of a seeded synthetic layer, routes its own T tokens and
 runs the expert-parallel block (mimo_moe/ep.py, NCCL).  Each rank then runs the single-GPU block on
 the same tokens with the whole layer resident and the outputs must be identical bit for bit, for
-T = 1 (stock-path rounding), 8 (decode) and 12 (prefill rounding).  Prints one JSON line per rank."""
+T = 1 (stock-path rounding), 8 (decode) and 12 (prefill rounding) through the NCCL all-gather block,
+T = 1 and 8 through the peer-memory block (eager and graphed), and T = 64 and 600 through the
+all-to-all prefill block.  Prints one JSON line per rank."""
 import json
 import os
 import sys
@@ -20,7 +22,8 @@ for p in (ROOT, os.path.join(ROOT, "mimo-on-a-mac_b200")):
         sys.path.insert(0, p)
 
 import mimo_moe  # noqa: E402
-from mimo_moe.ep import ExpertParallelMoE, GraphedStep, PeerExpertParallelMoE, expert_range  # noqa: E402
+from mimo_moe.ep import (ExpertParallelMoE, ExpertParallelPrefill, GraphedStep,  # noqa: E402
+                         PeerExpertParallelMoE, expert_range)
 from oracle import synth  # noqa: E402
 
 
@@ -64,6 +67,16 @@ def main() -> int:
             ok &= res[f"peer_T{T}_status"] == 0
             del g
             peer.close()
+        # prefill sizes: each route travels to its expert's rank and back (NCCL all-to-all)
+        pre = ExpertParallelPrefill(shard, W, bias)
+        for T in (64, 600):
+            x = synth.hidden(T, seed=700 + 13 * rank + T).to(dev)
+            y_ep = pre(x)
+            y_1 = mimo_moe.moe_block(x, W, bias, full)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(y_ep.view(torch.int16), y_1.view(torch.int16)))
+            res[f"prefill_T{T}_bit_identical"] = same
+            ok &= same
     finally:
         dist.barrier()
         dist.destroy_process_group()

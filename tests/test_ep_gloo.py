@@ -3,8 +3,9 @@
 The compute steps are replaced by small deterministic CPU functions (router: top-k of x @ Wr with
 normalised sigmoid weights; expert e: tanh(x @ M_e) * w; combine: float32 sum over k in order ->
 bf16), so the test checks what the multi-GPU path adds: expert ownership, the all-gather dispatch,
-zero partials for other ranks' experts, the exact reduce-scatter return and the fixed-order combine.
-The EP output must equal the single-process output bit for bit."""
+zero partials for other ranks' experts, the exact reduce-scatter return and the fixed-order combine;
+for the prefill path, the all-to-all of each route to its expert's rank (variable and empty splits),
+the return and the weighted combine.  The EP output must equal the single-process output bit for bit."""
 import os
 import socket
 
@@ -90,6 +91,56 @@ def test_ep_matches_single_process_bit_for_bit():
         ref = _combine(_experts(0, E)(x, idx, w, False), T, K)
         got = np.frombuffer(out[rank], dtype=np.float32).reshape(T, H)
         assert np.array_equal(got, ref.float().numpy()), rank
+
+
+def _pairs(lo: int):
+    """Per-route bf16 products of the received routes (local expert ids), as the expert side of the
+    all-to-all prefill computes them."""
+    mats = _expert_mats()
+
+    def fn(X, e):
+        return torch.stack([torch.tanh(X[r].float() @ mats[lo + int(e[r])]).to(torch.bfloat16)
+                            for r in range(X.shape[0])]) if X.shape[0] else torch.empty(0, H, dtype=torch.bfloat16)
+    return fn
+
+
+def _combine_pairs(back, inv, w, T_, k):
+    y = torch.zeros(T_, back.shape[1], dtype=torch.float32)
+    for t in range(T_):
+        for j in range(k):
+            y[t] += back[int(inv[t * k + j])].float() * w[t, j]
+    return y.to(torch.bfloat16)
+
+
+def _prefill_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mimo_moe.ep import ExpertParallelPrefill, expert_range
+        lo, _ = expert_range(rank, world, E)
+        blk = ExpertParallelPrefill(None, None, None, num_experts=E, topk=K, router_fn=_router,
+                                    pairs_fn=_pairs(lo), combine_fn=_combine_pairs)
+        # rank 1 routes no tokens in the second call: empty splits both ways
+        for n in (T, T if rank == 0 else 0):
+            y = blk(_tokens(rank)[:n])
+            assert y.shape == (n, H)
+            out[(rank, n)] = y.float().numpy().tobytes()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_prefill_all_to_all_matches_single_process():
+    world = 2
+    port = _free_port()
+    out = mp.Manager().dict()
+    mp.start_processes(_prefill_worker, args=(world, port, out), nprocs=world, start_method="spawn")
+    for rank in range(world):
+        x = _tokens(rank)
+        idx, w = _router(x)
+        ref = _combine(_experts(0, E)(x, idx, w, True), T, K)
+        got = np.frombuffer(out[(rank, T)], dtype=np.float32).reshape(T, H)
+        assert np.array_equal(got, ref.float().numpy()), rank
+    assert out[(1, 0)] == b""
 
 
 def test_expert_ranges_and_rounding_rule():
