@@ -276,6 +276,8 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    if ep and not peer:
+        blk.routes_received = 0
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for i in range(args.steps):
@@ -286,6 +288,9 @@ def main():
         dist.barrier()
     ms = ev0.elapsed_time(ev1)
     clk = clocks.stop()
+    # routes this rank's expert kernels computed per step (expert-parallel prefill: skewed routing
+    # gives the ranks unequal shares; otherwise each rank computes its own B * k routes)
+    routes_step = blk.routes_received / args.steps if ep and not peer else B * K_TOP
     launches = (np.zeros(4, np.int32), np.zeros(4, np.float32))
     _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
     if gstep is not None:  # graph replays carry no profiling events: time the kernels in an eager pass
@@ -334,7 +339,7 @@ def main():
                     "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
                     "algorithmic_bytes_per_launch": gu_bytes}
     else:        # prefill: algorithmic FLOPs 2 (gate, up) x 2 x I x H per routed pair
-        flops = B * K_TOP * 2 * 2 * I * H
+        flops = routes_step * 2 * 2 * I * H
         tf = flops / (gu_ms * 1e-3) / 1e12
         roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=64,MODE=0> (prefill gate/up + SwiGLU)", "bound": "tensor",
                     "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
@@ -389,6 +394,7 @@ def main():
             "config": {"workload": args.workload, "B": B * world, "experts": NE, "hidden": H, "inter": I,
                        "topk": K_TOP, "routing": f"Zipf(1.1) bias, c={ZIPF_C}" if zipf else "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
                        "mean_distinct_experts_this_gpu": statistics.mean(steps_Ul),
+                       "routes_this_gpu_per_step": routes_step,
                        "parallelism": (f"ep{world} (experts sharded {NE // world} per GPU; " +
                                        ("dispatch and return as NVLink peer stores inside the route and "
                                         "down kernels, flag barriers; one CUDA graph per step" if peer else

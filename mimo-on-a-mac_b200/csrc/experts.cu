@@ -692,8 +692,8 @@ __global__ void combine_decode_kernel(const float* __restrict__ part, const int3
                                       const int32_t* __restrict__ urows, const int32_t* __restrict__ ucnt,
                                       const int32_t* __restrict__ num_unique, int ucap, int R, int M,
                                       int topk, int H, uint16_t* __restrict__ y) {
-  const int t = blockIdx.y;
-  const int m = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const int t = blockIdx.x;  // rows on x: gridDim.y stops at 65535
+  const int m = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (t >= M || m >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   auto add = [&](int slot) {
@@ -724,7 +724,7 @@ __global__ void combine_decode_kernel(const float* __restrict__ part, const int3
 cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const int32_t* urows,
                                   const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
                                   int M, int topk, int H, uint16_t* y, cudaStream_t st) {
-  dim3 grid((H / 4 + 255) / 256, M);
+  dim3 grid(M, (H / 4 + 255) / 256);
   combine_decode_kernel<<<grid, 256, 0, st>>>(part, gidx, urows, ucnt, num_unique, ucap, R, M, topk, H,
                                               y);
   return cudaGetLastError();
@@ -734,8 +734,8 @@ cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const 
 // m * topk + k without gidx (kernels.py:194-199).
 __global__ void combine_rows_kernel(const float* __restrict__ part, const int32_t* __restrict__ gidx, int M,
                                     int topk, int H, uint16_t* __restrict__ y) {
-  const int t = blockIdx.y;
-  const int m = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const int t = blockIdx.x;  // rows on x: gridDim.y stops at 65535
+  const int m = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (t >= M || m >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < topk; ++k) {
@@ -754,7 +754,7 @@ __global__ void combine_rows_kernel(const float* __restrict__ part, const int32_
 
 cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H, uint16_t* y,
                                 cudaStream_t st) {
-  dim3 grid((H / 4 + 255) / 256, M);
+  dim3 grid(M, (H / 4 + 255) / 256);
   combine_rows_kernel<<<grid, 256, 0, st>>>(part, gidx, M, topk, H, y);
   return cudaGetLastError();
 }
@@ -763,8 +763,8 @@ cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, i
 __global__ void combine_prefill_kernel(const uint16_t* __restrict__ ypair, const int32_t* __restrict__ inv,
                                        const float* __restrict__ w, int T, int topk, int H,
                                        uint16_t* __restrict__ y) {
-  const int t = blockIdx.y;
-  const int m = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int t = blockIdx.x;  // rows on x: gridDim.y stops at 65535
+  const int m = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
   if (t >= T || m >= H) return;
   float acc[8];
 #pragma unroll
@@ -789,7 +789,7 @@ __global__ void combine_prefill_kernel(const uint16_t* __restrict__ ypair, const
 
 cudaError_t launch_combine_prefill(const uint16_t* ypair, const int32_t* inv, const float* w, int T,
                                    int topk, int H, uint16_t* y, cudaStream_t st) {
-  dim3 grid((H / 8 + 255) / 256, T);
+  dim3 grid(T, (H / 8 + 255) / 256);
   combine_prefill_kernel<<<grid, 256, 0, st>>>(ypair, inv, w, T, topk, H, y);
   return cudaGetLastError();
 }

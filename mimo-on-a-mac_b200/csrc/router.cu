@@ -69,8 +69,8 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t* __re
                                                             float* __restrict__ logits, int T, int H,
                                                             int E) {
   const int warp = threadIdx.x >> 5;
-  const int e = blockIdx.x * 8 + warp;
-  const int t0 = blockIdx.y * 8;
+  const int e = blockIdx.y * 8 + warp;
+  const int t0 = blockIdx.x * 8;  // token blocks on x: gridDim.y stops at 65535
   if (e >= E) return;
   logits_warp(x, w, logits, t0, min(8, T - t0), H, E, e);
 }
@@ -338,7 +338,7 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* lo
     router_logits_small_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, T, H, E, logits);
     return cudaGetLastError();
   }
-  dim3 grid((E + 7) / 8, (T + 7) / 8);
+  dim3 grid((T + 7) / 8, (E + 7) / 8);
   router_logits_kernel<<<grid, 256, 0, st>>>(x, w, logits, T, H, E);
   return cudaGetLastError();
 }

@@ -249,6 +249,7 @@ class ExpertParallelPrefill:
         self.pairs_fn = pairs_fn or (lambda X, e: ops.moe_prefill(
             X, self.pools, e[:, None], torch.ones(e.shape[0], 1, device=X.device), E=self.per_rank))
         self.combine_fn = combine_fn or (lambda yp, inv, w, T, k: ops.combine_pairs(yp, inv, w, T, k))
+        self.routes_received = 0  # routes this rank's experts computed, summed over calls
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
@@ -264,6 +265,7 @@ class ExpertParallelPrefill:
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         sc, rc = send_counts.tolist(), recv_counts.tolist()      # the step's one host crossing
+        self.routes_received += sum(rc)
         send_x = x[order // k].contiguous()
         send_e = (idx[order] - dest[order].to(torch.int32) * self.per_rank).to(torch.int32).contiguous()
         recv_x = torch.empty(sum(rc), H, dtype=x.dtype, device=dev)

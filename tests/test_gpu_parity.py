@@ -368,3 +368,22 @@ def test_prefill_at_full_size_equals_the_per_route_path(gpu):
     rows = [0, 1000, 2047]
     ref = O.moe_pairs(x[rows].float().cpu().numpy(), opool, idx[rows].cpu().numpy(), w[rows].cpu().numpy())
     assert O.rel_err(f32(y_pref[rows]), ref) <= TOL_ORACLE
+
+
+def test_combine_pairs_rows_beyond_the_grid_y_limit(gpu):
+    """The weighted pair combine launches one block row per token on grid x, so an expert-parallel
+    rank that receives more than 65535 routes still combines them: with one route per row, weight 1
+    and the identity permutation the output equals the input bit for bit."""
+    import mimo_moe
+    T, H = 70001, 4096
+    g = torch.Generator(device=gpu).manual_seed(11)
+    yp = torch.randn(T, H, generator=g, device=gpu).to(torch.bfloat16)
+    inv = torch.arange(T, dtype=torch.int32, device=gpu)
+    y = mimo_moe.combine_pairs(yp, inv, torch.ones(T, 1, device=gpu), T, 1)
+    assert torch.equal(y.view(torch.int16), yp.view(torch.int16))
+    # two routes per token: y = bf16(fp32(a) * 0.25 + fp32(b) * 0.75), the last row included
+    inv2 = torch.arange(2 * T, dtype=torch.int32, device=gpu) % T
+    w2 = torch.tensor([0.25, 0.75], device=gpu).repeat(T, 1)
+    y2 = mimo_moe.combine_pairs(yp, inv2, w2, T, 2)
+    a, b = yp[(2 * torch.arange(T, device=gpu)) % T].float(), yp[(2 * torch.arange(T, device=gpu) + 1) % T].float()
+    assert torch.equal(y2.view(torch.int16), (a * 0.25 + b * 0.75).to(torch.bfloat16).view(torch.int16))
