@@ -1,6 +1,7 @@
 """Benchmark of the B200 MiMo MoE block (BASELINE.json metric: MoE-layer tok/s + expert HBM GB/s).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode8|decode4|decode2|decode1|prefill2048|prefill16384z]
+  python bench.py --workload stack48_decode8 [--layers L]   # config 3: a 48-layer decode stack
   python bench.py --impl reference ...     # the reference path's CPU restatement on the host cores
 
 One step = one MoE layer (router -> dispatch -> MXFP4 experts -> combine) over one batch of synthetic
@@ -28,7 +29,9 @@ H, I, E, K_TOP = 4096, 2048, 256, 8
 EXPERT_BYTES = 3 * (I * H // 2 + I * H // 32)      # 13,369,344
 GATEUP_BYTES = 2 * (I * H // 2 + I * H // 32)      # per distinct expert, kernel A
 DOWN_BYTES = H * I // 2 + H * I // 32
-WORKLOADS = {"decode1": 1, "decode2": 2, "decode4": 4, "decode8": 8, "prefill2048": 2048, "prefill16384z": 16384}
+WORKLOADS = {"decode1": 1, "decode2": 2, "decode4": 4, "decode8": 8, "prefill2048": 2048, "prefill16384z": 16384,
+             "stack48_decode1": 1, "stack48_decode8": 8}
+STACK_LAYERS = 48  # config 3: 48 MoE layers (~164 GB of experts), RMSNorm (unit weight) between layers
 # config 4: Zipf(1.1)-biased routing, bias_e = c * log(p_e * E); c = 0.055 puts the most loaded
 # expert at ~10x the mean load on the seeded 16384-token batch (tuned once on the CPU router)
 ZIPF_C = 0.055
@@ -90,9 +93,9 @@ class ClockSampler:
 
 
 def make_inputs(B, dev, torch, rank=0):
-    from oracle import synth  # seeded generators only (no oracle math on this path)
-    xs = [synth.hidden(B, seed=2 + 1000 * i + 100000 * rank).to(dev) for i in range(NBATCH)]
-    W = synth.router_weight().to(dev)
+    from mimo_moe import synthetic
+    xs = [synthetic.hidden(B, seed=2 + 1000 * i + 100000 * rank).to(dev) for i in range(NBATCH)]
+    W = synthetic.router_weight().to(dev)
     return xs, W
 
 
@@ -171,13 +174,186 @@ def run_reference(args):
         if s >= args.warmup:
             rates.append(r)
     v = statistics.median(rates)
-    out = {"impl": "reference", "metric": f"MoE-layer tok/s ({args.workload})", "value": v,
+    metric = f"MoE-layer tok/s ({args.workload})"
+    if args.workload.startswith("stack"):  # L layers per token: the one-layer rate / L
+        v /= args.layers
+        metric = f"MoE-stack tok/s ({args.workload}, {args.layers} layers)"
+        sample = f"one layer's rate / {args.layers} layers; {sample}"
+    out = {"impl": "reference", "metric": metric, "value": v,
            "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
            "higher_is_better": True, "dtype": "f32 (the reference's kernel code on the CPU)", "data": "synthetic",
            "config": {"workload": args.workload, "B": B, "experts": E, "hidden": H, "inter": I},
            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
+
+
+def bench_stack(args):
+    """one decode step = B tokens per GPU through L MoE layers (RMSNorm, unit weight,
+    between layers), experts sharded 256/N per GPU for every layer, the peer-memory exchange per layer
+    on N > 1; the whole step replays as one CUDA graph.  Every layer's experts are seeded independently
+    (pool layer index l, router W seed 1 + 1000 l, bias 0)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import mimo_moe
+    from mimo_moe import _lib, synthetic
+    from mimo_moe.ep import GraphedStep, PeerExpertParallelMoE, expert_range
+    from mimo_moe.stack import MoEStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    B, L = WORKLOADS[args.workload], args.layers
+    lo, hi = expert_range(rank, world, E)
+    layers = []
+    for l in range(L):
+        W = synthetic.router_weight(seed=1 + 1000 * l).to(dev)
+        pool = mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=l, first_expert=lo, device=dev)
+        layers.append((W, None, pool))
+    torch.cuda.synchronize()
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    peer = None
+    if world > 1:
+        peer = PeerExpertParallelMoE(layers[0][2], layers[0][0], None, B, num_experts=E)
+        stack = MoEStack(layers, layer_fn=lambda x, l: peer.layer(x, layers[l][2], layers[l][0], None))
+    else:
+        stack = MoEStack(layers, status=status)
+    xs = [synthetic.hidden(B, seed=2 + 1000 * i + 100000 * rank).to(dev) for i in range(NBATCH)]
+    gstep = GraphedStep(stack, B, H, dev)
+    for i in range(max(3, args.warmup)):
+        gstep(xs[i % NBATCH])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        gstep(xs[i % NBATCH])
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # eager pass: per-launch kernel times, and every layer's routes (all ranks' tokens) per batch ->
+    # distinct experts per layer, U (all GPUs) and U_local (this GPU's shard)
+    L_ = mimo_moe.lib()
+    U, U_local = [], []
+
+    def on_layer(l, x):
+        idx, _ = mimo_moe.router(x, layers[l][0], None)
+        idx = idx.contiguous()
+        if world > 1:
+            allidx = torch.empty(world * idx.shape[0], idx.shape[1], dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(allidx, idx)
+            idx = allidx
+        u = torch.unique(idx)
+        U.append(int(u.numel()))
+        U_local.append(int(((u >= lo) & (u < hi)).sum().item()))
+
+    nprof = 4
+    _lib.check(L_.mimo_moe_profile_enable(2 * L * nprof + 8), "profile_enable")
+    for i in range(nprof):
+        stack(xs[i % NBATCH])
+    torch.cuda.synchronize()
+    launches = (np.zeros(4, np.int32), np.zeros(4, np.float32))
+    _lib.check(L_.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
+    _lib.check(L_.mimo_moe_profile_enable(0), "profile_disable")
+    stack.on_layer = on_layer
+    for i in range(NBATCH):
+        stack(xs[i])
+    stack.on_layer = None
+    torch.cuda.synchronize()
+    st_val = int((peer.status if peer is not None else status).item())
+    if st_val != 0:
+        raise RuntimeError(f"device status {st_val} during the bench")
+    hbm, _, peak_kind = peaks()
+    gu_ms = float(launches[1][0]) / max(1, int(launches[0][0]))
+    dn_ms = float(launches[1][1]) / max(1, int(launches[0][1]))
+    gu_bytes = statistics.mean(U_local) * GATEUP_BYTES
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    step_U = sum(U) / NBATCH                       # distinct experts summed over the L layers, per step
+    expert_gbs = step_U * EXPERT_BYTES * args.steps / (ms * 1e-3) / 1e9
+
+    xh = [x.cpu().pin_memory() for x in xs]
+    yh = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        yd = gstep(xh[i % NBATCH].to(dev, non_blocking=True))
+        yh.copy_(yd, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r, cores, kind, sample = cpu_reference_rate(B, args.cpu_budget)
+        cpu = {"value": r / L, "unit": "tok/s", "cores": cores, "kind": kind,
+               "sample": f"one layer's rate / {L} layers; {sample}"}
+    if rank == 0:
+        tok = B * args.steps * world
+        # per layer: single GPU = route (+ memset), gate/up, down, combine; peer exchange = router
+        # logits, route+scatter, 2 barriers, unit builder, term split, gate/up, down, combine; plus
+        # one RMSNorm between layers
+        per_layer = 8 if world > 1 else 4
+        out = {
+            "metric": f"MoE-stack tok/s ({args.workload}, {L} layers)", "value": tok / (ms * 1e-3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e2m1 x e4m3 (two-term activations) -> f32, tcgen05 block-scaled",
+            "data": "synthetic (48 independently seeded MXFP4 layers, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
+            "config": {"workload": args.workload, "layers": L, "B": B * world, "tokens_per_gpu": B,
+                       "experts": E, "hidden": H, "inter": I, "topk": K_TOP, "norm": "RMSNorm eps 1e-6, unit weight",
+                       "expert_bytes_per_gpu": L * (hi - lo) * EXPERT_BYTES,
+                       "mean_distinct_experts_per_layer": statistics.mean(U),
+                       "mean_distinct_experts_per_layer_this_gpu": statistics.mean(U_local),
+                       "parallelism": (f"ep{world} (experts sharded {E // world} per GPU in every layer; NVLink "
+                                       "peer-store exchange per layer, flag barriers)") if world > 1 else "single",
+                       "graph": "the whole L-layer step is one CUDA graph",
+                       "l2": f"inputs > L2: {L * (hi - lo) * EXPERT_BYTES / 1e9:.1f} GB of experts per GPU"},
+            "expert_gbs": expert_gbs,
+            "expert_frac_of_measured_hbm": expert_gbs / world / hbm,
+            "roofline": {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
+                         "algorithmic_bytes_per_launch": gu_bytes, "kernel_ms": {"gate_up": gu_ms, "down": dn_ms}},
+            "clocks": clk,
+            "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2,
+                    "d2h_bytes_per_step": B * H * 2},
+            "gpu_launches": (per_layer * L + (L - 1)) * args.steps,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out))
+    del gstep
+    torch.cuda.synchronize()
+    if peer is not None:
+        peer.close()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def main():
@@ -191,9 +367,12 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--pool-experts", type=int, default=E,
                     help="experts in the pool and router (small cases for profiling; default 256)")
+    ap.add_argument("--layers", type=int, default=STACK_LAYERS, help="layers of the stack workloads")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload.startswith("stack"):
+        return bench_stack(args)
 
     import numpy as np
     import torch
@@ -224,8 +403,8 @@ def main():
     W = W[:NE].contiguous()
     zipf = args.workload.endswith("z")
     if zipf:
-        from oracle import synth as _synth  # seeded generator only
-        bias = _synth.zipf_bias(E=NE, c=ZIPF_C).to(dev)
+        from mimo_moe import synthetic
+        bias = synthetic.zipf_bias(E=NE, c=ZIPF_C).to(dev)
     else:
         bias = torch.zeros(NE, device=dev)
     y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)

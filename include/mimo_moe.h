@@ -178,6 +178,11 @@ int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, in
  * weight[t*topk+k]), skipping inv < 0.  ypair bf16 [*, H] (per-route expert outputs). */
 int mimo_moe_combine_pairs(const uint16_t* ypair, const int32_t* inv, const float* weight, int32_t T, int32_t topk,
                            int32_t H, uint16_t* y, void* stream);
+/* RMSNorm of each row before an MoE layer (model.py:75 `post_attention_layernorm`, MLX
+ * fast.rms_norm): y = bf16(x * rsqrt(mean(x^2) + eps)), times weight (bf16 [H]) when weight is not
+ * null.  x, y bf16 [T, H], 16-byte aligned, H a multiple of 8; x == y is allowed. */
+int mimo_moe_rmsnorm(const uint16_t* x, const uint16_t* weight, int32_t T, int32_t H, float eps, uint16_t* y,
+                     void* stream);
 int mimo_moe_peer_alloc(size_t bytes, void** ptr, void* handle);
 int mimo_moe_peer_open(const void* handle, void** ptr);
 int mimo_moe_peer_close(void* ptr);

@@ -722,6 +722,15 @@ int mimo_moe_combine_pairs(const uint16_t* ypair, const int32_t* inv, const floa
   return MIMO_OK;
 }
 
+int mimo_moe_rmsnorm(const uint16_t* x, const uint16_t* weight, int32_t T, int32_t H, float eps, uint16_t* y,
+                     void* stream) {
+  const auto a16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (!x || !y || T < 1 || H < 8 || H % 8 || !(eps >= 0.f) || !a16(x) || !a16(y) || (weight && !a16(weight)))
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_rmsnorm(x, weight, T, H, eps, y, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
 int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up_w, uint8_t* up_s,
                                  uint32_t* down_w, uint8_t* down_s, int32_t S, int32_t H, int32_t I,
                                  uint64_t seed, int32_t layer, int32_t first_expert, void* stream) {

@@ -147,6 +147,8 @@ cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, i
 cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const int32_t* urows,
                                   const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
                                   int M, int topk, int H, uint16_t* y, cudaStream_t st);
+cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* weight, int T, int H, float eps, uint16_t* y,
+                           cudaStream_t st);
 cudaError_t launch_combine_prefill(const uint16_t* ypair, const int32_t* inv, const float* w, int T,
                                    int topk, int H, uint16_t* y, cudaStream_t st);
 cudaError_t launch_fill_synthetic(uint32_t* gw, uint8_t* gs, uint32_t* uw, uint8_t* us, uint32_t* dw,

@@ -5,8 +5,9 @@ Drop-in for the expert path of cialanjcampbell-coder/mimo-on-a-mac's engine/mimo
 (libmimo_moe.so, C ABI in include/mimo_moe.h); there is no CPU fallback."""
 from ._lib import LIB_PATH, MimoError, lib
 from .ops import (ExpertPools, Groups, MoEBlock, MoEConfig, Router, combine, combine_pairs, dispatch, group_routes,
-                  moe_block, moe_experts, moe_experts_routes, moe_prefill, read_status, router, topk)
+                  moe_block, moe_experts, moe_experts_routes, moe_prefill, read_status, rmsnorm, router, topk)
+from .stack import MoEStack
 
-__all__ = ["LIB_PATH", "MimoError", "lib", "ExpertPools", "Groups", "MoEBlock", "MoEConfig", "Router",
+__all__ = ["LIB_PATH", "MimoError", "lib", "ExpertPools", "Groups", "MoEBlock", "MoEConfig", "MoEStack", "Router",
            "combine", "combine_pairs", "dispatch", "group_routes", "moe_block", "moe_experts", "moe_experts_routes",
-           "moe_prefill", "read_status", "router", "topk"]
+           "moe_prefill", "read_status", "rmsnorm", "router", "topk"]

@@ -5,7 +5,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_int32, c_size_t, c_uint64, c_void_p
+from ctypes import POINTER, c_float, c_int32, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(os.environ.get("MIMO_MOE_LIBRARY") or Path(__file__).resolve().with_name("libmimo_moe.so"))
@@ -52,6 +52,7 @@ SIGNATURES = {
     "mimo_moe_route_scatter": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                          c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mimo_moe_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
+    "mimo_moe_rmsnorm": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     "mimo_moe_combine_pairs": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
                                          c_void_p]),
     "mimo_moe_prefill": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_int32, c_void_p, c_void_p,

@@ -182,19 +182,26 @@ class PeerExpertParallelMoE:
                    "peer_barrier")
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return self.layer(x, self.pools, self.router_w, self.bias)
+
+    def layer(self, x: torch.Tensor, pools, router_w: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+        """One step with another layer's weights (same shapes) through this object's exchange buffers:
+        a stack of layers shares one set of peer buffers.  bias: float32 [E] or None."""
         if tuple(x.shape) != (self.T, self.H):
             raise ValueError(f"x must be [{self.T}, {self.H}]")
+        if pools.S != self.pools.S or router_w.shape != self.router_w.shape:
+            raise ValueError("layer shapes differ from the exchange's")
         x = x.to(torch.bfloat16).contiguous()
         st = torch.cuda.current_stream(self.dev).cuda_stream
         T, k, H, N = self.T, self.k, self.H, self.world
         self.check(self.L.mimo_moe_route_scatter(
-            x.data_ptr(), T, H, self.router_w.data_ptr(), None if self.bias is None else self.bias.data_ptr(),
+            x.data_ptr(), T, H, router_w.data_ptr(), None if bias is None else bias.data_ptr(),
             self.E, k, self.tab["rows"].data_ptr(), self.ld, self.rank, N, self.logits.data_ptr(), st),
             "route_scatter")
         self._barrier(st)
         rows = self.local["rows"]
         self.check(self.L.mimo_moe_experts_routes(
-            rows, 2 * self.ld, N * T, self.pools.struct, self.expert_base, rows + 2 * H,
+            rows, 2 * self.ld, N * T, pools.struct, self.expert_base, rows + 2 * H,
             rows + 2 * H + 4 * k, self.ld, k, int(pairs_rounding_for(T)), None, self.tab["recv"].data_ptr(),
             T * k, self.ws.data_ptr(), self.ws.numel(), self.status.data_ptr(), st), "experts_routes")
         self._barrier(st)

@@ -359,6 +359,19 @@ def combine(part: torch.Tensor, M: int, k: int = TOPK, gather_idx: Optional[torc
     return y
 
 
+def rmsnorm(x: torch.Tensor, weight: Optional[torch.Tensor] = None, eps: float = 1e-6,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """model.py:75 (`post_attention_layernorm`, the norm in front of each MoE block):
+    y = bf16(x * rsqrt(mean(x^2) + eps)) [* weight], per row, float32 math."""
+    _need_cuda(x, "x")
+    x = x.to(torch.bfloat16).contiguous()
+    T, H = x.shape
+    w = None if weight is None else weight.to(device=x.device, dtype=torch.bfloat16).contiguous()
+    y = out if out is not None else torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    check(lib().mimo_moe_rmsnorm(x.data_ptr(), _ptr(w), T, H, float(eps), y.data_ptr(), _stream()), "rmsnorm")
+    return y
+
+
 def combine_pairs(ypair: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, T: int, k: int = TOPK,
                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """model.py:266-271: y[t] = bf16(sum over j in order of fp32(ypair[inv[t*k + j]]) * w[t, j])."""

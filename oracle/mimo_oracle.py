@@ -353,3 +353,30 @@ def moe_block(x, W, bias, pool: Pool, R: int = R):
     """Router + reference dispatch rule, end to end."""
     logits, inds, w = router(x, W, bias)
     return logits, inds, w, moe_layer(x, pool, inds, w, R)
+
+
+def rmsnorm(x, weight=None, eps: float = 1e-6) -> np.ndarray:
+    """model.py:75 (`nn.RMSNorm`, MLX fast.rms_norm): y = bf16(x * rsqrt(mean(x^2) + eps)) [* weight].
+    Sum of squares exact in float64, rounded to float32; mean, +eps and rsqrt each rounded to float32
+    (MLX's own float32 reduction order is parity unpinned at the ulp level)."""
+    x32 = np.asarray(x, np.float32)
+    ss = np.float32(np.sum(x32.astype(np.float64) ** 2, axis=-1))
+    ms = np.float32(ss / np.float32(x32.shape[-1]))
+    inv = np.float32(1.0 / np.sqrt(np.float64(np.float32(ms + np.float32(eps)))))
+    y = bf16_round(x32 * inv[..., None])
+    if weight is not None:
+        y = bf16_round(np.asarray(weight, np.float32) * y)
+    return y
+
+
+def moe_stack(x, layers, eps: float = 1e-6, R: int = R):
+    """BASELINE config 3's decode stack: x_{l+1} = rmsnorm(moe_block_l(x_l)) between layers, unit weight;
+    returns the last layer's MoE output and every layer's routes.  layers: [(W, bias, Pool), ...]."""
+    routes = []
+    y = None
+    for li, (W, bias, pool) in enumerate(layers):
+        if li:
+            x = rmsnorm(y, None, eps)
+        _, inds, w, y = moe_block(x, W, bias, pool, R)
+        routes.append(inds)
+    return y, routes

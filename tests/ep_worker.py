@@ -7,7 +7,8 @@ runs the expert-parallel block (mimo_moe/ep.py, NCCL).  Each rank then runs the 
 the same tokens with the whole layer resident and the outputs must be identical bit for bit, for
 T = 1 (stock-path rounding), 8 (decode) and 12 (prefill rounding) through the NCCL all-gather block,
 T = 1 and 8 through the peer-memory block (eager and graphed), and T = 64 and 600 through the
-all-to-all prefill block.  Prints one JSON line per rank."""
+all-to-all prefill block, and a 3-layer decode stack over the peer exchange at T = 1 and 8 against
+the single-GPU stack.  Prints one JSON line per rank."""
 import json
 import os
 import sys
@@ -67,6 +68,31 @@ def main() -> int:
             ok &= res[f"peer_T{T}_status"] == 0
             del g
             peer.close()
+        # a 3-layer decode stack (RMSNorm between layers): one peer exchange serves every layer
+        from mimo_moe.stack import MoEStack
+        lay_full, lay_shard = [], []
+        for l in range(3):
+            Wl = synth.router_weight(seed=1 + 1000 * l).to(dev)
+            lay_full.append((Wl, None, mimo_moe.ExpertPools.synthetic(256, seed=0, layer=10 + l, device=dev)))
+            lay_shard.append((Wl, None, mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=10 + l,
+                                                                        first_expert=lo, device=dev)))
+        single = MoEStack(lay_full)
+        for T in (1, 8):
+            ex = PeerExpertParallelMoE(lay_shard[0][2], lay_shard[0][0], None, T)
+            st = MoEStack(lay_shard, layer_fn=lambda x, l, ex=ex: ex.layer(x, lay_shard[l][2], lay_shard[l][0], None))
+            g = GraphedStep(st, T, 4096, dev)
+            for rep in range(2):
+                x = synth.hidden(T, seed=1300 + 31 * rank + 7 * rep + T).to(dev)
+                y_1 = single(x).clone()
+                y_g = g(x).clone()
+                torch.cuda.synchronize()
+                same = bool(torch.equal(y_g.view(torch.int16), y_1.view(torch.int16)))
+                res[f"stack3_T{T}_rep{rep}_bit_identical"] = same
+                ok &= same
+            ok &= int(ex.status.item()) == 0
+            del g
+            ex.close()
+        del lay_full, lay_shard, single
         # prefill sizes: each route travels to its expert's rank and back (NCCL all-to-all)
         pre = ExpertParallelPrefill(shard, W, bias)
         for T in (64, 600):

@@ -143,3 +143,28 @@ def test_kernel_math_accuracy_and_negative_control():
     inds = np.stack([rng.choice(S, 8, replace=False) for _ in range(4)])
     sc = np.full((4, 8), 1 / 8, np.float32)
     assert O.rel_err(O.moe_layer(x, bad, inds, sc), O.reference_fp32(x, pool, inds, sc)) > 0.5
+
+
+def test_package_input_generators_match_the_oracle_fixtures():
+    """bench.py draws its inputs from mimo_moe.synthetic; the oracle's generators (which the parity
+    tests and golden fixtures use) must give the same tensors bit for bit."""
+    import torch
+    from mimo_moe import synthetic
+    assert torch.equal(synthetic.hidden(5, seed=1234).view(torch.int16), synth.hidden(5, seed=1234).view(torch.int16))
+    assert torch.equal(synthetic.router_weight(E=64).view(torch.int16), synth.router_weight(E=64).view(torch.int16))
+    for c in (1.0, 0.055):
+        assert torch.equal(synthetic.zipf_bias(c=c), synth.zipf_bias(c=c))
+    assert torch.equal(synthetic.overlap_bias(), synth.overlap_bias())
+
+
+def test_rmsnorm_oracle_properties():
+    """Unit RMS after the norm, invariance under power-of-two scaling (eps 0: every step scales
+    exactly), the weight as a bf16 multiply of the normalised row, zero rows stay zero."""
+    rng = np.random.default_rng(4)
+    x = O.bf16_round(rng.standard_normal((6, 4096)).astype(np.float32))
+    y = O.rmsnorm(x)
+    assert np.allclose(np.sqrt((y.astype(np.float64) ** 2).mean(-1)), 1.0, atol=4e-3)
+    assert np.array_equal(O.rmsnorm(x, eps=0.0), O.rmsnorm(x * np.float32(64), eps=0.0))
+    w = O.bf16_round(rng.standard_normal(4096).astype(np.float32))
+    assert np.array_equal(O.rmsnorm(x, w), O.bf16_round(w * y))
+    assert np.array_equal(O.rmsnorm(np.zeros((1, 64), np.float32)), np.zeros((1, 64), np.float32))
