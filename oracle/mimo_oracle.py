@@ -360,9 +360,10 @@ def rmsnorm(x, weight=None, eps: float = 1e-6) -> np.ndarray:
     Sum of squares exact in float64, rounded to float32; mean, +eps and rsqrt each rounded to float32
     (MLX's own float32 reduction order is parity unpinned at the ulp level)."""
     x32 = np.asarray(x, np.float32)
-    ss = np.float32(np.sum(x32.astype(np.float64) ** 2, axis=-1))
-    ms = np.float32(ss / np.float32(x32.shape[-1]))
-    inv = np.float32(1.0 / np.sqrt(np.float64(np.float32(ms + np.float32(eps)))))
+    ss = np.sum(x32.astype(np.float64) ** 2, axis=-1).astype(np.float32)
+    ms = (ss / np.float32(x32.shape[-1])).astype(np.float32)
+    v = (ms + np.float32(eps)).astype(np.float32)
+    inv = (1.0 / np.sqrt(v.astype(np.float64))).astype(np.float32)
     y = bf16_round(x32 * inv[..., None])
     if weight is not None:
         y = bf16_round(np.asarray(weight, np.float32) * y)

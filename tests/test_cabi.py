@@ -65,6 +65,12 @@ def test_bad_arguments_return_einval_without_a_device():
                               None) == EINVAL                                  # E != S without slot_of
     assert L.mimo_moe_fill_synthetic_pool(None, None, None, None, None, None, 1, 4096, 2048, 0, 0, 0,
                                           None) == EINVAL
+    assert L.mimo_moe_rmsnorm(None, None, 1, 4096, 1e-6, None, None) == EINVAL
+    assert L.mimo_moe_rmsnorm(256, None, 1, 12, 1e-6, 256, None) == EINVAL       # H % 8
+    assert L.mimo_moe_rmsnorm(264, None, 1, 4096, 1e-6, 256, None) == EINVAL     # x not 16-byte aligned
+    assert L.mimo_moe_rmsnorm(256, None, 1, 4096, -1.0, 256, None) == EINVAL     # eps < 0
+    assert L.mimo_moe_combine_pairs(None, None, None, 1, 8, 4096, None, None) == EINVAL
+    assert L.mimo_moe_combine_pairs(256, 256, 256, 1, 9, 4096, 256, None) == EINVAL  # topk > 8
 
 
 def test_ops_refuse_cpu_tensors():

@@ -54,7 +54,7 @@ def test_rmsnorm_weight_and_in_place(gpu):
 
 def test_rmsnorm_rejects_bad_shapes(gpu):
     import mimo_moe
-    with pytest.raises(mimo_moe.MimoError):
+    with pytest.raises(ValueError):          # MIMO_EINVAL, raised as the reference raises shape errors
         mimo_moe.rmsnorm(torch.zeros(2, 12, dtype=torch.bfloat16, device=gpu))
 
 
