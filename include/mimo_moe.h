@@ -37,6 +37,7 @@ enum mimo_moe_error {
   MIMO_ERANGE = 2,    /* expert id outside [0,E), more than R rows on one expert, activation overflow */
   MIMO_ETIMEOUT = 3,  /* a bounded device-side wait expired; the kernel returned without the result */
   MIMO_ECUDA = 4,     /* CUDA launch / runtime error (see mimo_moe_last_cuda_error) */
+  MIMO_EIO = 5,       /* file open / read failure or short read (expert-file loader) */
 };
 
 /* Expert pool of one MoE layer (device pointers, reference layout above). */
@@ -183,6 +184,23 @@ int mimo_moe_combine_pairs(const uint16_t* ypair, const int32_t* inv, const floa
  * null.  x, y bf16 [T, H], 16-byte aligned, H a multiple of 8; x == y is allowed. */
 int mimo_moe_rmsnorm(const uint16_t* x, const uint16_t* weight, int32_t T, int32_t H, float eps, uint16_t* y,
                      void* stream);
+/* Expert-file loader.  One contiguous byte range of a file and where it goes. */
+typedef struct mimo_moe_file_span {
+  int64_t file_offset;
+  int64_t nbytes;
+  void* dst; /* device memory (dst_host == 0) or host memory */
+} mimo_moe_file_span;
+
+/* Copies the spans of one file (a converted experts-LNN.safetensors: expert e of a projection at
+ * base + e * stride, 16 KiB aligned; scripts/convert-mimo-v26-mlx.py:92-131) to their destinations.
+ * Replaces the reference's SSD streaming (engine/mimo_stream/store.py:14-82: ExpertStore.jobs +
+ * IOPool.run, a preadv thread pool into GPU-visible slot memory).  `threads` reader threads pread in
+ * chunks of `chunk_bytes` (a multiple of 4096) into pinned staging buffers and copy them on their own
+ * streams, ordered after the work already queued on `stream`; O_DIRECT for 4 KiB-aligned chunks when
+ * `direct` is set.  With dst_host the reads go straight into host memory (no CUDA calls).  Blocks
+ * until every byte has landed.  Returns MIMO_EIO when the file cannot be opened or is too short. */
+int mimo_moe_read_file_spans(const char* path, const mimo_moe_file_span* spans, int32_t n, int32_t threads,
+                             int64_t chunk_bytes, int32_t direct, int32_t dst_host, void* stream);
 int mimo_moe_peer_alloc(size_t bytes, void** ptr, void* handle);
 int mimo_moe_peer_open(const void* handle, void** ptr);
 int mimo_moe_peer_close(void* ptr);

@@ -464,6 +464,7 @@ const char* mimo_moe_strerror(int code) {
     case MIMO_ERANGE: return "value out of range (expert id, rows per expert, or activation beyond f16)";
     case MIMO_ETIMEOUT: return "bounded device wait expired";
     case MIMO_ECUDA: return "CUDA error";
+    case MIMO_EIO: return "file open or read failed (or the file is shorter than the spans)";
     default: return "unknown error";
   }
 }

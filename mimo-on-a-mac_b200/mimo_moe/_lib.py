@@ -10,7 +10,7 @@ from pathlib import Path
 
 LIB_PATH = Path(os.environ.get("MIMO_MOE_LIBRARY") or Path(__file__).resolve().with_name("libmimo_moe.so"))
 
-MIMO_OK, MIMO_EINVAL, MIMO_ERANGE, MIMO_ETIMEOUT, MIMO_ECUDA = 0, 1, 2, 3, 4
+MIMO_OK, MIMO_EINVAL, MIMO_ERANGE, MIMO_ETIMEOUT, MIMO_ECUDA, MIMO_EIO = 0, 1, 2, 3, 4, 5
 
 
 class Pools(ctypes.Structure):
@@ -52,6 +52,8 @@ SIGNATURES = {
     "mimo_moe_route_scatter": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                          c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mimo_moe_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
+    "mimo_moe_read_file_spans": (c_int32, [ctypes.c_char_p, c_void_p, c_int32, c_int32, ctypes.c_int64, c_int32,
+                                           c_int32, c_void_p]),
     "mimo_moe_rmsnorm": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     "mimo_moe_combine_pairs": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
                                          c_void_p]),

@@ -10,7 +10,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 INCLUDE = PKG.parent.parent / "include"
 LIB = PKG / "libmimo_moe.so"
-SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "synth.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu", "norm.cu"]
+SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "synth.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu", "norm.cu", "loader.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -60,7 +60,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if not ok:
         raise RuntimeError("nvcc failed")
     tmp = LIB.with_suffix(".so.tmp")
-    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(tmp)] + [str(o) for o in objs], check=True)
+    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ["-lpthread"], check=True)
     os.replace(tmp, LIB)
     return LIB
 

@@ -71,6 +71,10 @@ def test_bad_arguments_return_einval_without_a_device():
     assert L.mimo_moe_rmsnorm(256, None, 1, 4096, -1.0, 256, None) == EINVAL     # eps < 0
     assert L.mimo_moe_combine_pairs(None, None, None, 1, 8, 4096, None, None) == EINVAL
     assert L.mimo_moe_combine_pairs(256, 256, 256, 1, 9, 4096, 256, None) == EINVAL  # topk > 8
+    assert L.mimo_moe_read_file_spans(None, None, 0, 1, 4096, 0, 1, None) == EINVAL     # no path
+    assert L.mimo_moe_read_file_spans(b"/dev/null", None, 0, 0, 4096, 0, 1, None) == EINVAL  # 0 threads
+    assert L.mimo_moe_read_file_spans(b"/dev/null", None, 0, 1, 5000, 0, 1, None) == EINVAL  # chunk % 4096
+    assert L.mimo_moe_read_file_spans(b"/dev/null", None, 0, 1, 4096, 0, 1, None) == 0       # nothing to read
 
 
 def test_ops_refuse_cpu_tensors():
