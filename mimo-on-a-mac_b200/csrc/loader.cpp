@@ -4,10 +4,10 @@
 // into unified memory (engine/mimo_stream/store.py:14-82: ExpertStore.jobs gives (fd, offset, view)
 // per slot tensor, IOPool runs them, F_NOCACHE and read-ahead off).  Here the HBM pools are filled
 // once at load time, so the reader is a bulk copier: reader threads pread the ranges in chunks into
-// pinned staging buffers (two per thread, so one chunk's host->device copy overlaps the next read),
-// each thread copying on its own stream.  O_DIRECT is used for chunks whose offset and size are
-// multiples of 4 KiB (every expert slice of a converted file is 16 KiB aligned), buffered reads for
-// the rest or when the filesystem refuses O_DIRECT.
+// pinned staging buffers (two per thread, so one chunk's host->device copy overlaps the next read;
+// the buffers are kept for the next call), each thread copying on its own stream.  O_DIRECT is used
+// for chunks whose offset and size are multiples of 4 KiB (every expert slice of a converted file is
+// 16 KiB aligned), buffered reads for the rest or when the filesystem refuses O_DIRECT.
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <unistd.h>
@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cerrno>
 #include <cstdint>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -47,6 +48,49 @@ int64_t read_full(int fd, char* buf, int64_t n, int64_t off) {
 
 bool direct_ok(const Chunk& c, const char* buf) {
   return c.off % kDirectAlign == 0 && c.n % kDirectAlign == 0 && ((uintptr_t)buf % kDirectAlign) == 0;
+}
+
+// Pinned staging buffers outlive a call (allocating pinned memory costs more than reading a layer
+// from the page cache): a process-wide free list of buffers of one size, refilled on demand.
+struct StagingPool {
+  std::mutex mu;
+  int64_t bytes = 0;
+  std::vector<char*> free_list;
+
+  char* take(int64_t n) {
+    {
+      std::lock_guard<std::mutex> g(mu);
+      if (n != bytes) {  // a new chunk size: drop the old buffers (none are in use between calls)
+        for (char* b : free_list) cudaFreeHost(b);
+        free_list.clear();
+        bytes = n;
+      }
+      if (!free_list.empty()) {
+        char* b = free_list.back();
+        free_list.pop_back();
+        return b;
+      }
+    }
+    char* b = nullptr;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&b), (size_t)n, cudaHostAllocDefault) != cudaSuccess) return nullptr;
+    return b;
+  }
+  void give(char* b, int64_t n) {
+    std::lock_guard<std::mutex> g(mu);
+    if (n == bytes && free_list.size() < 64) free_list.push_back(b);
+    else cudaFreeHost(b);
+  }
+};
+
+StagingPool& staging() {
+  static StagingPool* pool = new StagingPool();  // never destroyed: no CUDA calls at process exit
+  return *pool;
+}
+
+// One call at a time per process shares the pool's chunk size.
+std::mutex& read_call_mutex() {
+  static std::mutex m;
+  return m;
 }
 
 }  // namespace
@@ -93,6 +137,7 @@ extern "C" int mimo_moe_read_file_spans(const char* path, const mimo_moe_file_sp
     return err.load();
   }
 
+  std::lock_guard<std::mutex> serial(read_call_mutex());
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     close(fd_buf);
@@ -116,8 +161,7 @@ extern "C" int mimo_moe_read_file_spans(const char* path, const mimo_moe_file_sp
     bool ok = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess &&
               cudaStreamWaitEvent(st, entry, 0) == cudaSuccess;
     for (int b = 0; b < 2 && ok; ++b)
-      ok = cudaHostAlloc(reinterpret_cast<void**>(&buf[b]), (size_t)chunk_bytes, cudaHostAllocDefault) ==
-               cudaSuccess &&
+      ok = (buf[b] = staging().take(chunk_bytes)) != nullptr &&
            cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming) == cudaSuccess;
     if (!ok) fail(MIMO_ECUDA);
     int b = 0;
@@ -147,7 +191,7 @@ extern "C" int mimo_moe_read_file_spans(const char* path, const mimo_moe_file_sp
     if (st && cudaStreamSynchronize(st) != cudaSuccess) fail(MIMO_ECUDA);
     for (int k = 0; k < 2; ++k) {
       if (done[k]) cudaEventDestroy(done[k]);
-      if (buf[k]) cudaFreeHost(buf[k]);
+      if (buf[k]) staging().give(buf[k], chunk_bytes);  // its copy completed: the stream was synchronised
     }
     if (st) cudaStreamDestroy(st);
   };
