@@ -272,7 +272,7 @@ def bench_stack(args):
     for i in range(nprof):
         stack(xs[i % NBATCH])
     torch.cuda.synchronize()
-    launches = (np.zeros(4, np.int32), np.zeros(4, np.float32))
+    launches = (np.zeros(8, np.int32), np.zeros(8, np.float32))
     _lib.check(L_.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
     _lib.check(L_.mimo_moe_profile_enable(0), "profile_disable")
     stack.on_layer = on_layer
@@ -284,10 +284,12 @@ def bench_stack(args):
     if st_val != 0:
         raise RuntimeError(f"device status {st_val} during the bench")
     hbm, _, peak_kind = peaks()
+    fused = int(launches[0][4]) > 0
     gu_ms = float(launches[1][0]) / max(1, int(launches[0][0]))
     dn_ms = float(launches[1][1]) / max(1, int(launches[0][1]))
-    gu_bytes = statistics.mean(U_local) * GATEUP_BYTES
-    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    fz_ms = float(launches[1][4]) / max(1, int(launches[0][4]))
+    gu_bytes = statistics.mean(U_local) * (EXPERT_BYTES if fused else GATEUP_BYTES)
+    achieved = gu_bytes / ((fz_ms if fused else gu_ms) * 1e-3) / 1e9
     step_U = sum(U) / NBATCH                       # distinct experts summed over the L layers, per step
     expert_gbs = step_U * EXPERT_BYTES * args.steps / (ms * 1e-3) / 1e9
 
@@ -319,7 +321,7 @@ def bench_stack(args):
         # per layer: single GPU = route (+ memset), gate/up, down, combine; peer exchange = router
         # logits, route+scatter, 2 barriers, unit builder, term split, gate/up, down, combine; plus
         # one RMSNorm between layers
-        per_layer = 8 if world > 1 else 4
+        per_layer = (8 if world > 1 else 4) - (1 if fused else 0)
         out = {
             "metric": f"MoE-stack tok/s ({args.workload}, {L} layers)", "value": tok / (ms * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -337,10 +339,12 @@ def bench_stack(args):
                        "l2": f"inputs > L2: {L * (hi - lo) * EXPERT_BYTES / 1e9:.1f} GB of experts per GPU"},
             "expert_gbs": expert_gbs,
             "expert_frac_of_measured_hbm": expert_gbs / world / hbm,
-            "roofline": {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
+            "roofline": {"kernel": "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight)" if fused else
+                         "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
-                         "algorithmic_bytes_per_launch": gu_bytes, "kernel_ms": {"gate_up": gu_ms, "down": dn_ms}},
+                         "algorithmic_bytes_per_launch": gu_bytes,
+                         "kernel_ms": {"fused": fz_ms} if fused else {"gate_up": gu_ms, "down": dn_ms}},
             "clocks": clk,
             "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2,
                     "d2h_bytes_per_step": B * H * 2},
@@ -470,7 +474,7 @@ def main():
     # routes this rank's expert kernels computed per step (expert-parallel prefill: skewed routing
     # gives the ranks unequal shares; otherwise each rank computes its own B * k routes)
     routes_step = blk.routes_received / args.steps if ep and not peer else B * K_TOP
-    launches = (np.zeros(4, np.int32), np.zeros(4, np.float32))
+    launches = (np.zeros(8, np.int32), np.zeros(8, np.float32))
     _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
     if gstep is not None:  # graph replays carry no profiling events: time the kernels in an eager pass
         nprof = min(args.steps, 50)
@@ -510,9 +514,17 @@ def main():
     kind_gu, kind_dn = (0, 1) if B <= 8 else (2, 3)
     gu_ms = float(launches[1][kind_gu]) / max(1, int(launches[0][kind_gu]))
     dn_ms = float(launches[1][kind_dn]) / max(1, int(launches[0][kind_dn]))
+    fz_ms = float(launches[1][4]) / max(1, int(launches[0][4]))
     gu_bytes = statistics.mean(steps_Ul) * GATEUP_BYTES
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
-    if B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
+    if B <= 8 and launches[0][4] > 0:  # decode, one launch streams every distinct expert's 3 matrices once
+        fz_bytes = statistics.mean(steps_Ul) * EXPERT_BYTES
+        fz_gbs = fz_bytes / (fz_ms * 1e-3) / 1e9
+        roofline = {"kernel": "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight, one launch)",
+                    "bound": "hbm", "achieved": fz_gbs, "peak": hbm, "unit": "GB/s", "frac": fz_gbs / hbm,
+                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
+                    "algorithmic_bytes_per_launch": fz_bytes}
+    elif B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
         roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                     "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
@@ -526,7 +538,7 @@ def main():
                                  "run at the fp8 rate, nominally 2x)",
                     "traffic": None, "algorithmic_flops_per_launch": flops,
                     "weight_gbs": gu_bytes / (gu_ms * 1e-3) / 1e9}
-    roofline["kernel_ms"] = {"gate_up": gu_ms, "down": dn_ms}
+    roofline["kernel_ms"] = {"fused": fz_ms} if launches[0][4] > 0 else {"gate_up": gu_ms, "down": dn_ms}
     expert_gbs = sum(steps_U) * EXPERT_BYTES / (ms * 1e-3) / 1e9
 
     # end to end through the public API: pinned host x -> device, block, y -> pinned host
@@ -556,14 +568,16 @@ def main():
 
     if rank == 0:
         tok = B * args.steps * world
-        # our kernels per step: decode = route (+ its counter memset, not counted), gate/up, down,
-        # combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
-        # down, combine
+        # our kernels per step: decode = route (+ its counter memsets, not counted), gate/up + down
+        # (one fused launch, or two), combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit
+        # builders, term split, gate/up, down, combine
         # expert parallelism, peer exchange: router logits, route+scatter, 2 barriers, unit builder, term
         # split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch, 2 unit
         # builders, term split, gate/up, down, per-route combine, weighted combine (the collectives and
         # the route sort / gathers are library kernels)
-        launches_per_step = (8 if peer else 12) if ep else (4 if B <= 8 else 11)
+        fused = int(launches[0][4]) > 0  # decode gate/up + down as one launch
+        launches_per_step = ((7 if fused else 8) if peer else 12) if ep else \
+            ((3 if fused else 4) if B <= 8 else 11)
         out = {
             "metric": f"MoE-layer tok/s ({args.workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,

@@ -243,9 +243,11 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
  * the library record a CUDA event pair around each of the next n expert-tile kernel launches on the
  * launching stream (the events are created here, once); n = 0 turns it off.  mimo_moe_profile_read()
  * synchronises those events and returns, per kernel kind (0 decode gate/up, 1 decode down, 2 prefill
- * gate/up, 3 prefill down), the launch count and the summed device milliseconds, then resets.
+ * gate/up, 3 prefill down, 4 decode gate/up + down in one launch; MIMO_MOE_PROFILE_KINDS entries in
+ * each array), the launch count and the summed device milliseconds, then resets.
  * Off by default; do not enable it while a stream is being captured.
  */
+#define MIMO_MOE_PROFILE_KINDS 8
 int mimo_moe_profile_enable(int32_t capacity);
 int mimo_moe_profile_read(int32_t* launches, float* milliseconds);
 

@@ -93,6 +93,7 @@ bool pools_ok(const mimo_moe_pools* p) {
 // Term matrices of the tcgen05 path: per unit 2 * routes rows of e4m3 terms + ue8m0 block scales.
 struct TermWs {
   uint8_t *bq, *bs, *hq, *hs;
+  int32_t* ready;  // fused decode: per-unit count of gate/up epilogue warps done
 };
 TermWs carve_terms(Carver& c, int units, int routes, int H, int I) {
   const size_t rows = (size_t)units * 2 * routes;
@@ -101,6 +102,7 @@ TermWs carve_terms(Carver& c, int units, int routes, int H, int I) {
   t.bs = c.take<uint8_t>(rows * (H / 32));
   t.hq = c.take<uint8_t>(rows * I);
   t.hs = c.take<uint8_t>(rows * (I / 32));
+  t.ready = c.take<int32_t>((size_t)units);
   return t;
 }
 
@@ -236,6 +238,15 @@ bool tc_path(const mimo_moe_pools* pools) {
          al(pools->gate_s, 16) && al(pools->up_s, 16) && al(pools->down_s, 16);
 }
 
+// MIMO_MOE_DECODE_FUSED=0 runs the decode passes as two launches (a comparison knob; same results).
+bool decode_fused() {
+  static const bool on = [] {
+    const char* e = getenv("MIMO_MOE_DECODE_FUSED");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
 // Gate/up + SwiGLU and down over units of up to `routes` routes, on the tensor cores.
 // Decode (routes 8): unit u's routes start at u * R, B rows come from rtok = urows, the down pass
 // writes part = dot * weight.  Prefill (routes 32): units from build_units, down writes ypair.
@@ -280,7 +291,8 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.hq = t.hq;
   p.hs = t.hs;
   p.status = status;
-  MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
+  const bool fused = decode && decode_fused();
+  if (!fused) MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
   TcParams q = p;  // down: two K chunks per stage through 3-D boxes
   MIMO_TRY(fp4_weight_map3(&q.amap[0], pools->down_w, (uint64_t)S * H, I, 2));
   q.amap[1] = q.amap[0];
@@ -301,6 +313,12 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   q.peer_rows = peer_rows;
   q.ypair = ypair;
   q.pairs_rounding = pairs_rounding;
+  if (fused) {  // both passes in one launch; the down tiles wait on per-unit counters
+    MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)ucap * sizeof(int32_t), st));
+    const TcFusedParams f{p, q, t.ready};
+    MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, sms, st); }));
+    return MIMO_OK;
+  }
   MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
   return MIMO_OK;
 }
@@ -760,7 +778,7 @@ int mimo_moe_profile_enable(int32_t capacity) {
 int mimo_moe_profile_read(int32_t* launches, float* milliseconds) {
   if (!launches || !milliseconds) return MIMO_EINVAL;
   std::lock_guard<std::mutex> lk(g_prof_mu);
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < MIMO_MOE_PROFILE_KINDS; ++k) {
     launches[k] = 0;
     milliseconds[k] = 0.f;
   }

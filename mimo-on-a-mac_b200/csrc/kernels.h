@@ -91,6 +91,13 @@ struct TcParams {
   int pairs_rounding;
   int32_t* status;
 };
+// Both decode passes in one launch (tc_experts.cu): gate/up params (kind 0 layout) and down params
+// (kind 1 layout) over the same units; ready: [units_cap] zeroed counters.
+struct TcFusedParams {
+  TcParams gu, dn;
+  int32_t* ready;
+};
+cudaError_t launch_tc_decode_fused(const TcFusedParams& f, int num_sms, cudaStream_t st);
 // kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (64 routes per
 // unit), 3: prefill down.
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);

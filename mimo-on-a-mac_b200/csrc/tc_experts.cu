@@ -61,6 +61,9 @@ constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment 
 #ifndef MIMO_TC_ST3
 #define MIMO_TC_ST3 3
 #endif
+#ifndef MIMO_TC_STF
+#define MIMO_TC_STF 5  // ring depth of the fused decode kernel
+#endif
 #ifndef MIMO_TC_WEIGHT_EVICT_FIRST
 #define MIMO_TC_WEIGHT_EVICT_FIRST 1  // decode streams each weight once: L2 evict-first
 #endif
@@ -542,6 +545,456 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   }
 }
 
+// ------------------------------------------------------------------- fused decode (gate/up -> down)
+// One persistent launch runs both passes of a decode call.  Work items: the gate/up tiles (unit,
+// 128 rows of I; 2 matrices x K = H) and the down tiles (unit, 128 rows of H; K = I).  CTA c takes
+// its gate/up tiles c, c + G, ... first, then its down tiles; the down tiles are dealt from the CTA
+// after the last one that got an extra gate/up tile, so the CTAs with less gate/up work start down
+// work first.  A down tile needs the unit's whole h: every gate/up epilogue warp adds 1 to
+// ready[unit] after its h stores (8 warps x I/128 tiles per unit), and the producer waits for that
+// count (acquire, bounded) before loading the unit's h terms.  Each CTA finishes issuing its gate/up
+// tiles before it waits on any unit, and the grid is one CTA per SM (all resident), so every wait
+// ends; a wait that outlasts the limit sets MIMO_ETIMEOUT and the CTA drains and returns.
+// Compared with two launches: one launch ramp instead of two, and down weights stream while other
+// CTAs finish their gate/up tiles.
+namespace fz {
+constexpr int kN = 2 * kTcDecodeRoutes;                   // MMA N: 8 routes x (hi, lo)
+constexpr int kSB = 2 * kATile + 2 * kN * kKC;            // stage: 2 A tiles + up to 2 B tiles
+constexpr int kSCB = 2 * kM * 16 + kN * 16;               // scale boxes of one 4-chunk group
+constexpr int kSFB = 4 * 512;                              // scale blocks of one stage
+template <int NSTAGE>
+constexpr int smem_bytes() { return kBarBytes + 1024 + NSTAGE * kSB + 2 * kSCB + NSTAGE * kSFB; }
+
+struct Sched {
+  int tiles_gu, tiles_dn, ns_gu, ns_dn;  // tiles per unit; stages per item
+  long long my_gu, my_dn, cdn;           // this CTA's item counts; its first down item
+  __device__ __forceinline__ long long items() const { return my_gu + my_dn; }
+  // item n of this CTA -> (down?, unit, tile)
+  __device__ __forceinline__ void at(long long n, bool& dn, int& unit, int& tile) const {
+    if (n < my_gu) {
+      const long long i = blockIdx.x + n * gridDim.x;
+      dn = false;
+      unit = (int)(i / tiles_gu);
+      tile = (int)(i % tiles_gu);
+    } else {
+      const long long j = cdn + (n - my_gu) * gridDim.x;
+      dn = true;
+      unit = (int)(j / tiles_dn);
+      tile = (int)(j % tiles_dn);
+    }
+  }
+};
+
+__device__ __forceinline__ Sched schedule(const TcParams& gu, const TcParams& dn, int units) {
+  Sched s;
+  s.tiles_gu = gu.tiles;
+  s.tiles_dn = dn.tiles;
+  s.ns_gu = gu.K / kKC;
+  s.ns_dn = dn.K / (2 * kKC);
+  const long long G = gridDim.x, c = blockIdx.x;
+  const long long n_gu = (long long)units * gu.tiles, n_dn = (long long)units * dn.tiles;
+  s.my_gu = n_gu > c ? (n_gu - c + G - 1) / G : 0;
+  s.cdn = (c - n_gu % G + G) % G;
+  s.my_dn = n_dn > s.cdn ? (n_dn - s.cdn + G - 1) / G : 0;
+  return s;
+}
+
+__device__ __forceinline__ int ld_acquire(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
+}
+}  // namespace fz
+
+template <int NSTAGE>
+__global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __grid_constant__ TcFusedParams f) {
+  constexpr int NTOK = kTcDecodeRoutes, N = fz::kN;
+  constexpr int SB = fz::kSB, SCB = fz::kSCB, SFB = fz::kSFB;
+  constexpr uint32_t TCOLS = tmem_cols<N, NSTAGE>();
+  constexpr int ABUF = abuf<N, NSTAGE>();
+  constexpr int QH = NTOK / 2, QC = QH;
+  static_assert(ABUF == 2, "double-buffered accumulators");
+  const TcParams& g = f.gu;
+  const TcParams& d = f.dn;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + NSTAGE;
+  uint64_t* sc_full = empty + NSTAGE;
+  uint64_t* sc_empty = sc_full + 2;
+  uint64_t* acc_full = sc_empty + 2;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + kBarBytes) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stages = base;
+  uint8_t* scbox = stages + NSTAGE * SB;
+  uint8_t* sfblk = scbox + 2 * SCB;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = g.num_units ? min(__ldg(g.num_units), g.units_cap) : g.units_cap;
+  const fz::Sched sch = fz::schedule(g, d, units);
+  const long long my_items = sch.items();
+  const int ready_target = kEpiWarps * g.tiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 2);
+      mbar_init(&empty[i], 2);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sc_full[b], 1);
+      mbar_init(&sc_empty[b], 1);
+      mbar_init(&acc_full[b], 2);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    mbar_init(drain, 2);
+    *s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 3) {
+    tmem_alloc(tmem_slot, TCOLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  constexpr uint32_t kSfCol0 = ABUF * 2 * N;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = MIMO_TC_WEIGHT_EVICT_FIRST ? l2_evict_first_policy() : l2_evict_normal_policy();
+      const uint64_t pol_b = l2_evict_normal_policy();
+      for (int m = 0; m < 2; ++m) {
+        tma_prefetch_map(&g.amap[m]);
+        tma_prefetch_map(&g.smap[m]);
+      }
+      tma_prefetch_map(&g.bmap);
+      tma_prefetch_map(&g.bsmap);
+      tma_prefetch_map(&d.amap[0]);
+      tma_prefetch_map(&d.smap[0]);
+      tma_prefetch_map(&d.bmap);
+      tma_prefetch_map(&d.bsmap);
+      int stage = 0;
+      uint32_t ph = 0;
+      long long issued = 0, groups = 0;
+      bool stop = false;
+      for (long long n = 0; n < my_items && !stop; ++n) {
+        bool dn;
+        int unit, tile;
+        sch.at(n, dn, unit, tile);
+        const TcParams& p = dn ? d : g;
+        int slot = __ldg(p.unit_slot + unit);
+        if (slot < 0 || slot >= p.S) {
+          set_status(p.status, MIMO_ERANGE);
+          slot = 0;
+        }
+        if (dn) {  // the unit's h must be complete: all its gate/up epilogue warps have signalled
+          bool ok = fz::ld_acquire(f.ready + unit) >= ready_target;
+          if (!ok) {
+            const uint64_t t0 = global_timer_ns();
+            while (!(ok = fz::ld_acquire(f.ready + unit) >= ready_target)) {
+              if (*s_abort || global_timer_ns() - t0 > 2000000000ull) break;
+              __nanosleep(64);
+            }
+          }
+          if (!ok) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            break;
+          }
+          fz::fence_proxy_async_global();  // h was written by generic stores; TMA reads it
+        }
+        const int NM = dn ? 1 : 2, KPS = dn ? 2 : 1;
+        const int ns = dn ? sch.ns_dn : sch.ns_gu;
+        const int row0 = slot * p.Nw + tile * kM;
+        const int brow = (!dn && p.btok) ? 0 : unit * N;
+        for (int ks = 0; ks < ns; ++ks) {
+          if (*s_abort) {
+            stop = true;
+            break;
+          }
+          const int kc = ks * KPS;
+          if ((kc & 3) == 0) {
+            const int e = (int)(groups & 1);
+            if (!mbar_wait(&sc_empty[e], (uint32_t)(((groups >> 1) & 1) ^ 1))) {
+              set_status(p.status, MIMO_ETIMEOUT);
+              *s_abort = 1;
+              stop = true;
+              break;
+            }
+            uint8_t* sc = scbox + e * SCB;
+            mbar_arrive_expect_tx(&sc_full[e], NM * kM * 16 + N * 16);
+            for (int m = 0; m < NM; ++m) tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0, &sc_full[e], pol_b);
+            tma_load_2d(sc + NM * kM * 16, &p.bsmap, kc * 4, brow, &sc_full[e], pol_b);
+            ++groups;
+          }
+          if (!mbar_wait(&empty[stage], ph ^ 1u)) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            stop = true;
+            break;
+          }
+          uint8_t* sb = stages + stage * SB;
+          mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * N * kKC);
+          if (!dn) {
+            tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol_a);
+            tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol_a);
+            tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+          } else {
+            tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol_a);
+            tma_load_3d(sb + 2 * kATile, &p.bmap, 0, brow, kc, &full[stage], pol_b);
+          }
+          ++issued;
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      bool ok = true;
+      for (long long k = 0; ok && k < (issued < NSTAGE ? issued : NSTAGE); ++k) {
+        const long long q = issued - 1 - k;
+        ok = mbar_wait(&full[(int)(q % NSTAGE)], (uint32_t)((q / NSTAGE) & 1));
+      }
+      for (long long k = 0; ok && k < (groups < 2 ? groups : 2); ++k) {
+        const long long q = groups - 1 - k;
+        ok = mbar_wait(&sc_full[(int)(q & 1)], (uint32_t)((q >> 1) & 1));
+      }
+      if (!ok) set_status(g.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------ scale-factor builder
+    int stage = 0;
+    uint32_t ph = 0;
+    uint32_t grp = 0;  // running 4-chunk group
+    bool stop = false;
+    for (long long n = 0; n < my_items && !stop; ++n) {
+      bool dn;
+      int unit, tile;
+      sch.at(n, dn, unit, tile);
+      const int NM = dn ? 1 : 2, KPS = dn ? 2 : 1;
+      const int ns = dn ? sch.ns_dn : sch.ns_gu;
+      for (int ks = 0; ks < ns; ++ks) {
+        if (*s_abort) {
+          stop = true;
+          break;
+        }
+        const int c = (ks * KPS) & 3;
+        const int e = (int)(grp & 1);
+        if (c == 0 && !mbar_wait(&sc_full[e], (grp >> 1) & 1)) {
+          if (lane == 0) set_status(g.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          stop = true;
+          break;
+        }
+        if (!mbar_wait(&empty[stage], ph ^ 1u)) {
+          if (lane == 0) set_status(g.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          stop = true;
+          break;
+        }
+        const uint8_t* sc = scbox + e * SCB;
+        uint8_t* blk = sfblk + stage * SFB;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int m = NM == 2 ? j : 0, cj = c + (KPS == 2 ? j : 0);
+          const uint8_t* box = sc + m * kM * 16 + cj * 4;
+          uint4 v;
+          v.x = *reinterpret_cast<const uint32_t*>(box + (lane + 0) * 16);
+          v.y = *reinterpret_cast<const uint32_t*>(box + (lane + 32) * 16);
+          v.z = *reinterpret_cast<const uint32_t*>(box + (lane + 64) * 16);
+          v.w = *reinterpret_cast<const uint32_t*>(box + (lane + 96) * 16);
+          *reinterpret_cast<uint4*>(blk + j * 512 + lane * 16) = v;
+        }
+        for (int j = 0; j < KPS; ++j) {
+          const uint8_t* box = sc + NM * kM * 16 + (c + j) * 4;
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int r = lane + 32 * q;
+            w[q] = r < N ? *reinterpret_cast<const uint32_t*>(box + r * 16) : 0x7F7F7F7Fu;
+          }
+          *reinterpret_cast<uint4*>(blk + (2 + j) * 512 + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full[stage]);
+          if (c + KPS == 4) mbar_arrive(&sc_empty[e]);
+        }
+        if (c + KPS == 4) ++grp;
+        if (++stage == NSTAGE) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------------------ MMA issuers
+    const int j = warp - 2;
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      bool aborted = false;
+      for (long long n = 0; n < my_items && !aborted; ++n) {
+        bool dn;
+        int unit, tile;
+        sch.at(n, dn, unit, tile);
+        const int KPS = dn ? 2 : 1;
+        const int ns = dn ? sch.ns_dn : sch.ns_gu;
+        const int buf = (int)(n & 1);
+        const uint32_t use = (uint32_t)((n >> 1) & 1);
+        if (!mbar_wait(&acc_empty[buf], use ^ 1u)) {
+          set_status(g.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dacc = tbase + (uint32_t)(2 * buf + j) * N;
+        for (int ks = 0; ks < ns; ++ks) {
+          if (!mbar_wait(&full[stage], ph)) {
+            set_status(g.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sb = smem_u32(stages + stage * SB);
+          const uint32_t blk = smem_u32(sfblk + stage * SFB);
+          const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * 16 + 8 * j;
+          const int bj = KPS == 2 ? j : 0;
+          tc_cp_sf(sf_col, desc_sf(blk + j * 512));
+          tc_cp_sf(sf_col + 4, desc_sf(blk + (2 + bj) * 512));
+          const uint32_t a0 = sb + j * kATile, b0 = sb + 2 * kATile + bj * N * kKC;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_mx(dacc, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc_mx(N, kk),
+                      sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30), (ks | kk) != 0);
+          tc_commit(&empty[stage]);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!aborted) tc_commit(&acc_full[buf]);
+      }
+      tc_commit(drain);
+      if (!mbar_wait(drain, 0)) set_status(g.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const int qlo = ((warp - 4) >> 2) * QH;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    bool aborted = false;
+    for (long long n = 0; n < my_items; ++n) {
+      bool dn;
+      int unit, tile;
+      sch.at(n, dn, unit, tile);
+      const TcParams& p = dn ? d : g;
+      const int buf = (int)(n & 1);
+      const uint32_t use = (uint32_t)((n >> 1) & 1);
+      const int slot = __ldg(p.unit_slot + unit);
+      const int cnt = min(__ldg(p.unit_cnt + unit), NTOK);
+      const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
+      if (!aborted && !mbar_wait(&acc_full[buf], use)) {
+        set_status(g.status, MIMO_ETIMEOUT);
+        aborted = true;
+      }
+      tc_fence_after();
+      const bool live = !aborted && slot >= 0 && slot < p.S;
+      const int row = tile * kM + quad * 32 + lane;
+      // gate/up: SwiGLU (kernels.py:79-82) and the split of h into the down pass's two e4m3 terms
+      auto emit_h = [&](int q, float h) {
+        uint32_t th, tl, b1, b2;
+        split_warp_block(h, th, tl, b1, b2);
+        const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
+        g.hq[rh * g.Nw + row] = (uint8_t)th;
+        g.hq[rl * g.Nw + row] = (uint8_t)tl;
+        if (lane == 0) {
+          g.hs[rh * (g.Nw / 32) + row / 32] = (uint8_t)b1;
+          g.hs[rl * (g.Nw / 32) + row / 32] = (uint8_t)b2;
+        }
+      };
+      if (!dn && live && g.btok) {
+        // columns are tokens: route q reads its token's hi/lo columns
+#pragma unroll 1
+        for (int q = qlo; q < qlo + QH; ++q) {
+          float h = 0.f;
+          if (q < cnt) {
+            const int t = __ldg(g.btok + p0 + q);
+            if (t >= 0 && t < NTOK) {
+              float gh[1], gl[1], uh[1], ul[1];
+              const uint32_t c0 = tbase + lane_base + (uint32_t)(2 * buf) * N + t;
+              tmem_ld<1>(c0, gh);
+              tmem_ld<1>(c0 + NTOK, gl);
+              tmem_ld<1>(c0 + N, uh);
+              tmem_ld<1>(c0 + N + NTOK, ul);
+              tmem_wait_ld();
+              h = swiglu_ref(gh[0] + gl[0], uh[0] + ul[0]);
+              if (!isfinite(h)) set_status(g.status, MIMO_ERANGE);
+            } else if (lane == 0) {
+              set_status(g.status, MIMO_ERANGE);
+            }
+          }
+          emit_h(q, h);
+        }
+      } else if (live) {
+        float hi[2][QC], lo[2][QC];
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          const uint32_t c = tbase + lane_base + (uint32_t)(2 * buf + a) * N + qlo;
+          tmem_ld<QC>(c, hi[a]);
+          tmem_ld<QC>(c + NTOK, lo[a]);
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < QC; ++i) {
+          const int q = qlo + i;
+          if (!dn) {
+            float h = 0.f;
+            if (q < cnt) {
+              h = swiglu_ref(hi[0][i] + lo[0][i], hi[1][i] + lo[1][i]);
+              if (!isfinite(h)) set_status(g.status, MIMO_ERANGE);
+            }
+            emit_h(q, h);
+          } else if (q < cnt) {
+            // down x route weight (kernels.py:120): the two K halves' hi and lo columns
+            const float v0 = (hi[0][i] + hi[1][i]) + (lo[0][i] + lo[1][i]);
+            const int orow = d.out_row ? __ldg(d.out_row + p0 + q) : p0 + q;
+            const float v = (d.pairs_rounding ? bf16_round(v0) : v0) * __ldg(d.rw + p0 + q);
+            if (d.peer_part)
+              d.peer_part[orow / d.peer_rows][(size_t)(orow % d.peer_rows) * d.Nw + row] = v;
+            else
+              d.part[(size_t)orow * d.Nw + row] = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (!dn) {  // publish this warp's share of the unit's h to the down tiles
+        __threadfence();
+        fz::fence_proxy_async_global();
+        __syncwarp();
+        if (lane == 0) atomicAdd(f.ready + unit, 1);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 3) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TCOLS);
+  }
+}
+
 template <int NM, int NTOK, int NSTAGE, int MODE>
 static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   auto kfn = tc_expert_kernel<NM, NTOK, NSTAGE, MODE>;
@@ -617,6 +1070,24 @@ cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, c
         x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld);
   else
     return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_decode_fused(const TcFusedParams& f, int num_sms, cudaStream_t st) {
+  constexpr int kSt = MIMO_TC_STF;
+  auto kfn = tc::tc_decode_fused_kernel<kSt>;
+  constexpr int smem = tc::fz::smem_bytes<kSt>();
+  static_assert(smem <= 232448, "shared memory budget");
+  static_assert(tc::tmem_cols_needed<tc::fz::kN, kSt>() <= 512, "TMEM budget");
+  static_assert((2 * kSt + 4 + 4 + 1) * 8 + 8 <= tc::kBarBytes, "barrier area");
+  const TcParams& g = f.gu;
+  const TcParams& d = f.dn;
+  if (g.K % (4 * tc::kKC) || d.K % (4 * tc::kKC) || g.Nw % tc::kM || d.Nw % tc::kM || g.tiles != g.Nw / tc::kM ||
+      d.tiles != d.Nw / tc::kM || g.Nw != d.K || !f.ready)
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kfn<<<num_sms, tc::kThreads, smem, st>>>(f);
   return cudaGetLastError();
 }
 
