@@ -516,7 +516,7 @@ def main():
     dn_ms = float(launches[1][kind_dn]) / max(1, int(launches[0][kind_dn]))
     fz_ms = float(launches[1][4]) / max(1, int(launches[0][4]))
     gu_bytes = statistics.mean(steps_Ul) * GATEUP_BYTES
-    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0
     if B <= 8 and launches[0][4] > 0:  # decode, one launch streams every distinct expert's 3 matrices once
         fz_bytes = statistics.mean(steps_Ul) * EXPERT_BYTES
         fz_gbs = fz_bytes / (fz_ms * 1e-3) / 1e9
@@ -531,13 +531,13 @@ def main():
                     "algorithmic_bytes_per_launch": gu_bytes}
     else:        # prefill: algorithmic FLOPs 2 (gate, up) x 2 x I x H per routed pair
         flops = routes_step * 2 * 2 * I * H
-        tf = flops / (gu_ms * 1e-3) / 1e12
+        tf = flops / (gu_ms * 1e-3) / 1e12 if gu_ms > 0 else 0.0
         roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=64,MODE=0> (prefill gate/up + SwiGLU)", "bound": "tensor",
                     "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
                     "peak_kind": f"{peak_kind} bf16_tflops_sustained (dense bf16; the e2m1 x e4m3 MMAs "
                                  "run at the fp8 rate, nominally 2x)",
                     "traffic": None, "algorithmic_flops_per_launch": flops,
-                    "weight_gbs": gu_bytes / (gu_ms * 1e-3) / 1e9}
+                    "weight_gbs": gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0}
     roofline["kernel_ms"] = {"fused": fz_ms} if launches[0][4] > 0 else {"gate_up": gu_ms, "down": dn_ms}
     expert_gbs = sum(steps_U) * EXPERT_BYTES / (ms * 1e-3) / 1e9
 

@@ -91,16 +91,22 @@ bool pools_ok(const mimo_moe_pools* p) {
 
 // ------------------------------------------------------------------- workspace layouts
 // Term matrices of the tcgen05 path: per unit 2 * routes rows of e4m3 terms + ue8m0 block scales.
+bool decode_fp4();
+
 struct TermWs {
   uint8_t *bq, *bs, *hq, *hs;
   int32_t* ready;  // fused decode: per-unit count of gate/up epilogue warps done
 };
+// Activation terms of `units` units: e4m3 (2 terms, one byte a value) or, for decode units on the
+// kind::mxf4 path, e2m1 (5 terms, half a byte a value).
 TermWs carve_terms(Carver& c, int units, int routes, int H, int I) {
-  const size_t rows = (size_t)units * 2 * routes;
+  const bool fp4 = routes == kTcDecodeRoutes && decode_fp4();
+  const size_t rows = (size_t)units * (fp4 ? kTcFp4Terms : 2) * routes;
+  const int vb = fp4 ? 2 : 1;  // values per byte
   TermWs t;
-  t.bq = c.take<uint8_t>(rows * H);
+  t.bq = c.take<uint8_t>(rows * H / vb);
   t.bs = c.take<uint8_t>(rows * (H / 32));
-  t.hq = c.take<uint8_t>(rows * I);
+  t.hq = c.take<uint8_t>(rows * I / vb);
   t.hs = c.take<uint8_t>(rows * (I / 32));
   t.ready = c.take<int32_t>((size_t)units);
   return t;
@@ -238,14 +244,20 @@ bool tc_path(const mimo_moe_pools* pools) {
          al(pools->gate_s, 16) && al(pools->up_s, 16) && al(pools->down_s, 16);
 }
 
-// MIMO_MOE_DECODE_FUSED=0 runs the decode passes as two launches (a comparison knob; same results).
-bool decode_fused() {
-  static const bool on = [] {
-    const char* e = getenv("MIMO_MOE_DECODE_FUSED");
-    return !(e && std::string(e) == "0");
+// Decode expert kernels (MIMO_MOE_DECODE_KERNEL, a comparison knob):
+//   fp4 (default)  one launch, kind::mxf4: packed weights, five e2m1 activation terms;
+//   e4m3           two launches (gate/up, then down), kind::mxf8f6f4 with two e4m3 terms;
+//   e4m3-fused     the e4m3 kernels' arithmetic in one launch (bit-identical to e4m3).
+enum DecodeKernel { kDecodeE4m3 = 0, kDecodeE4m3Fused = 1, kDecodeFp4 = 2 };
+int decode_kernel() {
+  static const int mode = [] {
+    const char* e = getenv("MIMO_MOE_DECODE_KERNEL");
+    const std::string v = e ? e : "";
+    return v == "e4m3" ? kDecodeE4m3 : v == "e4m3-fused" ? kDecodeE4m3Fused : kDecodeFp4;
   }();
-  return on;
+  return mode;
 }
+bool decode_fp4() { return decode_kernel() == kDecodeFp4; }
 
 // Gate/up + SwiGLU and down over units of up to `routes` routes, on the tensor cores.
 // Decode (routes 8): unit u's routes start at u * R, B rows come from rtok = urows, the down pass
@@ -258,21 +270,31 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
            const int32_t* out_row = nullptr, int x_ld = 0, float* const* peer_part = nullptr, int peer_rows = 0) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
-  const int N = 2 * routes;
   const bool decode = routes == kTcDecodeRoutes;
+  const bool fp4 = decode && decode_fp4();
+  const int N = (fp4 ? kTcFp4Terms : 2) * routes;  // term rows per unit (MMA N)
   // by_token_rows = M > 0: B holds the M (<= 8) token rows once, shared by every unit (decode).
   if (!terms_ready) {
-    if (by_token_rows) MIMO_TRY(launch_tc_split_tokens(x, by_token_rows, H, t.bq, t.bs, status, st));
+    if (fp4 && by_token_rows) MIMO_TRY(launch_tc_split_tokens_fp4(x, by_token_rows, H, t.bq, t.bs, status, st));
+    else if (fp4) MIMO_TRY(launch_tc_split_fp4(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, t.bq, t.bs, status,
+                                               st, x_ld));
+    else if (by_token_rows) MIMO_TRY(launch_tc_split_tokens(x, by_token_rows, H, t.bq, t.bs, status, st));
     else MIMO_TRY(launch_tc_split(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, routes, t.bq, t.bs, status, st,
                                   x_ld));
   }
   const uint64_t brows = by_token_rows ? (uint64_t)N : (uint64_t)ucap * N;
   TcParams p{};
-  MIMO_TRY(fp4_weight_map(&p.amap[0], pools->gate_w, (uint64_t)S * I, H));
-  MIMO_TRY(fp4_weight_map(&p.amap[1], pools->up_w, (uint64_t)S * I, H));
+  if (fp4) {  // packed weights as stored, 64-byte (128-value) boxes
+    MIMO_TRY(packed64_map(&p.amap[0], pools->gate_w, (uint64_t)S * I, H / 2, 128));
+    MIMO_TRY(packed64_map(&p.amap[1], pools->up_w, (uint64_t)S * I, H / 2, 128));
+    MIMO_TRY(packed64_map(&p.bmap, t.bq, brows, H / 2, N));
+  } else {
+    MIMO_TRY(fp4_weight_map(&p.amap[0], pools->gate_w, (uint64_t)S * I, H));
+    MIMO_TRY(fp4_weight_map(&p.amap[1], pools->up_w, (uint64_t)S * I, H));
+    MIMO_TRY(rows_map(&p.bmap, t.bq, brows, H, N));
+  }
   MIMO_TRY(sf_map(&p.smap[0], pools->gate_s, (uint64_t)S * I, H / 32, 128));
   MIMO_TRY(sf_map(&p.smap[1], pools->up_s, (uint64_t)S * I, H / 32, 128));
-  MIMO_TRY(rows_map(&p.bmap, t.bq, brows, H, N));
   MIMO_TRY(sf_map(&p.bsmap, t.bs, brows, H / 32, N));
   p.btok = by_token_rows ? rtok : nullptr;
   p.S = S;
@@ -291,14 +313,19 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.hq = t.hq;
   p.hs = t.hs;
   p.status = status;
-  const bool fused = decode && decode_fused();
+  const bool fused = decode && decode_kernel() != kDecodeE4m3;
   if (!fused) MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
-  TcParams q = p;  // down: two K chunks per stage through 3-D boxes
-  MIMO_TRY(fp4_weight_map3(&q.amap[0], pools->down_w, (uint64_t)S * H, I, 2));
+  TcParams q = p;  // down: two K chunks per stage (3-D boxes, or two 2-D boxes when packed)
+  if (fp4) {
+    MIMO_TRY(packed64_map(&q.amap[0], pools->down_w, (uint64_t)S * H, I / 2, 128));
+    MIMO_TRY(packed64_map(&q.bmap, t.hq, (uint64_t)ucap * N, I / 2, N));
+  } else {
+    MIMO_TRY(fp4_weight_map3(&q.amap[0], pools->down_w, (uint64_t)S * H, I, 2));
+    MIMO_TRY(rows_map3(&q.bmap, t.hq, (uint64_t)ucap * N, I, N, 2));
+  }
   q.amap[1] = q.amap[0];
   MIMO_TRY(sf_map(&q.smap[0], pools->down_s, (uint64_t)S * H, I / 32, 128));
   q.smap[1] = q.smap[0];
-  MIMO_TRY(rows_map3(&q.bmap, t.hq, (uint64_t)ucap * N, I, N, 2));
   MIMO_TRY(sf_map(&q.bsmap, t.hs, (uint64_t)ucap * N, I / 32, N));
   q.Nw = H;
   q.K = I;
@@ -316,7 +343,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   if (fused) {  // both passes in one launch; the down tiles wait on per-unit counters
     MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)ucap * sizeof(int32_t), st));
     const TcFusedParams f{p, q, t.ready};
-    MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, sms, st); }));
+    MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, fp4, sms, st); }));
     return MIMO_OK;
   }
   MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
@@ -622,7 +649,8 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
     const bool tc = tc_path(pools);
     MIMO_TRY(launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, counter, g.uids,
                                  g.urows, g.ucnt, g.uw, g.gidx, g.nu, tc ? nullptr : dw.x16,
-                                 tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, score, status, st));
+                                 tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, score, status, st,
+                                 tc && decode_fp4() ? 1 : 0));
     return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
                        T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/!tc, /*terms_ready=*/tc);
   }

@@ -97,10 +97,19 @@ struct TcFusedParams {
   TcParams gu, dn;
   int32_t* ready;
 };
-cudaError_t launch_tc_decode_fused(const TcFusedParams& f, int num_sms, cudaStream_t st);
+// fp4: kind::mxf4 with packed weight maps and five e2m1 activation terms (maps from packed64_map,
+// term rows unit * 40 + t * 8 + q); else kind::mxf8f6f4 with the kind 0 / kind 1 maps.
+cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms, cudaStream_t st);
 // kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (64 routes per
 // unit), 3: prefill down.
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
+// Same splits into five e2m1 terms (kind::mxf4 decode): by-token rows (token t's term j at row
+// j * 8 + t), or per-unit rows (unit u, route q, term j at row u * 40 + j * 8 + q); K / 2 bytes a row.
+cudaError_t launch_tc_split_tokens_fp4(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
+                                       cudaStream_t st);
+cudaError_t launch_tc_split_fp4(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
+                                int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
+                                uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld = 0);
 // Splits bf16 activation rows into the two e4m3 terms + ue8m0 scales of each unit's routes.
 // x rows are x_ld elements apart.
 cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
@@ -118,6 +127,7 @@ cudaError_t launch_routes_prep(const int32_t* idx, const float* w, int route_ld,
 cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
                                    cudaStream_t st);
 constexpr int kTcDecodeRoutes = 8;   // routes per decode unit on the tcgen05 path
+constexpr int kTcFp4Terms = 5;  // e2m1 activation terms of the kind::mxf4 decode path
 constexpr int kTcPrefillRoutes = 64; // routes per prefill unit on the tcgen05 path
 
 // T > 8: tcgen05 GEMM (128 x 64 tiles; an expired wait sets MIMO_ETIMEOUT in `status` when given);
@@ -130,7 +140,7 @@ cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const floa
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
-                                float* score, int32_t* status, cudaStream_t st);
+                                float* score, int32_t* status, cudaStream_t st, int fp4 = 0);
 cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);

@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
     float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
     int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
-    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status) {
+    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status, int fp4) {
   __shared__ float red[kRouteWarps][128];
   // e4m3 terms of x for the tensor-core expert path (token t -> rows t (hi) and 8 + t (lo)): 32-value
   // blocks spread evenly over the CTAs, split after the logits (off the critical path; in the last
@@ -166,9 +166,13 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     for (int b = (threadIdx.x - first_thread) * gridDim.x + blockIdx.x; b < T * nb;
          b += gridDim.x * (blockDim.x - first_thread)) {
       const int t = b / nb, blk = b - t * nb;
-      tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
-                        xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
-                        xs + (size_t)(8 + t) * nb + blk, status);
+      if (fp4)  // e2m1 terms: token t's term j at row j * 8 + t (H / 2 bytes per row)
+        tc::split_block32_fp4(x + (size_t)t * H + blk * 32, xq + (size_t)t * (H / 2) + blk * 16,
+                              (size_t)8 * (H / 2), xs + (size_t)t * nb + blk, (size_t)8 * nb, status);
+      else
+        tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
+                          xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
+                          xs + (size_t)(8 + t) * nb + blk, status);
     }
   };
   __shared__ int32_t sid[64], s_idx[64];
@@ -353,13 +357,13 @@ cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const floa
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
-                                float* score, int32_t* status, cudaStream_t st) {
+                                float* score, int32_t* status, cudaStream_t st, int fp4) {
   if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
   route_decode_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, bias, T, H, E, topk, R, logits, idx, wts,
                                                            counter, uids, urows, ucnt, uw, gidx, num_unique,
-                                                           x16, xq, xs, score, status);
+                                                           x16, xq, xs, score, status, fp4);
   return cudaGetLastError();
 }
 

@@ -62,7 +62,10 @@ constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment 
 #define MIMO_TC_ST3 3
 #endif
 #ifndef MIMO_TC_STF
-#define MIMO_TC_STF 5  // ring depth of the fused decode kernel
+#define MIMO_TC_STF 5  // ring depth of the fused decode kernel, e4m3 activation terms
+#endif
+#ifndef MIMO_TC_STF4
+#define MIMO_TC_STF4 9  // ring depth of the fused decode kernel, e2m1 activation terms (packed weights)
 #endif
 #ifndef MIMO_TC_WEIGHT_EVICT_FIRST
 #define MIMO_TC_WEIGHT_EVICT_FIRST 1  // decode streams each weight once: L2 evict-first
@@ -473,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
           }
         } else {
           if (q < cnt) {
-            const float d = (h0 + h1) + (l0 + l1);
+            const float d = (h0 + l0) + (h1 + l1);  // each K half's hi + lo, then the halves
             const int orow = MODE == 1 && p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q;
             if constexpr (MODE == 1) {
               const float v = (p.pairs_rounding ? bf16_round(d) : d) * __ldg(p.rw + p0 + q);
@@ -555,15 +558,33 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
 // count (acquire, bounded) before loading the unit's h terms.  Each CTA finishes issuing its gate/up
 // tiles before it waits on any unit, and the grid is one CTA per SM (all resident), so every wait
 // ends; a wait that outlasts the limit sets MIMO_ETIMEOUT and the CTA drains and returns.
-// Compared with two launches: one launch ramp instead of two, and down weights stream while other
-// CTAs finish their gate/up tiles.
+//
+// Two operand formats (template FP4):
+//   FP4 = false  kind::mxf8f6f4: weights in the padded e2m1 layout (16 KiB per 128 x 128 tile in shared
+//                memory for 8 KiB of weights), activations as two e4m3 terms (N = 16);
+//   FP4 = true   kind::mxf4: weights packed as stored (8 KiB per tile, 64B swizzle), activations as five
+//                e2m1 terms (N = 40).  Twice the weight bytes fit in the same shared memory, so each SM
+//                keeps about twice as many weight bytes in flight, which is what bounds decode: an
+//                SM's streaming rate is its bytes in flight over the memory latency.
+static_assert(kFp4Terms == kTcFp4Terms, "term count");
 namespace fz {
-constexpr int kN = 2 * kTcDecodeRoutes;                   // MMA N: 8 routes x (hi, lo)
-constexpr int kSB = 2 * kATile + 2 * kN * kKC;            // stage: 2 A tiles + up to 2 B tiles
-constexpr int kSCB = 2 * kM * 16 + kN * 16;               // scale boxes of one 4-chunk group
-constexpr int kSFB = 4 * 512;                              // scale blocks of one stage
-template <int NSTAGE>
-constexpr int smem_bytes() { return kBarBytes + 1024 + NSTAGE * kSB + 2 * kSCB + NSTAGE * kSFB; }
+template <bool FP4>
+struct Fmt {
+  static constexpr int kTerms = FP4 ? kFp4Terms : 2;
+  static constexpr int kN = kTerms * kTcDecodeRoutes;       // MMA N: 8 routes x terms
+  static constexpr int kATileS = FP4 ? kM * kKC / 2 : kATile;  // shared bytes of one weight tile
+  static constexpr int kBRow = FP4 ? kKC / 2 : kKC;          // bytes of one term row per K chunk
+  static constexpr int kBTile = kN * kBRow;
+  static constexpr int kSB = 2 * kATileS + 2 * kBTile;       // stage: 2 A tiles + up to 2 B tiles
+  static constexpr int kSCB = 2 * kM * 16 + kN * 16;         // scale boxes of one 4-chunk group
+  static constexpr int kSFB = 4 * 512;                        // scale blocks of one stage
+  static_assert(kSB % 1024 == 0 || (FP4 && kSB % 512 == 0), "tile alignment");
+};
+template <int NSTAGE, bool FP4>
+constexpr int smem_bytes() {
+  using F = Fmt<FP4>;
+  return kBarBytes + 1024 + NSTAGE * F::kSB + 2 * F::kSCB + NSTAGE * F::kSFB;
+}
 
 struct Sched {
   int tiles_gu, tiles_dn, ns_gu, ns_dn;  // tiles per unit; stages per item
@@ -609,13 +630,14 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 }
 }  // namespace fz
 
-template <int NSTAGE>
+template <int NSTAGE, bool FP4>
 __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __grid_constant__ TcFusedParams f) {
-  constexpr int NTOK = kTcDecodeRoutes, N = fz::kN;
-  constexpr int SB = fz::kSB, SCB = fz::kSCB, SFB = fz::kSFB;
+  using F = fz::Fmt<FP4>;
+  constexpr int NTOK = kTcDecodeRoutes, N = F::kN, NT = F::kTerms;
+  constexpr int SB = F::kSB, SCB = F::kSCB, SFB = F::kSFB, AT = F::kATileS, BT = F::kBTile;
   constexpr uint32_t TCOLS = tmem_cols<N, NSTAGE>();
   constexpr int ABUF = abuf<N, NSTAGE>();
-  constexpr int QH = NTOK / 2, QC = QH;
+  constexpr int QH = NTOK / 2;
   static_assert(ABUF == 2, "double-buffered accumulators");
   const TcParams& g = f.gu;
   const TcParams& d = f.dn;
@@ -741,14 +763,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
             break;
           }
           uint8_t* sb = stages + stage * SB;
-          mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * N * kKC);
-          if (!dn) {
-            tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol_a);
-            tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol_a);
-            tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+          mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * BT);
+          if constexpr (FP4) {  // 2-D boxes of 64 bytes (128 values) per row
+            if (!dn) {
+              tma_load_2d(sb, &p.amap[0], kc * 64, row0, &full[stage], pol_a);
+              tma_load_2d(sb + AT, &p.amap[1], kc * 64, row0, &full[stage], pol_a);
+              tma_load_2d(sb + 2 * AT, &p.bmap, kc * 64, brow, &full[stage], pol_b);
+            } else {
+              for (int c = 0; c < 2; ++c) {
+                tma_load_2d(sb + c * AT, &p.amap[0], (kc + c) * 64, row0, &full[stage], pol_a);
+                tma_load_2d(sb + 2 * AT + c * BT, &p.bmap, (kc + c) * 64, brow, &full[stage], pol_b);
+              }
+            }
           } else {
-            tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol_a);
-            tma_load_3d(sb + 2 * kATile, &p.bmap, 0, brow, kc, &full[stage], pol_b);
+            if (!dn) {
+              tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol_a);
+              tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol_a);
+              tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+            } else {
+              tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol_a);
+              tma_load_3d(sb + 2 * kATile, &p.bmap, 0, brow, kc, &full[stage], pol_b);
+            }
           }
           ++issued;
           if (++stage == NSTAGE) {
@@ -871,11 +906,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
           const int bj = KPS == 2 ? j : 0;
           tc_cp_sf(sf_col, desc_sf(blk + j * 512));
           tc_cp_sf(sf_col + 4, desc_sf(blk + (2 + bj) * 512));
-          const uint32_t a0 = sb + j * kATile, b0 = sb + 2 * kATile + bj * N * kKC;
+          const uint32_t a0 = sb + j * AT, b0 = sb + 2 * AT + bj * BT;
+          if constexpr (FP4) {  // 2 MMAs of K = 64: scale bytes 0-1, then 2-3 of each row's cell
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_mx(dacc, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc_mx(N, kk),
-                      sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30), (ks | kk) != 0);
+            for (int kk = 0; kk < 2; ++kk)
+              tc_mma_mxf4(dacc, desc_sw64(a0 + kk * 32), desc_sw64(b0 + kk * 32), idesc_mxf4(kM, N, 2 * kk),
+                          sf_col | ((uint32_t)(2 * kk) << 30), (sf_col + 4) | ((uint32_t)(2 * kk) << 30),
+                          (ks | kk) != 0);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_mx(dacc, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc_mx(N, kk),
+                        sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30), (ks | kk) != 0);
+          }
           tc_commit(&empty[stage]);
           if (++stage == NSTAGE) {
             stage = 0;
@@ -910,63 +953,88 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
       tc_fence_after();
       const bool live = !aborted && slot >= 0 && slot < p.S;
       const int row = tile * kM + quad * 32 + lane;
-      // gate/up: SwiGLU (kernels.py:79-82) and the split of h into the down pass's two e4m3 terms
-      auto emit_h = [&](int q, float h) {
-        uint32_t th, tl, b1, b2;
-        split_warp_block(h, th, tl, b1, b2);
-        const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
-        g.hq[rh * g.Nw + row] = (uint8_t)th;
-        g.hq[rl * g.Nw + row] = (uint8_t)tl;
-        if (lane == 0) {
-          g.hs[rh * (g.Nw / 32) + row / 32] = (uint8_t)b1;
-          g.hs[rl * (g.Nw / 32) + row / 32] = (uint8_t)b2;
-        }
-      };
-      if (!dn && live && g.btok) {
-        // columns are tokens: route q reads its token's hi/lo columns
-#pragma unroll 1
-        for (int q = qlo; q < qlo + QH; ++q) {
-          float h = 0.f;
-          if (q < cnt) {
-            const int t = __ldg(g.btok + p0 + q);
-            if (t >= 0 && t < NTOK) {
-              float gh[1], gl[1], uh[1], ul[1];
-              const uint32_t c0 = tbase + lane_base + (uint32_t)(2 * buf) * N + t;
-              tmem_ld<1>(c0, gh);
-              tmem_ld<1>(c0 + NTOK, gl);
-              tmem_ld<1>(c0 + N, uh);
-              tmem_ld<1>(c0 + N + NTOK, ul);
-              tmem_wait_ld();
-              h = swiglu_ref(gh[0] + gl[0], uh[0] + ul[0]);
-              if (!isfinite(h)) set_status(g.status, MIMO_ERANGE);
-            } else if (lane == 0) {
-              set_status(g.status, MIMO_ERANGE);
-            }
-          }
-          emit_h(q, h);
-        }
-      } else if (live) {
-        float hi[2][QC], lo[2][QC];
+      // Per accumulator a and MMA column c (a route, or a token when B rows are tokens): the sum of
+      // its term columns c, 8 + c, ... in term order.
+      float acc[2][NTOK];
+      if (live) {
 #pragma unroll
         for (int a = 0; a < 2; ++a) {
-          const uint32_t c = tbase + lane_base + (uint32_t)(2 * buf + a) * N + qlo;
-          tmem_ld<QC>(c, hi[a]);
-          tmem_ld<QC>(c + NTOK, lo[a]);
-        }
-        tmem_wait_ld();
+          float t8[NTOK];
+          const uint32_t col = tbase + lane_base + (uint32_t)(2 * buf + a) * N;
+          tmem_ld<NTOK>(col, t8);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < QC; ++i) {
-          const int q = qlo + i;
+          for (int c = 0; c < NTOK; ++c) acc[a][c] = t8[c];
+#pragma unroll
+          for (int t = 1; t < NT; ++t) {
+            tmem_ld<NTOK>(col + t * NTOK, t8);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < NTOK; ++c) acc[a][c] += t8[c];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (live) {
+#pragma unroll 1
+        for (int q = qlo; q < qlo + QH; ++q) {
+          int col = q;  // B rows per route; with by-token rows, route q's token
+          bool ok = q < cnt;
+          if (!dn && g.btok && ok) {
+            col = __ldg(g.btok + p0 + q);
+            if (col < 0 || col >= NTOK) {
+              if (lane == 0) set_status(g.status, MIMO_ERANGE);
+              ok = false;
+              col = 0;
+            }
+          }
+          float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < NTOK; ++c)
+            if (c == col) {
+              a0 = acc[0][c];
+              a1 = acc[1][c];
+            }
           if (!dn) {
+            // gate/up: SwiGLU with the reference's roundings (kernels.py:79-82), then h as the down
+            // pass's activation terms
             float h = 0.f;
-            if (q < cnt) {
-              h = swiglu_ref(hi[0][i] + lo[0][i], hi[1][i] + lo[1][i]);
+            if (ok) {
+              h = swiglu_ref(a0, a1);
               if (!isfinite(h)) set_status(g.status, MIMO_ERANGE);
             }
-            emit_h(q, h);
-          } else if (q < cnt) {
-            // down x route weight (kernels.py:120): the two K halves' hi and lo columns
-            const float v0 = (hi[0][i] + hi[1][i]) + (lo[0][i] + lo[1][i]);
+            const size_t r0 = (size_t)unit * N + q;  // term t of route q: row r0 + t * NTOK
+            if constexpr (FP4) {
+#pragma unroll 1
+              for (int t = 0; t < NT; ++t) {
+                const float amax = __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, __float_as_uint(fabsf(h))));
+                const uint32_t b = e2m1_scale_byte(amax);
+                const uint32_t code = f32x2_to_e2m1x2(h * inv_exp2_byte(b), 0.f) & 0xFu;
+                h -= e2m1x2_to_f32x2(code).x * exp2_byte(b);
+                uint32_t word = code << (4 * (lane & 7));  // 8 lanes = 8 values = one 32-bit word
+                word |= __shfl_xor_sync(0xFFFFFFFFu, word, 1);
+                word |= __shfl_xor_sync(0xFFFFFFFFu, word, 2);
+                word |= __shfl_xor_sync(0xFFFFFFFFu, word, 4);
+                const size_t rr = r0 + (size_t)t * NTOK;
+                if ((lane & 7) == 0) *reinterpret_cast<uint32_t*>(g.hq + rr * (g.Nw / 2) + row / 2) = word;
+                if (lane == 0) g.hs[rr * (g.Nw / 32) + row / 32] = (uint8_t)b;
+              }
+            } else {
+              uint32_t th, tl, b1, b2;
+              split_warp_block(h, th, tl, b1, b2);
+              const size_t rl = r0 + NTOK;
+              g.hq[r0 * g.Nw + row] = (uint8_t)th;
+              g.hq[rl * g.Nw + row] = (uint8_t)tl;
+              if (lane == 0) {
+                g.hs[r0 * (g.Nw / 32) + row / 32] = (uint8_t)b1;
+                g.hs[rl * (g.Nw / 32) + row / 32] = (uint8_t)b2;
+              }
+            }
+          } else if (ok) {
+            // down x route weight (kernels.py:120): the two K halves' partial sums
+            const float v0 = a0 + a1;
             const int orow = d.out_row ? __ldg(d.out_row + p0 + q) : p0 + q;
             const float v = (d.pairs_rounding ? bf16_round(v0) : v0) * __ldg(d.rw + p0 + q);
             if (d.peer_part)
@@ -976,9 +1044,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
       if (!dn) {  // publish this warp's share of the unit's h to the down tiles
         __threadfence();
         fz::fence_proxy_async_global();
@@ -1047,9 +1112,58 @@ __global__ void __launch_bounds__(128) split_tokens_kernel(const uint16_t* __res
                   bs + (size_t)(kTcDecodeRoutes + t) * nb + blk, status);
 }
 
+// e2m1 terms (kind::mxf4 decode).  Block t: token row t -> rows j * 8 + t.
+__global__ void __launch_bounds__(128) split_tokens_fp4_kernel(const uint16_t* __restrict__ x, int K,
+                                                               uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
+                                                               int32_t* status) {
+  const int t = blockIdx.x, nb = K / 32;
+  for (int blk = threadIdx.x; blk < nb; blk += blockDim.x)
+    split_block32_fp4(x + (size_t)t * K + blk * 32, bq + (size_t)t * (K / 2) + blk * 16,
+                      (size_t)kTcDecodeRoutes * (K / 2), bs + (size_t)t * nb + blk, (size_t)kTcDecodeRoutes * nb,
+                      status);
+}
+// Block (unit, q): route q of the unit -> rows unit * 40 + j * 8 + q.
+__global__ void __launch_bounds__(128) split_rows_fp4_kernel(const uint16_t* __restrict__ x, int K,
+                                                             const int32_t* __restrict__ unit_cnt,
+                                                             const int32_t* __restrict__ unit_p0, int p0_stride,
+                                                             const int32_t* __restrict__ rtok,
+                                                             const int32_t* __restrict__ num_units, int units_cap,
+                                                             uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
+                                                             int32_t* status, int x_ld) {
+  constexpr int NTOK = kTcDecodeRoutes, N = kFp4Terms * NTOK;
+  const int unit = blockIdx.x / NTOK, q = blockIdx.x % NTOK;
+  const int units = num_units ? min(*num_units, units_cap) : units_cap;
+  if (unit >= units) return;
+  const int cnt = min(unit_cnt[unit], NTOK);
+  if (q >= cnt) return;
+  const int p0 = unit_p0 ? unit_p0[unit] : unit * p0_stride;
+  const int tok = rtok ? rtok[p0 + q] : p0 + q;
+  const size_t r0 = (size_t)unit * N + q;
+  const int nb = K / 32;
+  for (int blk = threadIdx.x; blk < nb; blk += blockDim.x)
+    split_block32_fp4(x + (size_t)tok * x_ld + blk * 32, bq + r0 * (K / 2) + blk * 16, (size_t)NTOK * (K / 2),
+                      bs + r0 * nb + blk, (size_t)NTOK * nb, status);
+}
+
 }  // namespace tc
 
 // ------------------------------------------------------------------------------ host entry
+cudaError_t launch_tc_split_tokens_fp4(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
+                                       cudaStream_t st) {
+  if (T < 1 || T > kTcDecodeRoutes || K % 128 != 0) return cudaErrorInvalidValue;
+  tc::split_tokens_fp4_kernel<<<T, 128, 0, st>>>(x, K, bq, bs, status);
+  return cudaGetLastError();
+}
+cudaError_t launch_tc_split_fp4(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
+                                int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
+                                uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld) {
+  if (K % 128 != 0 || units_cap < 1) return cudaErrorInvalidValue;
+  if (x_ld <= 0) x_ld = K;
+  if (x_ld < K || x_ld % 8) return cudaErrorInvalidValue;
+  tc::split_rows_fp4_kernel<<<units_cap * kTcDecodeRoutes, 128, 0, st>>>(x, K, unit_cnt, unit_p0, p0_stride, rtok,
+                                                                         num_units, units_cap, bq, bs, status, x_ld);
+  return cudaGetLastError();
+}
 cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
                                    cudaStream_t st) {
   if (T < 1 || T > kTcDecodeRoutes || K % 128 != 0) return cudaErrorInvalidValue;
@@ -1073,12 +1187,12 @@ cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, c
   return cudaGetLastError();
 }
 
-cudaError_t launch_tc_decode_fused(const TcFusedParams& f, int num_sms, cudaStream_t st) {
-  constexpr int kSt = MIMO_TC_STF;
-  auto kfn = tc::tc_decode_fused_kernel<kSt>;
-  constexpr int smem = tc::fz::smem_bytes<kSt>();
+template <int kSt, bool FP4>
+static cudaError_t launch_fused(const TcFusedParams& f, int num_sms, cudaStream_t st) {
+  auto kfn = tc::tc_decode_fused_kernel<kSt, FP4>;
+  constexpr int smem = tc::fz::smem_bytes<kSt, FP4>();
   static_assert(smem <= 232448, "shared memory budget");
-  static_assert(tc::tmem_cols_needed<tc::fz::kN, kSt>() <= 512, "TMEM budget");
+  static_assert(tc::tmem_cols_needed<tc::fz::Fmt<FP4>::kN, kSt>() <= 512, "TMEM budget");
   static_assert((2 * kSt + 4 + 4 + 1) * 8 + 8 <= tc::kBarBytes, "barrier area");
   const TcParams& g = f.gu;
   const TcParams& d = f.dn;
@@ -1089,6 +1203,10 @@ cudaError_t launch_tc_decode_fused(const TcFusedParams& f, int num_sms, cudaStre
   if (e != cudaSuccess) return e;
   kfn<<<num_sms, tc::kThreads, smem, st>>>(f);
   return cudaGetLastError();
+}
+
+cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms, cudaStream_t st) {
+  return fp4 ? launch_fused<MIMO_TC_STF4, true>(f, num_sms, st) : launch_fused<MIMO_TC_STF, false>(f, num_sms, st);
 }
 
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st) {

@@ -113,6 +113,36 @@ __device__ __forceinline__ uint64_t desc_sf(uint32_t saddr) {
   d |= (uint64_t)1 << 46;
   return d;
 }
+//   K-major, 64B swizzle: 8-row groups of 64-byte rows (packed e2m1, 128 values per row), SBO = 512.
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;
+  return d;
+}
+// kind::mxf4 block-scaled MMA: A and B packed e2m1 (2 values per byte, low nibble first), one ue8m0
+// scale per 32 values (scale_vec::2X: an MMA of K = 64 reads 2 scale bytes of each row's 32-bit TMEM
+// cell, the pair picked by sf id 0 or 2).
+__device__ __forceinline__ void tc_mma_mxf4(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t sfa_taddr, uint32_t sfb_taddr, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(
+          d_taddr),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_taddr), "r"(sfb_taddr)
+      : "memory");
+}
+// Instruction descriptor of kind::mxf4.block_scale: A and B e2m1 (format 1), ue8m0 scales (bit 23),
+// both K-major, M = m, N = n, dense K = 64; sf id (0 or 2) for both operands at bits 4-5 and 29-30.
+__device__ __forceinline__ uint32_t idesc_mxf4(int m, int n, uint32_t sfid) {
+  return ((sfid & 3u) << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(m >> 4) << 24) | ((sfid & 3u) << 29);
+}
+
 // kind::f16 MMA (bf16/f16 operands from shared memory, f32 accumulate), no disabled lanes.
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -198,6 +228,77 @@ __device__ __forceinline__ void split_block32(const uint16_t* src, uint8_t* dh, 
   l4[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
   *sh = (uint8_t)b1;
   *sl = (uint8_t)b2;
+}
+
+// ------------------------------------------------------------------ e2m1 multi-term activations
+// A value block of 32 becomes kFp4Terms e2m1 terms, each with one ue8m0 scale: term t quantises the
+// residual r_t (r_0 = v) with the scale s_t that puts max |r_t| / s_t in (3, 6], and
+// r_{t+1} = r_t - q_t * s_t.  Each subtraction is exact (q_t * s_t is 0 or within a factor of 2 of
+// r_t), and |r_{t+1}| <= s_t (half the widest e2m1 step), so the block's residual maximum falls at
+// least 4x per term; on bf16 activations five terms leave dot products within ~1e-6 of exact.
+constexpr int kFp4Terms = 5;
+// Two floats -> one byte of two e2m1 codes (lo in bits 0-3), round to nearest even, saturating at 6.
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n.reg .b8 b0;\ncvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\nmov.b32 %0, {b0, b0, b0, b0};\n}\n"
+      : "=r"(r)
+      : "f"(lo), "f"(hi));
+  return r & 0xFFu;
+}
+// One byte of two e2m1 codes -> their values (exact).
+__device__ __forceinline__ float2 e2m1x2_to_f32x2(uint32_t byte) {
+  uint32_t h2;
+  asm("{\n.reg .b8 b0, b1, b2, b3;\nmov.b32 {b0, b1, b2, b3}, %1;\ncvt.rn.f16x2.e2m1x2 %0, b0;\n}\n"
+      : "=r"(h2)
+      : "r"(byte));
+  return __half22float2(*reinterpret_cast<__half2*>(&h2));
+}
+// ue8m0 byte of the scale 2^e with the smallest e such that amax <= 6 * 2^e.
+__device__ __forceinline__ uint32_t e2m1_scale_byte(float amax) {
+  if (!(amax > 0.f)) return 127u;
+  const uint32_t u = __float_as_uint(amax);
+  const int b = (int)((u >> 23) & 0xFFu) - 2 + ((u & 0x7FFFFFu) > 0x400000u ? 1 : 0);
+  return (uint32_t)(b < 1 ? 1 : (b > 254 ? 254 : b));
+}
+// Splits 32 bf16 values (src, 16-byte aligned) into kFp4Terms e2m1 terms: term t's 16 bytes go to
+// dq + t * tstride, its scale byte to ds[t * sstride].  Non-finite inputs set MIMO_ERANGE.
+__device__ __forceinline__ void split_block32_fp4(const uint16_t* src, uint8_t* dq, size_t tstride, uint8_t* ds,
+                                                  size_t sstride, int32_t* status) {
+  float v[32];
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 w = s4[i];
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[i * 8 + 2 * j] = __uint_as_float(ww[j] << 16);
+      v[i * 8 + 2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+    }
+  }
+  bool bad = false;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) bad |= !isfinite(v[i]);
+  if (bad) set_status(status, MIMO_ERANGE);
+#pragma unroll 1
+  for (int t = 0; t < kFp4Terms; ++t) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const uint32_t b = e2m1_scale_byte(amax);
+    const float inv = inv_exp2_byte(b), sc = exp2_byte(b);
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t q = f32x2_to_e2m1x2(v[2 * i] * inv, v[2 * i + 1] * inv);
+      const float2 d = e2m1x2_to_f32x2(q);
+      v[2 * i] -= d.x * sc;
+      v[2 * i + 1] -= d.y * sc;
+      w[i >> 2] |= q << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint4*>(dq + (size_t)t * tstride) = make_uint4(w[0], w[1], w[2], w[3]);
+    ds[(size_t)t * sstride] = (uint8_t)b;
+  }
 }
 
 }  // namespace tc

@@ -261,4 +261,24 @@ cudaError_t rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t
   return cudaSuccess;
 }
 
+cudaError_t packed64_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows) {
+  const Key key{(uint64_t)base, rows, row_bytes, 7, box_rows};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || row_bytes % 64 != 0 || box_rows < 1 || box_rows > 256 || ((uint64_t)base & 15) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {row_bytes, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
 }  // namespace mimo

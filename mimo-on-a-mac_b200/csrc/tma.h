@@ -38,5 +38,8 @@ cudaError_t sf_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t r
 cudaError_t bf16_rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, int box_rows);
 // Byte-matrix map [rows][row_bytes], box [128 bytes, box_rows], 128B swizzle.
 cudaError_t rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
+// Packed rows (e2m1, two values per byte: pool weights [rows][K/2] or activation terms) read 64 bytes
+// (128 values) of box_rows rows per box, 64B swizzle (the layout kind::mxf4 reads).
+cudaError_t packed64_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
 
 }  // namespace mimo

@@ -1,7 +1,13 @@
-"""The fused decode launch (gate/up and down in one kernel, down tiles waiting on per-unit counters)
-against the two-launch path: same kernels' arithmetic, so the block output must be identical bit for
-bit.  MIMO_MOE_DECODE_FUSED is read once per process, so the two-launch results come from a child
-process."""
+"""Decode expert kernels (MIMO_MOE_DECODE_KERNEL, read once per process, so each variant runs in a
+child process):
+
+  fp4         (default) one launch, kind::mxf4, packed weights, five e2m1 activation terms;
+  e4m3        two launches, kind::mxf8f6f4, two e4m3 activation terms;
+  e4m3-fused  the e4m3 arithmetic in one launch (down tiles wait on per-unit counters).
+
+e4m3-fused must equal e4m3 bit for bit; fp4 differs from them only by the activation terms' residual
+(about 1e-6 of a dot product), so its block output stays within rel_err 1e-2 of the e4m3 path's
+(the oracle bar, engine/tests/test_kernels.py:54-56) and almost all bf16 outputs agree exactly."""
 import os
 import subprocess
 import sys
@@ -22,34 +28,40 @@ from oracle import synth
 dev = torch.device("cuda", 0)
 pool = mimo_moe.ExpertPools.synthetic({S}, seed=0, layer=2, device=dev)
 W = synth.router_weight(E={S}).to(dev)
+status = torch.zeros(1, dtype=torch.int32, device=dev)
 out = []
 for T in {Ts}:
     x = synth.hidden(T, seed=70 + T).to(dev)
-    y = mimo_moe.moe_block(x, W, None, pool)
+    y = mimo_moe.moe_block(x, W, None, pool, status=status)
     out.append(y.view(torch.int16).cpu().numpy())
+assert int(status.item()) == 0, int(status.item())
 np.savez({path!r}, *out)
 """
+TS = [1, 2, 3, 8]
+
+
+def _run(tmp_path, S, kernel):
+    path = str(tmp_path / f"{kernel}_{S}.npz")
+    env = dict(os.environ, MIMO_MOE_DECODE_KERNEL=kernel)
+    code = CHILD.format(root=str(ROOT), pkg=str(PKG_DIR), S=S, Ts=TS, path=path)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    z = np.load(path)
+    return [z[f"arr_{i}"] for i in range(len(TS))]
 
 
 @pytest.mark.parametrize("S", [32, 256])
-def test_fused_decode_equals_two_launches(gpu, tmp_path, S):
-    import mimo_moe
-    from oracle import synth
-    Ts = [1, 2, 3, 8]
-    path = str(tmp_path / "two.npz")
-    env = dict(os.environ, MIMO_MOE_DECODE_FUSED="0")
-    code = CHILD.format(root=str(ROOT), pkg=str(PKG_DIR), S=S, Ts=Ts, path=path)
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0, r.stderr[-2000:]
-    two = np.load(path)
-    pool = mimo_moe.ExpertPools.synthetic(S, seed=0, layer=2, device=gpu)
-    W = synth.router_weight(E=S).to(gpu)
-    status = torch.zeros(1, dtype=torch.int32, device=gpu)
-    for i, T in enumerate(Ts):
-        x = synth.hidden(T, seed=70 + T).to(gpu)
-        y = mimo_moe.moe_block(x, W, None, pool, status=status)
-        assert np.array_equal(y.view(torch.int16).cpu().numpy(), two[f"arr_{i}"]), T
-    assert int(status.item()) == 0
+def test_decode_kernels_agree(gpu, tmp_path, S):
+    e4 = _run(tmp_path, S, "e4m3")
+    e4f = _run(tmp_path, S, "e4m3-fused")
+    fp4 = _run(tmp_path, S, "fp4")
+    for T, a, b, c in zip(TS, e4, e4f, fp4):
+        assert np.array_equal(a, b), T
+        fa = torch.from_numpy(a).view(torch.bfloat16).float().numpy()
+        fc = torch.from_numpy(c).view(torch.bfloat16).float().numpy()
+        rel = np.abs(fa - fc).max() / np.abs(fa).max()
+        assert rel <= 1e-2, (T, rel)
+        assert (a == c).mean() >= 0.9, (T, (a == c).mean())
 
 
 def test_fused_decode_repeated_calls_and_graph(gpu):
