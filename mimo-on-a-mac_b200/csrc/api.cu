@@ -244,16 +244,19 @@ bool tc_path(const mimo_moe_pools* pools) {
          al(pools->gate_s, 16) && al(pools->up_s, 16) && al(pools->down_s, 16);
 }
 
-// Decode expert kernels (MIMO_MOE_DECODE_KERNEL, a comparison knob):
-//   fp4 (default)  one launch, kind::mxf4: packed weights, five e2m1 activation terms;
-//   e4m3           two launches (gate/up, then down), kind::mxf8f6f4 with two e4m3 terms;
-//   e4m3-fused     the e4m3 kernels' arithmetic in one launch (bit-identical to e4m3).
+// Decode expert kernels (MIMO_MOE_DECODE_KERNEL, a comparison knob; all measured on B200):
+//   e4m3 (default)  two launches (gate/up, then down), kind::mxf8f6f4 with two e4m3 terms;
+//   e4m3-fused      the same arithmetic in one launch (bit-identical), down tiles waiting on
+//                   per-unit counters: ~2 us less kernel time, no faster per step;
+//   fp4             one launch, kind::mxf4: packed weights, five e2m1 activation terms: twice the
+//                   weight bytes in flight per SM, yet ~4% slower (the per-SM ingress rate, not the
+//                   bytes in flight, bounds these kernels).
 enum DecodeKernel { kDecodeE4m3 = 0, kDecodeE4m3Fused = 1, kDecodeFp4 = 2 };
 int decode_kernel() {
   static const int mode = [] {
     const char* e = getenv("MIMO_MOE_DECODE_KERNEL");
     const std::string v = e ? e : "";
-    return v == "e4m3" ? kDecodeE4m3 : v == "e4m3-fused" ? kDecodeE4m3Fused : kDecodeFp4;
+    return v == "fp4" ? kDecodeFp4 : v == "e4m3-fused" ? kDecodeE4m3Fused : kDecodeE4m3;
   }();
   return mode;
 }
