@@ -262,6 +262,7 @@ int decode_kernel() {
 }
 bool decode_fp4() { return decode_kernel() == kDecodeFp4; }
 
+
 // Gate/up + SwiGLU and down over units of up to `routes` routes, on the tensor cores.
 // Decode (routes 8): unit u's routes start at u * R, B rows come from rtok = urows, the down pass
 // writes part = dot * weight.  Prefill (routes 32): units from build_units, down writes ypair.

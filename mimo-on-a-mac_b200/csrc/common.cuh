@@ -171,6 +171,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, int c0, 
       "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Programmatic dependent launch (kernels launched with launch_k): pdl_wait() returns once the
+// preceding grid has completed and its writes are visible (at once when there is no such grid);
+// pdl_launch_dependents() lets the next grid be scheduled as SMs free up, so its launch and prologue
+// overlap this grid's tail.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 __device__ __forceinline__ void tma_prefetch_map(const void* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
 }

@@ -692,6 +692,8 @@ __global__ void combine_decode_kernel(const float* __restrict__ part, const int3
                                       const int32_t* __restrict__ urows, const int32_t* __restrict__ ucnt,
                                       const int32_t* __restrict__ num_unique, int ucap, int R, int M,
                                       int topk, int H, uint16_t* __restrict__ y) {
+  pdl_wait();  // the partials come from the preceding kernel
+  pdl_launch_dependents();
   const int t = blockIdx.x;  // rows on x: gridDim.y stops at 65535
   const int m = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (t >= M || m >= H) return;
@@ -725,9 +727,8 @@ cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const 
                                   const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
                                   int M, int topk, int H, uint16_t* y, cudaStream_t st) {
   dim3 grid(M, (H / 4 + 255) / 256);
-  combine_decode_kernel<<<grid, 256, 0, st>>>(part, gidx, urows, ucnt, num_unique, ucap, R, M, topk, H,
-                                              y);
-  return cudaGetLastError();
+  return launch_k(combine_decode_kernel, grid, dim3(256), 0, st, part, gidx, urows, ucnt, num_unique, ucap, R, M,
+                  topk, H, y);
 }
 
 // y[m] = bf16(sum over k in order of part[row]) with row = gidx[m * topk + k] (skipped when < 0), or

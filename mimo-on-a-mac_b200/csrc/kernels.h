@@ -11,6 +11,26 @@
 
 namespace mimo {
 
+// Kernel launch with programmatic stream serialization: the kernel may start while the preceding
+// kernel on the stream finishes; it calls pdl_wait() before touching that kernel's results.
+// MIMO_MOE_PDL=0 launches plainly (a comparison knob).
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Parameters of the expert tile kernel (see experts.cu).
 struct ExpertParams {
   const uint8_t* w[2];  // packed e2m1 bytes of matrix m: [S][N][K/2]

@@ -180,6 +180,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
   __shared__ uint32_t bitmap[32];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5;
+  pdl_wait();  // x may come from the preceding kernel
+  pdl_launch_dependents();
   route_logits_cta(x, w, T, H, E, logits, score, red);
   __threadfence();
   __syncthreads();
@@ -361,10 +363,9 @@ cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const floa
   if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
-  route_decode_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, bias, T, H, E, topk, R, logits, idx, wts,
-                                                           counter, uids, urows, ucnt, uw, gidx, num_unique,
-                                                           x16, xq, xs, score, status, fp4);
-  return cudaGetLastError();
+  return launch_k(route_decode_kernel, dim3(E / 16), dim3(kRouteWarps * 32), 0, st, x, w, bias, T, H, E, topk, R,
+                  logits, idx, wts, counter, uids, urows, ucnt, uw, gidx, num_unique, x16, xq, xs, score, status,
+                  fp4);
 }
 
 }  // namespace mimo

@@ -31,7 +31,9 @@
 // The producer does its per-item work (coordinates, slot, row base) once per item: at decode sizes a
 // stage lasts ~600 cycles and the single issuing threads are the critical path.
 // Every wait is bounded; an expired wait sets MIMO_ETIMEOUT and the CTA drains and returns.
+#include <cstdlib>
 #include <cstring>
+#include <string>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -205,6 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the unit tables and activation terms come from the preceding kernel
+  pdl_launch_dependents();
   const uint32_t tbase = *tmem_slot;
   constexpr int ABUF = abuf<N, NSTAGE>();
   constexpr uint32_t kSfCol0 = ABUF * 2 * N;  // accumulator (buf, j) at columns (2 * buf + j) * N
@@ -684,6 +688,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the unit tables and activation terms come from the preceding kernel
+  pdl_launch_dependents();
   const uint32_t tbase = *tmem_slot;
   constexpr uint32_t kSfCol0 = ABUF * 2 * N;
 
@@ -1070,8 +1076,7 @@ static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   if (p.K % (4 * kKC) != 0 || p.Nw % kM != 0 || p.tiles != p.Nw / kM) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kfn<<<grid, kThreads, smem, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(kfn, dim3(grid), dim3(kThreads), smem, st, p);
 }
 
 // ---------------------------------------------------------------------- activation term split
@@ -1148,6 +1153,14 @@ __global__ void __launch_bounds__(128) split_rows_fp4_kernel(const uint16_t* __r
 }  // namespace tc
 
 // ------------------------------------------------------------------------------ host entry
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MIMO_MOE_PDL");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
 cudaError_t launch_tc_split_tokens_fp4(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
                                        cudaStream_t st) {
   if (T < 1 || T > kTcDecodeRoutes || K % 128 != 0) return cudaErrorInvalidValue;
@@ -1201,8 +1214,7 @@ static cudaError_t launch_fused(const TcFusedParams& f, int num_sms, cudaStream_
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kfn<<<num_sms, tc::kThreads, smem, st>>>(f);
-  return cudaGetLastError();
+  return launch_k(kfn, dim3(num_sms), dim3(tc::kThreads), smem, st, f);
 }
 
 cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms, cudaStream_t st) {
