@@ -175,15 +175,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   uint8_t* sfblk = scbox + 2 * SCB;         // NSTAGE x [2 weight scale blocks | KPS activation blocks]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
-  const long long items = (long long)units * p.tiles;
-  // Items are dealt round-robin: at any time the CTAs work on consecutive items (the tiles and units
-  // of the same experts), so a weight tile shared by an expert's units and a unit's activation tile
-  // shared by its weight tiles are read from L2 by CTAs running side by side.  CTA-local item n is
-  // item blockIdx.x + n * gridDim.x.
-  const long long my_items = items > blockIdx.x ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-  const int ns = p.K / (kKC * KPS);  // stages per item; K chunks per item are a multiple of 4
-  const long long nsteps = my_items * ns;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
@@ -210,6 +201,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
   pdl_wait();  // the unit tables and activation terms come from the preceding kernel
   pdl_launch_dependents();
   const uint32_t tbase = *tmem_slot;
+  // after the wait: the unit count is written by the preceding kernel
+  const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
+  const long long items = (long long)units * p.tiles;
+  // Items are dealt round-robin: at any time the CTAs work on consecutive items (the tiles and units
+  // of the same experts), so a weight tile shared by an expert's units and a unit's activation tile
+  // shared by its weight tiles are read from L2 by CTAs running side by side.  CTA-local item n is
+  // item blockIdx.x + n * gridDim.x.
+  const long long my_items = items > blockIdx.x ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int ns = p.K / (kKC * KPS);  // stages per item; K chunks per item are a multiple of 4
+  const long long nsteps = my_items * ns;
   constexpr int ABUF = abuf<N, NSTAGE>();
   constexpr uint32_t kSfCol0 = ABUF * 2 * N;  // accumulator (buf, j) at columns (2 * buf + j) * N
 
@@ -661,10 +662,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
   uint8_t* sfblk = scbox + 2 * SCB;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int units = g.num_units ? min(__ldg(g.num_units), g.units_cap) : g.units_cap;
-  const fz::Sched sch = fz::schedule(g, d, units);
-  const long long my_items = sch.items();
-  const int ready_target = kEpiWarps * g.tiles;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
@@ -692,6 +689,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
   pdl_launch_dependents();
   const uint32_t tbase = *tmem_slot;
   constexpr uint32_t kSfCol0 = ABUF * 2 * N;
+  // after the wait: the unit count is written by the preceding kernel
+  const int units = g.num_units ? min(__ldg(g.num_units), g.units_cap) : g.units_cap;
+  const fz::Sched sch = fz::schedule(g, d, units);
+  const long long my_items = sch.items();
+  const int ready_target = kEpiWarps * g.tiles;
+
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------ TMA producer

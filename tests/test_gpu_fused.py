@@ -79,3 +79,23 @@ def test_fused_decode_repeated_calls_and_graph(gpu):
         for x, r in zip(xs, ref):
             assert torch.equal(mimo_moe.moe_block(x, W, None, pool).view(torch.int16), r.view(torch.int16))
             assert torch.equal(g(x).view(torch.int16), r.view(torch.int16))
+
+
+def test_back_to_back_calls_with_changing_unit_counts(gpu):
+    """Launches overlap their predecessors' tails (programmatic dependent launch): a kernel must not
+    read the unit count or tables before its predecessor is done.  Calls whose distinct-expert counts
+    change from call to call, issued back to back, must equal the same calls run one at a time."""
+    import mimo_moe
+    from oracle import synth
+    pool = mimo_moe.ExpertPools.synthetic(64, seed=0, layer=6, device=gpu)
+    W = synth.router_weight(E=64).to(gpu)
+    Ts = [8, 1, 3, 8, 2, 5, 1, 8, 4, 7]
+    xs = [synth.hidden(T, seed=300 + i).to(gpu) for i, T in enumerate(Ts)]
+    status = torch.zeros(1, dtype=torch.int32, device=gpu)
+    fast = [mimo_moe.moe_block(x, W, None, pool, status=status) for x in xs]
+    torch.cuda.synchronize()
+    for x, y in zip(xs, fast):
+        ref = mimo_moe.moe_block(x, W, None, pool)
+        torch.cuda.synchronize()
+        assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+    assert int(status.item()) == 0
