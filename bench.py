@@ -372,6 +372,9 @@ def main():
     ap.add_argument("--pool-experts", type=int, default=E,
                     help="experts in the pool and router (small cases for profiling; default 256)")
     ap.add_argument("--layers", type=int, default=STACK_LAYERS, help="layers of the stack workloads")
+    ap.add_argument("--fixed-batch", type=int, default=None,
+                    help="route every step from this one seeded batch (profiling: every captured launch "
+                         "then processes the same distinct experts)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -404,6 +407,8 @@ def main():
         lo, hi = 0, NE
         pool = mimo_moe.ExpertPools.synthetic(NE, seed=0, layer=0, device=dev)
     xs, W = make_inputs(B, dev, torch, rank)
+    if args.fixed_batch is not None:
+        xs = [xs[args.fixed_batch % NBATCH]] * NBATCH
     W = W[:NE].contiguous()
     zipf = args.workload.endswith("z")
     if zipf:
@@ -594,6 +599,7 @@ def main():
                                         "NCCL all-to-all of each route to its expert's rank and back") +
                                        "; fixed-order combine)") if ep else "single",
                        "tokens_per_gpu": B,
+                       "fixed_batch": args.fixed_batch,
                        "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
             "expert_gbs": expert_gbs,
             "expert_frac_of_measured_hbm": expert_gbs / hbm,
