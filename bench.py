@@ -36,6 +36,9 @@ STACK_LAYERS = 48  # config 3: 48 MoE layers (~164 GB of experts), RMSNorm (unit
 # expert at ~10x the mean load on the seeded 16384-token batch (tuned once on the CPU router)
 ZIPF_C = 0.055
 NBATCH = 16
+# DRAM bytes of one decode gate/up launch per distinct expert, from one ncu capture
+# (profiles/tc_expert_kernel_decode8_traffic.md): 1.005x the algorithmic 8,912,896
+GATEUP_TRAFFIC_PER_EXPERT = 8_957_075
 
 
 def peaks():
@@ -532,7 +535,10 @@ def main():
     elif B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
         roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
+                    "peak_kind": f"{peak_kind} hbm_gbs",
+                    "traffic": statistics.mean(steps_Ul) * GATEUP_TRAFFIC_PER_EXPERT,
+                    "traffic_source": "ncu dram__bytes_read+write per distinct expert (one capture) x this "
+                                      "workload's mean distinct experts",
                     "algorithmic_bytes_per_launch": gu_bytes}
     else:        # prefill: algorithmic FLOPs 2 (gate, up) x 2 x I x H per routed pair
         flops = routes_step * 2 * 2 * I * H
