@@ -63,6 +63,9 @@ constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment 
 #ifndef MIMO_TC_ST3
 #define MIMO_TC_ST3 3
 #endif
+#ifndef MIMO_TC_EPI_PREFILL
+#define MIMO_TC_EPI_PREFILL 16  // epilogue warps of the prefill kernels
+#endif
 #ifndef MIMO_TC_STF
 #define MIMO_TC_STF 5  // ring depth of the fused decode kernel, e4m3 activation terms
 #endif
@@ -147,16 +150,20 @@ __device__ __forceinline__ void item_coords(const TcParams& p, long long i, int&
   }
 }
 
-template <int NM, int NTOK, int NSTAGE, int MODE>
-__global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_constant__ TcParams p) {
+// EPI epilogue warps (a multiple of 4): EPI / 4 per TMEM lane quadrant, each taking NTOK / (EPI / 4) of
+// the routes.  Prefill uses 16: its per-route SwiGLU and term split are long dependent chains, and
+// four warps per SM sub-partition hide their latency where two cannot.
+template <int NM, int NTOK, int NSTAGE, int MODE, int EPI>
+__global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __grid_constant__ TcParams p) {
   constexpr int N = 2 * NTOK;
   constexpr int KPS = kps<NM>();
   constexpr int SB = stage_bytes<NM, N>();
   constexpr int SCB = scale_box_bytes<NM, N>();
   constexpr int SFB = sf_block_bytes<NM>();
   constexpr uint32_t TCOLS = tmem_cols<N, NSTAGE>();
-  constexpr int QH = NTOK / 2;               // routes per epilogue warp
+  constexpr int QH = NTOK / (EPI / 4);       // routes per epilogue warp
   constexpr int QC = QH < 16 ? QH : 16;      // routes per TMEM load in the epilogue
+  static_assert(EPI % 4 == 0 && NTOK % (EPI / 4) == 0 && QH % QC == 0, "epilogue split");
   static_assert(NM * KPS == 2, "two slots per stage");
   static_assert(N % 16 == 0 && N <= 256 && QH % QC == 0, "MMA N");
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -185,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_expert_kernel(const __grid_con
       mbar_init(&sc_full[b], 1);
       mbar_init(&sc_empty[b], 1);
       mbar_init(&acc_full[b], 2);
-      mbar_init(&acc_empty[b], kEpiWarps);
+      mbar_init(&acc_empty[b], EPI);
     }
     mbar_init(drain, 2);
     *s_abort = 0;
@@ -1069,9 +1076,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
   }
 }
 
-template <int NM, int NTOK, int NSTAGE, int MODE>
+template <int NM, int NTOK, int NSTAGE, int MODE, int EPI>
 static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
-  auto kfn = tc_expert_kernel<NM, NTOK, NSTAGE, MODE>;
+  auto kfn = tc_expert_kernel<NM, NTOK, NSTAGE, MODE, EPI>;
   constexpr int smem = smem_bytes<NM, 2 * NTOK, NSTAGE>();
   static_assert(smem <= 232448, "shared memory budget");
   static_assert(tmem_cols_needed<2 * NTOK, NSTAGE>() <= 512, "TMEM budget");
@@ -1079,7 +1086,7 @@ static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   if (p.K % (4 * kKC) != 0 || p.Nw % kM != 0 || p.tiles != p.Nw / kM) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return launch_k(kfn, dim3(grid), dim3(kThreads), smem, st, p);
+  return launch_k(kfn, dim3(grid), dim3((4 + EPI) * 32), smem, st, p);
 }
 
 // ---------------------------------------------------------------------- activation term split
@@ -1226,10 +1233,10 @@ cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms
 
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st) {
   switch (kind) {
-    case 0: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 0>(p, num_sms, st);
-    case 1: return tc::launch<1, kTcDecodeRoutes, tc::kStages[1], 1>(p, num_sms, st);
-    case 2: return tc::launch<2, kTcPrefillRoutes, tc::kStages[2], 0>(p, num_sms, st);
-    case 3: return tc::launch<1, kTcPrefillRoutes, tc::kStages[3], 2>(p, num_sms, st);
+    case 0: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 0, 8>(p, num_sms, st);
+    case 1: return tc::launch<1, kTcDecodeRoutes, tc::kStages[1], 1, 8>(p, num_sms, st);
+    case 2: return tc::launch<2, kTcPrefillRoutes, tc::kStages[2], 0, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
+    case 3: return tc::launch<1, kTcPrefillRoutes, tc::kStages[3], 2, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
 }
