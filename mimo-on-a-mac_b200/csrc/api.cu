@@ -271,6 +271,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
            const int32_t* unsub, const int32_t* rtok, const float* rw,
            const int32_t* num_units, int ucap, int pairs_rounding, const TermWs& t, float* part,
            uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false,
+           bool ready_zeroed = false,
            const int32_t* out_row = nullptr, int x_ld = 0, float* const* peer_part = nullptr, int peer_rows = 0) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
@@ -345,7 +346,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   q.ypair = ypair;
   q.pairs_rounding = pairs_rounding;
   if (fused) {  // both passes in one launch; the down tiles wait on per-unit counters
-    MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)ucap * sizeof(int32_t), st));
+    if (!ready_zeroed) MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)ucap * sizeof(int32_t), st));
     const TcFusedParams f{p, q, t.ready};
     MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, fp4, sms, st); }));
     return MIMO_OK;
@@ -429,7 +430,8 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
   if (R <= kTcDecodeRoutes && tc_path(pools)) {
     const int rc = run_tc(x, pools, kTcDecodeRoutes, uslot, ucnt, nullptr, R, nullptr, nullptr, urows, uw,
                           num_unique, U, pairs_rounding, w.t, w.part, nullptr, status, st,
-                          M <= kTcDecodeRoutes ? M : 0, terms_ready && M <= kTcDecodeRoutes);
+                          M <= kTcDecodeRoutes ? M : 0, terms_ready && M <= kTcDecodeRoutes,
+                          /*ready_zeroed=*/terms_ready);
     if (rc != MIMO_OK) return rc;
     MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
     return MIMO_OK;
@@ -654,7 +656,7 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
     MIMO_TRY(launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, counter, g.uids,
                                  g.urows, g.ucnt, g.uw, g.gidx, g.nu, tc ? nullptr : dw.x16,
                                  tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, score, status, st,
-                                 tc && decode_fp4() ? 1 : 0));
+                                 tc && decode_fp4() ? 1 : 0, tc ? dw.t.ready : nullptr, g.ucap));
     return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
                        T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/!tc, /*terms_ready=*/tc);
   }
@@ -702,8 +704,8 @@ int mimo_moe_experts_routes(const uint16_t* x, int32_t x_ld, int32_t rows, const
                                 w.rw, status, st));
   }
   return run_tc(x, pools, kTcDecodeRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, nullptr, nullptr, w.rtok,
-                w.rw, w.num_units, w.ucap, pairs_rounding, w.t, part, nullptr, status, st, 0, false, w.order, x_ld,
-                peer_part, rows_per_rank);
+                w.rw, w.num_units, w.ucap, pairs_rounding, w.t, part, nullptr, status, st, 0, false, false, w.order,
+                x_ld, peer_part, rows_per_rank);
 }
 
 // ------------------------------------------------------------------- peer-memory exchange

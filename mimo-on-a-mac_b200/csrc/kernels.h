@@ -156,11 +156,13 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* lo
                                  int E, cudaStream_t st, int32_t* status = nullptr);
 cudaError_t launch_router_topk(const float* logits, const float* bias, int T, int E, int topk,
                                int32_t* idx, float* weight, cudaStream_t st);
+// ready (optional): ready_n counters of the fused decode experts, zeroed by the last CTA.
 cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
-                                float* score, int32_t* status, cudaStream_t st, int fp4 = 0);
+                                float* score, int32_t* status, cudaStream_t st, int fp4 = 0,
+                                int32_t* ready = nullptr, int ready_n = 0);
 cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, int topk, int R,
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);

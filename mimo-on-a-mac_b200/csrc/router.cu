@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
     float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
     int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
-    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status, int fp4) {
+    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status, int fp4, int32_t* ready, int ready_n) {
   __shared__ float red[kRouteWarps][128];
   // e4m3 terms of x for the tensor-core expert path (token t -> rows t (hi) and 8 + t (lo)): 32-value
   // blocks spread evenly over the CTAs, split after the logits (off the critical path; in the last
@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     }
     *reinterpret_cast<__half2*>(x16 + i) = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
   }
+  for (int i = threadIdx.x; ready && i < ready_n; i += blockDim.x) ready[i] = 0;  // fused experts' counters
   if (threadIdx.x == 0) *counter = 0;
 }
 
@@ -359,13 +360,14 @@ cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const floa
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
                                 int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
-                                float* score, int32_t* status, cudaStream_t st, int fp4) {
+                                float* score, int32_t* status, cudaStream_t st, int fp4, int32_t* ready,
+                                int ready_n) {
   if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
   return launch_k(route_decode_kernel, dim3(E / 16), dim3(kRouteWarps * 32), 0, st, x, w, bias, T, H, E, topk, R,
                   logits, idx, wts, counter, uids, urows, ucnt, uw, gidx, num_unique, x16, xq, xs, score, status,
-                  fp4);
+                  fp4, ready, ready_n);
 }
 
 }  // namespace mimo
