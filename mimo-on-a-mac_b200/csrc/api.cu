@@ -262,6 +262,16 @@ int decode_kernel() {
 }
 bool decode_fp4() { return decode_kernel() == kDecodeFp4; }
 
+// Prefill expert kernels (MIMO_MOE_PREFILL_KERNEL, a comparison knob): "pair" runs each pass on SM
+// pairs with M = 256 tcgen05.mma.cta_group::2; "single" (default) on one SM per 128-row tile.
+bool prefill_pair() {
+  static const bool on = [] {
+    const char* e = getenv("MIMO_MOE_PREFILL_KERNEL");
+    return e && std::string(e) == "pair";
+  }();
+  return on;
+}
+
 
 // Gate/up + SwiGLU and down over units of up to `routes` routes, on the tensor cores.
 // Decode (routes 8): unit u's routes start at u * R, B rows come from rtok = urows, the down pass
@@ -278,6 +288,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   const bool decode = routes == kTcDecodeRoutes;
   const bool fp4 = decode && decode_fp4();
   const int N = (fp4 ? kTcFp4Terms : 2) * routes;  // term rows per unit (MMA N)
+  const bool pair = !decode && prefill_pair();     // prefill on SM pairs (256-row tiles)
   // by_token_rows = M > 0: B holds the M (<= 8) token rows once, shared by every unit (decode).
   if (!terms_ready) {
     if (fp4 && by_token_rows) MIMO_TRY(launch_tc_split_tokens_fp4(x, by_token_rows, H, t.bq, t.bs, status, st));
@@ -296,7 +307,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   } else {
     MIMO_TRY(fp4_weight_map(&p.amap[0], pools->gate_w, (uint64_t)S * I, H));
     MIMO_TRY(fp4_weight_map(&p.amap[1], pools->up_w, (uint64_t)S * I, H));
-    MIMO_TRY(rows_map(&p.bmap, t.bq, brows, H, N));
+    MIMO_TRY(rows_map(&p.bmap, t.bq, brows, H, pair ? N / 2 : N));  // pairs: half the term rows per CTA
   }
   MIMO_TRY(sf_map(&p.smap[0], pools->gate_s, (uint64_t)S * I, H / 32, 128));
   MIMO_TRY(sf_map(&p.smap[1], pools->up_s, (uint64_t)S * I, H / 32, 128));
@@ -305,7 +316,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.S = S;
   p.Nw = I;
   p.K = H;
-  p.tiles = I / 128;
+  p.tiles = I / (pair ? 256 : 128);
   p.unit_slot = uslot;
   p.unit_cnt = ucnt;
   p.unit_p0 = up0;
@@ -319,14 +330,15 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.hs = t.hs;
   p.status = status;
   const bool fused = decode && decode_kernel() != kDecodeE4m3;
-  if (!fused) MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
+  if (pair) MIMO_TRY(profiled(2, st, [&] { return launch_tc_pair(p, 2, sms, st); }));
+  else if (!fused) MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
   TcParams q = p;  // down: two K chunks per stage (3-D boxes, or two 2-D boxes when packed)
   if (fp4) {
     MIMO_TRY(packed64_map(&q.amap[0], pools->down_w, (uint64_t)S * H, I / 2, 128));
     MIMO_TRY(packed64_map(&q.bmap, t.hq, (uint64_t)ucap * N, I / 2, N));
   } else {
     MIMO_TRY(fp4_weight_map3(&q.amap[0], pools->down_w, (uint64_t)S * H, I, 2));
-    MIMO_TRY(rows_map3(&q.bmap, t.hq, (uint64_t)ucap * N, I, N, 2));
+    MIMO_TRY(rows_map3(&q.bmap, t.hq, (uint64_t)ucap * N, I, pair ? N / 2 : N, 2));
   }
   q.amap[1] = q.amap[0];
   MIMO_TRY(sf_map(&q.smap[0], pools->down_s, (uint64_t)S * H, I / 32, 128));
@@ -334,7 +346,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   MIMO_TRY(sf_map(&q.bsmap, t.hs, (uint64_t)ucap * N, I / 32, N));
   q.Nw = H;
   q.K = I;
-  q.tiles = H / 128;
+  q.tiles = H / (pair ? 256 : 128);
   q.btok = nullptr;
   q.hq = nullptr;
   q.hs = nullptr;
@@ -351,7 +363,8 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
     MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, fp4, sms, st); }));
     return MIMO_OK;
   }
-  MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
+  if (pair) MIMO_TRY(profiled(3, st, [&] { return launch_tc_pair(q, 3, sms, st); }));
+  else MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));
   return MIMO_OK;
 }
 

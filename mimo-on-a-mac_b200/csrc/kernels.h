@@ -123,6 +123,9 @@ cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms
 // kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (64 routes per
 // unit), 3: prefill down.
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
+// Prefill kinds 2 / 3 on SM pairs (clusters of two CTAs, tcgen05 cta_group::2): 256-row weight tiles
+// (tiles = Nw / 256) and term maps whose boxes hold half a unit's term rows (64).
+cudaError_t launch_tc_pair(const TcParams& p, int kind, int num_sms, cudaStream_t st);
 // Same splits into five e2m1 terms (kind::mxf4 decode): by-token rows (token t's term j at row
 // j * 8 + t), or per-unit rows (unit u, route q, term j at row u * 40 + j * 8 + q); K / 2 bytes a row.
 cudaError_t launch_tc_split_tokens_fp4(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,

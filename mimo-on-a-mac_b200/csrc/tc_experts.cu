@@ -31,6 +31,8 @@
 // The producer does its per-item work (coordinates, slot, row base) once per item: at decode sizes a
 // stage lasts ~600 cycles and the single issuing threads are the critical path.
 // Every wait is bounded; an expired wait sets MIMO_ETIMEOUT and the CTA drains and returns.
+#include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -65,6 +67,12 @@ constexpr int kBarBytes = 2048;   // barriers + TMEM slot, then 1 KiB alignment 
 #endif
 #ifndef MIMO_TC_EPI_PREFILL
 #define MIMO_TC_EPI_PREFILL 16  // epilogue warps of the prefill kernels
+#endif
+#ifndef MIMO_TC_PST2
+#define MIMO_TC_PST2 5  // ring depth of the paired prefill gate/up kernel
+#endif
+#ifndef MIMO_TC_PST3
+#define MIMO_TC_PST3 4  // ring depth of the paired prefill down kernel
 #endif
 #ifndef MIMO_TC_STF
 #define MIMO_TC_STF 5  // ring depth of the fused decode kernel, e4m3 activation terms
@@ -1076,6 +1084,434 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
   }
 }
 
+// ------------------------------------------------------------ prefill on SM pairs (cta_group::2)
+// The prefill passes on pairs of SMs.  A cluster of two CTAs takes one 256-row weight tile per item:
+// rows [0, 128) of the tile sit in CTA 0's shared memory and rows [128, 256) in CTA 1's, and the unit's
+// N = 128 activation-term rows are split in N between them (hi terms in CTA 0, lo terms in CTA 1).
+// CTA 0 issues tcgen05.mma.cta_group::2 with M = 256: each SM's tensor core multiplies its own 128
+// weight rows by all 128 term rows (it reads the other half of B from its peer) into its own TMEM.
+// Against the single-SM kernel, each MMA instruction does twice the work and each SM loads half as
+// many activation bytes per stage.  The B scale factors of all 128 term rows are kept in both CTAs'
+// TMEM (each CTA loads and builds them), the A scale factors of its own rows in each.
+// Barriers: each CTA's copies complete on its own stage `full` barrier; CTA 0's `full` also waits for
+// a 4-byte st.async from CTA 1's scale builder, sent once CTA 1's stage has landed and its scale blocks
+// are written (the asynchronous store releases at cluster scope without stalling the builder; a
+// remote mbarrier arrive held it ~1 us per stage and made it the pair's bottleneck).  The
+// accumulator's `acc_empty` lives in CTA 0 (CTA 1's epilogue warps arrive there remotely, once per
+// item); `empty`, `acc_full` and `drain` exist in both CTAs and CTA 0's issuers commit to both.
+// Every wait is bounded; both CTAs always reach the final cluster barrier.
+namespace pr {
+constexpr int kNB = kTcPrefillRoutes;  // term rows per CTA: N / 2
+constexpr int kN = 2 * kTcPrefillRoutes;
+template <int NM>
+constexpr int stage_bytes() { return 2 * kATile + kps<NM>() * kNB * kKC; }
+template <int NM>
+constexpr int scale_box_bytes() { return NM * kM * 16 + kN * 16; }
+template <int NM, int NSTAGE>
+constexpr int smem_bytes() {
+  return kBarBytes + 1024 + NSTAGE * stage_bytes<NM>() + 2 * scale_box_bytes<NM>() + NSTAGE * sf_block_bytes<NM>();
+}
+// kind::mxf8f6f4 block-scaled instruction descriptor for the pair: M = 256 (bits 24-28 hold M / 16).
+__device__ __forceinline__ uint32_t idesc_mx2(int n, uint32_t kb) {
+  return (idesc_mx(n, kb) & ~(0x1Fu << 24)) | ((uint32_t)(256 >> 4) << 24);
+}
+}  // namespace pr
+
+template <int NM, int NSTAGE, int MODE, int EPI>
+__global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_pair_kernel(const __grid_constant__ TcParams p) {
+  constexpr int NTOK = kTcPrefillRoutes;
+  constexpr int N = pr::kN;
+  constexpr int NB = pr::kNB;
+  constexpr int KPS = kps<NM>();
+  constexpr int SB = pr::stage_bytes<NM>();
+  constexpr int SCB = pr::scale_box_bytes<NM>();
+  constexpr int SFB = sf_block_bytes<NM>();
+  constexpr uint32_t TCOLS = 512;
+  constexpr int QH = NTOK / (EPI / 4);
+  constexpr int QC = QH < 16 ? QH : 16;
+  static_assert(2 * N + NSTAGE * 16 <= (int)TCOLS, "TMEM: one accumulator buffer + scale columns");
+  static_assert(EPI % 4 == 0 && NTOK % (EPI / 4) == 0 && QH % QC == 0, "epilogue split");
+  static_assert(NM * KPS == 2 && MODE != 1, "two slots per stage; prefill modes");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NSTAGE] own tiles landed (+ CTA 0: both scale builders)
+  uint64_t* empty = full + NSTAGE;                     // [NSTAGE] both issuers' MMAs of the stage done
+  uint64_t* sc_full = empty + NSTAGE;                  // [2] this CTA's scale boxes landed
+  uint64_t* sc_empty = sc_full + 2;                    // [2] scale boxes read
+  uint64_t* acc_full = sc_empty + 2;                   // accumulators written (both issuers)
+  uint64_t* acc_empty = acc_full + 1;                  // (CTA 0) both CTAs' epilogues copied them out
+  uint64_t* drain = acc_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint32_t* fwd = tmem_slot + 2;  // [NSTAGE] (CTA 0) words CTA 1's stage signals land in
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + kBarBytes) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stages = base;                 // NSTAGE x [2 A tiles | KPS B half-tiles]
+  uint8_t* scbox = stages + NSTAGE * SB;  // 2 x [NM x A scale box | B scale box]
+  uint8_t* sfblk = scbox + 2 * SCB;       // NSTAGE x [2 weight scale blocks | KPS activation blocks]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool lead = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], lead ? 2 : 1);  // own expect-tx arrival (+ CTA 0: its scale builder)
+      mbar_init(&empty[i], 2);  // one commit per issuer
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sc_full[b], 1);
+      mbar_init(&sc_empty[b], 1);
+    }
+    mbar_init(acc_full, 2);
+    mbar_init(acc_empty, 2 * EPI);
+    mbar_init(drain, 2);
+    *s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 3) {
+    tmem_alloc2(tmem_slot, TCOLS);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs before any remote use
+  tc_fence_after();
+  pdl_wait();  // the unit tables and activation terms come from the preceding kernel
+  pdl_launch_dependents();
+  const uint32_t tbase = *tmem_slot;
+  const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
+  const long long items = (long long)units * p.tiles;  // p.tiles: 256-row tiles per expert
+  const long long pair = cluster_id_x(), npairs = cluster_count_x();
+  const long long my_items = items > pair ? (items - pair + npairs - 1) / npairs : 0;
+  const int ns = p.K / (kKC * KPS);
+  const long long nsteps = my_items * ns;
+  const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // CTA 0's barriers, cluster addresses
+  const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
+  const uint32_t fwd0 = mapa_shared(smem_u32(fwd), 0);
+  constexpr uint32_t kSfCol0 = 2 * N;  // accumulator j at columns j * N
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_normal_policy();
+      for (int m = 0; m < NM; ++m) {
+        tma_prefetch_map(&p.amap[m]);
+        tma_prefetch_map(&p.smap[m]);
+      }
+      tma_prefetch_map(&p.bmap);
+      tma_prefetch_map(&p.bsmap);
+      int stage = 0;
+      uint32_t ph = 0;
+      long long issued = 0, groups = 0;
+      bool stop = false;
+      for (long long n = 0; n < my_items && !stop; ++n) {
+        const long long it = pair + n * npairs;
+        int unit, tile;
+        item_coords(p, it, unit, tile);
+        int slot = __ldg(p.unit_slot + unit);
+        if (slot < 0 || slot >= p.S) {
+          set_status(p.status, MIMO_ERANGE);
+          slot = 0;
+        }
+        const int row0 = slot * p.Nw + tile * (2 * kM) + (int)rank * kM;  // this CTA's 128 weight rows
+        const int brow = unit * N;                                       // the unit's term rows
+        for (int ks = 0; ks < ns; ++ks) {
+          if (*s_abort) {
+            stop = true;
+            break;
+          }
+          const int kc = ks * KPS;
+          if ((kc & 3) == 0) {  // scale boxes for chunks kc..kc+3: own weight rows, all term rows
+            const int e = (int)(groups & 1);
+            if (!mbar_wait(&sc_empty[e], (uint32_t)(((groups >> 1) & 1) ^ 1))) {
+              set_status(p.status, MIMO_ETIMEOUT);
+              *s_abort = 1;
+              stop = true;
+              break;
+            }
+            uint8_t* sc = scbox + e * SCB;
+            mbar_arrive_expect_tx(&sc_full[e], NM * kM * 16 + N * 16);
+            for (int m = 0; m < NM; ++m) tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0, &sc_full[e], pol);
+            tma_load_2d(sc + NM * kM * 16, &p.bsmap, kc * 4, brow, &sc_full[e], pol);
+            ++groups;
+          }
+          if (!mbar_wait(&empty[stage], ph ^ 1u)) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            stop = true;
+            break;
+          }
+          uint8_t* sb = stages + stage * SB;
+          // CTA 0's stage also waits for CTA 1's 4-byte signal (its tiles landed, scale blocks written).
+          mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * NB * kKC + (lead ? 4 : 0));
+          if constexpr (KPS == 1) {
+            tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol);
+            tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol);
+            tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow + (int)rank * NB, &full[stage], pol);
+          } else {
+            tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol);
+            tma_load_3d(sb + 2 * kATile, &p.bmap, 0, brow + (int)rank * NB, kc, &full[stage], pol);
+          }
+          ++issued;
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Shared memory must not be released with copies still landing.
+      bool ok = true;
+      for (long long k = 0; ok && k < (issued < NSTAGE ? issued : NSTAGE); ++k) {
+        const long long f = issued - 1 - k;
+        ok = mbar_wait(&full[(int)(f % NSTAGE)], (uint32_t)((f / NSTAGE) & 1));
+      }
+      for (long long k = 0; ok && k < (groups < 2 ? groups : 2); ++k) {
+        const long long g = groups - 1 - k;
+        ok = mbar_wait(&sc_full[(int)(g & 1)], (uint32_t)((g >> 1) & 1));
+      }
+      if (!ok) set_status(p.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------ scale-factor builder
+    // As in the single-SM kernel (this CTA's weight rows; all N term rows).  CTA 0's builder arrives on
+    // its own full barrier; CTA 1's first waits for its own stage to land, then arrives on CTA 0's.
+    int stage = 0;
+    uint32_t ph = 0;
+    for (long long s = 0; s < nsteps; ++s) {
+      if (*s_abort) break;
+      const uint32_t kc = (uint32_t)(s * KPS);
+      const int c = (int)(kc & 3);
+      const uint32_t g = kc >> 2;
+      const int e = (int)(g & 1);
+      if (c == 0 && !mbar_wait(&sc_full[e], (g >> 1) & 1)) {
+        if (lane == 0) set_status(p.status, MIMO_ETIMEOUT);
+        *s_abort = 1;
+        break;
+      }
+      if (!mbar_wait(&empty[stage], ph ^ 1u)) {
+        if (lane == 0) set_status(p.status, MIMO_ETIMEOUT);
+        *s_abort = 1;
+        break;
+      }
+      const uint8_t* sc = scbox + e * SCB;
+      uint8_t* blk = sfblk + stage * SFB;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int m = NM == 2 ? j : 0, cj = c + (KPS == 2 ? j : 0);
+        const uint8_t* box = sc + m * kM * 16 + cj * 4;
+        uint4 v;
+        v.x = *reinterpret_cast<const uint32_t*>(box + (lane + 0) * 16);
+        v.y = *reinterpret_cast<const uint32_t*>(box + (lane + 32) * 16);
+        v.z = *reinterpret_cast<const uint32_t*>(box + (lane + 64) * 16);
+        v.w = *reinterpret_cast<const uint32_t*>(box + (lane + 96) * 16);
+        *reinterpret_cast<uint4*>(blk + j * 512 + lane * 16) = v;
+      }
+#pragma unroll
+      for (int j = 0; j < KPS; ++j) {
+        const uint8_t* box = sc + NM * kM * 16 + (c + j) * 4;
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) w[q] = *reinterpret_cast<const uint32_t*>(box + (lane + 32 * q) * 16);
+        *reinterpret_cast<uint4*>(blk + (2 + j) * 512 + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (c + KPS == 4) mbar_arrive(&sc_empty[e]);
+        if (lead) {
+          mbar_arrive(&full[stage]);
+        } else if (mbar_wait(&full[stage], ph)) {
+          // A remote arrive blocked this thread ~1 us per stage; the asynchronous store does not.
+          st_async_signal(fwd0 + (uint32_t)stage * 4u, 1u, full0 + (uint32_t)stage * 8u);
+        } else {
+          set_status(p.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+        }
+      }
+      __syncwarp();
+      if (*s_abort) break;
+      if (++stage == NSTAGE) {
+        stage = 0;
+        ph ^= 1u;
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------------------ MMA issuers
+    // CTA 0 only.  Issuer j owns slot j of every stage (gate / up, or the stage's first / second K
+    // chunk of down) and accumulator j; its commits go to the barrier in each CTA.
+    const int j = warp - 2;
+    const uint32_t peer = 1u;
+    if (lead && lane == 0) {
+      const uint32_t empty_l = mapa_shared(smem_u32(empty), 0), empty_p = mapa_shared(smem_u32(empty), peer);
+      const uint32_t accf_l = mapa_shared(smem_u32(acc_full), 0), accf_p = mapa_shared(smem_u32(acc_full), peer);
+      int stage = 0;
+      uint32_t ph = 0;
+      bool aborted = false;
+      for (long long n = 0; n < my_items && !aborted; ++n) {
+        if (!mbar_wait_cluster(acc_empty, (uint32_t)(n & 1) ^ 1u)) {
+          set_status(p.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)j * N;
+        for (int ks = 0; ks < ns; ++ks) {
+          if (!mbar_wait_cluster(&full[stage], ph)) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sb = smem_u32(stages + stage * SB);
+          const uint32_t blk = smem_u32(sfblk + stage * SFB);
+          const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * 16 + 8 * j;
+          const int bj = KPS == 2 ? j : 0;
+          tc_cp_sf2(sf_col, desc_sf(blk + j * 512));
+          tc_cp_sf2(sf_col + 4, desc_sf(blk + (2 + bj) * 512));
+          const uint32_t a0 = sb + j * kATile, b0 = sb + 2 * kATile + bj * NB * kKC;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_mx2(d, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), pr::idesc_mx2(N, kk),
+                       sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30), (ks | kk) != 0);
+          tc_commit2(empty_l + (uint32_t)stage * 8u);
+          tc_commit2(empty_p + (uint32_t)stage * 8u);
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!aborted) {
+          tc_commit2(accf_l);
+          tc_commit2(accf_p);
+        }
+      }
+      // Nothing may still read either CTA's shared memory or TMEM when they are released.
+      tc_commit2(mapa_shared(smem_u32(drain), 0));
+      tc_commit2(mapa_shared(smem_u32(drain), peer));
+      if (!mbar_wait(drain, 0)) set_status(p.status, MIMO_ETIMEOUT);
+    } else if (!lead && warp == 2 && lane == 0) {
+      // CTA 1 waits for CTA 0's last MMAs, which read its shared memory and write its TMEM (CTA 0's
+      // issuers always commit to this barrier at their end).
+      if (!mbar_wait(drain, 0)) set_status(p.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------------------------------- epilogue
+    // This CTA's 128 weight rows of the item's tile, all routes (single accumulator buffer: copy the
+    // warp's columns out, release the accumulator to CTA 0's issuers, then compute).
+    const int quad = warp & 3;
+    const int qlo = ((warp - 4) >> 2) * QH;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    bool aborted = false;
+    for (long long n = 0; n < my_items; ++n) {
+      const long long it = pair + n * npairs;
+      int unit, tile;
+      item_coords(p, it, unit, tile);
+      const int slot = __ldg(p.unit_slot + unit);
+      const int cnt = min(__ldg(p.unit_cnt + unit), NTOK);
+      const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
+      if (!aborted && !mbar_wait(acc_full, (uint32_t)(n & 1))) {
+        set_status(p.status, MIMO_ETIMEOUT);
+        aborted = true;
+      }
+      tc_fence_after();
+      const bool live = !aborted && slot >= 0 && slot < p.S;
+      const int row = tile * (2 * kM) + (int)rank * kM + quad * 32 + lane;  // output feature of this lane
+      float hv[2][QH], lv[2][QH];
+      if (live) {
+#pragma unroll
+        for (int q0 = 0; q0 < QH; q0 += QC) {
+#pragma unroll
+          for (int a = 0; a < 2; ++a) {
+            float th[QC], tl[QC];
+            const uint32_t c = tbase + lane_base + (uint32_t)a * N + qlo + q0;
+            tmem_ld<QC>(c, th);
+            tmem_ld<QC>(c + NTOK, tl);
+#pragma unroll
+            for (int i = 0; i < QC; ++i) {
+              hv[a][q0 + i] = th[i];
+              lv[a][q0 + i] = tl[i];
+            }
+          }
+        }
+        tmem_wait_ld();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0);
+      if (!live) continue;
+#pragma unroll
+      for (int i = 0; i < QH; ++i) {
+        const int q = qlo + i;
+        if constexpr (MODE == 0) {
+          float h = 0.f;
+          if (q < cnt) {
+            h = swiglu_ref(hv[0][i] + lv[0][i], hv[1][i] + lv[1][i]);
+            if (!isfinite(h)) set_status(p.status, MIMO_ERANGE);
+          }
+          uint32_t th, tl, b1, b2;
+          split_warp_block(h, th, tl, b1, b2);
+          const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
+          p.hq[rh * p.Nw + row] = (uint8_t)th;
+          p.hq[rl * p.Nw + row] = (uint8_t)tl;
+          if (lane == 0) {
+            p.hs[rh * (p.Nw / 32) + row / 32] = (uint8_t)b1;
+            p.hs[rl * (p.Nw / 32) + row / 32] = (uint8_t)b2;
+          }
+        } else {
+          if (q < cnt) {
+            const float dsum = (hv[0][i] + lv[0][i]) + (hv[1][i] + lv[1][i]);  // each K half's hi + lo
+            p.ypair[(size_t)(p0 + q) * p.Nw + row] = (uint16_t)f32_to_bf16(dsum);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still reach its shared memory
+  if (warp == 3) {
+    tc_fence_after();
+    tmem_dealloc2(tbase, TCOLS);
+  }
+}
+
+// Pair kernels: clusters of two CTAs, as many clusters as can be resident at once.
+template <int NM, int NSTAGE, int MODE, int EPI>
+static cudaError_t launch_pair(const TcParams& p, int num_sms, cudaStream_t st) {
+  auto kfn = tc_pair_kernel<NM, NSTAGE, MODE, EPI>;
+  constexpr int smem = pr::smem_bytes<NM, NSTAGE>();
+  static_assert(smem <= 232448, "shared memory budget");
+  static_assert((2 * NSTAGE + 4 + 3) * 8 + 8 + NSTAGE * 4 <= kBarBytes, "barrier area");
+  if (p.K % (4 * kKC) != 0 || p.Nw % (2 * kM) != 0 || p.tiles != p.Nw / (2 * kM)) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3((4 + EPI) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  static int nc = 0;
+  if (nc <= 0) {
+    cfg.gridDim = dim3(num_sms & ~1);
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kfn, &cfg);
+    if (e != cudaSuccess) return e;
+    nc = n > 0 ? std::min(n, num_sms / 2) : num_sms / 2;
+    const char* o = getenv("MIMO_MOE_PAIR_CLUSTERS");  // comparison knob: fewer resident clusters
+    if (o && atoi(o) > 0) nc = std::min(nc, atoi(o));
+    if (getenv("MIMO_MOE_VERBOSE")) fprintf(stderr, "[mimo_moe] pair kernel NM=%d: %d clusters (occupancy %d)\n", NM, nc, n);
+  }
+  cfg.gridDim = dim3(2 * nc);
+  return cudaLaunchKernelEx(&cfg, kfn, p);
+}
+
 template <int NM, int NTOK, int NSTAGE, int MODE, int EPI>
 static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   auto kfn = tc_expert_kernel<NM, NTOK, NSTAGE, MODE, EPI>;
@@ -1229,6 +1665,14 @@ static cudaError_t launch_fused(const TcFusedParams& f, int num_sms, cudaStream_
 
 cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms, cudaStream_t st) {
   return fp4 ? launch_fused<MIMO_TC_STF4, true>(f, num_sms, st) : launch_fused<MIMO_TC_STF, false>(f, num_sms, st);
+}
+
+cudaError_t launch_tc_pair(const TcParams& p, int kind, int num_sms, cudaStream_t st) {
+  switch (kind) {
+    case 2: return tc::launch_pair<2, MIMO_TC_PST2, 0, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
+    case 3: return tc::launch_pair<1, MIMO_TC_PST3, 2, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st) {

@@ -43,6 +43,42 @@ __device__ __forceinline__ void tc_mma_mx(uint32_t d_taddr, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_taddr), "r"(sfb_taddr)
       : "memory");
 }
+// ---- CTA pairs (cta_group::2): a cluster of two CTAs whose tensor cores run one M = 256 MMA together.
+// Both CTAs allocate (the same warp in each) and free; CTA 0 (the leader) issues the copies, MMAs and
+// commits, which act on both CTAs' shared memory and TMEM at the same addresses.
+__device__ __forceinline__ void tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrives on the barrier at cluster address `bar` (this CTA's or the peer's) once the pair's tcgen05
+// operations this thread issued before have completed.
+__device__ __forceinline__ void tc_commit2(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+// Scale-factor copy in both CTAs: each CTA's 512-byte block at `sdesc` into its own TMEM columns.
+__device__ __forceinline__ void tc_cp_sf2(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// M = 256 block-scaled MMA over the pair: each CTA's 128 A rows x all N columns (half of B from each
+// CTA's shared memory) into its own TMEM.
+__device__ __forceinline__ void tc_mma_mx2(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t sfa_taddr, uint32_t sfb_taddr, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(
+          d_taddr),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_taddr), "r"(sfb_taddr)
+      : "memory");
+}
 template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[NC]);
 template <>

@@ -1,0 +1,65 @@
+"""Prefill expert kernels on SM pairs (MIMO_MOE_PREFILL_KERNEL, read once per process, so each variant
+runs in a child process):
+
+  single  (default) one CTA per 128-row weight tile, tcgen05.mma.cta_group::1 (M = 128);
+  pair    clusters of two CTAs, 256-row weight tiles, tcgen05.mma.cta_group::2 (M = 256).
+
+Each SM of a pair computes its own 128 weight rows against all of the unit's term rows with the same
+K blocks and scales as the single-SM kernel, so the block outputs agree within the oracle bar
+(engine/tests/test_kernels.py:54-56) and nearly all bf16 outputs are identical."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import PKG_DIR, ROOT
+
+pytestmark = pytest.mark.gpu
+
+CHILD = r"""
+import sys, numpy as np, torch
+sys.path[:0] = [{root!r}, {pkg!r}]
+import mimo_moe
+from oracle import synth
+dev = torch.device("cuda", 0)
+pool = mimo_moe.ExpertPools.synthetic({S}, seed=0, layer=3, device=dev)
+W = synth.router_weight(E={S}).to(dev)
+status = torch.zeros(1, dtype=torch.int32, device=dev)
+out = []
+for T in {Ts}:
+    x = synth.hidden(T, seed=90 + T).to(dev)
+    y = mimo_moe.moe_block(x, W, None, pool, status=status)
+    out.append(y.view(torch.int16).cpu().numpy())
+torch.cuda.synchronize()
+assert int(status.item()) == 0, int(status.item())
+np.savez({path!r}, *out)
+"""
+TS = [9, 64, 600]
+
+
+def _run(tmp_path, S, kernel):
+    path = str(tmp_path / f"{kernel}_{S}.npz")
+    env = dict(os.environ, MIMO_MOE_PREFILL_KERNEL=kernel)
+    code = CHILD.format(root=str(ROOT), pkg=str(PKG_DIR), S=S, Ts=TS, path=path)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    z = np.load(path)
+    return [z[f"arr_{i}"] for i in range(len(TS))]
+
+
+@pytest.mark.parametrize("S", [32, 256])
+def test_pair_prefill_agrees_with_single_sm(gpu, tmp_path, S):
+    single = _run(tmp_path, S, "single")
+    pair = _run(tmp_path, S, "pair")
+    for T, a, b in zip(TS, single, pair):
+        fa = torch.from_numpy(a).view(torch.bfloat16).float().numpy()
+        fb = torch.from_numpy(b).view(torch.bfloat16).float().numpy()
+        assert np.isfinite(fb).all(), T
+        rel = np.abs(fa - fb).max() / np.abs(fa).max()
+        same = (a == b).mean()
+        print(f"T={T} S={S}: rel_err {rel:.2e}, identical {same:.4f}")
+        assert rel <= 1e-2, (T, rel)
+        assert same >= 0.99, (T, same)
