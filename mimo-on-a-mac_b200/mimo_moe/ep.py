@@ -230,11 +230,13 @@ class ExpertParallelPrefill:
     every rank.  One step:
 
       1. route the rank's own T tokens (model.py:58-65);
-      2. dispatch: routes sorted by destination rank (stable), per-destination counts exchanged, then
-         one all-to-all of the routes' token rows and local expert ids (variable splits; the counts
-         cross to the host once per step, acceptable at prefill sizes);
-      3. expert side: per-route bf16 products of the received routes (`moe_prefill` with one route per
-         row and weight 1, which returns each route's bf16 pair output unchanged, model.py:221-228);
+      2. dispatch: routes sorted by destination rank (stable); each token row travels once to every
+         rank that owns one of its experts, with a (row, local expert id) tag per route; the counts
+         of routes and rows per destination are exchanged first (they cross to the host once per
+         step, acceptable at prefill sizes), then one all-to-all of the rows and one of the tags;
+      3. expert side: the received routes' rows gathered from the received token rows, per-route bf16
+         products (`moe_prefill` with one route per row and weight 1, which returns each route's bf16
+         pair output unchanged, model.py:221-228);
       4. return: the inverse all-to-all;
       5. combine: y[t] = bf16(sum over k in order of fp32(out[t, k]) * w[t, k]) (model.py:266-271).
 
@@ -264,22 +266,41 @@ class ExpertParallelPrefill:
         idx, w = self.router_fn(x)
         idx = idx.to(torch.int32).reshape(-1)
         w = w.to(torch.float32).contiguous()
+        P = idx.numel()
         dest = (idx // self.per_rank).to(torch.int64)
         order = torch.sort(dest, stable=True).indices            # send position -> route t*k + j
         inv = torch.empty_like(order)
-        inv[order] = torch.arange(order.numel(), device=dev)     # route -> send position
+        inv[order] = torch.arange(P, device=dev)                 # route -> send position
+        d_s, t_s = dest[order], order // k
+        # Within a destination, routes keep route order, so a token's routes there are adjacent: the
+        # first of them sends the token's row, every route carries that row's index in the segment.
+        new = torch.ones(P, dtype=torch.bool, device=dev)
+        if P > 1:
+            new[1:] = (d_s[1:] != d_s[:-1]) | (t_s[1:] != t_s[:-1])
         send_counts = torch.bincount(dest, minlength=N).to(torch.int64)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()      # the step's one host crossing
+        row_counts = torch.bincount(d_s[new], minlength=N).to(torch.int64)
+        row_first = torch.cumsum(row_counts, 0) - row_counts
+        row_in_seg = (torch.cumsum(new.to(torch.int64), 0) - 1) - row_first[d_s]
+        counts = torch.stack([send_counts, row_counts], 1)      # [N, 2]: routes, rows per destination
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        sc, rows_sc = send_counts.tolist(), row_counts.tolist()  # the step's one host crossing
+        rc, rows_rc = recv_counts[:, 0].tolist(), recv_counts[:, 1].tolist()
         self.routes_received += sum(rc)
-        send_x = x[order // k].contiguous()
-        send_e = (idx[order] - dest[order].to(torch.int32) * self.per_rank).to(torch.int32).contiguous()
-        recv_x = torch.empty(sum(rc), H, dtype=x.dtype, device=dev)
-        recv_e = torch.empty(sum(rc), dtype=torch.int32, device=dev)
-        dist.all_to_all_single(recv_x, send_x, rc, sc, group=self.group)
-        dist.all_to_all_single(recv_e, send_e, rc, sc, group=self.group)
-        out = self.pairs_fn(recv_x, recv_e) if recv_x.shape[0] else torch.empty(0, H, dtype=x.dtype, device=dev)
+        send_x = x[t_s[new]].contiguous()
+        send_tag = torch.stack([row_in_seg.to(torch.int32),
+                                idx[order] - d_s.to(torch.int32) * self.per_rank], 1).contiguous()
+        recv_rows = torch.empty(sum(rows_rc), H, dtype=x.dtype, device=dev)
+        recv_tag = torch.empty(sum(rc), 2, dtype=torch.int32, device=dev)
+        dist.all_to_all_single(recv_rows, send_x, rows_rc, rows_sc, group=self.group)
+        dist.all_to_all_single(recv_tag, send_tag, rc, sc, group=self.group)
+        if recv_tag.shape[0]:
+            rrc = torch.tensor(rows_rc, dtype=torch.int64, device=dev)
+            src = torch.repeat_interleave(torch.arange(N, device=dev), torch.tensor(rc, device=dev))
+            rows = (torch.cumsum(rrc, 0) - rrc)[src] + recv_tag[:, 0].to(torch.int64)
+            out = self.pairs_fn(recv_rows[rows].contiguous(), recv_tag[:, 1].contiguous())
+        else:
+            out = torch.empty(0, H, dtype=x.dtype, device=dev)
         back = torch.empty(sum(sc), H, dtype=out.dtype, device=dev)
         dist.all_to_all_single(back, out.contiguous(), sc, rc, group=self.group)
         return self.combine_fn(back, inv.to(torch.int32), w, T, k)

@@ -112,13 +112,23 @@ def _combine_pairs(back, inv, w, T_, k):
     return y.to(torch.bfloat16)
 
 
-def _prefill_worker(rank, world, port, out):
+def _clustered_router(x: torch.Tensor):
+    """Routes that share ranks: even tokens send all K routes to rank 0's experts, odd tokens two of
+    them to rank 1's (so one token row serves several routes on the receiving rank)."""
+    idx, w = _router(x)
+    for t in range(idx.shape[0]):
+        idx[t] = torch.tensor([0, 2, 3] if t % 2 == 0 else [5, 1, 7], dtype=idx.dtype)[:K]
+    return idx, w
+
+
+def _prefill_worker(rank, world, port, out, clustered=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from mimo_moe.ep import ExpertParallelPrefill, expert_range
         lo, _ = expert_range(rank, world, E)
-        blk = ExpertParallelPrefill(None, None, None, num_experts=E, topk=K, router_fn=_router,
+        blk = ExpertParallelPrefill(None, None, None, num_experts=E, topk=K,
+                                    router_fn=_clustered_router if clustered else _router,
                                     pairs_fn=_pairs(lo), combine_fn=_combine_pairs)
         # rank 1 routes no tokens in the second call: empty splits both ways
         for n in (T, T if rank == 0 else 0):
@@ -129,14 +139,16 @@ def _prefill_worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_ep_prefill_all_to_all_matches_single_process():
+@pytest.mark.parametrize("clustered", [False, True])
+def test_ep_prefill_all_to_all_matches_single_process(clustered):
+    """Each token row crosses once per destination rank and serves all of its routes there."""
     world = 2
     port = _free_port()
     out = mp.Manager().dict()
-    mp.start_processes(_prefill_worker, args=(world, port, out), nprocs=world, start_method="spawn")
+    mp.start_processes(_prefill_worker, args=(world, port, out, clustered), nprocs=world, start_method="spawn")
     for rank in range(world):
         x = _tokens(rank)
-        idx, w = _router(x)
+        idx, w = (_clustered_router if clustered else _router)(x)
         ref = _combine(_experts(0, E)(x, idx, w, True), T, K)
         got = np.frombuffer(out[(rank, T)], dtype=np.float32).reshape(T, H)
         assert np.array_equal(got, ref.float().numpy()), rank
