@@ -50,6 +50,35 @@ def peaks():
         return 6650.0, 1400.0, "fallback"
 
 
+def tensor_peaks(dev) -> dict:
+    """Dense block-scaled tensor peaks of this GPU measured by the library's own probe
+    (mimo_moe_tensor_peak): kind::mxf8f6f4 with e2m1 x e4m3 operands (the expert kernels' MMA form)
+    and kind::mxf4 (e2m1 x e2m1, the FP4 rate); best of three 4000-step launches after one warm-up."""
+    import ctypes
+    import torch
+    import mimo_moe
+    L = mimo_moe.lib()
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    out = {}
+    for kind, name in ((0, "mxf8f6f4"), (1, "mxf4")):
+        best = 0.0
+        for rep in range(4):
+            t = ctypes.c_float(0.0)
+            _lib_check(L.mimo_moe_tensor_peak(kind, 4000, ctypes.byref(t), status.data_ptr(), stream), "tensor_peak")
+            if rep:
+                best = max(best, float(t.value))
+        out[name] = best
+    if int(status.item()) != 0:
+        raise RuntimeError(f"device status {int(status.item())} in the tensor peak probe")
+    return out
+
+
+def _lib_check(rc, what):
+    from mimo_moe import _lib
+    _lib.check(rc, what)
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -549,6 +578,12 @@ def main():
                                  "run at the fp8 rate, nominally 2x)",
                     "traffic": None, "algorithmic_flops_per_launch": flops,
                     "weight_gbs": gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0}
+        # the library's own tcgen05 probe: the MMA form these kernels run (two e4m3 terms per activation,
+        # so algorithmic FLOPs are half the executed ones) and the FP4 rate the survey's target names
+        tp = tensor_peaks(dev)
+        roofline["measured_tensor_tflops"] = tp
+        roofline["frac_of_measured_mxf8f6f4"] = tf / tp["mxf8f6f4"] if tp["mxf8f6f4"] > 0 else None
+        roofline["frac_of_measured_mxf4"] = tf / tp["mxf4"] if tp["mxf4"] > 0 else None
     roofline["kernel_ms"] = {"fused": fz_ms} if launches[0][4] > 0 else {"gate_up": gu_ms, "down": dn_ms}
     expert_gbs = sum(steps_U) * EXPERT_BYTES / (ms * 1e-3) / 1e9
 

@@ -251,6 +251,16 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
 int mimo_moe_profile_enable(int32_t capacity);
 int mimo_moe_profile_read(int32_t* launches, float* milliseconds);
 
+/*
+ * Benchmark support (no counterpart in the reference).  Measures this GPU's dense block-scaled tensor
+ * peak for an MMA form the expert kernels use: kind 0 = tcgen05.mma.kind::mxf8f6f4 (e2m1 weights x
+ * e4m3 activations, the expert kernels' form), kind 1 = kind::mxf4 (e2m1 x e2m1, the FP4 rate).  One
+ * CTA per SM issues `iters` x (M 128, N 256, K 128) MMAs on operands held in shared memory; the launch
+ * is timed with CUDA events on `stream` and synchronised.  *tflops receives 2*M*N*K*iters*SMs / time.
+ * status: device int32 word (MIMO_ETIMEOUT if the final wait expired).
+ */
+int mimo_moe_tensor_peak(int32_t kind, int32_t iters, float* tflops, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -822,6 +822,26 @@ int mimo_moe_profile_enable(int32_t capacity) {
   return MIMO_OK;
 }
 
+int mimo_moe_tensor_peak(int32_t kind, int32_t iters, float* tflops, int32_t* status, void* stream) {
+  if ((kind != 0 && kind != 1) || iters < 1 || iters > (1 << 24) || !tflops || !status) return MIMO_EINVAL;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = num_sms_current();
+  cudaEvent_t a = nullptr, b = nullptr;
+  MIMO_TRY(cudaEventCreate(&a));
+  cudaError_t e = cudaEventCreate(&b);
+  if (e == cudaSuccess) e = cudaEventRecord(a, st);
+  if (e == cudaSuccess) e = launch_tc_peak(kind, iters, sms, status, st);
+  if (e == cudaSuccess) e = cudaEventRecord(b, st);
+  if (e == cudaSuccess) e = cudaEventSynchronize(b);
+  float ms = 0.f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  if (b) cudaEventDestroy(b);
+  if (e != cudaSuccess) return MIMO_ECUDA;
+  *tflops = ms > 0.f ? (float)(2.0 * 128 * 256 * 128 * (double)iters * sms / (ms * 1e-3) / 1e12) : 0.f;
+  return MIMO_OK;
+}
+
 int mimo_moe_profile_read(int32_t* launches, float* milliseconds) {
   if (!launches || !milliseconds) return MIMO_EINVAL;
   std::lock_guard<std::mutex> lk(g_prof_mu);

@@ -68,6 +68,7 @@ SIGNATURES = {
                                           c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "mimo_moe_profile_enable": (c_int32, [c_int32]),
     "mimo_moe_profile_read": (c_int32, [c_void_p, c_void_p]),
+    "mimo_moe_tensor_peak": (c_int32, [c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "mimo_moe_fill_synthetic_pool": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                                c_void_p, c_int32, c_int32, c_int32, c_uint64, c_int32,
                                                c_int32, c_void_p]),
