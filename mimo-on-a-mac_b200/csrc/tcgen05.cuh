@@ -207,6 +207,19 @@ __device__ __forceinline__ float e4m3_to_f32(uint32_t b) {  // exact (every e4m3
   asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(h2) : "h"(in));
   return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
 }
+// Two values at once: byte 0 = e4m3(lo), byte 1 = e4m3(hi) (RNE, saturating), and back (exact).
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(hi), "f"(lo));
+  return (uint32_t)r;
+}
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t b2) {
+  uint32_t h2;
+  const uint16_t in = (uint16_t)b2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;\n" : "=r"(h2) : "h"(in));
+  return make_float2(__half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu))),
+                     __half2float(__ushort_as_half((unsigned short)(h2 >> 16))));
+}
 // ue8m0 byte of a block whose largest magnitude is amax: 2^(e(amax) - 7), so |v| / s < 256 <= 448.
 __device__ __forceinline__ uint32_t block_scale_byte(float amax) {
   if (!(amax > 0.f)) return 127u;
@@ -246,16 +259,20 @@ __device__ __forceinline__ void split_block32(const uint16_t* src, uint8_t* dh, 
   const uint32_t b1 = block_scale_byte(amax);
   uint32_t hw[8] = {0, 0, 0, 0, 0, 0, 0, 0}, lw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   float r[32], rmax = 0.f;
+  // Pairs of values per conversion (e4m3x2 / f16x2 forms): the same per-element roundings as one at a time.
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const uint32_t e = f32_to_e4m3(v[i] * inv_exp2_byte(b1));
-    r[i] = v[i] - e4m3_to_f32(e) * exp2_byte(b1);
-    rmax = fmaxf(rmax, fabsf(r[i]));
-    hw[i >> 2] |= e << (8 * (i & 3));
+  for (int i = 0; i < 32; i += 2) {
+    const uint32_t e2 = f32x2_to_e4m3x2(v[i] * inv_exp2_byte(b1), v[i + 1] * inv_exp2_byte(b1));
+    const float2 q = e4m3x2_to_f32x2(e2);
+    r[i] = v[i] - q.x * exp2_byte(b1);
+    r[i + 1] = v[i + 1] - q.y * exp2_byte(b1);
+    rmax = fmaxf(rmax, fmaxf(fabsf(r[i]), fabsf(r[i + 1])));
+    hw[i >> 2] |= e2 << (8 * (i & 3));
   }
   const uint32_t b2 = block_scale_byte(rmax);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) lw[i >> 2] |= f32_to_e4m3(r[i] * inv_exp2_byte(b2)) << (8 * (i & 3));
+  for (int i = 0; i < 32; i += 2)
+    lw[i >> 2] |= f32x2_to_e4m3x2(r[i] * inv_exp2_byte(b2), r[i + 1] * inv_exp2_byte(b2)) << (8 * (i & 3));
   uint4* h4 = reinterpret_cast<uint4*>(dh);
   uint4* l4 = reinterpret_cast<uint4*>(dl);
   h4[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
