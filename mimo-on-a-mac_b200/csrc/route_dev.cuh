@@ -44,8 +44,11 @@ __device__ __forceinline__ void topk_warp_impl(const float* row, const float* bi
       sv[j] = 0.f;
     }
   }
-  // Branch-free selection: candidate keys as (order-preserving bits of sel, ~id) pairs, so "larger
-  // sel, then smaller id" is a lexicographic maximum; each round takes two warp max-reductions.
+  // Candidate keys as (order-preserving bits of sel, ~id) pairs, so "larger sel, then smaller id" is a
+  // lexicographic maximum.  Each lane sorts its 8 candidates once (Batcher's 19-comparator network,
+  // descending); a round then takes the warp maximum of the lanes' heads — one redux.sync on the
+  // high words and a ballot, a second redux only when heads tie on sel — and the winning lane drops
+  // its head.  Same selection order as scanning all candidates every round.
   uint32_t kh[kMaxPer], kl[kMaxPer];
 #pragma unroll
   for (int j = 0; j < kMaxPer; ++j) {
@@ -53,31 +56,47 @@ __device__ __forceinline__ void topk_warp_impl(const float* row, const float* bi
     kh[j] = j < per ? ((u >> 31) ? ~u : (u | 0x80000000u)) : 0u;  // valid keys are > 0 (-inf -> 0x007FFFFF)
     kl[j] = j < per ? ~(uint32_t)(lane + 32 * j) : 0u;
   }
+  auto cx = [&](int a, int b) {  // keep the larger key at a
+    const bool sw = kh[b] > kh[a] || (kh[b] == kh[a] && kl[b] > kl[a]);
+    const uint32_t h = sw ? kh[b] : kh[a], l = sw ? kl[b] : kl[a];
+    const float v = sw ? sv[b] : sv[a];
+    kh[b] = sw ? kh[a] : kh[b];
+    kl[b] = sw ? kl[a] : kl[b];
+    sv[b] = sw ? sv[a] : sv[b];
+    kh[a] = h;
+    kl[a] = l;
+    sv[a] = v;
+  };
+  cx(0, 1); cx(2, 3); cx(4, 5); cx(6, 7);
+  cx(0, 2); cx(1, 3); cx(4, 6); cx(5, 7);
+  cx(1, 2); cx(5, 6);
+  cx(0, 4); cx(1, 5); cx(2, 6); cx(3, 7);
+  cx(2, 4); cx(3, 5);
+  cx(1, 2); cx(3, 4); cx(5, 6);
   float tot = 0.f, my_s = 0.f;
   int my_id = 0;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     if (r < topk) {
-      uint32_t bh = 0u, bl = 0u;
-#pragma unroll
-      for (int j = 0; j < kMaxPer; ++j) {
-        const bool better = kh[j] > bh || (kh[j] == bh && kl[j] > bl);
-        bh = better ? kh[j] : bh;
-        bl = better ? kl[j] : bl;
+      const uint32_t wh = __reduce_max_sync(0xFFFFFFFFu, kh[0]);
+      uint32_t m = __ballot_sync(0xFFFFFFFFu, kh[0] == wh);
+      if (__popc(m) > 1) {  // warp-uniform: heads tie on sel, the larger ~id (smaller id) wins
+        const uint32_t wl = __reduce_max_sync(0xFFFFFFFFu, kh[0] == wh ? kl[0] : 0u);
+        m = __ballot_sync(0xFFFFFFFFu, kh[0] == wh && kl[0] == wl);
       }
-      const uint32_t wh = __reduce_max_sync(0xFFFFFFFFu, bh);
-      const uint32_t wl = __reduce_max_sync(0xFFFFFFFFu, bh == wh ? bl : 0u);
-      const int bid = (int)~wl;
-      const int owner = bid & 31, jw = bid >> 5;
-      float s_own = 0.f;
+      const int owner = __ffs(m) - 1;
+      const int bid = (int)~__shfl_sync(0xFFFFFFFFu, kl[0], owner);
+      const float bs = __shfl_sync(0xFFFFFFFFu, sv[0], owner);
+      if (lane == owner) {
 #pragma unroll
-      for (int j = 0; j < kMaxPer; ++j) {
-        const bool hit = (j == jw) && (lane == owner);
-        s_own = hit ? sv[j] : s_own;
-        kh[j] = hit ? 0u : kh[j];
-        kl[j] = hit ? 0u : kl[j];
+        for (int j = 0; j < kMaxPer - 1; ++j) {
+          kh[j] = kh[j + 1];
+          kl[j] = kl[j + 1];
+          sv[j] = sv[j + 1];
+        }
+        kh[kMaxPer - 1] = 0u;
+        kl[kMaxPer - 1] = 0u;
       }
-      const float bs = __shfl_sync(0xFFFFFFFFu, s_own, owner);
       tot = __fadd_rn(tot, bs);
       if (lane == r) {
         my_s = bs;
