@@ -139,10 +139,10 @@ def _prefill_worker(rank, world, port, out, clustered=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("clustered", [False, True])
-def test_ep_prefill_all_to_all_matches_single_process(clustered):
-    """Each token row crosses once per destination rank and serves all of its routes there."""
-    world = 2
+@pytest.mark.parametrize("world,clustered", [(2, False), (2, True), (4, False), (4, True)])
+def test_ep_prefill_all_to_all_matches_single_process(world, clustered):
+    """Each token row crosses once per destination rank and serves all of its routes there (world 4:
+    two experts per rank, uneven splits, ranks that send nothing to some peers)."""
     port = _free_port()
     out = mp.Manager().dict()
     mp.start_processes(_prefill_worker, args=(world, port, out, clustered), nprocs=world, start_method="spawn")
