@@ -1,13 +1,17 @@
-"""Benchmark of the B200 MiMo MoE block (BASELINE.json metric: MoE-layer tok/s + expert HBM GB/s).
+"""Benchmark of the B200 MiMo MoE block (BASELINE.json metric: MoE-layer tok/s, decode 1-8 rows and prefill
+2k, + expert HBM GB/s against the measured peak).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode8|decode4|decode2|decode1|prefill2048|prefill16384z]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
   python bench.py --workload stack48_decode8 [--layers L]   # config 3: a 48-layer decode stack
-  python bench.py --impl reference ...     # the reference path's CPU restatement on the host cores
+  python bench.py --impl reference ...     # the reference path on the host cores (no GPU)
 
 One step = one MoE layer (router -> dispatch -> MXFP4 experts -> combine) over one batch of synthetic
-tokens, inputs resident in HBM.  Default workload: BASELINE config 1 at B = 8 rows (decode / MTP
-verify), free routing, 256 experts of 13,369,344 B.  Routes rotate over 16 seeded batches, so each step
-streams ~0.77 GB of experts chosen from a 3.42 GB pool (inputs > the 126 MB L2).
+tokens, inputs resident in HBM.  The default run prints ONE JSON line: the headline workload (BASELINE
+config 1 at B = 8 rows, decode / MTP verify, free routing, 256 experts of 13,369,344 B) and, on one GPU,
+nested results under "configs" for the other configurations the metric names: decode1 (config 0),
+decode8_overlap (config 1's forced-overlap variant: rows share experts) and prefill2048 (config 2), each
+with its own roofline, end-to-end number and CPU baseline.  Decode routes rotate over 16 seeded batches,
+so each step streams experts chosen from a 3.42 GB pool (inputs > the 126 MB L2).
 """
 from __future__ import annotations
 
@@ -29,15 +33,18 @@ H, I, E, K_TOP = 4096, 2048, 256, 8
 EXPERT_BYTES = 3 * (I * H // 2 + I * H // 32)      # 13,369,344
 GATEUP_BYTES = 2 * (I * H // 2 + I * H // 32)      # per distinct expert, kernel A
 DOWN_BYTES = H * I // 2 + H * I // 32
-WORKLOADS = {"decode1": 1, "decode2": 2, "decode4": 4, "decode8": 8, "prefill2048": 2048, "prefill16384z": 16384,
-             "stack48_decode1": 1, "stack48_decode8": 8}
+# workload -> (tokens per GPU, routing)
+WORKLOADS = {"decode1": (1, "free"), "decode2": (2, "free"), "decode4": (4, "free"), "decode8": (8, "free"),
+             "decode8_overlap": (8, "overlap"), "prefill2048": (2048, "free"), "prefill16384z": (16384, "zipf"),
+             "stack48_decode1": (1, "free"), "stack48_decode8": (8, "free")}
+NESTED = ("decode1", "decode8_overlap", "prefill2048")   # measured beside the default headline on one GPU
 STACK_LAYERS = 48  # config 3: 48 MoE layers (~164 GB of experts), RMSNorm (unit weight) between layers
 # config 4: Zipf(1.1)-biased routing, bias_e = c * log(p_e * E); c = 0.055 puts the most loaded
 # expert at ~10x the mean load on the seeded 16384-token batch (tuned once on the CPU router)
 ZIPF_C = 0.055
 NBATCH = 16
-# DRAM bytes of one decode gate/up launch per distinct expert, from one ncu capture
-# (profiles/tc_expert_kernel_decode8_traffic.md): 1.005x the algorithmic 8,912,896
+# DRAM bytes of one decode gate/up launch per distinct expert, from an ncu capture of the decode8 workload
+# (dram__bytes_read.sum + dram__bytes_write.sum / distinct experts): 1.005x the algorithmic 8,912,896
 GATEUP_TRAFFIC_PER_EXPERT = 8_957_075
 
 
@@ -124,100 +131,464 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons)}
 
 
-def make_inputs(B, dev, torch, rank=0):
+# ------------------------------------------------------------------------------------ workloads
+def routing_bias(workload: str, NE: int = E):
+    """Router bias of a workload (float32 [NE], CPU): free routing, the forced-overlap variant of config 1
+    (+beta on a seeded hot subset, so consecutive rows share experts) or config 4's Zipf skew."""
+    import torch
     from mimo_moe import synthetic
-    xs = [synthetic.hidden(B, seed=2 + 1000 * i + 100000 * rank).to(dev) for i in range(NBATCH)]
-    W = synthetic.router_weight().to(dev)
-    return xs, W
+    routing = WORKLOADS[workload][1]
+    if routing == "zipf":
+        return synthetic.zipf_bias(E=NE, c=ZIPF_C)
+    if routing == "overlap":
+        return synthetic.overlap_bias(E=NE)
+    return torch.zeros(NE, dtype=torch.float32)
 
 
-def _host_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        return max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        return 1
+def routing_text(workload: str) -> str:
+    return {"free": "free (bias 0)", "overlap": "forced overlap (overlap_bias: +0.05 on 24 seeded experts)",
+            "zipf": f"Zipf(1.1) bias, c={ZIPF_C}"}[WORKLOADS[workload][1]]
 
 
-def cpu_reference_rate(B, budget_s, seed_batch=0):
-    """The reference path on the host cores, on a bounded sample of one decode batch of B <= 8 rows:
-    the reference's own kernels A/B (engine/mimo_stream/kernels.py:33-123, compiled for the CPU into
-    oracle/_ref with OpenMP) and its own group_routes; the router rule (model.py:58-65, MLX on the
-    reference's side) and the fixed-order combine restated in numpy.  The batch's distinct experts are
-    processed one at a time until `budget_s` is spent (at least one) and the batch time is
-    extrapolated by U / k.  Expert bytes are generated before each expert's clock starts.  Without
-    oracle/_ref the numpy restatement of the same path is timed instead (kind "port")."""
+def batches(workload: str, rank: int = 0):
+    """The seeded token batches a workload's steps rotate over (bf16, CPU): 16 for decode, 2 for prefill."""
+    from mimo_moe import synthetic
+    T = WORKLOADS[workload][0]
+    n = NBATCH if T <= 8 else 2
+    return [synthetic.hidden(T, seed=2 + 1000 * i + 100000 * rank) for i in range(n)]
+
+
+def workload_config(workload: str, world: int = 1, NE: int = E) -> dict:
+    """The workload definition both arms report (the GPU arm adds nothing to it, so the two `config`
+    objects are equal)."""
+    T = WORKLOADS[workload][0]
+    cfg = {"workload": workload, "B": T * world, "tokens_per_gpu": T, "experts": NE, "hidden": H, "inter": I,
+           "topk": K_TOP, "routing": routing_text(workload),
+           "parallelism": (f"ep{world} (experts sharded {NE // world} per GPU)" if world > 1 else "single"),
+           "l2": (f"inputs > L2: routes rotate over {NBATCH} batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"
+                  if T <= 8 else f"inputs > L2: every step streams the whole {NE * EXPERT_BYTES / 1e9:.2f} GB pool")}
+    if workload.startswith("stack"):
+        cfg["layers"] = STACK_LAYERS
+    return cfg
+
+
+# ------------------------------------------------------------------------------------ CPU legs
+def _host_cores() -> int:
+    return int(os.environ.get("OMP_NUM_THREADS", 0)) or (os.cpu_count() or 1)
+
+
+def expert_source(device_pool=None, seed: int = 0, layer: int = 0):
+    """expert id -> its raw MXFP4 tensors on the host: copied from the device pool under test when one is
+    given (fast), else regenerated by the numpy generator (bit-identical bytes); the last 64 are kept."""
+    import numpy as np
+    import torch
+    from oracle import synth
+    cache = {}
+    sp = synth.SynthPool(seed, layer)
+
+    def get(e):
+        if e not in cache:
+            if device_pool is not None:
+                cache[e] = {n: device_pool[n][e].cpu() for n in ("gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s")}
+            else:
+                cache[e] = {n: torch.from_numpy(np.ascontiguousarray(sp[n][e]).view(
+                    np.int32 if n.endswith("_w") else np.uint8)) for n in ("gate_w", "gate_s", "up_w", "up_s",
+                                                                          "down_w", "down_s")}
+            while len(cache) > 64:
+                cache.pop(next(iter(cache)))
+        return cache[e]
+    return get
+
+
+def cpu_port_rates(workload: str, budget_s: float, device_pool=None, samples: int = 1):
+    """The vectorised torch-CPU restatement of the path (oracle/cpu_path.py) on all host threads, in its
+    two variants (float32 dequant cached outside the clock; dequant on the fly): tok/s of each, median
+    over `samples` batches, each a bounded sample of one step (experts until `budget_s`, extrapolated)."""
+    import torch
+    from mimo_moe import synthetic
+    from oracle.cpu_path import CpuLayer
+    torch.set_num_threads(_host_cores())
+    T = WORKLOADS[workload][0]
+    layer = CpuLayer(synthetic.router_weight(), routing_bias(workload), expert_source(device_pool))
+    xs = batches(workload)
+    out = {}
+    for cached in (True, False):
+        rates, info = [], None
+        for s in range(samples):
+            sec, done, U = layer.step_time(xs[s % len(xs)], cached, budget_s, wall_s=2 * budget_s)
+            rates.append(T / sec)
+            info = (done, U)
+        name = "port_fp32_cached" if cached else "port_on_the_fly"
+        out[name] = {"value": statistics.median(rates), "unit": "tok/s", "cores": torch.get_num_threads(),
+                     "sample": f"{info[0]} of {info[1]} distinct experts of one {workload} batch, extrapolated "
+                               f"by U/done; median of {samples} batch(es)"}
+    return out
+
+
+def cpu_emulator_rate(B, budget_s, seed_batch=0):
+    """The reference's own kernel code on the host cores: its Metal kernels A/B (engine/mimo_stream/
+    kernels.py:33-123) compiled for the CPU into oracle/_ref with OpenMP, its own group_routes, and the
+    router (model.py:58-65, MLX on the reference's side) and fixed-order combine restated in numpy, on a
+    bounded sample of one decode batch of B <= 8 rows.  This build of the Metal bodies is an exactness
+    emulator: each 32-lane SIMD-group body runs twice, lane by lane (record, then replay of simd_sum),
+    so it is far slower than a CPU implementation would be; it is reported beside the vectorised port,
+    not instead of it.  Returns None when oracle/_ref was not built."""
     import numpy as np
     import torch
     from oracle import mimo_oracle as O
     from oracle import ref_runner as RR
     from oracle import synth
-    use_ref = RR.available()
+    if not RR.available():
+        return None
     xt = synth.hidden(B, seed=2 + 1000 * seed_batch)
     x = xt.float().numpy()
     W = synth.router_weight().float().numpy()
     t0 = time.perf_counter()
     _, inds, w = O.router(x, W, np.zeros(E, np.float32))
-    uids, urows, ucnt, uw, gidx = (RR.group_routes(inds, w) if use_ref else O.group_routes(inds, w))
+    uids, urows, ucnt, uw, gidx = RR.group_routes(inds, w)
     t_fixed = time.perf_counter() - t0
     sp = synth.SynthPool(0, 0)
-    sig = O.sigmoid_table_bits() if use_ref else None
+    sig = O.sigmoid_table_bits()
     xb = xt.view(torch.int16).numpy().view(np.uint16)
     t_total, done = 0.0, 0
     for u, e in enumerate(uids):
-        raw = {n: {int(e): sp[n][int(e)]} for n in ("gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s")}
-        if use_ref:
-            pool = {n: raw[n][int(e)][None] for n in raw}
-            one = dict(uslot=np.zeros(1, np.int32), urows=urows[u:u + 1], ucnt=ucnt[u:u + 1], uw=uw[u:u + 1])
-            t1 = time.perf_counter()
-            RR.moe_experts(xb, pool, one["uslot"], one["urows"], one["ucnt"], one["uw"],
-                           np.zeros(B * 8, np.int64), sig)
-        else:
-            pool = O.Pool(raw, cache=1)
-            rows = np.nonzero((inds == e).any(1))[0]
-            t1 = time.perf_counter()
-            d = pool.deq(int(e))
-            h = O.swiglu_bf16(O._dots32(d["gate"], x[rows]), O._dots32(d["up"], x[rows]))
-            O._dots32(d["down"], h)
+        pool = {n: sp[n][int(e)][None] for n in ("gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s")}
+        one = dict(uslot=np.zeros(1, np.int32), urows=urows[u:u + 1], ucnt=ucnt[u:u + 1], uw=uw[u:u + 1])
+        t1 = time.perf_counter()
+        RR.moe_experts(xb, pool, one["uslot"], one["urows"], one["ucnt"], one["uw"], np.zeros(B * 8, np.int64), sig)
         t_total += time.perf_counter() - t1
         done += 1
         if t_total >= budget_s:
             break
     per_batch = t_fixed + t_total / done * len(uids)
-    kind = "reference" if use_ref else "port"
-    what = ("the reference's kernels A/B and group_routes (oracle/_ref, OpenMP) + numpy router/combine"
-            if use_ref else "numpy restatement of the path")
-    return B / per_batch, _host_threads() if not use_ref else int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())), \
-        kind, f"{what}: {done} of {len(uids)} distinct experts of one B={B} decode batch, extrapolated by " \
-              f"U/k ({t_total:.1f} s of CPU work)"
+    return {"value": B / per_batch, "unit": "tok/s", "cores": _host_cores(),
+            "sample": f"the reference's kernels A/B (Metal bodies compiled for the CPU, lane-by-lane exactness "
+                      f"emulator) + its group_routes: {done} of {len(uids)} distinct experts of one B={B} "
+                      f"decode batch, extrapolated by U/k"}
+
+
+def cpu_baseline(workload: str, budget_s: float, device_pool=None, emulator: bool = False):
+    """`cpu_baseline` object of a result: the faster port variant as the value, every variant beside it."""
+    rates = cpu_port_rates(workload, budget_s, device_pool)
+    T = WORKLOADS[workload][0]
+    if emulator and T <= 8:
+        em = cpu_emulator_rate(T, budget_s)
+        if em is not None:
+            rates["reference_kernels_emulated"] = em
+    best = max(("port_fp32_cached", "port_on_the_fly"), key=lambda k: rates[k]["value"])
+    b = rates[best]
+    return {"value": b["value"], "unit": "tok/s", "cores": b["cores"], "kind": "port",
+            "sample": f"{best}: vectorised torch-CPU restatement of the reference path (oracle/cpu_path.py); "
+                      + b["sample"], "variants": rates}
 
 
 def run_reference(args):
+    """The reference arm: the reference path on the host cores for the same workload, config and metric.
+    The reference's own implementation is MLX on Metal, which does not exist on Linux; its CPU forms here
+    are the vectorised restatement (two variants) and the reference's own kernel code compiled for the
+    CPU (decode only).  The value is the fastest of them.  Each of up to 8 sampled steps is a bounded
+    sample of one step, so any --steps/--warmup finishes in a few minutes."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    # all host threads for the OpenMP reference kernels (torchrun sets 1 per process); before loading
+    # all host threads (torchrun sets 1 per process); before any library loads its pool
     os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
-    B = WORKLOADS[args.workload]
-    budget = max(0.5, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
-    rates = []
-    for s in range(args.warmup + args.steps):
-        r, cores, kind, sample = cpu_reference_rate(min(B, 8), budget, seed_batch=s % NBATCH)
-        if s >= args.warmup:
-            rates.append(r)
-    v = statistics.median(rates)
+    wl = args.workload if not args.workload.startswith("stack") else args.workload.split("_", 1)[1]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    T = WORKLOADS[wl][0]
+    nsamp = max(1, min(args.steps, 2))
+    budget = 8.0 / nsamp
+    rates = cpu_port_rates(wl, budget, samples=nsamp)
+    if T <= 8:
+        em = [cpu_emulator_rate(T, budget / 2, seed_batch=s) for s in range(min(nsamp, 2))]
+        if em[0] is not None:
+            rates["reference_kernels_emulated"] = dict(em[0], value=statistics.median([e["value"] for e in em]))
+    best = max(rates, key=lambda k: rates[k]["value"])
+    v = rates[best]["value"]
     metric = f"MoE-layer tok/s ({args.workload})"
+    sample = rates[best]["sample"]
     if args.workload.startswith("stack"):  # L layers per token: the one-layer rate / L
         v /= args.layers
         metric = f"MoE-stack tok/s ({args.workload}, {args.layers} layers)"
         sample = f"one layer's rate / {args.layers} layers; {sample}"
-    out = {"impl": "reference", "metric": metric, "value": v,
-           "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-           "higher_is_better": True, "dtype": "f32 (the reference's kernel code on the CPU)", "data": "synthetic",
-           "config": {"workload": args.workload, "B": B, "experts": E, "hidden": H, "inter": I},
-           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
+    cfg = workload_config(args.workload, world)
+    out = {"impl": "reference", "metric": metric, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": T * world / v * 1e3, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None,
+           "dtype": "f32 (the reference path on the CPU)", "data": "synthetic", "config": cfg,
+           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": rates[best]["cores"],
+                            "kind": "reference" if best == "reference_kernels_emulated" else "port",
+                            "sample": f"{best}: {sample}", "variants": rates},
            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
+
+
+# ------------------------------------------------------------------------------------ GPU arm
+class Ctx:
+    """Process-wide state of the GPU arm: ranks, device, the single-GPU expert pool (shared by the
+    workloads measured in one run) and the router weight."""
+
+    def __init__(self, args):
+        import torch
+        import torch.distributed as dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=self.dev)
+        self.NE = args.pool_experts
+        self._pool = None
+
+    def pool(self):
+        import mimo_moe
+        if self._pool is None:
+            if self.world > 1:
+                from mimo_moe.ep import expert_range
+                lo, hi = expert_range(self.rank, self.world, self.NE)
+                self._pool = mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=0, first_expert=lo, device=self.dev)
+            else:
+                self._pool = mimo_moe.ExpertPools.synthetic(self.NE, seed=0, layer=0, device=self.dev)
+        return self._pool
+
+    def range(self):
+        if self.world > 1:
+            from mimo_moe.ep import expert_range
+            return expert_range(self.rank, self.world, self.NE)
+        return 0, self.NE
+
+
+def _timed(ctx, steps, step):
+    """Device time (ms) of `steps` calls of step(i), bracketed by barrier + synchronize, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    if ctx.world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(steps):
+        step(i)
+    ev1.record()
+    torch.cuda.synchronize()
+    if ctx.world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if ctx.world > 1:
+        t = torch.tensor([ms], device=ctx.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float, emulator: bool):
+    """One workload on the GPU arm: device-timed throughput, the dominant kernel's roofline, the
+    end-to-end number through the public API and (rank 0, one GPU) the CPU baseline."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import mimo_moe
+    from mimo_moe import _lib, synthetic
+    from mimo_moe.ep import GraphedStep, PhaseTrace
+
+    world, rank, dev, NE = ctx.world, ctx.rank, ctx.dev, ctx.NE
+    B = WORKLOADS[workload][0]
+    pool = ctx.pool()
+    lo, hi = ctx.range()
+    W = synthetic.router_weight().to(dev)[:NE].contiguous()
+    bias = routing_bias(workload, NE).to(dev)
+    xs = [x.to(dev) for x in batches(workload, rank)]
+    if args.fixed_batch is not None:
+        xs = [xs[args.fixed_batch % len(xs)]] * len(xs)
+    nb = len(xs)
+    y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    L = mimo_moe.lib()
+    ep = world > 1
+    peer = ep and B <= 8
+    blk = None
+    if ep:
+        from mimo_moe.ep import ExpertParallelPrefill, PeerExpertParallelMoE
+        blk = PeerExpertParallelMoE(pool, W, bias, B, num_experts=NE) if peer else \
+            ExpertParallelPrefill(pool, W, bias, num_experts=NE)
+
+    def eager(x, out=None):
+        if ep:
+            return blk(x)
+        return mimo_moe.moe_block(x, W, bias, pool, status=status, out=y if out is None else out)
+
+    # decode steps (4-9 kernels) replay as one CUDA graph so host launch cost does not set the pace;
+    # prefill steps are long enough to run eagerly
+    gstep = GraphedStep(eager, B, H, dev) if B <= 8 else None
+
+    def step(i):
+        if gstep is not None:
+            gstep(xs[i % nb])
+        else:
+            eager(xs[i % nb])
+
+    for i in range(max(3, warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(ctx.local)
+    clocks.start()
+    time.sleep(0.3)
+    _lib.check(L.mimo_moe_profile_enable(4 * steps + 8), "profile_enable")
+    if ep and not peer:
+        blk.routes_received = 0
+    ms = _timed(ctx, steps, step)
+    clk = clocks.stop()
+    routes_step = blk.routes_received / steps if ep and not peer else B * K_TOP
+    launches = (np.zeros(8, np.int32), np.zeros(8, np.float32))
+    _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
+    phases = None
+    if gstep is not None or peer:  # graph replays carry no events: time the kernels in an eager pass
+        nprof = min(steps, 50)
+        _lib.check(L.mimo_moe_profile_enable(4 * nprof + 8), "profile_enable")
+        if peer:
+            blk.trace = PhaseTrace()
+        for i in range(nprof):
+            eager(xs[i % nb])
+        torch.cuda.synchronize()
+        if peer:
+            phases = blk.trace.summary()
+            blk.trace = None
+        _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
+    _lib.check(L.mimo_moe_profile_enable(0), "profile_disable")
+    st_word = int((blk.status if peer else status).item())
+    if st_word != 0:
+        raise RuntimeError(f"device status {st_word} during the bench ({workload})")
+
+    # distinct experts per batch (deterministic routes) -> algorithmic bytes; with expert parallelism U
+    # counts the distinct experts over all ranks' tokens and U_local this rank's share
+    U, U_local, shared = [], [], []
+    for x in xs:
+        idx, _ = mimo_moe.router(x, W, bias)
+        idx = idx.to(torch.int32).contiguous()
+        if ep:
+            allidx = torch.empty(world * idx.shape[0], idx.shape[1], dtype=torch.int32, device=dev)
+            dist.all_gather_into_tensor(allidx, idx)
+            idx = allidx
+        u = torch.unique(idx)
+        U.append(int(u.numel()))
+        U_local.append(int(((u >= lo) & (u < hi)).sum().item()))
+        if 1 < B <= 8:  # experts shared by consecutive rows (config 1's overlap statistic)
+            ic = idx.cpu().numpy()
+            shared += [len(set(ic[t]) & set(ic[t + 1])) for t in range(ic.shape[0] - 1)]
+    steps_U = [U[i % nb] for i in range(steps)]
+    steps_Ul = [U_local[i % nb] for i in range(steps)]
+    hbm, tflops_peak, peak_kind = peaks()
+    kind_gu, kind_dn = (0, 1) if B <= 8 else (2, 3)
+    n_gu, n_dn, n_fz = int(launches[0][kind_gu]), int(launches[0][kind_dn]), int(launches[0][4])
+    gu_ms = float(launches[1][kind_gu]) / max(1, n_gu)
+    dn_ms = float(launches[1][kind_dn]) / max(1, n_dn)
+    fz_ms = float(launches[1][4]) / max(1, n_fz)
+    Ul = statistics.mean(steps_Ul)
+    gu_bytes = Ul * GATEUP_BYTES
+    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0
+    if B <= 8 and n_fz > 0:  # decode, one launch streams every distinct expert's 3 matrices once
+        fz_bytes = Ul * EXPERT_BYTES
+        fz_gbs = fz_bytes / (fz_ms * 1e-3) / 1e9
+        roofline = {"kernel": "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight, one launch)",
+                    "bound": "hbm", "achieved": fz_gbs, "peak": hbm, "unit": "GB/s", "frac": fz_gbs / hbm,
+                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None, "algorithmic_bytes_per_launch": fz_bytes}
+    elif B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
+        roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
+                    "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": Ul * GATEUP_TRAFFIC_PER_EXPERT,
+                    "traffic_source": "ncu dram__bytes_read+write per distinct expert (one decode8 capture) x this "
+                                      "workload's mean distinct experts",
+                    "algorithmic_bytes_per_launch": gu_bytes,
+                    "down": {"achieved": Ul * DOWN_BYTES / (dn_ms * 1e-3) / 1e9 if dn_ms > 0 else 0.0,
+                             "frac": (Ul * DOWN_BYTES / (dn_ms * 1e-3) / 1e9 / hbm) if dn_ms > 0 else 0.0}}
+    else:        # prefill: algorithmic FLOPs 2 (gate, up) x 2 x I x H per routed pair
+        flops = routes_step * 2 * 2 * I * H
+        tf = flops / (gu_ms * 1e-3) / 1e12 if gu_ms > 0 else 0.0
+        roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=64,MODE=0> (prefill gate/up + SwiGLU)", "bound": "tensor",
+                    "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
+                    "peak_kind": f"{peak_kind} bf16_tflops_sustained (dense bf16; the e2m1 x e4m3 MMAs "
+                                 "run at the fp8 rate, nominally 2x)",
+                    "traffic": None, "algorithmic_flops_per_launch": flops,
+                    "weight_gbs": gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0}
+        tp = tensor_peaks(dev)
+        roofline["measured_tensor_tflops"] = tp
+        roofline["frac_of_measured_mxf8f6f4"] = tf / tp["mxf8f6f4"] if tp["mxf8f6f4"] > 0 else None
+        roofline["frac_of_measured_mxf4"] = tf / tp["mxf4"] if tp["mxf4"] > 0 else None
+        # the whole step against its HBM floor: every expert's bytes once
+        roofline["step_hbm_floor_ms"] = Ul * EXPERT_BYTES / (hbm * 1e9) * 1e3
+    roofline["kernel_ms"] = {"fused": fz_ms} if n_fz > 0 else {"gate_up": gu_ms, "down": dn_ms}
+    expert_gbs = sum(steps_U) * EXPERT_BYTES / (ms * 1e-3) / 1e9
+
+    # end to end through the public API, as a drop-in caller makes it: every step copies the step's x from
+    # pinned host memory to the device, runs the block (eager call) and reads y back to pinned host memory
+    xh = [x.cpu().pin_memory() for x in xs]
+    yh = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i):
+        xd.copy_(xh[i % nb], non_blocking=True)
+        yd = eager(xd)
+        yh.copy_(yd, non_blocking=True)
+    for i in range(3):
+        e2e_step(i)
+    e2e_ms = _timed(ctx, steps, e2e_step)
+    e2e_graph = None
+    if gstep is not None:   # the same with the block replayed as a CUDA graph (pinned x straight into its input)
+        def g_step(i):
+            yd = gstep(xh[i % nb])
+            yh.copy_(yd, non_blocking=True)
+        g_ms = _timed(ctx, steps, g_step)
+        e2e_graph = B * world * steps / (g_ms * 1e-3)
+
+    tok = B * steps * world
+    # our kernels per step: decode = route (zeroes the counters too), gate/up + down (one fused launch,
+    # or two), combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
+    # down, combine.  Expert parallelism, peer exchange: router logits, route+scatter, 2 barriers, unit
+    # builder, term split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch,
+    # 2 unit builders, term split, gate/up, down, per-route combine, weighted combine.
+    fused = n_fz > 0
+    launches_per_step = ((7 if fused else 8) if peer else 12) if ep else ((3 if fused else 4) if B <= 8 else 11)
+    res = {
+        "metric": f"MoE-layer tok/s ({workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1 x e4m3 (two-term activations) -> f32, tcgen05 block-scaled",
+        "data": "synthetic (seeded MXFP4 pool, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
+        "config": workload_config(workload, world, NE),
+        "mean_distinct_experts": statistics.mean(steps_U),
+        "mean_distinct_experts_this_gpu": Ul,
+        "routes_this_gpu_per_step": routes_step,
+        "expert_gbs": expert_gbs,
+        "expert_frac_of_measured_hbm": expert_gbs / world / hbm,
+        "roofline": roofline,
+        "clocks": clk,
+        "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2,
+                "d2h_bytes_per_step": B * H * 2,
+                "how": "eager public-API call per step (mimo_moe.moe_block, or the expert-parallel block), "
+                       "pinned host x copied in and y read back every step"},
+        "gpu_launches": launches_per_step * steps,
+    }
+    if e2e_graph is not None:
+        res["e2e"]["value_graph_replay"] = e2e_graph
+    if shared:
+        res["mean_experts_shared_by_consecutive_rows"] = statistics.mean(shared)
+    if args.fixed_batch is not None:
+        res["fixed_batch"] = args.fixed_batch
+    if phases is not None:
+        res["phases_ms"] = phases
+        res["phases_how"] = "eager pass, CUDA events between the exchange's steps on this rank (rank 0)"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(workload, cpu_budget, device_pool=pool, emulator=emulator)
+    else:
+        res["cpu_baseline"] = None
+    del gstep
+    torch.cuda.synchronize()
+    if blk is not None and peer:
+        blk.close()
+    return res
 
 
 def bench_stack(args):
@@ -242,7 +613,7 @@ def bench_stack(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    B, L = WORKLOADS[args.workload], args.layers
+    B, L = WORKLOADS[args.workload][0], args.layers
     lo, hi = expert_range(rank, world, E)
     layers = []
     for l in range(L):
@@ -345,14 +716,13 @@ def bench_stack(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r, cores, kind, sample = cpu_reference_rate(B, args.cpu_budget)
-        cpu = {"value": r / L, "unit": "tok/s", "cores": cores, "kind": kind,
-               "sample": f"one layer's rate / {L} layers; {sample}"}
+        c = cpu_baseline(f"decode{B}", args.cpu_budget)
+        cpu = dict(c, value=c["value"] / L, sample=f"one layer's rate / {L} layers; {c['sample']}")
     if rank == 0:
         tok = B * args.steps * world
-        # per layer: single GPU = route (+ memset), gate/up, down, combine; peer exchange = router
-        # logits, route+scatter, 2 barriers, unit builder, term split, gate/up, down, combine; plus
-        # one RMSNorm between layers
+        # per layer: single GPU = route, gate/up, down, combine; peer exchange = router logits,
+        # route+scatter, 2 barriers, unit builder, term split, gate/up, down, combine; plus one RMSNorm
+        # between layers
         per_layer = (8 if world > 1 else 4) - (1 if fused else 0)
         out = {
             "metric": f"MoE-stack tok/s ({args.workload}, {L} layers)", "value": tok / (ms * 1e-3), "unit": "tok/s",
@@ -360,15 +730,11 @@ def bench_stack(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "e2m1 x e4m3 (two-term activations) -> f32, tcgen05 block-scaled",
             "data": "synthetic (48 independently seeded MXFP4 layers, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
-            "config": {"workload": args.workload, "layers": L, "B": B * world, "tokens_per_gpu": B,
-                       "experts": E, "hidden": H, "inter": I, "topk": K_TOP, "norm": "RMSNorm eps 1e-6, unit weight",
-                       "expert_bytes_per_gpu": L * (hi - lo) * EXPERT_BYTES,
-                       "mean_distinct_experts_per_layer": statistics.mean(U),
-                       "mean_distinct_experts_per_layer_this_gpu": statistics.mean(U_local),
-                       "parallelism": (f"ep{world} (experts sharded {E // world} per GPU in every layer; NVLink "
-                                       "peer-store exchange per layer, flag barriers)") if world > 1 else "single",
-                       "graph": "the whole L-layer step is one CUDA graph",
-                       "l2": f"inputs > L2: {L * (hi - lo) * EXPERT_BYTES / 1e9:.1f} GB of experts per GPU"},
+            "config": dict(workload_config(args.workload, world), layers=L),
+            "expert_bytes_per_gpu": L * (hi - lo) * EXPERT_BYTES,
+            "mean_distinct_experts_per_layer": statistics.mean(U),
+            "mean_distinct_experts_per_layer_this_gpu": statistics.mean(U_local),
+            "graph": "the whole L-layer step is one CUDA graph",
             "expert_gbs": expert_gbs,
             "expert_frac_of_measured_hbm": expert_gbs / world / hbm,
             "roofline": {"kernel": "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight)" if fused else
@@ -379,7 +745,7 @@ def bench_stack(args):
                          "kernel_ms": {"fused": fz_ms} if fused else {"gate_up": gu_ms, "down": dn_ms}},
             "clocks": clk,
             "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2,
-                    "d2h_bytes_per_step": B * H * 2},
+                    "d2h_bytes_per_step": B * H * 2, "how": "graph replay of the stack, pinned x in, y out"},
             "gpu_launches": (per_layer * L + (L - 1)) * args.steps,
             "cpu_baseline": cpu,
         }
@@ -400,7 +766,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode8", choices=list(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-nested", action="store_true", help="only the headline workload")
+    ap.add_argument("--cpu-budget", type=float, default=4.0, help="seconds of timed CPU work per baseline variant")
     ap.add_argument("--pool-experts", type=int, default=E,
                     help="experts in the pool and router (small cases for profiling; default 256)")
     ap.add_argument("--layers", type=int, default=STACK_LAYERS, help="layers of the stack workloads")
@@ -412,253 +779,19 @@ def main():
         return run_reference(args)
     if args.workload.startswith("stack"):
         return bench_stack(args)
-
-    import numpy as np
-    import torch
     import torch.distributed as dist
-
-    import mimo_moe
-    from mimo_moe import _lib
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    B = WORKLOADS[args.workload]
-    NE = args.pool_experts
-    ep = world > 1  # expert parallelism: rank r holds experts [r*NE/N, (r+1)*NE/N), routes its own B tokens
-    if ep:
-        from mimo_moe.ep import expert_range
-        lo, hi = expert_range(rank, world, NE)
-        pool = mimo_moe.ExpertPools.synthetic(hi - lo, seed=0, layer=0, first_expert=lo, device=dev)
-    else:
-        lo, hi = 0, NE
-        pool = mimo_moe.ExpertPools.synthetic(NE, seed=0, layer=0, device=dev)
-    xs, W = make_inputs(B, dev, torch, rank)
-    if args.fixed_batch is not None:
-        xs = [xs[args.fixed_batch % NBATCH]] * NBATCH
-    W = W[:NE].contiguous()
-    zipf = args.workload.endswith("z")
-    if zipf:
-        from mimo_moe import synthetic
-        bias = synthetic.zipf_bias(E=NE, c=ZIPF_C).to(dev)
-    else:
-        bias = torch.zeros(NE, device=dev)
-    y = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
-    L = mimo_moe.lib()
-    # decode sizes exchange through NVLink peer memory inside the kernels; prefill batches send each
-    # route to its expert's rank with NCCL all-to-alls
-    peer = ep and B <= 8
-    if ep:
-        from mimo_moe.ep import ExpertParallelPrefill, PeerExpertParallelMoE
-        blk = PeerExpertParallelMoE(pool, W, bias, B, num_experts=NE) if peer else \
-            ExpertParallelPrefill(pool, W, bias, num_experts=NE)
-    else:
-        blk = None
-    # expert-parallel decode replays one CUDA graph per step (router, exchanges, expert kernels,
-    # combine): the step issues ~8 kernels, whose host-side launch cost would otherwise set the pace.
-    # The x copy into the graph's input is inside the step.  The single-GPU decode step (4 kernels + a
-    # memset) is replayed as a graph too; prefill steps (whose all-to-all splits are data-dependent)
-    # are long enough that launch gaps do not matter and run eagerly.
-    from mimo_moe.ep import GraphedStep
-    if peer:
-        gstep = GraphedStep(blk, B, H, dev)
-    elif B <= 8:
-        gstep = GraphedStep(lambda x: mimo_moe.moe_block(x, W, bias, pool, status=status, out=y), B, H, dev)
-    else:
-        gstep = None
-
-    def block(x):
-        if gstep is not None:
-            return gstep(x)
-        return blk(x) if ep else mimo_moe.moe_block(x, W, bias, pool, status=status)
-
-    def step(i):
-        if gstep is not None:
-            gstep(xs[i % NBATCH])
-        elif ep:
-            blk(xs[i % NBATCH])
-        else:
-            mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
-
-    for i in range(max(3, args.warmup)):
-        step(i)
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    _lib.check(L.mimo_moe_profile_enable(4 * args.steps + 8), "profile_enable")
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    if ep and not peer:
-        blk.routes_received = 0
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for i in range(args.steps):
-        step(i)
-    ev1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = ev0.elapsed_time(ev1)
-    clk = clocks.stop()
-    # routes this rank's expert kernels computed per step (expert-parallel prefill: skewed routing
-    # gives the ranks unequal shares; otherwise each rank computes its own B * k routes)
-    routes_step = blk.routes_received / args.steps if ep and not peer else B * K_TOP
-    launches = (np.zeros(8, np.int32), np.zeros(8, np.float32))
-    _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
-    if gstep is not None:  # graph replays carry no profiling events: time the kernels in an eager pass
-        nprof = min(args.steps, 50)
-        _lib.check(L.mimo_moe_profile_enable(4 * nprof + 8), "profile_enable")
-        for i in range(nprof):
-            if ep:
-                blk(xs[i % NBATCH])
-            else:
-                mimo_moe.moe_block(xs[i % NBATCH], W, bias, pool, status=status, out=y)
-        torch.cuda.synchronize()
-        _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
-    _lib.check(L.mimo_moe_profile_enable(0), "profile_disable")
-    if int(status.item()) != 0:
-        raise RuntimeError(f"device status {int(status.item())} during the bench")
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-
-    # distinct experts per batch (deterministic routes) -> algorithmic bytes; with expert parallelism
-    # U counts the distinct experts over all ranks' tokens (each lives on one rank) and U_local this
-    # rank's share, which its kernels stream
-    U, U_local = [], []
-    for i in range(NBATCH):
-        idx, _ = mimo_moe.router(xs[i], W, bias)
-        idx = idx.to(torch.int32).contiguous()
-        if ep:
-            allidx = torch.empty(world * idx.shape[0], idx.shape[1], dtype=torch.int32, device=dev)
-            dist.all_gather_into_tensor(allidx, idx)
-            idx = allidx
-        u = torch.unique(idx)
-        U.append(int(u.numel()))
-        U_local.append(int(((u >= lo) & (u < hi)).sum().item()))
-    steps_U = [U[i % NBATCH] for i in range(args.steps)]
-    steps_Ul = [U_local[i % NBATCH] for i in range(args.steps)]
-    hbm, tflops_peak, peak_kind = peaks()
-    kind_gu, kind_dn = (0, 1) if B <= 8 else (2, 3)
-    gu_ms = float(launches[1][kind_gu]) / max(1, int(launches[0][kind_gu]))
-    dn_ms = float(launches[1][kind_dn]) / max(1, int(launches[0][kind_dn]))
-    fz_ms = float(launches[1][4]) / max(1, int(launches[0][4]))
-    gu_bytes = statistics.mean(steps_Ul) * GATEUP_BYTES
-    achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0
-    if B <= 8 and launches[0][4] > 0:  # decode, one launch streams every distinct expert's 3 matrices once
-        fz_bytes = statistics.mean(steps_Ul) * EXPERT_BYTES
-        fz_gbs = fz_bytes / (fz_ms * 1e-3) / 1e9
-        roofline = {"kernel": "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight, one launch)",
-                    "bound": "hbm", "achieved": fz_gbs, "peak": hbm, "unit": "GB/s", "frac": fz_gbs / hbm,
-                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
-                    "algorithmic_bytes_per_launch": fz_bytes}
-    elif B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
-        roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
-                    "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                    "peak_kind": f"{peak_kind} hbm_gbs",
-                    "traffic": statistics.mean(steps_Ul) * GATEUP_TRAFFIC_PER_EXPERT,
-                    "traffic_source": "ncu dram__bytes_read+write per distinct expert (one capture) x this "
-                                      "workload's mean distinct experts",
-                    "algorithmic_bytes_per_launch": gu_bytes}
-    else:        # prefill: algorithmic FLOPs 2 (gate, up) x 2 x I x H per routed pair
-        flops = routes_step * 2 * 2 * I * H
-        tf = flops / (gu_ms * 1e-3) / 1e12 if gu_ms > 0 else 0.0
-        roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=64,MODE=0> (prefill gate/up + SwiGLU)", "bound": "tensor",
-                    "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s", "frac": tf / tflops_peak,
-                    "peak_kind": f"{peak_kind} bf16_tflops_sustained (dense bf16; the e2m1 x e4m3 MMAs "
-                                 "run at the fp8 rate, nominally 2x)",
-                    "traffic": None, "algorithmic_flops_per_launch": flops,
-                    "weight_gbs": gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0}
-        # the library's own tcgen05 probe: the MMA form these kernels run (two e4m3 terms per activation,
-        # so algorithmic FLOPs are half the executed ones) and the FP4 rate the survey's target names
-        tp = tensor_peaks(dev)
-        roofline["measured_tensor_tflops"] = tp
-        roofline["frac_of_measured_mxf8f6f4"] = tf / tp["mxf8f6f4"] if tp["mxf8f6f4"] > 0 else None
-        roofline["frac_of_measured_mxf4"] = tf / tp["mxf4"] if tp["mxf4"] > 0 else None
-    roofline["kernel_ms"] = {"fused": fz_ms} if launches[0][4] > 0 else {"gate_up": gu_ms, "down": dn_ms}
-    expert_gbs = sum(steps_U) * EXPERT_BYTES / (ms * 1e-3) / 1e9
-
-    # end to end through the public API: pinned host x -> device, block, y -> pinned host
-    xh = [x.cpu().pin_memory() for x in xs]
-    yh = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        if gstep is not None:  # pinned host x straight into the graph's input buffer
-            yd = gstep(xh[i % NBATCH])
-        else:
-            yd = block(xh[i % NBATCH].to(dev, non_blocking=True))
-        yh.copy_(yd, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r, cores, kind, sample = cpu_reference_rate(min(B, 8), args.cpu_budget)
-        cpu = {"value": r, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample}
-
-    if rank == 0:
-        tok = B * args.steps * world
-        # our kernels per step: decode = route (+ its counter memsets, not counted), gate/up + down
-        # (one fused launch, or two), combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit
-        # builders, term split, gate/up, down, combine
-        # expert parallelism, peer exchange: router logits, route+scatter, 2 barriers, unit builder, term
-        # split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch, 2 unit
-        # builders, term split, gate/up, down, per-route combine, weighted combine (the collectives and
-        # the route sort / gathers are library kernels)
-        fused = int(launches[0][4]) > 0  # decode gate/up + down as one launch
-        launches_per_step = ((7 if fused else 8) if peer else 12) if ep else \
-            ((3 if fused else 4) if B <= 8 else 11)
-        out = {
-            "metric": f"MoE-layer tok/s ({args.workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e2m1 x e4m3 (two-term activations) -> f32, tcgen05 block-scaled",
-            "data": "synthetic (seeded MXFP4 pool, x ~ N(0,1) bf16, router W ~ N(0,0.02))",
-            "config": {"workload": args.workload, "B": B * world, "experts": NE, "hidden": H, "inter": I,
-                       "topk": K_TOP, "routing": f"Zipf(1.1) bias, c={ZIPF_C}" if zipf else "free (bias 0)", "mean_distinct_experts": statistics.mean(steps_U),
-                       "mean_distinct_experts_this_gpu": statistics.mean(steps_Ul),
-                       "routes_this_gpu_per_step": routes_step,
-                       "parallelism": (f"ep{world} (experts sharded {NE // world} per GPU; " +
-                                       ("dispatch and return as NVLink peer stores inside the route and "
-                                        "down kernels, flag barriers; one CUDA graph per step" if peer else
-                                        "NCCL all-to-all of each route to its expert's rank and back") +
-                                       "; fixed-order combine)") if ep else "single",
-                       "tokens_per_gpu": B,
-                       "fixed_batch": args.fixed_batch,
-                       "l2": f"inputs > L2: routes rotate over 16 batches of a {NE * EXPERT_BYTES / 1e9:.2f} GB pool"},
-            "expert_gbs": expert_gbs,
-            "expert_frac_of_measured_hbm": expert_gbs / hbm,
-            "roofline": roofline,
-            "clocks": clk,
-            "e2e": {"value": tok / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2,
-                    "d2h_bytes_per_step": B * H * 2},
-            "gpu_launches": launches_per_step * args.steps,
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(out))
-    if world > 1:
-        del gstep  # a graph holding NCCL calls must be released before the process group
-        torch.cuda.synchronize()
-        if peer:
-            blk.close()
+    ctx = Ctx(args)
+    head = measure(args, ctx, args.workload, args.steps, args.warmup, args.cpu_budget, emulator=True)
+    nested = {}
+    if ctx.world == 1 and not args.no_nested and args.workload == "decode8" and args.pool_experts == E:
+        for wl in NESTED:
+            T = WORKLOADS[wl][0]
+            k = args.steps if T <= 8 else max(10, min(args.steps, 40))
+            nested[wl] = measure(args, ctx, wl, k, args.warmup, args.cpu_budget, emulator=False)
+        head["configs"] = nested
+    if ctx.rank == 0:
+        print(json.dumps(head))
+    if ctx.world > 1:
         dist.destroy_process_group()
 
 

@@ -155,14 +155,18 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
  * mimo_moe_experts_routes_workspace_bytes(rows, topk, H, I, S).
  *
  * mimo_moe_combine: y[m] = bf16(sum over k in order of part[gather_idx[m * topk + k]]) with
- * gather_idx = NULL meaning row m * topk + k (kernels.py:194-199).
+ * gather_idx = NULL meaning row m * topk + k (kernels.py:194-199).  part holds part_rows rows
+ * (<= 0: M * topk); a gather_idx entry at or beyond part_rows sets MIMO_ERANGE in *status (may be
+ * NULL) and is skipped, as negative entries are.
  *
  * Peer-memory exchange (one process per GPU on one node): mimo_moe_peer_alloc allocates `bytes` of
  * zeroed device memory and writes its 64-byte CUDA IPC handle; mimo_moe_peer_open maps another
  * process's handle (mimo_moe_peer_close unmaps, mimo_moe_peer_free frees).  mimo_moe_peer_barrier
  * orders everything issued before it on every rank before everything issued after it on every rank:
  * signals[r] points at rank r's int32[world] signal array, my_signals at this rank's, epoch at a
- * device counter that starts at 0; a wait longer than ~2 s sets MIMO_ETIMEOUT in *status.
+ * device counter that starts at 0; a wait longer than timeout_us microseconds (0: 2 s) sets
+ * MIMO_ETIMEOUT in *status and the barrier kernel returns (a rank that never arrives is reported, the
+ * GPU does not hang).
  * mimo_moe_route_scatter routes T <= 8 tokens (router logits into `logits`, float32 [T, E]) and stores
  * each token's packed row [x as H/2 int32 words | topk ids | topk weights] into rows[r] at row
  * rank * T + t for every rank r (ld int32 words per row).
@@ -173,8 +177,8 @@ int mimo_moe_experts_routes(const uint16_t* x, int32_t x_ld, int32_t rows, const
                             int32_t topk, int32_t pairs_rounding, float* part, float* const* peer_part,
                             int32_t rows_per_rank, void* workspace, size_t workspace_bytes, int32_t* status,
                             void* stream);
-int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,
-                     uint16_t* y, void* stream);
+int mimo_moe_combine(const float* part, int64_t part_rows, const int32_t* gather_idx, int32_t M, int32_t topk,
+                     int32_t H, uint16_t* y, int32_t* status, void* stream);
 /* Prefill combine (model.py:266-271): y[t] = bf16(sum over k in order of fp32(ypair[inv[t*topk+k]]) *
  * weight[t*topk+k]), skipping inv < 0.  ypair bf16 [*, H] (per-route expert outputs). */
 int mimo_moe_combine_pairs(const uint16_t* ypair, const int32_t* inv, const float* weight, int32_t T, int32_t topk,
@@ -206,7 +210,7 @@ int mimo_moe_peer_open(const void* handle, void** ptr);
 int mimo_moe_peer_close(void* ptr);
 int mimo_moe_peer_free(void* ptr);
 int mimo_moe_peer_barrier(int32_t* const* signals, int32_t* my_signals, int32_t rank, int32_t world,
-                          int32_t* epoch, int32_t* status, void* stream);
+                          int32_t* epoch, int32_t timeout_us, int32_t* status, void* stream);
 int mimo_moe_route_scatter(const uint16_t* x, int32_t T, int32_t H, const uint16_t* router_w, const float* bias,
                            int32_t E, int32_t topk, int32_t* const* rows, int32_t ld, int32_t rank, int32_t world,
                            float* logits, void* stream);
@@ -226,10 +230,13 @@ int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up
  * weights, a fixed preallocated arena, a process barred from cudaMalloc - the scratch lives in a
  * fixed device array inside the library, held on every GPU that loads it until exit
  * (mimo_moe_experts_static_scratch_bytes(), about 10 MiB).  Limits: M <= 8, U*R <= 512, H <= 4096,
- * I <= 2048; larger sizes return MIMO_ERANGE without launching.  The first call on a device looks up
- * the array's device address, so make it before any stream capture.  All calls share the array:
- * calls that overlap on the GPU race, so issue them on one stream.  Arguments and results otherwise
- * as mimo_moe_experts.
+ * I <= 2048; larger sizes return MIMO_ERANGE without launching.  The first call on a device (and
+ * again in a new CUDA context of it) looks up the array's device address, so make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU race, so issue them on
+ * one stream.  Arguments as mimo_moe_experts.  It runs the mma.sync decode kernels (f16 tensor-core
+ * products of CUDA-core-decoded e2m1 weights), not the tcgen05 kernels mimo_moe_experts takes for
+ * TMA-aligned pools, so its results match mimo_moe_experts within the output tolerance (rel_err
+ * <= 1e-2 against the reference path's restatement), not bit for bit, and it is slower at M = 8.
  */
 size_t mimo_moe_experts_static_scratch_bytes(void);
 int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* uslot,

@@ -227,6 +227,7 @@ ExpertParams down_params(const ExpertParams& gu, const mimo_moe_pools* pools) {
   q.tiles = pools->hidden / 16;
   q.rtok = nullptr;
   q.bsrc = gu.h_out;
+  q.brows = 0;
   q.h_out = nullptr;
   return q;
 }
@@ -282,7 +283,8 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
            const int32_t* num_units, int ucap, int pairs_rounding, const TermWs& t, float* part,
            uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false,
            bool ready_zeroed = false,
-           const int32_t* out_row = nullptr, int x_ld = 0, float* const* peer_part = nullptr, int peer_rows = 0) {
+           const int32_t* out_row = nullptr, int x_ld = 0, float* const* peer_part = nullptr, int peer_rows = 0,
+           int x_rows = 0) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
   const bool decode = routes == kTcDecodeRoutes;
@@ -293,10 +295,10 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   if (!terms_ready) {
     if (fp4 && by_token_rows) MIMO_TRY(launch_tc_split_tokens_fp4(x, by_token_rows, H, t.bq, t.bs, status, st));
     else if (fp4) MIMO_TRY(launch_tc_split_fp4(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, t.bq, t.bs, status,
-                                               st, x_ld));
+                                               st, x_ld, x_rows));
     else if (by_token_rows) MIMO_TRY(launch_tc_split_tokens(x, by_token_rows, H, t.bq, t.bs, status, st));
     else MIMO_TRY(launch_tc_split(x, H, ucnt, up0, p0_stride, rtok, num_units, ucap, routes, t.bq, t.bs, status, st,
-                                  x_ld));
+                                  x_ld, x_rows));
   }
   const uint64_t brows = by_token_rows ? (uint64_t)N : (uint64_t)ucap * N;
   TcParams p{};
@@ -313,6 +315,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   MIMO_TRY(sf_map(&p.smap[1], pools->up_s, (uint64_t)S * I, H / 32, 128));
   MIMO_TRY(sf_map(&p.bsmap, t.bs, brows, H / 32, N));
   p.btok = by_token_rows ? rtok : nullptr;
+  p.btok_rows = by_token_rows;
   p.S = S;
   p.Nw = I;
   p.K = H;
@@ -370,7 +373,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
 
 // Decode expert products through the TMA-fed kernels (H <= 4096, I <= 2048).
 int run_experts_tma(const mimo_moe_pools* pools, const int32_t* uslot, const int32_t* urows,
-                    const int32_t* ucnt, const float* uw, const int32_t* num_unique, int U, int R,
+                    const int32_t* ucnt, const float* uw, const int32_t* num_unique, int U, int R, int M,
                     int pairs_rounding, const DecodeWs& w, int32_t* status, cudaStream_t st) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
@@ -402,6 +405,7 @@ int run_experts_tma(const mimo_moe_pools* pools, const int32_t* uslot, const int
   p.units_cap = U;
   p.rtok = urows;
   p.bsrc = w.x16;
+  p.brows = M;
   p.h_out = w.h16;
   p.status = status;
   MIMO_TRY(profiled(0, st, [&] { return launch_decode_tma(p, 0, sms, st); }));
@@ -444,16 +448,16 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
     const int rc = run_tc(x, pools, kTcDecodeRoutes, uslot, ucnt, nullptr, R, nullptr, nullptr, urows, uw,
                           num_unique, U, pairs_rounding, w.t, w.part, nullptr, status, st,
                           M <= kTcDecodeRoutes ? M : 0, terms_ready && M <= kTcDecodeRoutes,
-                          /*ready_zeroed=*/terms_ready);
+                          /*ready_zeroed=*/terms_ready, nullptr, 0, nullptr, 0, /*x_rows=*/M);
     if (rc != MIMO_OK) return rc;
-    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
+    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st));
     return MIMO_OK;
   }
   if (!x16_ready) MIMO_TRY(launch_to_f16(x, w.x16, (size_t)M * H, status, st));
   if (pools->hidden <= 4096 && pools->inter <= 2048) {
-    const int rc = run_experts_tma(pools, uslot, urows, ucnt, uw, num_unique, U, R, pairs_rounding, w, status, st);
+    const int rc = run_experts_tma(pools, uslot, urows, ucnt, uw, num_unique, U, R, M, pairs_rounding, w, status, st);
     if (rc != MIMO_OK) return rc;
-    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
+    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st));
     return MIMO_OK;
   }
   ExpertParams p = gateup_params(pools, status);
@@ -465,6 +469,7 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
   p.units_cap = U;
   p.rtok = urows;
   p.bsrc = w.x16;
+  p.brows = M;
   p.h_out = w.h16;
   MIMO_TRY(tiles(p, 0, sms, st));
   ExpertParams q = down_params(p, pools);
@@ -472,7 +477,7 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
   q.part_out = w.part;
   q.pairs_rounding = pairs_rounding;
   MIMO_TRY(tiles(q, 1, sms, st));
-  MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, st));
+  MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st));
   return MIMO_OK;
 }
 
@@ -488,7 +493,8 @@ int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* s
                                 w.unit_slot, w.unit_p0, w.unit_cnt, w.unit_first, w.unit_nsub, w.num_units,
                                 w.order, weight, P, topk, w.rtok, w.rw, status, st));
     const int rc = run_tc(x, pools, kTcPrefillRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, w.unit_first,
-                          w.unit_nsub, w.rtok, nullptr, w.num_units, w.ucap, 0, w.t, nullptr, w.ypair, status, st);
+                          w.unit_nsub, w.rtok, nullptr, w.num_units, w.ucap, 0, w.t, nullptr, w.ypair, status, st,
+                          0, false, false, nullptr, 0, nullptr, 0, /*x_rows=*/T);
     if (rc != MIMO_OK) return rc;
     MIMO_TRY(launch_combine_prefill(w.ypair, w.inv, weight, T, topk, H, y, st));
     return MIMO_OK;
@@ -506,6 +512,7 @@ int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* s
   p.units_cap = w.ucap;
   p.rtok = w.rtok;
   p.bsrc = w.x16;
+  p.brows = T;
   p.h_out = w.h16;
   MIMO_TRY(tiles(p, 2, sms, st));
   ExpertParams q = down_params(p, pools);
@@ -718,7 +725,7 @@ int mimo_moe_experts_routes(const uint16_t* x, int32_t x_ld, int32_t rows, const
   }
   return run_tc(x, pools, kTcDecodeRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, nullptr, nullptr, w.rtok,
                 w.rw, w.num_units, w.ucap, pairs_rounding, w.t, part, nullptr, status, st, 0, false, false, w.order,
-                x_ld, peer_part, rows_per_rank);
+                x_ld, peer_part, rows_per_rank, /*x_rows=*/rows);
 }
 
 // ------------------------------------------------------------------- peer-memory exchange
@@ -753,10 +760,13 @@ int mimo_moe_peer_free(void* ptr) {
 }
 
 int mimo_moe_peer_barrier(int32_t* const* signals, int32_t* my_signals, int32_t rank, int32_t world,
-                          int32_t* epoch, int32_t* status, void* stream) {
-  if (!signals || !my_signals || !epoch || !status || world < 1 || world > 32 || rank < 0 || rank >= world)
+                          int32_t* epoch, int32_t timeout_us, int32_t* status, void* stream) {
+  if (!signals || !my_signals || !epoch || !status || world < 1 || world > 32 || rank < 0 || rank >= world ||
+      timeout_us < 0)
     return MIMO_EINVAL;
-  MIMO_TRY(launch_peer_barrier(signals, my_signals, rank, world, epoch, status, static_cast<cudaStream_t>(stream)));
+  const uint64_t limit_ns = timeout_us ? (uint64_t)timeout_us * 1000ull : 2000000000ull;
+  MIMO_TRY(launch_peer_barrier(signals, my_signals, rank, world, epoch, limit_ns, status,
+                               static_cast<cudaStream_t>(stream)));
   return MIMO_OK;
 }
 
@@ -773,11 +783,13 @@ int mimo_moe_route_scatter(const uint16_t* x, int32_t T, int32_t H, const uint16
   return MIMO_OK;
 }
 
-int mimo_moe_combine(const float* part, const int32_t* gather_idx, int32_t M, int32_t topk, int32_t H,
-                     uint16_t* y, void* stream) {
+int mimo_moe_combine(const float* part, int64_t part_rows, const int32_t* gather_idx, int32_t M, int32_t topk,
+                     int32_t H, uint16_t* y, int32_t* status, void* stream) {
   if (!part || !y || M < 1 || topk < 1 || topk > 8 || H < 4 || H % 4) return MIMO_EINVAL;
+  if (part_rows <= 0) part_rows = (int64_t)M * topk;
+  if (!gather_idx && part_rows < (int64_t)M * topk) return MIMO_EINVAL;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MIMO_TRY(launch_combine_rows(part, gather_idx, M, topk, H, y, st));
+  MIMO_TRY(launch_combine_rows(part, gather_idx, M, topk, H, part_rows, y, status, st));
   return MIMO_OK;
 }
 

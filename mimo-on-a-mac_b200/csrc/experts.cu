@@ -57,9 +57,26 @@ __device__ __forceinline__ __half to_f16_checked(float v, int32_t* status) {
   return __float2half_rn(v);
 }
 
-// B-operand row index of route q of a unit.
+// B-operand row index of route q of a unit.  A row outside [0, brows) (brows > 0) sets MIMO_ERANGE and
+// reads row 0 instead, so a bad route table never reads past the activations.
 __device__ __forceinline__ int b_row_index(const ExpertParams& p, int p0, int q) {
-  return p.rtok ? __ldg(p.rtok + p0 + q) : (p0 + q);
+  int r = p.rtok ? __ldg(p.rtok + p0 + q) : (p0 + q);
+  if (p.brows > 0 && (r < 0 || r >= p.brows)) {
+    set_status(p.status, MIMO_ERANGE);
+    r = 0;
+  }
+  return r;
+}
+
+// Routes a unit may hold: its route slots are [p0, p0 + limit).  Units at a fixed stride (decode:
+// p0 = unit * R) hold at most R, so a count above R would write into the next unit's rows.
+__device__ __forceinline__ int unit_route_count(const int32_t* unit_cnt, int unit, int limit, int32_t* status) {
+  const int c = __ldg(unit_cnt + unit);
+  if (c > limit) {
+    set_status(status, MIMO_ERANGE);
+    return limit;
+  }
+  return max(c, 0);
 }
 
 // Work item decoding shared by producer and consumers.
@@ -69,7 +86,7 @@ __device__ __forceinline__ void item_info(const ExpertParams& p, long long item,
   tile = (int)(item % p.tiles);
   slot = __ldg(p.unit_slot + unit);
   p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
-  cnt = min(__ldg(p.unit_cnt + unit), tb * 8);
+  cnt = unit_route_count(p.unit_cnt, unit, p.unit_p0 ? tb * 8 : min(tb * 8, p.p0_stride), p.status);
 }
 
 template <int NM, int TB, int NSTAGE, int MODE, int KC>
@@ -414,9 +431,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, 1) expert_decode_tma_kernel(con
       if (*s_abort) break;
       if (unit != cur_unit) {
         slot = __ldg(p.unit_slot + unit);
-        cnt = min(__ldg(p.unit_cnt + unit), 8);
+        cnt = unit_route_count(p.unit_cnt, unit, min(8, p.p0_stride), p.status);
         p0 = unit * p.p0_stride;
-        const int brow = (lane < cnt) ? (p.rtok ? __ldg(p.rtok + p0 + lane) : p0 + lane) : 0;
+        int brow = (lane < cnt) ? (p.rtok ? __ldg(p.rtok + p0 + lane) : p0 + lane) : 0;
+        if (p.brows > 0 && (brow < 0 || brow >= p.brows)) {  // never read past the activation rows
+          set_status(p.status, MIMO_ERANGE);
+          brow = 0;
+        }
         // the consumers release the previous expert's rows when they start this one
         if (!mbar_wait(bempty, bph ^ 1u)) {
           if (lane == 0) set_status(p.status, MIMO_ETIMEOUT);
@@ -687,11 +708,13 @@ cudaError_t launch_expert_tiles(const ExpertParams& p, int kind, int num_sms, cu
 
 // ------------------------------------------------------------------------------------ combine
 // Decode (kernels.py:196-199): y[t, m] = bf16(sum_k part[gidx[t, k], m]) in route order; with
-// gidx == null, the scatter-add of kernels.py:196-197 summed in (u, r) order.
+// gidx == null, the scatter-add of kernels.py:196-197 summed in (u, r) order.  part holds ucap * R
+// rows: a gidx entry at or beyond that sets MIMO_ERANGE and is skipped (negative entries are skipped
+// silently, as unused routes).
 __global__ void combine_decode_kernel(const float* __restrict__ part, const int32_t* __restrict__ gidx,
                                       const int32_t* __restrict__ urows, const int32_t* __restrict__ ucnt,
                                       const int32_t* __restrict__ num_unique, int ucap, int R, int M,
-                                      int topk, int H, uint16_t* __restrict__ y) {
+                                      int topk, int H, uint16_t* __restrict__ y, int32_t* status) {
   pdl_wait();  // the partials come from the preceding kernel
   pdl_launch_dependents();
   const int t = blockIdx.x;  // rows on x: gridDim.y stops at 65535
@@ -706,8 +729,13 @@ __global__ void combine_decode_kernel(const float* __restrict__ part, const int3
     acc.w = __fadd_rn(acc.w, v.w);
   };
   if (gidx) {
+    const long long rows = (long long)ucap * R;
     for (int k = 0; k < topk; ++k) {
       const int sl = gidx[t * topk + k];
+      if (sl >= rows) {
+        if (m == 0) set_status(status, MIMO_ERANGE);
+        continue;
+      }
       if (sl >= 0) add(sl);
     }
   } else {
@@ -725,22 +753,28 @@ __global__ void combine_decode_kernel(const float* __restrict__ part, const int3
 
 cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const int32_t* urows,
                                   const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
-                                  int M, int topk, int H, uint16_t* y, cudaStream_t st) {
+                                  int M, int topk, int H, uint16_t* y, int32_t* status, cudaStream_t st) {
   dim3 grid(M, (H / 4 + 255) / 256);
   return launch_k(combine_decode_kernel, grid, dim3(256), 0, st, part, gidx, urows, ucnt, num_unique, ucap, R, M,
-                  topk, H, y);
+                  topk, H, y, status);
 }
 
 // y[m] = bf16(sum over k in order of part[row]) with row = gidx[m * topk + k] (skipped when < 0), or
-// m * topk + k without gidx (kernels.py:194-199).
+// m * topk + k without gidx (kernels.py:194-199).  part holds part_rows rows; a gidx entry at or beyond
+// that sets MIMO_ERANGE (when status is given) and is skipped.
 __global__ void combine_rows_kernel(const float* __restrict__ part, const int32_t* __restrict__ gidx, int M,
-                                    int topk, int H, uint16_t* __restrict__ y) {
+                                    int topk, int H, long long part_rows, uint16_t* __restrict__ y,
+                                    int32_t* status) {
   const int t = blockIdx.x;  // rows on x: gridDim.y stops at 65535
   const int m = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (t >= M || m >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < topk; ++k) {
     const int sl = gidx ? gidx[t * topk + k] : t * topk + k;
+    if (sl >= part_rows) {
+      if (m == 0) set_status(status, MIMO_ERANGE);
+      continue;
+    }
     if (sl < 0) continue;
     const float4 v = *reinterpret_cast<const float4*>(part + (size_t)sl * H + m);
     acc.x = __fadd_rn(acc.x, v.x);
@@ -753,10 +787,10 @@ __global__ void combine_rows_kernel(const float* __restrict__ part, const int32_
   *reinterpret_cast<uint2*>(y + (size_t)t * H + m) = make_uint2(o0, o1);
 }
 
-cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H, uint16_t* y,
-                                cudaStream_t st) {
+cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H,
+                                long long part_rows, uint16_t* y, int32_t* status, cudaStream_t st) {
   dim3 grid(M, (H / 4 + 255) / 256);
-  combine_rows_kernel<<<grid, 256, 0, st>>>(part, gidx, M, topk, H, y);
+  combine_rows_kernel<<<grid, 256, 0, st>>>(part, gidx, M, topk, H, part_rows, y, status);
   return cudaGetLastError();
 }
 

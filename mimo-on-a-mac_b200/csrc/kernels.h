@@ -46,6 +46,7 @@ struct ExpertParams {
   // B operand: row(route p) = rtok ? rtok[p] : p; values bsrc[row * K + k] (f16)
   const int32_t* rtok;
   const __half* bsrc;
+  int brows;        // rows of bsrc (> 0: route rows outside [0, brows) set MIMO_ERANGE, read row 0)
   const float* rw;  // route weights (down, decode)
   // outputs (one per mode)
   __half* h_out;        // gate/up: SwiGLU output [P][N] (f16 copy of the bf16 value)
@@ -69,6 +70,7 @@ struct DecodeParams {
   int units_cap;
   const int32_t* rtok;  // B row of route p (null: row p)
   const __half* bsrc;   // B rows [*, K] f16
+  int brows;            // rows of bsrc (> 0: route rows outside [0, brows) set MIMO_ERANGE, read row 0)
   const float* rw;
   __half* h_out;
   float* part_out;
@@ -95,6 +97,7 @@ struct TcParams {
   int p0_stride;
   const int32_t* btok;        // non-null: B rows are token rows (hi t, lo ntok + t) shared by every unit,
                               // and route q of a unit reads column btok[p0 + q]; null: B rows per route
+  int btok_rows;              // token rows behind btok (a btok entry outside [0, btok_rows) sets MIMO_ERANGE)
   const int32_t* unit_first;  // first unit of the unit's expert group (null: one unit per group)
   const int32_t* unit_nsub;   // units in that group
   const int32_t* num_units;   // device count, null: units_cap
@@ -135,15 +138,17 @@ cudaError_t launch_tc_split_tokens_fp4(const uint16_t* x, int T, int K, uint8_t*
                                        cudaStream_t st);
 cudaError_t launch_tc_split_fp4(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
                                 int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
-                                uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld = 0);
+                                uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld = 0,
+                                int x_rows = 0);
 // Splits bf16 activation rows into the two e4m3 terms + ue8m0 scales of each unit's routes.
-// x rows are x_ld elements apart.
+// x rows are x_ld elements apart; x_rows > 0 bounds the route rows (outside: MIMO_ERANGE, row 0 read).
 cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
                             int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
-                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld = 0);
+                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld = 0,
+                            int x_rows = 0);
 // Expert-parallel exchange over peer memory (peer.cu).
 cudaError_t launch_peer_barrier(int32_t* const* signals, int32_t* my_signals, int rank, int world, int32_t* epoch,
-                                int32_t* status, cudaStream_t st);
+                                uint64_t limit_ns, int32_t* status, cudaStream_t st);
 cudaError_t launch_route_scatter(const uint16_t* x, const float* logits, const float* bias, int T, int H, int E,
                                  int topk, int32_t* const* rows, int ld, int rank, int world, cudaStream_t st);
 cudaError_t launch_routes_prep(const int32_t* idx, const float* w, int route_ld, int rows, int topk, int base, int S,
@@ -187,11 +192,12 @@ cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, i
 cudaError_t launch_to_f16(const uint16_t* x, __half* y, size_t n, int32_t* status, cudaStream_t st);
 // kind: 0 decode gate/up, 1 decode down, 2 prefill gate/up, 3 prefill down
 cudaError_t launch_expert_tiles(const ExpertParams& p, int kind, int num_sms, cudaStream_t st);
-cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H, uint16_t* y,
-                                cudaStream_t st);
+// part_rows: rows of part (gidx entries at or beyond it set MIMO_ERANGE in status and are skipped).
+cudaError_t launch_combine_rows(const float* part, const int32_t* gidx, int M, int topk, int H, long long part_rows,
+                                uint16_t* y, int32_t* status, cudaStream_t st);
 cudaError_t launch_combine_decode(const float* part, const int32_t* gidx, const int32_t* urows,
                                   const int32_t* ucnt, const int32_t* num_unique, int ucap, int R,
-                                  int M, int topk, int H, uint16_t* y, cudaStream_t st);
+                                  int M, int topk, int H, uint16_t* y, int32_t* status, cudaStream_t st);
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* weight, int T, int H, float eps, uint16_t* y,
                            cudaStream_t st);
 cudaError_t launch_combine_prefill(const uint16_t* ypair, const int32_t* inv, const float* w, int T,

@@ -8,11 +8,20 @@
 // caller-provided workspace.  Every GPU that loads the library holds that array (kScratchBytes) until
 // the process exits.
 //
-// Set-up: the device address of the array is looked up once per device (cudaGetSymbolAddress with that
-// device current), on the first call made on that device.  Make that first call before any stream
-// capture begins.  Calls share the array and each call overwrites it, so calls whose work overlaps on
-// the GPU (two streams, or two threads) race; serialise them on one stream.  No part of the scratch has
-// to start at zero: each call writes every scratch word before it reads it.
+// Set-up: the device address of the array is looked up once per device and CUDA context
+// (cudaGetSymbolAddress with that device current), on the first call made there; a later call in a new
+// context of the same device (after cudaDeviceReset, say) looks it up again, because the module and
+// its array are loaded afresh.  Make that first call before any stream capture begins.  Calls share the
+// array and each call overwrites it, so calls whose work overlaps on the GPU (two streams, or two
+// threads) race; serialise them on one stream.  No part of the scratch has to start at zero: for valid
+// route tables each call writes every scratch word before it reads it, and a route row outside [0, M)
+// sets MIMO_ERANGE and reads row 0 instead of stale rows.
+//
+// Kernels: the mma.sync (f16 tensor core, CUDA-core e2m1 decode) decode kernels, not the tcgen05
+// kernels of mimo_moe_experts (those need workspace for their activation term matrices).  The results
+// therefore agree with mimo_moe_experts within the output tolerance, not bit for bit.
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -33,7 +42,26 @@ constexpr size_t kScratchBytes = kX16Bytes + kH16Bytes + kPartBytes;
 static __device__ __align__(256) unsigned char g_expert_scratch[kScratchBytes];
 
 std::mutex g_mu;
-void* g_scratch_ptr[128] = {nullptr};
+struct ScratchAddr {
+  void* ctx = nullptr;  // the CUDA context the address belongs to
+  void* ptr = nullptr;
+};
+ScratchAddr g_scratch[128];
+
+// The current CUDA context (driver handle), or null when it cannot be queried.
+void* current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  }();
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
 
 }  // namespace
 
@@ -64,13 +92,16 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
   void* base = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (g_scratch_ptr[dev] == nullptr) {
+    void* ctx = current_context();
+    ScratchAddr& a = g_scratch[dev];
+    if (a.ptr == nullptr || ctx == nullptr || a.ctx != ctx) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_expert_scratch);
       if (e != cudaSuccess || p == nullptr) return MIMO_ECUDA;
-      g_scratch_ptr[dev] = p;
+      a.ptr = p;
+      a.ctx = ctx;
     }
-    base = g_scratch_ptr[dev];
+    base = a.ptr;
   }
   uint8_t* b = static_cast<uint8_t*>(base);
   __half* x16 = reinterpret_cast<__half*>(b);
@@ -100,6 +131,7 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
   p.units_cap = U;
   p.rtok = urows;
   p.bsrc = x16;
+  p.brows = M;
   p.h_out = h16;
   p.status = status;
   if ((e = launch_expert_tiles(p, 0, sms, st)) != cudaSuccess) return MIMO_ECUDA;
@@ -113,12 +145,13 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
   q.tiles = H / 16;
   q.rtok = nullptr;
   q.bsrc = h16;
+  q.brows = 0;
   q.h_out = nullptr;
   q.rw = uw;
   q.part_out = part;
   q.pairs_rounding = pairs_rounding;
   if ((e = launch_expert_tiles(q, 1, sms, st)) != cudaSuccess) return MIMO_ECUDA;
-  if ((e = launch_combine_decode(part, gather_idx, urows, ucnt, num_unique, U, R, M, topk, H, y, st)) !=
+  if ((e = launch_combine_decode(part, gather_idx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st)) !=
       cudaSuccess)
     return MIMO_ECUDA;
   return MIMO_OK;

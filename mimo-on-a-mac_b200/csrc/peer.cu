@@ -29,9 +29,10 @@ __device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
 
 // One warp: lane r < world signals rank r and then waits for rank r's signal here.  `epoch` is this
 // rank's device counter (the same count of barriers runs on every rank).  Waits give up after
-// ~2 s with MIMO_ETIMEOUT.
+// limit_ns with MIMO_ETIMEOUT; the kernel then returns, so a rank that never arrives costs its peers
+// one expired wait, not a hung GPU.
 __global__ void peer_barrier_kernel(int32_t* const* signals, int32_t* my_signals, int rank, int world,
-                                    int32_t* epoch, int32_t* status) {
+                                    int32_t* epoch, uint64_t limit_ns, int32_t* status) {
   const int lane = threadIdx.x;
   const int32_t e = *epoch + 1;
   __syncwarp();
@@ -40,7 +41,7 @@ __global__ void peer_barrier_kernel(int32_t* const* signals, int32_t* my_signals
   if (lane < world) {
     const uint64_t t0 = global_timer_ns();
     while (ld_acquire_sys(my_signals + lane) < e) {
-      if (global_timer_ns() - t0 > 2000000000ull) {
+      if (global_timer_ns() - t0 > limit_ns) {
         set_status(status, MIMO_ETIMEOUT);
         break;
       }
@@ -173,9 +174,9 @@ cudaError_t launch_routes_prep(const int32_t* idx, const float* w, int route_ld,
 }
 
 cudaError_t launch_peer_barrier(int32_t* const* signals, int32_t* my_signals, int rank, int world, int32_t* epoch,
-                                int32_t* status, cudaStream_t st) {
+                                uint64_t limit_ns, int32_t* status, cudaStream_t st) {
   if (world < 1 || world > 32) return cudaErrorInvalidValue;
-  peer_barrier_kernel<<<1, 32, 0, st>>>(signals, my_signals, rank, world, epoch, status);
+  peer_barrier_kernel<<<1, 32, 0, st>>>(signals, my_signals, rank, world, epoch, limit_ns, status);
   return cudaGetLastError();
 }
 

@@ -158,6 +158,19 @@ __device__ __forceinline__ void item_coords(const TcParams& p, long long i, int&
   }
 }
 
+// Routes of a unit, at most `cap`: units at a fixed stride (unit_p0 null: p0 = unit * p0_stride) own
+// p0_stride route slots, so a count above that sets MIMO_ERANGE and is cut (it would write into the
+// next unit's rows, or past the last one's).
+__device__ __forceinline__ int unit_routes(const TcParams& p, int unit, int cap) {
+  const int lim = p.unit_p0 ? cap : min(cap, p.p0_stride);
+  const int c = __ldg(p.unit_cnt + unit);
+  if (c > lim) {
+    set_status(p.status, MIMO_ERANGE);
+    return lim;
+  }
+  return max(c, 0);
+}
+
 // EPI epilogue warps (a multiple of 4): EPI / 4 per TMEM lane quadrant, each taking NTOK / (EPI / 4) of
 // the routes.  Prefill uses 16: its per-route SwiGLU and term split are long dependent chains, and
 // four warps per SM sub-partition hide their latency where two cannot.
@@ -435,7 +448,7 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
       int unit, tile;
       item_coords(p, it, unit, tile);
       const int slot = __ldg(p.unit_slot + unit);
-      const int cnt = min(__ldg(p.unit_cnt + unit), NTOK);
+      const int cnt = unit_routes(p, unit, NTOK);
       const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
       if (!aborted && !mbar_wait(&acc_full[buf], use)) {
         set_status(p.status, MIMO_ETIMEOUT);
@@ -451,7 +464,7 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
           float h = 0.f;
           if (q < cnt) {
             const int t = __ldg(p.btok + p0 + q);
-            if (t >= 0 && t < NTOK) {
+            if (t >= 0 && t < (p.btok_rows > 0 ? min(p.btok_rows, NTOK) : NTOK)) {
               float gh[1], gl[1], uh[1], ul[1];
               const uint32_t c0 = tbase + lane_base + (uint32_t)(2 * buf) * N + t;
               tmem_ld<1>(c0, gh);
@@ -968,7 +981,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
       const int buf = (int)(n & 1);
       const uint32_t use = (uint32_t)((n >> 1) & 1);
       const int slot = __ldg(p.unit_slot + unit);
-      const int cnt = min(__ldg(p.unit_cnt + unit), NTOK);
+      const int cnt = unit_routes(p, unit, NTOK);
       const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
       if (!aborted && !mbar_wait(&acc_full[buf], use)) {
         set_status(g.status, MIMO_ETIMEOUT);
@@ -1008,7 +1021,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
           bool ok = q < cnt;
           if (!dn && g.btok && ok) {
             col = __ldg(g.btok + p0 + q);
-            if (col < 0 || col >= NTOK) {
+            if (col < 0 || col >= (g.btok_rows > 0 ? min(g.btok_rows, NTOK) : NTOK)) {
               if (lane == 0) set_status(g.status, MIMO_ERANGE);
               ok = false;
               col = 0;
@@ -1406,7 +1419,7 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_pair_kernel(const __grid
       int unit, tile;
       item_coords(p, it, unit, tile);
       const int slot = __ldg(p.unit_slot + unit);
-      const int cnt = min(__ldg(p.unit_cnt + unit), NTOK);
+      const int cnt = unit_routes(p, unit, NTOK);
       const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
       if (!aborted && !mbar_wait(acc_full, (uint32_t)(n & 1))) {
         set_status(p.status, MIMO_ETIMEOUT);
@@ -1535,15 +1548,21 @@ __global__ void __launch_bounds__(128) split_rows_kernel(const uint16_t* __restr
                                                          const int32_t* __restrict__ rtok,
                                                          const int32_t* __restrict__ num_units, int units_cap,
                                                          uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
-                                                         int32_t* status, int x_ld) {
+                                                         int32_t* status, int x_ld, int x_rows) {
   constexpr int N = 2 * NTOK;
   const int unit = blockIdx.x / NTOK, q = blockIdx.x % NTOK;
   const int units = num_units ? min(*num_units, units_cap) : units_cap;
   if (unit >= units) return;
-  const int cnt = min(unit_cnt[unit], NTOK);
+  const int lim = unit_p0 ? NTOK : min(NTOK, p0_stride);
+  const int cnt = min(unit_cnt[unit], lim);
+  if (q == 0 && unit_cnt[unit] > lim) set_status(status, MIMO_ERANGE);
   if (q >= cnt) return;
   const int p0 = unit_p0 ? unit_p0[unit] : unit * p0_stride;
-  const int tok = rtok ? rtok[p0 + q] : p0 + q;
+  int tok = rtok ? rtok[p0 + q] : p0 + q;
+  if (x_rows > 0 && (tok < 0 || tok >= x_rows)) {  // never read past the activation rows
+    if (threadIdx.x == 0) set_status(status, MIMO_ERANGE);
+    tok = 0;
+  }
   const size_t rh = (size_t)unit * N + q, rl = rh + NTOK;
   const int nb = K / 32;
   for (int blk = threadIdx.x; blk < nb; blk += blockDim.x) {
@@ -1580,15 +1599,21 @@ __global__ void __launch_bounds__(128) split_rows_fp4_kernel(const uint16_t* __r
                                                              const int32_t* __restrict__ rtok,
                                                              const int32_t* __restrict__ num_units, int units_cap,
                                                              uint8_t* __restrict__ bq, uint8_t* __restrict__ bs,
-                                                             int32_t* status, int x_ld) {
+                                                             int32_t* status, int x_ld, int x_rows) {
   constexpr int NTOK = kTcDecodeRoutes, N = kFp4Terms * NTOK;
   const int unit = blockIdx.x / NTOK, q = blockIdx.x % NTOK;
   const int units = num_units ? min(*num_units, units_cap) : units_cap;
   if (unit >= units) return;
-  const int cnt = min(unit_cnt[unit], NTOK);
+  const int lim = unit_p0 ? NTOK : min(NTOK, p0_stride);
+  const int cnt = min(unit_cnt[unit], lim);
+  if (q == 0 && unit_cnt[unit] > lim) set_status(status, MIMO_ERANGE);
   if (q >= cnt) return;
   const int p0 = unit_p0 ? unit_p0[unit] : unit * p0_stride;
-  const int tok = rtok ? rtok[p0 + q] : p0 + q;
+  int tok = rtok ? rtok[p0 + q] : p0 + q;
+  if (x_rows > 0 && (tok < 0 || tok >= x_rows)) {  // never read past the activation rows
+    if (threadIdx.x == 0) set_status(status, MIMO_ERANGE);
+    tok = 0;
+  }
   const size_t r0 = (size_t)unit * N + q;
   const int nb = K / 32;
   for (int blk = threadIdx.x; blk < nb; blk += blockDim.x)
@@ -1685,12 +1710,13 @@ cudaError_t launch_tc_split_tokens_fp4(const uint16_t* x, int T, int K, uint8_t*
 }
 cudaError_t launch_tc_split_fp4(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
                                 int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
-                                uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld) {
+                                uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld, int x_rows) {
   if (K % 128 != 0 || units_cap < 1) return cudaErrorInvalidValue;
   if (x_ld <= 0) x_ld = K;
   if (x_ld < K || x_ld % 8) return cudaErrorInvalidValue;
   tc::split_rows_fp4_kernel<<<units_cap * kTcDecodeRoutes, 128, 0, st>>>(x, K, unit_cnt, unit_p0, p0_stride, rtok,
-                                                                         num_units, units_cap, bq, bs, status, x_ld);
+                                                                         num_units, units_cap, bq, bs, status, x_ld,
+                                                                         x_rows);
   return cudaGetLastError();
 }
 cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
@@ -1701,16 +1727,17 @@ cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq,
 }
 cudaError_t launch_tc_split(const uint16_t* x, int K, const int32_t* unit_cnt, const int32_t* unit_p0,
                             int p0_stride, const int32_t* rtok, const int32_t* num_units, int units_cap,
-                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld) {
+                            int ntok, uint8_t* bq, uint8_t* bs, int32_t* status, cudaStream_t st, int x_ld,
+                            int x_rows) {
   if (K % 128 != 0 || units_cap < 1) return cudaErrorInvalidValue;
   if (x_ld <= 0) x_ld = K;
   if (x_ld < K || x_ld % 8) return cudaErrorInvalidValue;  // 16-byte aligned rows
   if (ntok == kTcDecodeRoutes)
     tc::split_rows_kernel<kTcDecodeRoutes><<<units_cap * kTcDecodeRoutes, 128, 0, st>>>(
-        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld);
+        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld, x_rows);
   else if (ntok == kTcPrefillRoutes)
     tc::split_rows_kernel<kTcPrefillRoutes><<<units_cap * kTcPrefillRoutes, 128, 0, st>>>(
-        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld);
+        x, K, unit_cnt, unit_p0, p0_stride, rtok, num_units, units_cap, bq, bs, status, x_ld, x_rows);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();

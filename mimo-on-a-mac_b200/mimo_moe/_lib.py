@@ -48,10 +48,12 @@ SIGNATURES = {
     "mimo_moe_peer_open": (c_int32, [c_void_p, c_void_p]),
     "mimo_moe_peer_close": (c_int32, [c_void_p]),
     "mimo_moe_peer_free": (c_int32, [c_void_p]),
-    "mimo_moe_peer_barrier": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_peer_barrier": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p,
+                                        c_void_p]),
     "mimo_moe_route_scatter": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                          c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
-    "mimo_moe_combine": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
+    "mimo_moe_combine": (c_int32, [c_void_p, ctypes.c_int64, c_void_p, c_int32, c_int32, c_int32, c_void_p,
+                                   c_void_p, c_void_p]),
     "mimo_moe_read_file_spans": (c_int32, [ctypes.c_char_p, c_void_p, c_int32, c_int32, ctypes.c_int64, c_int32,
                                            c_int32, c_void_p]),
     "mimo_moe_rmsnorm": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),

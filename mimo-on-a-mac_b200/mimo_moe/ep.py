@@ -30,6 +30,34 @@ import torch.distributed as dist
 from . import ops
 
 RouterFn = Callable[[torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
+
+
+class PhaseTrace:
+    """Optional per-phase timing of an eager step: `mark(name)` records a CUDA event on the current
+    stream after the work issued since the previous mark; `summary()` gives the mean milliseconds of
+    each phase over the recorded steps (call after synchronising).  Never active inside graph capture."""
+
+    def __init__(self):
+        self.steps = []
+
+    def start(self):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.steps.append([("start", ev)])
+
+    def mark(self, name: str):
+        if self.steps:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.steps[-1].append((name, ev))
+
+    def summary(self):
+        out = {}
+        for marks in self.steps:
+            for (_, a), (name, b) in zip(marks, marks[1:]):
+                out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        n = max(1, len(self.steps))
+        return {k: v / n for k, v in out.items()}
 ExpertsFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, bool], torch.Tensor]
 CombineFn = Callable[[torch.Tensor, int, int], torch.Tensor]
 
@@ -134,8 +162,10 @@ class PeerExpertParallelMoE:
     process group is destroyed.  T is fixed at construction."""
 
     def __init__(self, pools_local, router_w: torch.Tensor, bias: Optional[torch.Tensor], T: int, *,
-                 num_experts: int = 256, topk: int = 8, group=None):
+                 num_experts: int = 256, topk: int = 8, group=None, timeout_us: int = 0):
         from ._lib import check, lib
+        self.timeout_us = timeout_us  # barrier wait limit (0: the library's 2 s)
+        self.trace: Optional[PhaseTrace] = None
         self.L, self.check = lib(), check
         self.group = group
         self.world = N = dist.get_world_size(group)
@@ -178,7 +208,8 @@ class PeerExpertParallelMoE:
 
     def _barrier(self, st: int) -> None:
         self.check(self.L.mimo_moe_peer_barrier(self.tab["sig"].data_ptr(), self.local["sig"], self.rank,
-                                                self.world, self.epoch.data_ptr(), self.status.data_ptr(), st),
+                                                self.world, self.epoch.data_ptr(), self.timeout_us,
+                                                self.status.data_ptr(), st),
                    "peer_barrier")
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
@@ -194,18 +225,32 @@ class PeerExpertParallelMoE:
         x = x.to(torch.bfloat16).contiguous()
         st = torch.cuda.current_stream(self.dev).cuda_stream
         T, k, H, N = self.T, self.k, self.H, self.world
+        tr = self.trace
+        if tr:
+            tr.start()
         self.check(self.L.mimo_moe_route_scatter(
             x.data_ptr(), T, H, router_w.data_ptr(), None if bias is None else bias.data_ptr(),
             self.E, k, self.tab["rows"].data_ptr(), self.ld, self.rank, N, self.logits.data_ptr(), st),
             "route_scatter")
+        if tr:
+            tr.mark("route_scatter")
         self._barrier(st)
+        if tr:
+            tr.mark("barrier_dispatch")
         rows = self.local["rows"]
         self.check(self.L.mimo_moe_experts_routes(
             rows, 2 * self.ld, N * T, pools.struct, self.expert_base, rows + 2 * H,
             rows + 2 * H + 4 * k, self.ld, k, int(pairs_rounding_for(T)), None, self.tab["recv"].data_ptr(),
             T * k, self.ws.data_ptr(), self.ws.numel(), self.status.data_ptr(), st), "experts_routes")
+        if tr:
+            tr.mark("experts")
         self._barrier(st)
-        self.check(self.L.mimo_moe_combine(self.local["recv"], None, T, k, H, self.y.data_ptr(), st), "combine")
+        if tr:
+            tr.mark("barrier_return")
+        self.check(self.L.mimo_moe_combine(self.local["recv"], T * k, None, T, k, H, self.y.data_ptr(),
+                                           self.status.data_ptr(), st), "combine")
+        if tr:
+            tr.mark("combine")
         return self.y
 
     def close(self) -> None:

@@ -355,7 +355,8 @@ def combine(part: torch.Tensor, M: int, k: int = TOPK, gather_idx: Optional[torc
     H = part.shape[1]
     y = out if out is not None else torch.empty(M, H, dtype=torch.bfloat16, device=part.device)
     gi = None if gather_idx is None else gather_idx.to(device=part.device, dtype=torch.int32).contiguous()
-    check(lib().mimo_moe_combine(part.data_ptr(), _ptr(gi), M, k, H, y.data_ptr(), _stream()), "combine")
+    check(lib().mimo_moe_combine(part.data_ptr(), part.shape[0], _ptr(gi), M, k, H, y.data_ptr(), None, _stream()),
+          "combine")
     return y
 
 

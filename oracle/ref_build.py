@@ -17,12 +17,23 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF_ROOT = Path(os.environ.get("MIMO_REFERENCE_ROOT", "/root/reference"))
-KERNELS = REF_ROOT / "engine" / "mimo_stream" / "kernels.py"
 LIB = OUT / "libref_kernels.so"
+ENV = "MIMO_REFERENCE_ROOT"  # the reference checkout (the directory holding engine/mimo_stream)
+
+
+def reference_root() -> Path:
+    root = os.environ.get(ENV)
+    if not root:
+        raise RuntimeError(f"set {ENV} to the reference checkout (the directory that holds engine/mimo_stream)")
+    return Path(root)
+
+
+def kernels_file() -> Path:
+    return reference_root() / "engine" / "mimo_stream" / "kernels.py"
 
 
 def extract():
+    KERNELS = kernels_file()
     src = KERNELS.read_text()
     tree = ast.parse(src)
     strings, funcs = {}, {}
@@ -47,10 +58,11 @@ def extract():
 
 
 def build(force: bool = False) -> Path:
+    KERNELS = kernels_file()
     if not KERNELS.exists():
         if LIB.exists():
             return LIB
-        raise RuntimeError(f"reference tree not found at {REF_ROOT}")
+        raise RuntimeError(f"{ENV}={reference_root()}: {KERNELS.relative_to(reference_root())} not found")
     cpp = HERE / "ref_kernels.cpp"
     if not force and LIB.exists() and LIB.stat().st_mtime > max(cpp.stat().st_mtime, KERNELS.stat().st_mtime):
         return LIB

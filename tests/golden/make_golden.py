@@ -1,7 +1,7 @@
 """Generate the golden fixtures of this directory from the reference's own code (run in a container that
 has the read-only reference tree; the outputs are committed, the reference code is not).
 
-  python oracle/ref_build.py && python tests/golden/make_golden.py
+  MIMO_REFERENCE_ROOT=<reference checkout> python oracle/ref_build.py && python tests/golden/make_golden.py
 
 Sources of truth:
   * group_routes.npz - the reference's numpy group_routes (engine/mimo_stream/kernels.py:149-173),

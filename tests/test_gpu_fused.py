@@ -8,7 +8,8 @@ child process):
 e4m3-fused must equal e4m3 bit for bit; fp4 differs from them only by the activation terms' residual
 (about 1e-6 of a dot product) and the sum of five accumulator columns instead of two, so its block
 output stays within rel_err 1e-2 of the e4m3 path's (the oracle bar, engine/tests/test_kernels.py:54-56)
-and most bf16 outputs agree exactly (the rest differ by bf16 rounding flips)."""
+and most bf16 outputs agree exactly (the rest differ by bf16 rounding flips).  Every variant is also
+held to rel_err <= 1e-2 against the CPU restatement of the reference path on the same routes."""
 import os
 import subprocess
 import sys
@@ -33,8 +34,8 @@ status = torch.zeros(1, dtype=torch.int32, device=dev)
 out = []
 for T in {Ts}:
     x = synth.hidden(T, seed=70 + T).to(dev)
-    y = mimo_moe.moe_block(x, W, None, pool, status=status)
-    out.append(y.view(torch.int16).cpu().numpy())
+    y, idx, w = mimo_moe.moe_block(x, W, None, pool, status=status, return_routes=True)
+    out += [y.view(torch.int16).cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy()]
 assert int(status.item()) == 0, int(status.item())
 np.savez({path!r}, *out)
 """
@@ -48,7 +49,23 @@ def _run(tmp_path, S, kernel):
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     z = np.load(path)
-    return [z[f"arr_{i}"] for i in range(len(TS))]
+    return [(z[f"arr_{3 * i}"], z[f"arr_{3 * i + 1}"], z[f"arr_{3 * i + 2}"]) for i in range(len(TS))]
+
+
+def _oracle(gpu, S, outs):
+    """The CPU restatement of the reference path (oracle/batched.py: the dispatch rule of
+    engine/mimo_stream/model.py:184-219 and 324-336 over the same pool) given each run's routes."""
+    import mimo_moe
+    from oracle import batched as B
+    from oracle import synth
+    pool = B.pool_to_cpu(mimo_moe.ExpertPools.synthetic(S, seed=0, layer=2, device=gpu))
+    return [B.moe_layer(synth.hidden(T, seed=70 + T).float().numpy(), pool, idx, w)
+            for T, (_, idx, w) in zip(TS, outs)]
+
+
+def _rel(a_bits, ref):
+    a = torch.from_numpy(a_bits).view(torch.bfloat16).float().numpy()
+    return float(np.abs(a - ref).max() / np.abs(ref).max())
 
 
 @pytest.mark.parametrize("S", [32, 256])
@@ -56,8 +73,14 @@ def test_decode_kernels_agree(gpu, tmp_path, S):
     e4 = _run(tmp_path, S, "e4m3")
     e4f = _run(tmp_path, S, "e4m3-fused")
     fp4 = _run(tmp_path, S, "fp4")
-    for T, a, b, c in zip(TS, e4, e4f, fp4):
+    refs = _oracle(gpu, S, e4)
+    for T, (a, ia, wa), (b, ib, wb), (c, ic, wc), ref in zip(TS, e4, e4f, fp4, refs):
+        assert np.array_equal(ia, ib) and np.array_equal(ia, ic) and np.array_equal(wa, wc), T  # same routes
         assert np.array_equal(a, b), T
+        for name, v in (("e4m3", a), ("fp4", c)):   # each variant against the oracle itself
+            rel = _rel(v, ref)
+            print(f"S={S} T={T} {name}: rel_err vs oracle {rel:.2e}")
+            assert rel <= 1e-2, (name, T, rel)
         fa = torch.from_numpy(a).view(torch.bfloat16).float().numpy()
         fc = torch.from_numpy(c).view(torch.bfloat16).float().numpy()
         rel = np.abs(fa - fc).max() / np.abs(fa).max()

@@ -6,7 +6,8 @@ runs in a child process):
 
 Each SM of a pair computes its own 128 weight rows against all of the unit's term rows with the same
 K blocks and scales as the single-SM kernel, so the block outputs agree within the oracle bar
-(engine/tests/test_kernels.py:54-56) and nearly all bf16 outputs are identical."""
+(engine/tests/test_kernels.py:54-56) and nearly all bf16 outputs are identical; both are also held to
+that bar against the CPU restatement of the reference path on the same routes."""
 import os
 import subprocess
 import sys
@@ -31,8 +32,8 @@ status = torch.zeros(1, dtype=torch.int32, device=dev)
 out = []
 for T in {Ts}:
     x = synth.hidden(T, seed=90 + T).to(dev)
-    y = mimo_moe.moe_block(x, W, None, pool, status=status)
-    out.append(y.view(torch.int16).cpu().numpy())
+    y, idx, w = mimo_moe.moe_block(x, W, None, pool, status=status, return_routes=True)
+    out += [y.view(torch.int16).cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy()]
 torch.cuda.synchronize()
 assert int(status.item()) == 0, int(status.item())
 np.savez({path!r}, *out)
@@ -47,19 +48,39 @@ def _run(tmp_path, S, kernel):
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
     z = np.load(path)
-    return [z[f"arr_{i}"] for i in range(len(TS))]
+    return [(z[f"arr_{3 * i}"], z[f"arr_{3 * i + 1}"], z[f"arr_{3 * i + 2}"]) for i in range(len(TS))]
+
+
+def _oracle(gpu, S, outs):
+    """The CPU restatement of the reference path (oracle/batched.py: the dispatch rule of
+    engine/mimo_stream/model.py:184-219 and 324-336 over the same pool) given each run's routes."""
+    import mimo_moe
+    from oracle import batched as B
+    from oracle import synth
+    pool = B.pool_to_cpu(mimo_moe.ExpertPools.synthetic(S, seed=0, layer=3, device=gpu))
+    return [B.moe_layer(synth.hidden(T, seed=90 + T).float().numpy(), pool, idx, w)
+            for T, (_, idx, w) in zip(TS, outs)]
+
+
+def _rel(a_bits, ref):
+    a = torch.from_numpy(a_bits).view(torch.bfloat16).float().numpy()
+    return float(np.abs(a - ref).max() / np.abs(ref).max())
 
 
 @pytest.mark.parametrize("S", [32, 256])
 def test_pair_prefill_agrees_with_single_sm(gpu, tmp_path, S):
     single = _run(tmp_path, S, "single")
     pair = _run(tmp_path, S, "pair")
-    for T, a, b in zip(TS, single, pair):
+    refs = _oracle(gpu, S, single)
+    for T, (a, ia, _), (b, ib, _), ref in zip(TS, single, pair, refs):
+        assert np.array_equal(ia, ib), T
         fa = torch.from_numpy(a).view(torch.bfloat16).float().numpy()
         fb = torch.from_numpy(b).view(torch.bfloat16).float().numpy()
         assert np.isfinite(fb).all(), T
         rel = np.abs(fa - fb).max() / np.abs(fa).max()
         same = (a == b).mean()
-        print(f"T={T} S={S}: rel_err {rel:.2e}, identical {same:.4f}")
+        ra, rb = _rel(a, ref), _rel(b, ref)
+        print(f"T={T} S={S}: rel_err {rel:.2e}, identical {same:.4f}; vs oracle single {ra:.2e} pair {rb:.2e}")
         assert rel <= 1e-2, (T, rel)
         assert same >= 0.99, (T, same)
+        assert ra <= 1e-2 and rb <= 1e-2, (T, ra, rb)

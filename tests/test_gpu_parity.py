@@ -247,7 +247,11 @@ def test_moe_block_end_to_end(gpu, T):
     y, idx, w = mimo_moe.moe_block(x.to(gpu), W.to(gpu), bias.to(gpu), pool, return_routes=True)
     idx_np, w_np = idx.cpu().numpy(), w.cpu().numpy()
     _, ri, _ = O.router(x.float().numpy(), W.float().numpy(), bias.numpy())
-    assert (np.sort(idx_np, 1) == np.sort(ri, 1)).mean() > 0.99
+    # routes chosen from the GPU's logits vs the oracle's float64-rounded logits: a route flips only
+    # when two selection scores sit within the logits' ~1e-6 float32 error of each other
+    flipped = int(sum(len(set(a) ^ set(b)) // 2 for a, b in zip(idx_np, ri)))
+    print(f"T={T}: {flipped} of {T * 8} routes differ from the oracle router's")
+    assert flipped <= max(1, T * 8 // 100)
     assert O.rel_err(f32(y), O.moe_layer(x.float().numpy(), opool, idx_np, w_np)) <= TOL_ORACLE
 
 

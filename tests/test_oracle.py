@@ -168,3 +168,36 @@ def test_rmsnorm_oracle_properties():
     w = O.bf16_round(rng.standard_normal(4096).astype(np.float32))
     assert np.array_equal(O.rmsnorm(x, w), O.bf16_round(w * y))
     assert np.array_equal(O.rmsnorm(np.zeros((1, 64), np.float32)), np.zeros((1, 64), np.float32))
+
+
+def test_batched_pair_path_equals_the_oracle_bit_for_bit():
+    """oracle/batched.py (torch, one float64 product per expert, used for the BASELINE-size GPU checks)
+    against mimo_oracle.moe_pairs on full-size experts: every output bit equal, with a slot map, shared
+    experts across rows and the M = 1 case."""
+    import torch
+    from oracle import batched as B
+    sp = synth.SynthPool(0, 6)
+    S = 4
+    pool = {n: torch.from_numpy(np.stack([sp[n][e] for e in range(S)]).view(np.int32 if n.endswith("_w") else np.uint8))
+            for n in ("gate_w", "gate_s", "up_w", "up_s", "down_w", "down_s")}
+    rng = np.random.default_rng(12)
+    for T, k in ((1, 3), (9, 3)):
+        x = synth.hidden(T, seed=60 + T).float().numpy()
+        inds = np.stack([rng.choice(S, k, replace=False) for _ in range(T)]).astype(np.int32)
+        w = rng.random((T, k)).astype(np.float32)
+        want = O.moe_pairs(x, O.Pool(sp, cache=S), inds, w)
+        assert np.array_equal(B.moe_pairs(x, pool, inds, w).view(np.uint32), want.view(np.uint32))
+        experts = np.array([200, 7, 31, 90])               # expert ids -> slots through slot_of
+        slot_of = np.full(256, -1, np.int32)
+        slot_of[experts] = np.arange(S)
+        got = B.moe_pairs(x, pool, experts[inds], w, slot_of=slot_of)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # the distinct-expert path (2 <= T <= 8): route-order combine and the scatter-add order
+    x = synth.hidden(5, seed=71).float().numpy()
+    inds = np.stack([rng.choice(S, 3, replace=False) for _ in range(5)]).astype(np.int32)
+    w = rng.random((5, 3)).astype(np.float32)
+    opool = O.Pool(sp, cache=S)
+    assert np.array_equal(B.moe_layer(x, pool, inds, w).view(np.uint32), O.moe_layer(x, opool, inds, w, R=8).view(np.uint32))
+    uids, urows, ucnt, uw, _ = O.group_routes(inds, w)
+    want = O.moe_experts(x, opool, uids, urows, ucnt, uw, gather_idx=None)
+    assert np.array_equal(B.moe_grouped(x, pool, inds, w, unit_order=True).view(np.uint32), want.view(np.uint32))
