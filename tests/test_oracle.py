@@ -201,3 +201,15 @@ def test_batched_pair_path_equals_the_oracle_bit_for_bit():
     uids, urows, ucnt, uw, _ = O.group_routes(inds, w)
     want = O.moe_experts(x, opool, uids, urows, ucnt, uw, gather_idx=None)
     assert np.array_equal(B.moe_grouped(x, pool, inds, w, unit_order=True).view(np.uint32), want.view(np.uint32))
+
+
+def test_overlap_bias_gives_the_config1_expert_sharing():
+    """BASELINE config 1's forced-overlap variant: consecutive rows of the seeded 8-row decode batches share
+    2.6 +- 0.1 of their 8 experts under synth.overlap_bias() (free routing shares ~0.25)."""
+    W = synth.router_weight().float().numpy()
+    b = synth.overlap_bias().numpy()
+    shared = []
+    for i in range(16):
+        inds, _ = O.topk_from_logits(O.router_logits(synth.hidden(8, seed=2 + 1000 * i).float().numpy(), W), b)
+        shared += [len(set(inds[t]) & set(inds[t + 1])) for t in range(7)]
+    assert abs(np.mean(shared) - 2.6) <= 0.1, np.mean(shared)
