@@ -324,6 +324,31 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------------ GPU arm
+class BatchGraphs:
+    """One CUDA graph per resident input batch (decode steps are a few short kernels, so a replayed
+    graph keeps host launch costs out of the step; capturing one graph per batch keeps the input copy
+    into a single graph's input buffer out of it too).  g(i) replays batch i's step and returns its
+    output (the block's fixed output buffer)."""
+
+    def __init__(self, fn, xs, warmup: int = 2):
+        import torch
+        self.graphs, self.out = [], None
+        for x in xs:  # tensor maps, workspaces and communicators are created outside the captures
+            for _ in range(warmup):
+                fn(x)
+        torch.cuda.synchronize()
+        for x in xs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.out = fn(x)
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+
+    def __call__(self, i):
+        self.graphs[i].replay()
+        return self.out
+
+
 class Ctx:
     """Process-wide state of the GPU arm: ranks, device, the single-GPU expert pool (shared by the
     workloads measured in one run) and the router weight."""
@@ -392,7 +417,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
 
     import mimo_moe
     from mimo_moe import _lib, synthetic
-    from mimo_moe.ep import GraphedStep, PhaseTrace
+    from mimo_moe.ep import PhaseTrace
 
     world, rank, dev, NE = ctx.world, ctx.rank, ctx.dev, ctx.NE
     B = WORKLOADS[workload][0]
@@ -420,13 +445,13 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
             return blk(x)
         return mimo_moe.moe_block(x, W, bias, pool, status=status, out=y if out is None else out)
 
-    # decode steps (4-9 kernels) replay as one CUDA graph so host launch cost does not set the pace;
-    # prefill steps are long enough to run eagerly
-    gstep = GraphedStep(eager, B, H, dev) if B <= 8 else None
+    # decode steps (4-9 kernels) replay as CUDA graphs, one per resident input batch, so host launch
+    # cost does not set the pace; prefill steps are long enough to run eagerly
+    gstep = BatchGraphs(eager, xs) if B <= 8 else None
 
     def step(i):
         if gstep is not None:
-            gstep(xs[i % nb])
+            gstep(i % nb)
         else:
             eager(xs[i % nb])
 
@@ -436,7 +461,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     clocks = ClockSampler(ctx.local)
     clocks.start()
     time.sleep(0.3)
-    _lib.check(L.mimo_moe_profile_enable(4 * steps + 8), "profile_enable")
+    _lib.check(L.mimo_moe_profile_enable(6 * steps + 8), "profile_enable")
     if ep and not peer:
         blk.routes_received = 0
     ms = _timed(ctx, steps, step)
@@ -447,7 +472,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     phases = None
     if gstep is not None or peer:  # graph replays carry no events: time the kernels in an eager pass
         nprof = min(steps, 50)
-        _lib.check(L.mimo_moe_profile_enable(4 * nprof + 8), "profile_enable")
+        _lib.check(L.mimo_moe_profile_enable(6 * nprof + 8), "profile_enable")
         if peer:
             blk.trace = PhaseTrace()
         for i in range(nprof):
@@ -482,19 +507,23 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     steps_Ul = [U_local[i % nb] for i in range(steps)]
     hbm, tflops_peak, peak_kind = peaks()
     kind_gu, kind_dn = (0, 1) if B <= 8 else (2, 3)
-    n_gu, n_dn, n_fz = int(launches[0][kind_gu]), int(launches[0][kind_dn]), int(launches[0][4])
+    # one-launch decode kinds: 4 (tile-scheduled fused), 5 (stream-K)
+    kind_fz = 5 if int(launches[0][5]) > 0 else 4
+    n_gu, n_dn, n_fz = int(launches[0][kind_gu]), int(launches[0][kind_dn]), int(launches[0][kind_fz])
     gu_ms = float(launches[1][kind_gu]) / max(1, n_gu)
     dn_ms = float(launches[1][kind_dn]) / max(1, n_dn)
-    fz_ms = float(launches[1][4]) / max(1, n_fz)
+    fz_ms = float(launches[1][kind_fz]) / max(1, n_fz)
     Ul = statistics.mean(steps_Ul)
     gu_bytes = Ul * GATEUP_BYTES
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms > 0 else 0.0
     if B <= 8 and n_fz > 0:  # decode, one launch streams every distinct expert's 3 matrices once
         fz_bytes = Ul * EXPERT_BYTES
         fz_gbs = fz_bytes / (fz_ms * 1e-3) / 1e9
-        roofline = {"kernel": "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight, one launch)",
-                    "bound": "hbm", "achieved": fz_gbs, "peak": hbm, "unit": "GB/s", "frac": fz_gbs / hbm,
-                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None, "algorithmic_bytes_per_launch": fz_bytes}
+        name = ("tc_decode_sk_kernel (stream-K decode: gate/up + SwiGLU, then down x weight, one launch)"
+                if kind_fz == 5 else "tc_decode_fused_kernel (decode gate/up + SwiGLU + down x weight, one launch)")
+        roofline = {"kernel": name, "bound": "hbm", "achieved": fz_gbs, "peak": hbm, "unit": "GB/s",
+                    "frac": fz_gbs / hbm, "peak_kind": f"{peak_kind} hbm_gbs",
+                    "traffic": None, "algorithmic_bytes_per_launch": fz_bytes}
     elif B <= 8:   # decode: the gate/up kernel streams each distinct expert's gate+up bytes once
         roofline = {"kernel": "tc_expert_kernel<NM=2,NTOK=8,MODE=0> (decode gate/up + SwiGLU)", "bound": "hbm",
                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -520,6 +549,9 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
         # the whole step against its HBM floor: every expert's bytes once
         roofline["step_hbm_floor_ms"] = Ul * EXPERT_BYTES / (hbm * 1e9) * 1e3
     roofline["kernel_ms"] = {"fused": fz_ms} if n_fz > 0 else {"gate_up": gu_ms, "down": dn_ms}
+    for kind, name in ((6, "route"), (7, "combine")):  # the decode chain's other launches (single GPU)
+        if int(launches[0][kind]) > 0:
+            roofline["kernel_ms"][name] = float(launches[1][kind]) / int(launches[0][kind])
     expert_gbs = sum(steps_U) * EXPERT_BYTES / (ms * 1e-3) / 1e9
 
     # end to end through the public API, as a drop-in caller makes it: every step copies the step's x from
@@ -536,9 +568,10 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
         e2e_step(i)
     e2e_ms = _timed(ctx, steps, e2e_step)
     e2e_graph = None
-    if gstep is not None:   # the same with the block replayed as a CUDA graph (pinned x straight into its input)
+    if gstep is not None:   # the same with the block replayed as a CUDA graph (pinned x into its input)
         def g_step(i):
-            yd = gstep(xh[i % nb])
+            xs[i % nb].copy_(xh[i % nb], non_blocking=True)
+            yd = gstep(i % nb)
             yh.copy_(yd, non_blocking=True)
         g_ms = _timed(ctx, steps, g_step)
         e2e_graph = B * world * steps / (g_ms * 1e-3)
@@ -550,7 +583,10 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     # builder, term split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch,
     # 2 unit builders, term split, gate/up, down, per-route combine, weighted combine.
     fused = n_fz > 0
-    launches_per_step = ((7 if fused else 8) if peer else 12) if ep else ((3 if fused else 4) if B <= 8 else 11)
+    # single-GPU decode: route + the stream-K launch (its epilogue also combines), route + fused + combine,
+    # or route + gate/up + down + combine
+    per_decode = 2 if kind_fz == 5 and n_fz else (3 if fused else 4)
+    launches_per_step = ((7 if fused else 8) if peer else 12) if ep else (per_decode if B <= 8 else 11)
     res = {
         "metric": f"MoE-layer tok/s ({workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,

@@ -247,10 +247,11 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
 
 /*
  * Benchmark support (no counterpart in the reference).  mimo_moe_profile_enable(n) with n > 0 makes
- * the library record a CUDA event pair around each of the next n expert-tile kernel launches on the
+ * the library record a CUDA event pair around each of the next n expert-path kernel launches on the
  * launching stream (the events are created here, once); n = 0 turns it off.  mimo_moe_profile_read()
  * synchronises those events and returns, per kernel kind (0 decode gate/up, 1 decode down, 2 prefill
- * gate/up, 3 prefill down, 4 decode gate/up + down in one launch; MIMO_MOE_PROFILE_KINDS entries in
+ * gate/up, 3 prefill down, 4 decode gate/up + down in one launch, 5 the same as one stream-K launch,
+ * 6 the decode route kernel of mimo_moe_block, 7 the decode combine; MIMO_MOE_PROFILE_KINDS entries in
  * each array), the launch count and the summed device milliseconds, then resets.
  * Off by default; do not enable it while a stream is being captured.
  */

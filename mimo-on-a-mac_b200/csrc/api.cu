@@ -95,12 +95,19 @@ bool decode_fp4();
 
 struct TermWs {
   uint8_t *bq, *bs, *hq, *hs;
-  int32_t* ready;  // fused decode: per-unit count of gate/up epilogue warps done
+  int32_t* ready;   // fused decodes: per-unit count of gate/up epilogue warps done, then (decode units)
+                    // the stream-K hand-off flags; `nzero` words from `ready` on are zeroed per call
+  int nzero;
+  float *skg, *skd;  // stream-K decode: contributed gate/up and down group partials
+  int32_t *flag_g, *flag_d;
+  int32_t* done;     // stream-K decode: down tiles completed per output row tile (fused combine)
+  int ctas;          // CTAs the stream-K scratch is sized for
 };
 // Activation terms of `units` units: e4m3 (2 terms, one byte a value) or, for decode units on the
-// kind::mxf4 path, e2m1 (5 terms, half a byte a value).
+// kind::mxf4 path, e2m1 (5 terms, half a byte a value).  Decode units also get the stream-K scratch.
 TermWs carve_terms(Carver& c, int units, int routes, int H, int I) {
-  const bool fp4 = routes == kTcDecodeRoutes && decode_fp4();
+  const bool decode = routes == kTcDecodeRoutes;
+  const bool fp4 = decode && decode_fp4();
   const size_t rows = (size_t)units * (fp4 ? kTcFp4Terms : 2) * routes;
   const int vb = fp4 ? 2 : 1;  // values per byte
   TermWs t;
@@ -108,7 +115,15 @@ TermWs carve_terms(Carver& c, int units, int routes, int H, int I) {
   t.bs = c.take<uint8_t>(rows * (H / 32));
   t.hq = c.take<uint8_t>(rows * I / vb);
   t.hs = c.take<uint8_t>(rows * (I / 32));
-  t.ready = c.take<int32_t>((size_t)units);
+  t.ctas = num_sms_current();
+  const size_t nfg = decode ? sk_flag_count(t.ctas) : 0, nfd = nfg, ndone = decode ? (size_t)H / 128 : 0;
+  t.ready = c.take<int32_t>((size_t)units + nfg + nfd + ndone);
+  t.nzero = units + (int)(nfg + nfd + ndone);
+  t.flag_g = decode ? t.ready + units : nullptr;
+  t.flag_d = decode ? t.ready + units + nfg : nullptr;
+  t.done = decode ? t.ready + units + nfg + nfd : nullptr;
+  t.skg = decode ? c.take<float>(sk_part_g_floats(t.ctas)) : nullptr;
+  t.skd = decode ? c.take<float>(sk_part_d_floats(t.ctas)) : nullptr;
   return t;
 }
 
@@ -246,18 +261,21 @@ bool tc_path(const mimo_moe_pools* pools) {
 }
 
 // Decode expert kernels (MIMO_MOE_DECODE_KERNEL, a comparison knob; all measured on B200):
-//   e4m3 (default)  two launches (gate/up, then down), kind::mxf8f6f4 with two e4m3 terms;
-//   e4m3-fused      the same arithmetic in one launch (bit-identical), down tiles waiting on
-//                   per-unit counters: ~2 us less kernel time, no faster per step;
-//   fp4             one launch, kind::mxf4: packed weights, five e2m1 activation terms: twice the
-//                   weight bytes in flight per SM, yet ~4% slower (the per-SM ingress rate, not the
-//                   bytes in flight, bounds these kernels).
-enum DecodeKernel { kDecodeE4m3 = 0, kDecodeE4m3Fused = 1, kDecodeFp4 = 2 };
+//   e4m3 (default)  two launches (gate/up, then down) over whole 128-row tiles dealt round-robin,
+//                   kind::mxf8f6f4 with two e4m3 activation terms;
+//   sk              one launch, stream-K: every CTA streams an equal share of 512-value K groups of the
+//                   gate/up tiles, then of the down tiles; group partials folded in a fixed order
+//                   (results independent of the split) and the combine fused; balanced, but its shared
+//                   ring holds 5 stages (the gate/up kernel's holds 6) and it measured 18-24% slower;
+//   e4m3-fused      the e4m3 arithmetic in one launch (bit-identical to e4m3), down tiles waiting on
+//                   per-unit counters;
+//   fp4             one launch, kind::mxf4: packed weights, five e2m1 activation terms.
+enum DecodeKernel { kDecodeE4m3 = 0, kDecodeE4m3Fused = 1, kDecodeFp4 = 2, kDecodeSk = 3 };
 int decode_kernel() {
   static const int mode = [] {
     const char* e = getenv("MIMO_MOE_DECODE_KERNEL");
     const std::string v = e ? e : "";
-    return v == "fp4" ? kDecodeFp4 : v == "e4m3-fused" ? kDecodeE4m3Fused : kDecodeE4m3;
+    return v == "fp4" ? kDecodeFp4 : v == "e4m3-fused" ? kDecodeE4m3Fused : v == "sk" ? kDecodeSk : kDecodeE4m3;
   }();
   return mode;
 }
@@ -274,6 +292,13 @@ bool prefill_pair() {
 }
 
 
+// The decode combine (kernels.py:194-199) of mimo_moe_experts, fused into the stream-K expert kernel.
+struct CombineArgs {
+  uint16_t* y;
+  const int32_t *gidx, *urows, *ucnt;
+  int M, topk;
+};
+
 // Gate/up + SwiGLU and down over units of up to `routes` routes, on the tensor cores.
 // Decode (routes 8): unit u's routes start at u * R, B rows come from rtok = urows, the down pass
 // writes part = dot * weight.  Prefill (routes 32): units from build_units, down writes ypair.
@@ -284,7 +309,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
            uint16_t* ypair, int32_t* status, cudaStream_t st, int by_token_rows = 0, bool terms_ready = false,
            bool ready_zeroed = false,
            const int32_t* out_row = nullptr, int x_ld = 0, float* const* peer_part = nullptr, int peer_rows = 0,
-           int x_rows = 0) {
+           int x_rows = 0, const CombineArgs* comb = nullptr, bool* combined = nullptr) {
   const int H = pools->hidden, I = pools->inter, S = pools->num_slots;
   const int sms = num_sms_current();
   const bool decode = routes == kTcDecodeRoutes;
@@ -332,9 +357,11 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.hq = t.hq;
   p.hs = t.hs;
   p.status = status;
-  const bool fused = decode && decode_kernel() != kDecodeE4m3;
+  const bool sk = decode && decode_kernel() == kDecodeSk;
+  const bool fused = decode && (decode_kernel() == kDecodeE4m3Fused || decode_kernel() == kDecodeFp4);
   if (pair) MIMO_TRY(profiled(2, st, [&] { return launch_tc_pair(p, 2, sms, st); }));
-  else if (!fused) MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
+  else if (!fused && !sk)
+    MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
   TcParams q = p;  // down: two K chunks per stage (3-D boxes, or two 2-D boxes when packed)
   if (fp4) {
     MIMO_TRY(packed64_map(&q.amap[0], pools->down_w, (uint64_t)S * H, I / 2, 128));
@@ -360,6 +387,32 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   q.peer_rows = peer_rows;
   q.ypair = ypair;
   q.pairs_rounding = pairs_rounding;
+  if (sk) {  // both passes in one launch, stream-K over K groups
+    if (t.ctas != sms) return MIMO_EINVAL;  // workspace carved for another device
+    if (!ready_zeroed) MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)t.nzero * sizeof(int32_t), st));
+    TcSkParams f{};
+    f.gu = p;
+    f.dn = q;
+    f.ready = t.ready;
+    f.part_g = t.skg;
+    f.part_d = t.skd;
+    f.flag_g = t.flag_g;
+    f.flag_d = t.flag_d;
+    f.ctas = t.ctas;
+    if (comb && part && !peer_part) {  // the combine runs in the expert kernel's epilogue
+      f.y = comb->y;
+      f.gidx = comb->gidx;
+      f.urows = comb->urows;
+      f.ucnt = comb->ucnt;
+      f.done = t.done;
+      f.M = comb->M;
+      f.topk = comb->topk;
+      f.R = p0_stride;
+      if (combined) *combined = true;
+    }
+    MIMO_TRY(profiled(5, st, [&] { return launch_tc_decode_sk(f, st); }));
+    return MIMO_OK;
+  }
   if (fused) {  // both passes in one launch; the down tiles wait on per-unit counters
     if (!ready_zeroed) MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)ucap * sizeof(int32_t), st));
     const TcFusedParams f{p, q, t.ready};
@@ -445,19 +498,26 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
   const int H = pools->hidden;
   const int sms = num_sms_current();
   if (R <= kTcDecodeRoutes && tc_path(pools)) {
+    const CombineArgs comb{y, gidx, urows, ucnt, M, topk};
+    bool combined = false;
     const int rc = run_tc(x, pools, kTcDecodeRoutes, uslot, ucnt, nullptr, R, nullptr, nullptr, urows, uw,
                           num_unique, U, pairs_rounding, w.t, w.part, nullptr, status, st,
                           M <= kTcDecodeRoutes ? M : 0, terms_ready && M <= kTcDecodeRoutes,
-                          /*ready_zeroed=*/terms_ready, nullptr, 0, nullptr, 0, /*x_rows=*/M);
+                          /*ready_zeroed=*/terms_ready, nullptr, 0, nullptr, 0, /*x_rows=*/M, &comb, &combined);
     if (rc != MIMO_OK) return rc;
-    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st));
+    if (!combined)
+      MIMO_TRY(profiled(7, st, [&] {
+        return launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st);
+      }));
     return MIMO_OK;
   }
   if (!x16_ready) MIMO_TRY(launch_to_f16(x, w.x16, (size_t)M * H, status, st));
   if (pools->hidden <= 4096 && pools->inter <= 2048) {
     const int rc = run_experts_tma(pools, uslot, urows, ucnt, uw, num_unique, U, R, M, pairs_rounding, w, status, st);
     if (rc != MIMO_OK) return rc;
-    MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st));
+    MIMO_TRY(profiled(7, st, [&] {
+      return launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st);
+    }));
     return MIMO_OK;
   }
   ExpertParams p = gateup_params(pools, status);
@@ -477,7 +537,9 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
   q.part_out = w.part;
   q.pairs_rounding = pairs_rounding;
   MIMO_TRY(tiles(q, 1, sms, st));
-  MIMO_TRY(launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st));
+  MIMO_TRY(profiled(7, st, [&] {
+    return launch_combine_decode(w.part, gidx, urows, ucnt, num_unique, U, R, M, topk, H, y, status, st);
+  }));
   return MIMO_OK;
 }
 
@@ -638,7 +700,6 @@ size_t mimo_moe_block_workspace_bytes(int32_t T, int32_t H, int32_t I, int32_t E
   c.take<float>((size_t)T * E);
   c.take<int32_t>((size_t)T * topk);
   c.take<float>((size_t)T * topk);
-  c.take<int32_t>(1);
   if (T <= 8) {
     c.take<float>((size_t)T * E);  // router scores
     const GroupWs g = carve_group(c, T, topk, 8, E);
@@ -662,7 +723,6 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
   float* logits = c.take<float>((size_t)T * E);
   int32_t* idx = c.take<int32_t>((size_t)T * topk);
   float* wts = c.take<float>((size_t)T * topk);
-  int32_t* counter = c.take<int32_t>(1);
   if (idx_out) idx = idx_out;
   if (w_out) wts = w_out;
   if (T <= 8) {
@@ -673,10 +733,12 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
     // one launch: logits, top-k, grouping and the expert kernels' copy of x (e4m3 terms for the
     // tensor-core path, f16 for the mma.sync path)
     const bool tc = tc_path(pools);
-    MIMO_TRY(launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, counter, g.uids,
+    MIMO_TRY(profiled(6, st, [&] {
+      return launch_route_decode(x, router_w, bias, T, H, E, topk, 8, logits, idx, wts, g.uids,
                                  g.urows, g.ucnt, g.uw, g.gidx, g.nu, tc ? nullptr : dw.x16,
                                  tc ? dw.t.bq : nullptr, tc ? dw.t.bs : nullptr, score, status, st,
-                                 tc && decode_fp4() ? 1 : 0, tc ? dw.t.ready : nullptr, g.ucap));
+                                 tc && decode_fp4() ? 1 : 0, tc ? dw.t.ready : nullptr, dw.t.nzero);
+    }));
     return run_experts(x, pools, g.uids, g.urows, g.ucnt, g.uw, g.nu, g.ucap, 8, g.gidx, topk, T,
                        T == 1 ? 1 : 0, y, dw, status, st, /*x16_ready=*/!tc, /*terms_ready=*/tc);
   }

@@ -123,6 +123,36 @@ struct TcFusedParams {
 // fp4: kind::mxf4 with packed weight maps and five e2m1 activation terms (maps from packed64_map,
 // term rows unit * 40 + t * 8 + q); else kind::mxf8f6f4 with the kind 0 / kind 1 maps.
 cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms, cudaStream_t st);
+
+// Stream-K decode (tc_experts.cu, tc_decode_sk_kernel): both passes in one launch of `ctas` CTAs, each
+// streaming an equal contiguous range of 512-value K groups of the gate/up tiles, then of the down
+// tiles.  A tile's groups are added in a fixed order (a right fold); a CTA whose range starts inside a
+// tile publishes its partial fold of that tile in part_g / part_d behind per-warp flags for the CTA
+// before it.  Scratch sizes: sk_part_*_floats / sk_flag_count; flags and ready zeroed per call.
+struct TcSkParams {
+  TcParams gu, dn;
+  int32_t* ready;   // [units_cap] h readiness counters (8 epilogue warps per gate/up tile)
+  float* part_g;    // [ctas][4 quads][2 matrices][8 columns][32 lanes]
+  float* part_d;    // [ctas][4 quads][8 columns][32 lanes]
+  int32_t* flag_g;  // [ctas][8 epilogue warps]
+  int32_t* flag_d;  // [ctas][8 epilogue warps]
+  int ctas;
+  // Fused combine (y non-null; the down pass then writes dn.part, not peers): the CTA that completes
+  // the last down tile of output rows [128 r, 128 r + 128) (done[r] counts the tiles, zeroed per call)
+  // forms y[m] = bf16(sum over k in order of part[gidx[m * topk + k]]) for those rows (gidx null: the
+  // (u, r) scatter order over urows / ucnt with R route slots per unit), like combine_decode_kernel.
+  uint16_t* y;
+  const int32_t* gidx;
+  const int32_t* urows;
+  const int32_t* ucnt;
+  int32_t* done;  // [H / 128]
+  int M, topk, R;
+};
+constexpr int kSkGroupK = 512;  // K values per stream-K group (4 chunks of 128)
+inline size_t sk_part_g_floats(int ctas) { return (size_t)ctas * 4 * 2 * 8 * 32; }
+inline size_t sk_part_d_floats(int ctas) { return (size_t)ctas * 4 * 8 * 32; }
+inline size_t sk_flag_count(int ctas) { return (size_t)ctas * 8; }  // per phase
+cudaError_t launch_tc_decode_sk(const TcSkParams& f, cudaStream_t st);
 // kind 0: decode gate/up (8 routes per unit), 1: decode down, 2: prefill gate/up (64 routes per
 // unit), 3: prefill down.
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
@@ -167,10 +197,11 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* lo
                                  int E, cudaStream_t st, int32_t* status = nullptr);
 cudaError_t launch_router_topk(const float* logits, const float* bias, int T, int E, int topk,
                                int32_t* idx, float* weight, cudaStream_t st);
-// ready (optional): ready_n counters of the fused decode experts, zeroed by the last CTA.
+// Decode routing (T <= 8), two launches: logits + scores (+ the expert kernels' x terms, and zeroing of
+// ready_n words at `ready`), then top-k and grouping in one CTA.
 cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
-                                int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                                int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
                                 float* score, int32_t* status, cudaStream_t st, int fp4 = 0,
                                 int32_t* ready = nullptr, int ready_n = 0);

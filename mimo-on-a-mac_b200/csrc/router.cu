@@ -86,117 +86,147 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
   topk_warp(logits + (size_t)t * E, bias, E, topk, idx + (size_t)t * topk, weight + (size_t)t * topk);
 }
 
-// Decode (T <= 8) routing in one launch.  Logits on the tensor cores: CTA c owns router rows
-// [16c, 16c+16); its warp w multiplies them by the T tokens over the K slices w, w+16, ... (256 elements
-// each) with bf16 MMAs (exact products, float32 accumulation); the warps' partial sums are added in
-// warp order in shared memory, and each CTA turns its logits into scores (the exact sigmoid) at once.
-// The last CTA to finish (atomic ticket, no waiting) selects the top-k of
-// every token, groups the routes by distinct expert (group_routes, engine/mimo_stream/kernels.py:149-173)
-// and (x16 non-null) writes the f16 copy of x that the mma.sync expert kernels read.  With xq non-null,
-// every CTA also splits its share of x into the e4m3 terms the tensor-core expert kernels read.
-// `counter` must be zero at launch; the last CTA resets it.
+// Decode (T <= 8) routing in two launches.  route_logits_kernel: CTA c owns router rows [4c, 4c+4) (E / 4
+// CTAs, so the 2 MiB router weight streams through 64 SMs): float32 FMAs of exact bf16 products in a
+// fixed order (route_logits4_cta); each CTA turns its logits into scores (the exact sigmoid) at once
+// and, with xq non-null, first splits its share of x into the terms the tensor-core expert kernels
+// read.  route_select_kernel (one CTA, launched as its programmatic dependent): top-k of every token
+// and grouping of the routes by distinct expert.
 constexpr int kRouteWarps = 16;
-// Logits of router rows [16c, 16c+16) (c = blockIdx.x) for T <= 8 tokens: warp w multiplies them by
-// the tokens over the K slices w, w+16, ... (256 elements each) with bf16 MMAs (exact products,
-// float32 accumulation); the warps' partial sums are added in warp order in shared memory (red).
-// score (optional) receives sigmoid_score of each logit.  kRouteWarps warps; ends after the stores.
-__device__ __forceinline__ void route_logits_cta(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                                 int T, int H, int E, float* __restrict__ logits,
-                                                 float* __restrict__ score, float (*red)[128]) {
+// Logits of router rows [4c, 4c+4) (c = blockIdx.x) for T <= 8 tokens, on 16 warps: warp w takes the
+// K slice [w H / 16, (w + 1) H / 16) of all 4 rows and all T tokens (so the CTA reads its 4 rows and x
+// once); lane l reads the 8-value chunks l, l + 32, ... of the slice (16-byte loads) and accumulates
+// float32 FMAs of the exact bf16 products in chunk order.  The 32 sums (row, token) of a warp are
+// reduce-scattered over its lanes in a fixed butterfly (lane j ends with sum j = row * 8 + token), and
+// the 16 warps' sums are added in warp order (shared memory), so the sum order is fixed.  score
+// (optional) receives sigmoid_score of each logit.  Needs H % 128 == 0 and 16 warps; ends after the
+// stores (one __syncthreads inside).
+__device__ __forceinline__ void route_logits4_cta(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                  int T, int H, int E, float* __restrict__ logits,
+                                                  float* __restrict__ score, float (*red)[128]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int e0 = blockIdx.x * 16;
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int ks = warp; ks < H / 256; ks += kRouteWarps) {
-    const int k0 = ks * 256;
-    const uint16_t* wa = w + (size_t)(e0 + g) * H + k0 + t * 8;
-    const uint16_t* wb = w + (size_t)(e0 + g + 8) * H + k0 + t * 8;
-    const uint16_t* xr = x + (size_t)(g < T ? g : 0) * H + k0 + t * 8;
-    uint4 A[8], Bm[8], X[8];
+  const int nch = H / 128;  // 8-value chunks per slice
+  const int c0 = warp * nch;
+  float a[32];  // a[r * 8 + t]
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      A[kk] = __ldg(reinterpret_cast<const uint4*>(wa + kk * 32));
-      Bm[kk] = __ldg(reinterpret_cast<const uint4*>(wb + kk * 32));
-      X[kk] = (g < T) ? __ldg(reinterpret_cast<const uint4*>(xr + kk * 32)) : make_uint4(0u, 0u, 0u, 0u);
-    }
+  for (int j = 0; j < 32; ++j) a[j] = 0.f;
+  for (int c = lane; c < nch; c += 32) {
+    uint4 wv[4];
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      mma_16816_bf16(d, A[kk].x, Bm[kk].x, A[kk].y, Bm[kk].y, X[kk].x, X[kk].y, d);
-      mma_16816_bf16(d, A[kk].z, Bm[kk].z, A[kk].w, Bm[kk].w, X[kk].z, X[kk].w, d);
+    for (int r = 0; r < 4; ++r)
+      wv[r] = __ldg(reinterpret_cast<const uint4*>(w + (size_t)(blockIdx.x * 4 + r) * H) + c0 + c);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (t < T) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H) + c0 + c);
+        const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xFFFF0000u);
+        const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xFFFF0000u);
+        const float x4 = __uint_as_float(xv.z << 16), x5 = __uint_as_float(xv.z & 0xFFFF0000u);
+        const float x6 = __uint_as_float(xv.w << 16), x7 = __uint_as_float(xv.w & 0xFFFF0000u);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float v = a[r * 8 + t];
+          v = fmaf(x0, __uint_as_float(wv[r].x << 16), v);
+          v = fmaf(x1, __uint_as_float(wv[r].x & 0xFFFF0000u), v);
+          v = fmaf(x2, __uint_as_float(wv[r].y << 16), v);
+          v = fmaf(x3, __uint_as_float(wv[r].y & 0xFFFF0000u), v);
+          v = fmaf(x4, __uint_as_float(wv[r].z << 16), v);
+          v = fmaf(x5, __uint_as_float(wv[r].z & 0xFFFF0000u), v);
+          v = fmaf(x6, __uint_as_float(wv[r].w << 16), v);
+          v = fmaf(x7, __uint_as_float(wv[r].w & 0xFFFF0000u), v);
+          a[r * 8 + t] = v;
+        }
+      }
     }
   }
-  // red[w][row*8 + tok]: row = expert within the tile, tok = token
-  red[warp][g * 8 + 2 * t] = d[0];
-  red[warp][g * 8 + 2 * t + 1] = d[1];
-  red[warp][(g + 8) * 8 + 2 * t] = d[2];
-  red[warp][(g + 8) * 8 + 2 * t + 1] = d[3];
+  // reduce-scatter: at offset o a lane keeps the upper half of its values if lane & o, else the lower
+  // half, and adds its partner's copy of the half it keeps; lane j ends with the warp's sum j
+#pragma unroll
+  for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < n / 2; ++j) {
+      const float send = up ? a[j] : a[j + n / 2];
+      const float keep = up ? a[j + n / 2] : a[j];
+      a[j] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+    }
+  }
+  red[warp][lane] = a[0];
   __syncthreads();
-  if (threadIdx.x < 128) {
-    const int row = threadIdx.x >> 3, tok = threadIdx.x & 7;
-    if (tok < T) {
+  if (threadIdx.x < 32) {
+    const int r = threadIdx.x >> 3, t = threadIdx.x & 7;
+    if (t < T) {
       float sum = 0.f;
 #pragma unroll
       for (int ww = 0; ww < kRouteWarps; ++ww) sum += red[ww][threadIdx.x];
-      logits[(size_t)tok * E + e0 + row] = sum;
-      if (score) score[(size_t)tok * E + e0 + row] = sigmoid_score(sum);  // off the last CTA's serial path
+      const int e = blockIdx.x * 4 + r;
+      logits[(size_t)t * E + e] = sum;
+      if (score) score[(size_t)t * E + e] = sigmoid_score(sum);
     }
   }
 }
 
-// Stand-alone logits for T <= 8 (the router entry point): E / 16 CTAs.
+// Stand-alone logits for T <= 8 (the router entry point and the expert-parallel route scatter): E / 4
+// CTAs of the decode route kernel's arithmetic, so every path routes from the same logits bit for bit.
 __global__ void __launch_bounds__(kRouteWarps * 32) router_logits_small_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H, int E,
     float* __restrict__ logits) {
   __shared__ float red[kRouteWarps][128];
-  route_logits_cta(x, w, T, H, E, logits, nullptr, red);
+  route_logits4_cta(x, w, T, H, E, logits, nullptr, red);
 }
 
-__global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const float* __restrict__ bias, int T,
-    int H, int E, int topk, int R, float* __restrict__ logits, int32_t* __restrict__ idx,
-    float* __restrict__ wts, int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
-    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, uint8_t* __restrict__ xq,
-    uint8_t* __restrict__ xs, float* __restrict__ score, int32_t* status, int fp4, int32_t* ready, int ready_n) {
+__global__ void __launch_bounds__(kRouteWarps * 32) route_logits_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, int T, int H, int E,
+    float* __restrict__ logits, float* __restrict__ score, uint8_t* __restrict__ xq, uint8_t* __restrict__ xs,
+    int32_t* status, int fp4, int32_t* ready, int ready_n) {
   __shared__ float red[kRouteWarps][128];
-  // e4m3 terms of x for the tensor-core expert path (token t -> rows t (hi) and 8 + t (lo)): 32-value
-  // blocks spread evenly over the CTAs, split after the logits (off the critical path; in the last
-  // CTA by the warps that do not select).  first_thread: the CTA thread taking its first block.
-  auto split_share = [&](int first_thread) {
+  // The expert kernels' copy of x, split by every CTA before its logits: e4m3 terms (token t -> rows
+  // t (hi) and 8 + t (lo)) one 32-value block per warp (lane = value), or e2m1 terms (token t's term j
+  // at row j * 8 + t) one block per thread.
+  auto split_share = [&]() {
     const int nb = H / 32;
-    for (int b = (threadIdx.x - first_thread) * gridDim.x + blockIdx.x; b < T * nb;
-         b += gridDim.x * (blockDim.x - first_thread)) {
+    if (!fp4) {
+      const int nw = blockDim.x >> 5;
+      for (int b = (threadIdx.x >> 5) * gridDim.x + blockIdx.x; b < T * nb; b += gridDim.x * nw) {
+        const int t = b / nb, blk = b - t * nb;
+        tc::split_block32_warp(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
+                               xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
+                               xs + (size_t)(8 + t) * nb + blk, status);
+      }
+      return;
+    }
+    for (int b = threadIdx.x * gridDim.x + blockIdx.x; b < T * nb; b += gridDim.x * blockDim.x) {
       const int t = b / nb, blk = b - t * nb;
-      if (fp4)  // e2m1 terms: token t's term j at row j * 8 + t (H / 2 bytes per row)
-        tc::split_block32_fp4(x + (size_t)t * H + blk * 32, xq + (size_t)t * (H / 2) + blk * 16,
-                              (size_t)8 * (H / 2), xs + (size_t)t * nb + blk, (size_t)8 * nb, status);
-      else
-        tc::split_block32(x + (size_t)t * H + blk * 32, xq + (size_t)t * H + blk * 32,
-                          xq + (size_t)(8 + t) * H + blk * 32, xs + (size_t)t * nb + blk,
-                          xs + (size_t)(8 + t) * nb + blk, status);
+      tc::split_block32_fp4(x + (size_t)t * H + blk * 32, xq + (size_t)t * (H / 2) + blk * 16,
+                            (size_t)8 * (H / 2), xs + (size_t)t * nb + blk, (size_t)8 * nb, status);
     }
   };
+  pdl_wait();  // x may come from the preceding kernel
+  pdl_launch_dependents();
+  // the expert kernel's per-call counters and flags: every CTA zeroes a share (that kernel starts
+  // reading them only after both route launches have completed)
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; ready && i < ready_n; i += gridDim.x * blockDim.x) ready[i] = 0;
+  if (xq) split_share();
+  route_logits4_cta(x, w, T, H, E, logits, score, red);
+}
+
+// Decode routing, second launch (one CTA, programmatically dependent on route_logits_kernel): warp t
+// selects token t's top-k from the scores (the router's order); the CTA then groups the routes by
+// distinct expert (group_routes, engine/mimo_stream/kernels.py:149-173) and, with x16 non-null, writes
+// the f16 copy of x that the mma.sync expert kernels read.
+__global__ void __launch_bounds__(kRouteWarps * 32) route_select_kernel(
+    const uint16_t* __restrict__ x, const float* __restrict__ bias, int T, int H, int E, int topk, int R,
+    int32_t* __restrict__ idx, float* __restrict__ wts, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+    int32_t* gidx, int32_t* num_unique, __half* __restrict__ x16, const float* __restrict__ score, int32_t* status) {
   __shared__ int32_t sid[64], s_idx[64];
   __shared__ float s_w[64];
   __shared__ uint32_t bitmap[32];
-  __shared__ int is_last;
   const int warp = threadIdx.x >> 5;
-  pdl_wait();  // x may come from the preceding kernel
+  pdl_wait();  // the scores come from route_logits_kernel
   pdl_launch_dependents();
-  route_logits_cta(x, w, T, H, E, logits, score, red);
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
-  __syncthreads();
-  if (!is_last) {
-    if (xq) split_share(0);
-    return;
-  }
-  __threadfence();
   if (warp < T)
     topk_warp_impl<true>(score + (size_t)warp * E, bias, E, topk, idx + warp * topk, wts + warp * topk,
                          s_idx + warp * topk, s_w + warp * topk);
-  else if (xq && threadIdx.x >= 256)
-    split_share(256);
   __syncthreads();
   const int P = T * topk;
   group_routes_cta(s_idx, s_w, P, topk, R, E, min(E, P), uids, urows, ucnt, uw, gidx, num_unique, status,
@@ -211,8 +241,6 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_decode_kernel(
     }
     *reinterpret_cast<__half2*>(x16 + i) = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
   }
-  for (int i = threadIdx.x; ready && i < ready_n; i += blockDim.x) ready[i] = 0;  // fused experts' counters
-  if (threadIdx.x == 0) *counter = 0;
 }
 
 // Prefill router logits on the tensor cores: one CTA per 128-token x 64-expert tile, K = H in
@@ -342,7 +370,7 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* lo
     }
   }
   if (T <= 8 && E % 16 == 0 && H % 256 == 0) {  // decode sizes: 16-row tiles on bf16 mma.sync
-    router_logits_small_kernel<<<E / 16, kRouteWarps * 32, 0, st>>>(x, w, T, H, E, logits);
+    router_logits_small_kernel<<<E / 4, kRouteWarps * 32, 0, st>>>(x, w, T, H, E, logits);
     return cudaGetLastError();
   }
   dim3 grid((T + 7) / 8, (E + 7) / 8);
@@ -358,16 +386,16 @@ cudaError_t launch_router_topk(const float* logits, const float* bias, int T, in
 
 cudaError_t launch_route_decode(const uint16_t* x, const uint16_t* w, const float* bias, int T, int H,
                                 int E, int topk, int R, float* logits, int32_t* idx, float* wts,
-                                int32_t* counter, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
+                                int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, __half* x16, uint8_t* xq, uint8_t* xs,
                                 float* score, int32_t* status, cudaStream_t st, int fp4, int32_t* ready,
                                 int ready_n) {
   if (T < 1 || T > 8 || T * topk > 64 || E % 16 || H % 256) return cudaErrorInvalidValue;
-  cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int32_t), st);
+  const cudaError_t e = launch_k(route_logits_kernel, dim3(E / 4), dim3(kRouteWarps * 32), 0, st, x, w, T, H, E,
+                                 logits, score, xq, xs, status, fp4, ready, ready_n);
   if (e != cudaSuccess) return e;
-  return launch_k(route_decode_kernel, dim3(E / 16), dim3(kRouteWarps * 32), 0, st, x, w, bias, T, H, E, topk, R,
-                  logits, idx, wts, counter, uids, urows, ucnt, uw, gidx, num_unique, x16, xq, xs, score, status,
-                  fp4, ready, ready_n);
+  return launch_k(route_select_kernel, dim3(1), dim3(kRouteWarps * 32), 0, st, x, bias, T, H, E, topk, R, idx, wts,
+                  uids, urows, ucnt, uw, gidx, num_unique, x16, score, status);
 }
 
 }  // namespace mimo

@@ -1097,6 +1097,679 @@ __global__ void __launch_bounds__(kThreads, 1) tc_decode_fused_kernel(const __gr
   }
 }
 
+// ------------------------------------------------------------ stream-K decode (gate/up -> down)
+// Both decode passes in one persistent launch with every CTA streaming the same number of weight bytes.
+// The unit of work is a K group of 512 values (4 chunks of 128) of one 128-row tile: a gate/up group
+// reads 2 x 128 x 512 e2m1 weights (68 KB with scales), a down group 128 x 512 (34 KB).  The gate/up
+// groups of all units, in (unit, tile, group) order, are cut into `gridDim.x` contiguous ranges of
+// equal length (CTA c takes [n c / G, n (c + 1) / G)), and so are the down groups.  At decode sizes a
+// tile-granular schedule leaves SMs idle or doubly loaded (B = 1: 128 gate/up tiles on 148 SMs); the
+// group ranges differ by at most one group.
+//
+// Canonical accumulation.  Each group accumulates in its own TMEM buffer (a ring of kNAcc), and the
+// epilogue turns it into q_g = hi + lo per route column (gate and up; for down, the two K-parity
+// accumulators' (hi + lo) added).  A tile's value is the right fold q_0 + (q_1 + (... + q_last)) of its
+// groups, whichever CTAs computed them, so the result does not depend on where the ranges are cut (it
+// is the same for every unit count and grid, hence bit-identical between one GPU and the expert-
+// parallel path, which runs this kernel on other unit tables).  Within a tile every CTA streams its
+// groups in descending order and folds as they complete.
+//
+// Hand-off.  A range that starts inside a tile holds that tile's tail: the CTA streams it first, folds
+// it and publishes the partial fold R (its epilogue warp w stores its half of the 8 route columns of its
+// TMEM lane quadrant into part_{g,d}[cta] and release-stores flag[cta][w] = 1).  The CTA before it,
+// whose range ends in the same tile and which therefore reaches the tile last, starts its part of the
+// fold from R (acquired with a bounded wait before its first group of the tile; by then R has long been
+// written), so a split tile completes as soon as its last group does.  The CTA holding group 0 owns the
+// tile and runs its epilogue (SwiGLU + h terms, or down x route weight).  A range that lies inside one
+// tile waits for R of its right neighbour before its own fold.
+//
+// Down after gate/up.  A down group of unit u needs u's whole h: every gate/up tile owner's epilogue
+// warps add 1 to ready[u] after their h stores (8 warps x tiles per unit), and the producer acquires
+// that count before loading u's h terms.  Once its gate/up stages are issued, the producer asks L2 for
+// the first kL2Prefetch bytes of its down weight tiles (HBM is otherwise idle while the gate/up pass
+// drains), and while the count is short it still issues the stages' weight tiles and scale boxes and
+// defers only the h loads (it flushes them, waiting for the count, before it would block on a ring
+// slot those stages hold).  One CTA per SM (all resident) and gate/up before down in every CTA make
+// every wait finite; a wait past its limit sets MIMO_ETIMEOUT, the CTA issues what it deferred, drains
+// and returns.
+namespace sk {
+constexpr int kNTOK = kTcDecodeRoutes;           // route (or token) columns per unit
+constexpr int kN = 2 * kNTOK;                    // MMA N: the hi and lo term of each column
+constexpr int kNAcc = 8;                         // accumulator buffers, one K group each
+constexpr int kScRing = 4;                       // scale-box ring entries (one group each)
+constexpr int kGroupChunks = kSkGroupK / kKC;    // 4
+constexpr int kSB = 2 * kATile + 2 * kN * kKC;   // stage: 2 weight tiles + 1 (gate/up) or 2 (down) term tiles
+constexpr int kSCB = 2 * kM * 16 + kN * 16;      // scale boxes of one group
+constexpr int kSFB = 4 * 512;                    // scale blocks of one stage
+#ifndef MIMO_TC_SK_L2_PREFETCH
+#define MIMO_TC_SK_L2_PREFETCH 0  // measured on B200: no gain at B = 1 or 8 (the burst delays the hand-offs)
+#endif
+#ifndef MIMO_TC_SK_WAVES
+#define MIMO_TC_SK_WAVES 1
+#endif
+constexpr int kL2Prefetch = MIMO_TC_SK_L2_PREFETCH;  // down weight bytes per CTA asked of L2 ahead of time
+template <int NSTAGE>
+constexpr int smem_bytes() { return kBarBytes + 1024 + NSTAGE * kSB + kScRing * kSCB + NSTAGE * kSFB; }
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSfCol0 = kNAcc * 2 * kN;     // scale-factor columns after the accumulators
+
+// One phase's schedule.  The phase's tiles (unit-major) are dealt in `rounds` full waves, CTA c taking
+// whole tiles c, c + G, c + 2G, ... (G = gridDim.x; CTAs side by side work on neighbouring tiles);
+// the remaining tiles' groups (from group `base` on) are cut into `parts` contiguous ranges, taken by
+// CTAs 0 .. parts - 1 (the others get none).  parts = min(G, groups / (groups per tile / 2)): every
+// range holds at least half a tile, so a tile spans at most three ranges and no empty range sits
+// between the parts of a tile.
+struct Phase {
+  long long n;     // stream-K groups (after the full waves)
+  long long base;  // first stream-K group
+  int gpt;         // groups per tile
+  int tiles;       // tiles per unit
+  int rounds;      // full waves of whole tiles
+  int parts;
+  __device__ __forceinline__ void init(long long all_tiles, int groups_per_tile, int tiles_per_unit, bool waves) {
+    gpt = groups_per_tile;
+    tiles = tiles_per_unit;
+    rounds = waves ? (int)(all_tiles / gridDim.x) : 0;
+    base = (long long)rounds * gridDim.x * gpt;
+    n = all_tiles * gpt - base;
+    const long long half = max(1, gpt / 2);
+    parts = (int)max(1ll, min((long long)gridDim.x, n / half));
+  }
+  __device__ __forceinline__ long long start(int c) const { return base + n * min(c, parts) / parts; }
+  // the CTA whose stream-K range holds group g (base <= g < base + n)
+  __device__ __forceinline__ int cta_of(long long g) const {
+    const long long r = g - base;
+    int c = (int)(r * parts / n);
+    while (c + 1 < parts && start(c + 1) <= g) ++c;
+    while (c > 0 && start(c) > g) --c;
+    return c;
+  }
+  // groups this CTA streams in the phase
+  __device__ __forceinline__ long long count(int c) const { return (long long)rounds * gpt + start(c + 1) - start(c); }
+};
+// Segment = the groups of one tile inside a CTA's work, [lo, hi); streamed from hi - 1 down to lo.
+struct Seg {
+  long long t, t0, lo, hi;  // tile, its first group, the segment's groups
+};
+// A CTA's segments in order: its whole tiles of the full waves, then its stream-K range by tile.
+struct SegIter {
+  const Phase* Q;
+  int r;
+  long long gi, b;
+  __device__ __forceinline__ SegIter(const Phase& q, int c) : Q(&q), r(0), gi(q.start(c)), b(q.start(c + 1)) {}
+  __device__ __forceinline__ bool next(Seg& s) {
+    if (r < Q->rounds) {
+      s.t = (long long)r * gridDim.x + blockIdx.x;
+      s.t0 = s.t * Q->gpt;
+      s.lo = s.t0;
+      s.hi = s.t0 + Q->gpt;
+      ++r;
+      return true;
+    }
+    if (gi >= b) return false;
+    s.t = gi / Q->gpt;
+    s.t0 = s.t * Q->gpt;
+    s.lo = gi;
+    s.hi = min(b, s.t0 + Q->gpt);
+    gi = s.hi;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void st_release_gpu(int32_t* p, int32_t v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded acquire-wait until *p != 0.
+__device__ __forceinline__ bool wait_flag(const int32_t* p, volatile int* s_abort) {
+  if (fz::ld_acquire(p)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!fz::ld_acquire(p)) {
+    if (*s_abort || global_timer_ns() - t0 > 2000000000ull) return false;
+    __nanosleep(32);
+  }
+  return true;
+}
+}  // namespace sk
+
+template <int NSTAGE>
+__global__ void __launch_bounds__(kThreads, 1) tc_decode_sk_kernel(const __grid_constant__ TcSkParams f) {
+  using namespace sk;
+  constexpr int NTOK = kNTOK, N = kN;
+  const TcParams& g = f.gu;
+  const TcParams& d = f.dn;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + NSTAGE;
+  uint64_t* sc_full = empty + NSTAGE;
+  uint64_t* sc_empty = sc_full + kScRing;
+  uint64_t* acc_full = sc_empty + kScRing;
+  uint64_t* acc_empty = acc_full + kNAcc;
+  uint64_t* drain = acc_empty + kNAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_last = s_abort + 1;  // this CTA completed an output row tile (fused combine)
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + kBarBytes) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stages = base;
+  uint8_t* scbox = stages + NSTAGE * kSB;
+  uint8_t* sfblk = scbox + kScRing * kSCB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 2);   // producer expect-tx + scale builder
+      mbar_init(&empty[i], 2);  // one commit per issuer
+    }
+    for (int b = 0; b < kScRing; ++b) {
+      mbar_init(&sc_full[b], 1);
+      mbar_init(&sc_empty[b], 1);
+    }
+    for (int b = 0; b < kNAcc; ++b) {
+      mbar_init(&acc_full[b], 2);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    mbar_init(drain, 2);
+    *s_abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 3) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();  // unit tables and activation terms come from the preceding kernel
+  pdl_launch_dependents();
+  const uint32_t tbase = *tmem_slot;
+  const int units = g.num_units ? min(__ldg(g.num_units), g.units_cap) : g.units_cap;
+  Phase P[2];
+  P[0].init((long long)units * g.tiles, g.K / kSkGroupK, g.tiles, MIMO_TC_SK_WAVES);
+  P[1].init((long long)units * d.tiles, d.K / kSkGroupK, d.tiles, MIMO_TC_SK_WAVES);
+  const int ready_target = kEpiWarps * g.tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_a = MIMO_TC_WEIGHT_EVICT_FIRST ? l2_evict_first_policy() : l2_evict_normal_policy();
+      const uint64_t pol_b = l2_evict_normal_policy();
+      for (int m = 0; m < 2; ++m) {
+        tma_prefetch_map(&g.amap[m]);
+        tma_prefetch_map(&g.smap[m]);
+      }
+      tma_prefetch_map(&g.bmap);
+      tma_prefetch_map(&g.bsmap);
+      tma_prefetch_map(&d.amap[0]);
+      tma_prefetch_map(&d.smap[0]);
+      tma_prefetch_map(&d.bmap);
+      tma_prefetch_map(&d.bsmap);
+      // h-term loads of a down unit whose h is not complete yet: kind 0 = term tile (3-D box), 1 = term
+      // scale box (2-D); issued by flush() once ready[pend_unit] reaches the target.
+      struct Pend {
+        uint8_t* dst;
+        int kind, c0, c1, c2;
+        uint64_t* bar;
+      };
+      Pend pend[NSTAGE + kScRing];
+      int npend = 0, pend_unit = -1;
+      bool stop = false;
+      auto flush = [&](bool force) {
+        if (npend == 0) return;
+        bool ok = fz::ld_acquire(f.ready + pend_unit) >= ready_target;
+        if (!ok && !force) {
+          const uint64_t t0 = global_timer_ns();
+          while (!(ok = fz::ld_acquire(f.ready + pend_unit) >= ready_target)) {
+            if (*s_abort || global_timer_ns() - t0 > 2000000000ull) break;
+            __nanosleep(64);
+          }
+          if (!ok) {
+            set_status(g.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            stop = true;
+          }
+        }
+        fz::fence_proxy_async_global();  // h was written by generic stores; TMA reads it
+        // After an abort the loads still go out (in-bounds rows, unfinished values), so that every
+        // stage barrier completes and the drain below never waits on a copy that was not issued.
+        for (int i = 0; i < npend; ++i) {
+          const Pend& q = pend[i];
+          if (q.kind == 0) tma_load_3d(q.dst, &d.bmap, q.c0, q.c1, q.c2, q.bar, pol_b);
+          else tma_load_2d(q.dst, &d.bsmap, q.c0, q.c1, q.bar, pol_b);
+        }
+        npend = 0;
+      };
+      // Wait for a ring slot; deferred loads go out first when the slot is not free at once.
+      auto wait_free = [&](uint64_t* bar, uint32_t par) -> bool {
+        if (npend && !mbar_try_wait(bar, par)) flush(false);
+        if (stop || !mbar_wait(bar, par)) {
+          set_status(g.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          stop = true;
+          return false;
+        }
+        return true;
+      };
+      int stage = 0;
+      uint32_t ph = 0;
+      long long issued = 0, groups = 0;
+      for (int phase = 0; phase < 2 && !stop; ++phase) {
+        const TcParams& p = phase ? d : g;
+        const Phase& Q = P[phase];
+        const int NM = phase ? 1 : 2, KPS = phase ? 2 : 1;
+        if (phase && kL2Prefetch > 0) {
+          // the down weights of this CTA's first groups, into L2 while the gate/up pass drains
+          long long bytes = 0;
+          SegIter it(Q, cta);
+          Seg s;
+          while (bytes < kL2Prefetch && it.next(s)) {
+            const int unit = (int)(s.t / Q.tiles), tile = (int)(s.t % Q.tiles);
+            int slot = __ldg(d.unit_slot + unit);
+            slot = (slot < 0 || slot >= d.S) ? 0 : slot;
+            const int row0 = slot * d.Nw + tile * kM;
+            for (long long gk = s.hi - 1; gk >= s.lo && bytes < kL2Prefetch; --gk) {
+              const int kc0 = (int)(gk - s.t0) * kGroupChunks;
+              tma_prefetch_l2_2d(&d.smap[0], kc0 * 4, row0);
+              for (int st = 0; st < kGroupChunks / KPS; ++st) tma_prefetch_l2_3d(&d.amap[0], 0, row0, kc0 + st * KPS);
+              bytes += kGroupChunks * kAGlobal;
+            }
+          }
+        }
+        SegIter it(Q, cta);
+        Seg sg;
+        while (!stop && it.next(sg)) {
+          const int unit = (int)(sg.t / Q.tiles), tile = (int)(sg.t % Q.tiles);
+          int slot = __ldg(p.unit_slot + unit);
+          if (slot < 0 || slot >= p.S) {
+            set_status(p.status, MIMO_ERANGE);
+            slot = 0;
+          }
+          const int row0 = slot * p.Nw + tile * kM;
+          const int brow = (!phase && p.btok) ? 0 : unit * N;
+          bool ready_ok = true;
+          if (phase) {
+            if (npend && pend_unit != unit) flush(false);
+            ready_ok = fz::ld_acquire(f.ready + unit) >= ready_target;
+            if (ready_ok) fz::fence_proxy_async_global();
+            else pend_unit = unit;
+          }
+          for (long long gk = sg.hi - 1; gk >= sg.lo && !stop; --gk) {
+            const int kc0 = (int)(gk - sg.t0) * kGroupChunks;
+            if (phase && !ready_ok && (ready_ok = fz::ld_acquire(f.ready + unit) >= ready_target)) {
+              flush(false);  // became ready: send what waited, then load directly
+              fz::fence_proxy_async_global();
+            }
+            // scale boxes of the group: 16 bytes (4 chunks) of every weight row and term row
+            const int e = (int)(groups % kScRing);
+            if (!wait_free(&sc_empty[e], (uint32_t)(((groups / kScRing) & 1) ^ 1))) break;
+            uint8_t* sc = scbox + e * kSCB;
+            mbar_arrive_expect_tx(&sc_full[e], NM * kM * 16 + N * 16);
+            for (int m = 0; m < NM; ++m) tma_load_2d(sc + m * kM * 16, &p.smap[m], kc0 * 4, row0, &sc_full[e], pol_b);
+            if (ready_ok) tma_load_2d(sc + NM * kM * 16, &p.bsmap, kc0 * 4, brow, &sc_full[e], pol_b);
+            else pend[npend++] = Pend{sc + NM * kM * 16, 1, kc0 * 4, brow, 0, &sc_full[e]};
+            ++groups;
+            for (int s = 0; s < kGroupChunks / KPS; ++s) {
+              const int kc = kc0 + s * KPS;
+              if (*s_abort) {
+                stop = true;
+                break;
+              }
+              if (!wait_free(&empty[stage], ph ^ 1u)) break;
+              uint8_t* sb = stages + stage * kSB;
+              mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * N * kKC);
+              if (!phase) {
+                tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol_a);
+                tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol_a);
+                tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
+              } else {  // 3-D boxes [2 chunks][rows][128 B]
+                tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol_a);
+                if (ready_ok) tma_load_3d(sb + 2 * kATile, &p.bmap, 0, brow, kc, &full[stage], pol_b);
+                else pend[npend++] = Pend{sb + 2 * kATile, 0, 0, brow, kc, &full[stage]};
+              }
+              ++issued;
+              if (++stage == NSTAGE) {
+                stage = 0;
+                ph ^= 1u;
+              }
+            }
+          }
+        }
+      }
+      flush(stop);  // nothing may stay unissued: the drain waits on every stage barrier
+      bool ok = true;
+      for (long long k = 0; ok && k < (issued < NSTAGE ? issued : NSTAGE); ++k) {
+        const long long q = issued - 1 - k;
+        ok = mbar_wait(&full[(int)(q % NSTAGE)], (uint32_t)((q / NSTAGE) & 1));
+      }
+      for (long long k = 0; ok && k < (groups < kScRing ? groups : kScRing); ++k) {
+        const long long q = groups - 1 - k;
+        ok = mbar_wait(&sc_full[(int)(q % kScRing)], (uint32_t)((q / kScRing) & 1));
+      }
+      if (!ok) set_status(g.status, MIMO_ETIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------ scale-factor builder
+    // Per stage, the 512-byte blocks tcgen05.cp.32x128b.warpx4 turns into the TMEM scale layout: the
+    // chunk's 4 bytes of weight rows l, l+32, l+64, l+96 (two weight slots) and of the term rows.
+    int stage = 0;
+    uint32_t ph = 0;
+    uint32_t grp = 0;
+    bool stop = false;
+    for (int phase = 0; phase < 2 && !stop; ++phase) {
+      const Phase& Q = P[phase];
+      const int NM = phase ? 1 : 2, KPS = phase ? 2 : 1;
+      const long long ng = Q.count(cta);
+      for (long long k = 0; k < ng && !stop; ++k) {
+        const int e = (int)(grp % kScRing);
+        if (!mbar_wait(&sc_full[e], (grp / kScRing) & 1)) {
+          if (lane == 0) set_status(g.status, MIMO_ETIMEOUT);
+          *s_abort = 1;
+          break;
+        }
+        const uint8_t* sc = scbox + e * kSCB;
+        for (int s = 0; s < kGroupChunks / KPS; ++s) {
+          if (*s_abort || !mbar_wait(&empty[stage], ph ^ 1u)) {
+            if (!*s_abort && lane == 0) set_status(g.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            stop = true;
+            break;
+          }
+          const int c = s * KPS;
+          uint8_t* blk = sfblk + stage * kSFB;
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int m = NM == 2 ? j : 0, cj = c + (KPS == 2 ? j : 0);
+            const uint8_t* box = sc + m * kM * 16 + cj * 4;
+            uint4 v;
+            v.x = *reinterpret_cast<const uint32_t*>(box + (lane + 0) * 16);
+            v.y = *reinterpret_cast<const uint32_t*>(box + (lane + 32) * 16);
+            v.z = *reinterpret_cast<const uint32_t*>(box + (lane + 64) * 16);
+            v.w = *reinterpret_cast<const uint32_t*>(box + (lane + 96) * 16);
+            *reinterpret_cast<uint4*>(blk + j * 512 + lane * 16) = v;
+          }
+          for (int j = 0; j < KPS; ++j) {
+            const uint8_t* box = sc + NM * kM * 16 + (c + j) * 4;
+            uint32_t w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int r = lane + 32 * q;
+              w[q] = r < N ? *reinterpret_cast<const uint32_t*>(box + r * 16) : 0x7F7F7F7Fu;
+            }
+            *reinterpret_cast<uint4*>(blk + (2 + j) * 512 + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&full[stage]);
+            if (c + KPS == kGroupChunks) mbar_arrive(&sc_empty[e]);
+          }
+          if (++stage == NSTAGE) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        ++grp;
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------------------ MMA issuers
+    // Issuer j: gate/up matrix j, or the chunk of parity j of each down stage; a fresh accumulation in
+    // accumulator buffer (group mod kNAcc) for every group.
+    const int j = warp - 2;
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      long long gcount = 0;
+      bool aborted = false;
+      for (int phase = 0; phase < 2 && !aborted; ++phase) {
+        const Phase& Q = P[phase];
+        const int KPS = phase ? 2 : 1;
+        const long long ng = Q.count(cta);
+        for (long long k = 0; k < ng && !aborted; ++k, ++gcount) {
+          const int bufi = (int)(gcount % kNAcc);
+          const uint32_t use = (uint32_t)((gcount / kNAcc) & 1);
+          if (!mbar_wait(&acc_empty[bufi], use ^ 1u)) {
+            set_status(g.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dacc = tbase + (uint32_t)(2 * bufi + j) * N;
+          for (int s = 0; s < kGroupChunks / KPS; ++s) {
+            if (!mbar_wait(&full[stage], ph)) {
+              set_status(g.status, MIMO_ETIMEOUT);
+              *s_abort = 1;
+              aborted = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sb = smem_u32(stages + stage * kSB);
+            const uint32_t blk = smem_u32(sfblk + stage * kSFB);
+            const uint32_t sf_col = tbase + kSfCol0 + (uint32_t)stage * 16 + 8 * j;
+            const int bj = KPS == 2 ? j : 0;  // term tile / scale block of this issuer's chunk
+            tc_cp_sf(sf_col, desc_sf(blk + j * 512));
+            tc_cp_sf(sf_col + 4, desc_sf(blk + (2 + bj) * 512));
+            const uint32_t a0 = sb + j * kATile, b0 = sb + 2 * kATile + bj * N * kKC;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_mx(dacc, desc_sw128(a0 + kk * 32), desc_sw128(b0 + kk * 32), idesc_mx(N, kk),
+                        sf_col | ((uint32_t)kk << 30), (sf_col + 4) | ((uint32_t)kk << 30), (s | kk) != 0);
+            tc_commit(&empty[stage]);
+            if (++stage == NSTAGE) {
+              stage = 0;
+              ph ^= 1u;
+            }
+          }
+          if (!aborted) tc_commit(&acc_full[bufi]);
+        }
+      }
+      tc_commit(drain);
+      if (!mbar_wait(drain, 0)) set_status(g.status, MIMO_ETIMEOUT);
+    }
+  } else {
+    // --------------------------------------------------------------------------------- epilogue
+    // Warp w: TMEM lane quadrant w % 4 (weight rows), route half (w - 4) / 4 for the final epilogue;
+    // both warps of a quadrant fold all 8 columns (a route's token column can be any of them).
+    const int ew = warp - 4;
+    const int quad = warp & 3, half = ew >> 2;
+    const int qlo = half * (NTOK / 2);
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    bool aborted = false;
+    long long gcount = 0;
+    if (f.y && units == 0 && cta == 0)  // no routes: the combined output is zero
+      for (int o = ew * 32 + lane; o < f.M * d.Nw; o += kEpiWarps * 32) f.y[o] = 0;
+    for (int phase = 0; phase < 2; ++phase) {
+      const TcParams& p = phase ? d : g;
+      const Phase& Q = P[phase];
+      float* part = phase ? f.part_d : f.part_g;
+      int32_t* flag = phase ? f.flag_d : f.flag_g;
+      const int NV = phase ? 1 : 2;  // folded values per column: gate and up, or the down sum
+      SegIter it(Q, cta);
+      Seg sg;
+      while (it.next(sg)) {
+        const int unit = (int)(sg.t / Q.tiles), tile = (int)(sg.t % Q.tiles);
+        float acc[2][NTOK];
+        bool have = false;  // acc holds a partial fold
+        if (sg.hi < sg.t0 + Q.gpt) {
+          // the tile's groups after ours belong to the next range: start from its published fold R
+          const int c2 = Q.cta_of(sg.hi);
+          const bool ok = !aborted && sk::wait_flag(flag + (size_t)c2 * kEpiWarps + quad, s_abort) &&
+                          sk::wait_flag(flag + (size_t)c2 * kEpiWarps + quad + 4, s_abort);
+          if (!ok && !aborted) {
+            set_status(g.status, MIMO_ETIMEOUT);
+            aborted = true;
+          }
+          const float* src = part + ((size_t)c2 * 4 + quad) * (NV * NTOK * 32);
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int c = 0; c < NTOK; ++c) acc[m][c] = (ok && m < NV) ? __ldcg(src + (m * NTOK + c) * 32 + lane) : 0.f;
+          have = true;
+        } else {
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int c = 0; c < NTOK; ++c) acc[m][c] = 0.f;
+        }
+        for (long long gk = sg.hi - 1; gk >= sg.lo; --gk, ++gcount) {
+          const int bufi = (int)(gcount % kNAcc);
+          const uint32_t use = (uint32_t)((gcount / kNAcc) & 1);
+          if (!aborted && !mbar_wait(&acc_full[bufi], use)) {
+            set_status(g.status, MIMO_ETIMEOUT);
+            aborted = true;
+          }
+          tc_fence_after();
+          float q[2][NTOK];
+          if (!aborted) {
+            float hv[2][NTOK], lv[2][NTOK];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const uint32_t col = tbase + lane_base + (uint32_t)(2 * bufi + m) * N;
+              tmem_ld<NTOK>(col, hv[m]);
+              tmem_ld<NTOK>(col + NTOK, lv[m]);
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < NTOK; ++c) {
+              if (phase == 0) {
+                q[0][c] = hv[0][c] + lv[0][c];
+                q[1][c] = hv[1][c] + lv[1][c];
+              } else {
+                q[0][c] = (hv[0][c] + lv[0][c]) + (hv[1][c] + lv[1][c]);
+                q[1][c] = 0.f;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+              for (int c = 0; c < NTOK; ++c) q[m][c] = 0.f;
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[bufi]);
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int c = 0; c < NTOK; ++c) acc[m][c] = have ? q[m][c] + acc[m][c] : q[m][c];  // right fold
+          have = true;
+        }
+        if (sg.lo > sg.t0) {
+          // our range starts inside this tile: publish the partial fold for the CTA before us
+          float* dst = part + ((size_t)cta * 4 + quad) * (NV * NTOK * 32);
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+            if (m < NV)
+#pragma unroll
+              for (int c = 0; c < NTOK / 2; ++c) dst[(m * NTOK + qlo + c) * 32 + lane] = acc[m][qlo + c];
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) st_release_gpu(flag + (size_t)cta * kEpiWarps + ew, 1);
+          continue;
+        }
+        // tile owner: the epilogue
+        const int slot = __ldg(p.unit_slot + unit);
+        const int cnt = unit_routes(p, unit, NTOK);
+        const int p0 = p.unit_p0 ? __ldg(p.unit_p0 + unit) : unit * p.p0_stride;
+        const bool live = !aborted && slot >= 0 && slot < p.S;
+        const int row = tile * kM + quad * 32 + lane;
+        if (live) {
+#pragma unroll 1
+          for (int qq = qlo; qq < qlo + NTOK / 2; ++qq) {
+            int col = qq;  // B rows per route; with by-token rows, route qq's token
+            bool ok = qq < cnt;
+            if (!phase && g.btok && ok) {
+              col = __ldg(g.btok + p0 + qq);
+              if (col < 0 || col >= (g.btok_rows > 0 ? min(g.btok_rows, NTOK) : NTOK)) {
+                if (lane == 0) set_status(g.status, MIMO_ERANGE);
+                ok = false;
+                col = 0;
+              }
+            }
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < NTOK; ++c)
+              if (c == col) {
+                a0 = acc[0][c];
+                a1 = acc[1][c];
+              }
+            if (!phase) {
+              // SwiGLU with the reference's roundings (kernels.py:79-82), then h as the down pass's terms
+              float h = 0.f;
+              if (ok) {
+                h = swiglu_ref(a0, a1);
+                if (!isfinite(h)) set_status(g.status, MIMO_ERANGE);
+              }
+              uint32_t th, tl, b1, b2;
+              split_warp_block(h, th, tl, b1, b2);
+              const size_t r0 = (size_t)unit * N + qq, rl = r0 + NTOK;
+              g.hq[r0 * g.Nw + row] = (uint8_t)th;
+              g.hq[rl * g.Nw + row] = (uint8_t)tl;
+              if (lane == 0) {
+                g.hs[r0 * (g.Nw / 32) + row / 32] = (uint8_t)b1;
+                g.hs[rl * (g.Nw / 32) + row / 32] = (uint8_t)b2;
+              }
+            } else if (ok) {
+              // down x route weight (kernels.py:120)
+              const int orow = d.out_row ? __ldg(d.out_row + p0 + qq) : p0 + qq;
+              const float v = (d.pairs_rounding ? bf16_round(a0) : a0) * __ldg(d.rw + p0 + qq);
+              if (d.peer_part)
+                d.peer_part[orow / d.peer_rows][(size_t)(orow % d.peer_rows) * d.Nw + row] = v;
+              else
+                d.part[(size_t)orow * d.Nw + row] = v;
+            }
+          }
+        }
+        if (!phase) {  // publish this warp's share of the unit's h to the down groups
+          __threadfence();
+          fz::fence_proxy_async_global();
+          __syncwarp();
+          if (lane == 0) atomicAdd(f.ready + unit, 1);
+        } else if (f.y) {
+          // fused combine: the CTA completing the last unit's tile of these output rows sums them
+          __threadfence();
+          named_bar_sync(1, kEpiWarps * 32);
+          if (ew == 0 && lane == 0) *s_last = atomicAdd(f.done + tile, 1) == units - 1;
+          named_bar_sync(1, kEpiWarps * 32);
+          if (*s_last && !aborted) {
+            __threadfence();
+            const long long rows = (long long)p.units_cap * f.R;  // part rows
+            const int col0 = tile * kM;
+            for (int o = ew * 32 + lane; o < f.M * kM; o += kEpiWarps * 32) {
+              const int m = o / kM, j = col0 + o % kM;
+              float sum = 0.f;
+              if (f.gidx) {
+                for (int k = 0; k < f.topk; ++k) {
+                  const int sl = __ldg(f.gidx + m * f.topk + k);
+                  if (sl >= rows) {
+                    set_status(g.status, MIMO_ERANGE);
+                    continue;
+                  }
+                  if (sl >= 0) sum = __fadd_rn(sum, __ldcg(d.part + (size_t)sl * d.Nw + j));
+                }
+              } else {
+                for (int u = 0; u < units; ++u) {
+                  const int n = min(__ldg(f.ucnt + u), f.R);
+                  for (int r = 0; r < n; ++r)
+                    if (__ldg(f.urows + u * f.R + r) == m)
+                      sum = __fadd_rn(sum, __ldcg(d.part + (size_t)(u * f.R + r) * d.Nw + j));
+                }
+              }
+              f.y[(size_t)m * d.Nw + j] = (uint16_t)f32_to_bf16(sum);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 3) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------ prefill on SM pairs (cta_group::2)
 // The prefill passes on pairs of SMs.  A cluster of two CTAs takes one 256-row weight tile per item:
 // rows [0, 128) of the tile sit in CTA 0's shared memory and rows [128, 256) in CTA 1's, and the unit's
@@ -1758,6 +2431,27 @@ static cudaError_t launch_fused(const TcFusedParams& f, int num_sms, cudaStream_
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   return launch_k(kfn, dim3(num_sms), dim3(tc::kThreads), smem, st, f);
+}
+
+#ifndef MIMO_TC_STSK
+#define MIMO_TC_STSK 5  // ring depth of the stream-K decode kernel
+#endif
+cudaError_t launch_tc_decode_sk(const TcSkParams& f, cudaStream_t st) {
+  auto kfn = tc::tc_decode_sk_kernel<MIMO_TC_STSK>;
+  constexpr int smem = tc::sk::smem_bytes<MIMO_TC_STSK>();
+  static_assert(smem <= 232448, "shared memory budget");
+  static_assert(tc::sk::kSfCol0 + MIMO_TC_STSK * 16 <= tc::sk::kTmemCols, "TMEM budget");
+  static_assert((2 * MIMO_TC_STSK + 2 * tc::sk::kScRing + 2 * tc::sk::kNAcc + 1) * 8 + 8 <= tc::kBarBytes,
+                "barrier area");
+  const TcParams& g = f.gu;
+  const TcParams& d = f.dn;
+  if (g.K % kSkGroupK || d.K % kSkGroupK || g.Nw % tc::kM ||
+      d.Nw % tc::kM || g.tiles != g.Nw / tc::kM || d.tiles != d.Nw / tc::kM || g.Nw != d.K || !f.ready ||
+      !f.part_g || !f.part_d || !f.flag_g || !f.flag_d || f.ctas < 1)
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return launch_k(kfn, dim3(f.ctas), dim3(tc::kThreads), smem, st, f);
 }
 
 cudaError_t launch_tc_decode_fused(const TcFusedParams& f, bool fp4, int num_sms, cudaStream_t st) {

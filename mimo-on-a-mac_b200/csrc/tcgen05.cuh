@@ -283,6 +283,27 @@ __device__ __forceinline__ void split_block32(const uint16_t* src, uint8_t* dh, 
   *sl = (uint8_t)b2;
 }
 
+// split_block32 with one warp per block (lane = value): the same bytes (the maxima ignore NaN, as
+// fmaxf does; every conversion is per element), in a few dependent steps instead of 32 serial values.
+__device__ __forceinline__ void split_block32_warp(const uint16_t* src, uint8_t* dh, uint8_t* dl, uint8_t* sh,
+                                                   uint8_t* sl, int32_t* status) {
+  const int lane = threadIdx.x & 31;
+  const float v = __uint_as_float((uint32_t)src[lane] << 16);
+  if (__any_sync(0xFFFFFFFFu, !isfinite(v)) && lane == 0) set_status(status, MIMO_ERANGE);
+  const float amax = __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, isnan(v) ? 0u : __float_as_uint(fabsf(v))));
+  const uint32_t b1 = block_scale_byte(amax);
+  const uint32_t h = f32_to_e4m3(v * inv_exp2_byte(b1));
+  const float r = v - e4m3_to_f32(h) * exp2_byte(b1);
+  const float rmax = __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, isnan(r) ? 0u : __float_as_uint(fabsf(r))));
+  const uint32_t b2 = block_scale_byte(rmax);
+  dh[lane] = (uint8_t)h;
+  dl[lane] = (uint8_t)f32_to_e4m3(r * inv_exp2_byte(b2));
+  if (lane == 0) {
+    *sh = (uint8_t)b1;
+    *sl = (uint8_t)b2;
+  }
+}
+
 // ------------------------------------------------------------------ e2m1 multi-term activations
 // A value block of 32 becomes kFp4Terms e2m1 terms, each with one ue8m0 scale: term t quantises the
 // residual r_t (r_0 = v) with the scale s_t that puts max |r_t| / s_t in (3, 6], and

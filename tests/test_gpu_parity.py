@@ -352,11 +352,13 @@ def test_downstream_logit_kl_through_a_random_head(gpu):
     assert kl < 1e-3
 
 
-def test_prefill_at_full_size_equals_the_per_route_path(gpu):
+def test_prefill_at_full_size_agrees_with_the_per_route_path(gpu):
     """Size-independent check at BASELINE scale (T = 2048, 256 experts): the prefill path (64-route
-    units, bf16 pair outputs, weighted fixed-order combine) equals, bit for bit, the per-route partials
-    of the expert-parallel building block with bf16 rounding (8-route units) followed by the route-order
-    combine — two different kernel configurations computing the same arithmetic."""
+    units, bf16 pair outputs, weighted fixed-order combine) against the per-route partials of the
+    expert-parallel building block with bf16 rounding (the stream-K decode kernel: 8-route units, each
+    512-value K group accumulated on its own and the groups added in order) followed by the route-order
+    combine.  The two kernels round their float32 sums at different points, so they agree within the
+    oracle bar and on nearly every bf16 output, not bit for bit."""
     import mimo_moe
     pool = mimo_moe.ExpertPools.synthetic(256, seed=0, layer=4, device=gpu)
     T = 2048
@@ -366,7 +368,10 @@ def test_prefill_at_full_size_equals_the_per_route_path(gpu):
     y_pref = mimo_moe.moe_prefill(x, pool, idx, w)
     part = mimo_moe.moe_experts_routes(x, pool, idx, w, expert_base=0, pairs_rounding=True)
     y_route = mimo_moe.combine(part, T, 8)
-    assert torch.equal(y_pref.view(torch.int16), y_route.view(torch.int16))
+    same = float((y_pref.view(torch.int16) == y_route.view(torch.int16)).float().mean())
+    rel = O.rel_err(f32(y_route), f32(y_pref))
+    print(f"prefill vs per-route path: rel_err {rel:.2e}, identical bf16 outputs {same:.5f}")
+    assert rel <= TOL_ORACLE and same >= 0.99
     # and a spot check of a few tokens against the oracle
     opool = O.Pool(synth.SynthPool(0, 4))
     rows = [0, 1000, 2047]
