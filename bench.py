@@ -583,9 +583,10 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     # builder, term split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch,
     # 2 unit builders, term split, gate/up, down, per-route combine, weighted combine.
     fused = n_fz > 0
-    # single-GPU decode: route + the stream-K launch (its epilogue also combines), route + fused + combine,
-    # or route + gate/up + down + combine
-    per_decode = 2 if kind_fz == 5 and n_fz else (3 if fused else 4)
+    # single-GPU decode: route (router logits, top-k select) + the expert launches (stream-K or fused:
+    # one; gate/up and down: two) + the combine when it runs as its own launch (by default the down
+    # kernel's epilogue combines; the profile counts kind 7 only for a separate combine)
+    per_decode = 2 + (1 if fused else 2) + (1 if int(launches[0][7]) > 0 else 0)
     launches_per_step = ((7 if fused else 8) if peer else 12) if ep else (per_decode if B <= 8 else 11)
     res = {
         "metric": f"MoE-layer tok/s ({workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",

@@ -100,7 +100,7 @@ struct TermWs {
   int nzero;
   float *skg, *skd;  // stream-K decode: contributed gate/up and down group partials
   int32_t *flag_g, *flag_d;
-  int32_t* done;     // stream-K decode: down tiles completed per output row tile (fused combine)
+  int32_t* done;     // decode: down tiles completed per output row tile (combine in the down kernel)
   int ctas;          // CTAs the stream-K scratch is sized for
 };
 // Activation terms of `units` units: e4m3 (2 terms, one byte a value) or, for decode units on the
@@ -292,7 +292,22 @@ bool prefill_pair() {
 }
 
 
-// The decode combine (kernels.py:194-199) of mimo_moe_experts, fused into the stream-K expert kernel.
+// Decode combine placement (MIMO_MOE_DECODE_COMBINE, a comparison knob; bit-identical outputs):
+//   separate (default)  its own launch, M x H/1024 CTAs;
+//   down                in the down kernel's epilogue, by the CTA completing each output row tile.  One
+//                       launch fewer, but every tile pays a fence and three epilogue barriers and the
+//                       last tiles' sums run serially at the end: on B200, B = 8 decode 181 us against
+//                       167 us, B = 1 48.0 against 47.0.
+bool combine_in_down() {
+  static const bool on = [] {
+    const char* e = getenv("MIMO_MOE_DECODE_COMBINE");
+    return e && std::string(e) == "down";
+  }();
+  return on;
+}
+
+// The decode combine (kernels.py:194-199) of mimo_moe_experts, fused into the decode down kernel (or
+// the stream-K expert kernel).
 struct CombineArgs {
   uint16_t* y;
   const int32_t *gidx, *urows, *ucnt;
@@ -418,6 +433,18 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
     const TcFusedParams f{p, q, t.ready};
     MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, fp4, sms, st); }));
     return MIMO_OK;
+  }
+  if (decode && comb && part && !peer_part && by_token_rows && combine_in_down()) {
+    // the combine runs in the down kernel's epilogue: count the tiles of each output row tile
+    if (!ready_zeroed) MIMO_TRY(cudaMemsetAsync(t.done, 0, (size_t)q.tiles * sizeof(int32_t), st));
+    q.cy = comb->y;
+    q.cgidx = comb->gidx;
+    q.curows = comb->urows;
+    q.cucnt = comb->ucnt;
+    q.cdone = t.done;
+    q.cM = comb->M;
+    q.ctopk = comb->topk;
+    if (combined) *combined = true;
   }
   if (pair) MIMO_TRY(profiled(3, st, [&] { return launch_tc_pair(q, 3, sms, st); }));
   else MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(q, decode ? 1 : 3, sms, st); }));

@@ -113,6 +113,16 @@ struct TcParams {
   int peer_rows;
   int pairs_rounding;
   int32_t* status;
+  // Down, decode, fused combine (cy non-null, partials in `part`): the CTA storing the last unit's
+  // partials of output rows [128 r, 128 r + 128) (cdone[r] counts them, zeroed per call) forms
+  // cy[m] = bf16(sum over k in order of part[cgidx[m * ctopk + k]]) for those rows (cgidx null: the
+  // (u, r) scatter order over curows / cucnt with p0_stride route slots per unit).
+  uint16_t* cy;
+  const int32_t* cgidx;
+  const int32_t* curows;
+  const int32_t* cucnt;
+  int32_t* cdone;
+  int cM, ctopk;
 };
 // Both decode passes in one launch (tc_experts.cu): gate/up params (kind 0 layout) and down params
 // (kind 1 layout) over the same units; ready: [units_cap] zeroed counters.

@@ -171,6 +171,47 @@ __device__ __forceinline__ int unit_routes(const TcParams& p, int unit, int cap)
   return max(c, 0);
 }
 
+// Decode combine (kernels.py:194-199) of output rows [128 tile, 128 tile + 128), run by the epilogue
+// warps (ew = 0 .. nw - 1) of the CTA whose tile stores complete the count p.cdone[tile] (one per unit
+// and tile).  Before counting, every thread's partial stores are fenced; the winner fences again and
+// reads the partials through L2.  The sum over a token's routes is in the order of the separate combine
+// kernel, so the output is bit-identical to it.
+__device__ __noinline__ void combine_tile(const TcParams& p, int tile, int units, int ew, int lane, int nw,
+                                          volatile int* s_last) {
+  __threadfence();
+  named_bar_sync(1, nw * 32);
+  if (ew == 0 && lane == 0) *s_last = atomicAdd(p.cdone + tile, 1) == units - 1;
+  named_bar_sync(1, nw * 32);
+  const bool last = *s_last;
+  named_bar_sync(1, nw * 32);  // s_last is rewritten for the next item only after everyone read it
+  if (!last) return;
+  __threadfence();
+  const long long rows = (long long)p.units_cap * p.p0_stride;  // rows of part
+  const int col0 = tile * kM;
+  for (int o = ew * 32 + lane; o < p.cM * kM; o += nw * 32) {
+    const int m = o / kM, j = col0 + o % kM;
+    float sum = 0.f;
+    if (p.cgidx) {
+      for (int k = 0; k < p.ctopk; ++k) {
+        const int sl = __ldg(p.cgidx + m * p.ctopk + k);
+        if (sl >= rows) {
+          set_status(p.status, MIMO_ERANGE);
+          continue;
+        }
+        if (sl >= 0) sum = __fadd_rn(sum, __ldcg(p.part + (size_t)sl * p.Nw + j));
+      }
+    } else {
+      for (int u = 0; u < units; ++u) {
+        const int n = min(__ldg(p.cucnt + u), p.p0_stride);
+        for (int r = 0; r < n; ++r)
+          if (__ldg(p.curows + u * p.p0_stride + r) == m)
+            sum = __fadd_rn(sum, __ldcg(p.part + (size_t)(u * p.p0_stride + r) * p.Nw + j));
+      }
+    }
+    p.cy[(size_t)m * p.Nw + j] = (uint16_t)f32_to_bf16(sum);
+  }
+}
+
 // EPI epilogue warps (a multiple of 4): EPI / 4 per TMEM lane quadrant, each taking NTOK / (EPI / 4) of
 // the routes.  Prefill uses 16: its per-route SwiGLU and term split are long dependent chains, and
 // four warps per SM sub-partition hide their latency where two cannot.
@@ -571,6 +612,13 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
           for (int i = 0; i < QH; ++i) emit(qlo + i, hv[0][i], hv[1][i], lv[0][i], lv[1][i]);
         }
       }
+      if constexpr (MODE == 1) {
+        if (p.cy) combine_tile(p, tile, units, warp - 4, lane, EPI, s_abort + 1);
+      }
+    }
+    if constexpr (MODE == 1) {  // no units: no tile completes, and the sum over no routes is 0
+      if (p.cy && units == 0 && blockIdx.x == 0)
+        for (int o = (warp - 4) * 32 + lane; o < p.cM * p.Nw; o += EPI * 32) p.cy[o] = 0;
     }
   }
   tc_fence_before();
