@@ -470,15 +470,15 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     launches = (np.zeros(8, np.int32), np.zeros(8, np.float32))
     _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
     phases = None
-    if gstep is not None or peer:  # graph replays carry no events: time the kernels in an eager pass
-        nprof = min(steps, 50)
+    if gstep is not None or ep:  # graph replays carry no events: time the kernels in an eager pass
+        nprof = min(steps, 50 if B <= 8 else 5)
         _lib.check(L.mimo_moe_profile_enable(6 * nprof + 8), "profile_enable")
-        if peer:
+        if ep:
             blk.trace = PhaseTrace()
         for i in range(nprof):
             eager(xs[i % nb])
         torch.cuda.synchronize()
-        if peer:
+        if ep:
             phases = blk.trace.summary()
             blk.trace = None
         _lib.check(L.mimo_moe_profile_read(launches[0].ctypes.data, launches[1].ctypes.data), "profile_read")
@@ -577,17 +577,18 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
         e2e_graph = B * world * steps / (g_ms * 1e-3)
 
     tok = B * steps * world
-    # our kernels per step: decode = route (zeroes the counters too), gate/up + down (one fused launch,
-    # or two), combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
+    # our kernels per step: decode = route (logits, select), gate/up + down (one fused launch, or two),
+    # combine; prefill = router GEMM, top-k, 3 dispatch, 2 unit builders, term split, gate/up,
     # down, combine.  Expert parallelism, peer exchange: router logits, route+scatter, 2 barriers, unit
-    # builder, term split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 dispatch,
-    # 2 unit builders, term split, gate/up, down, per-route combine, weighted combine.
+    # builder, term split, gate/up, down, combine; all-to-all prefill: router GEMM, top-k, 3 exchange plan,
+    # send-row gather, received-route gather, 3 dispatch, 2 unit builders, term split, gate/up, down,
+    # per-route combine, weighted combine.
     fused = n_fz > 0
     # single-GPU decode: route (router logits, top-k select) + the expert launches (stream-K or fused:
-    # one; gate/up and down: two) + the combine when it runs as its own launch (by default the down
-    # kernel's epilogue combines; the profile counts kind 7 only for a separate combine)
+    # one; gate/up and down: two) + the combine when it runs as its own launch (the default; when the
+    # down kernel's epilogue combines, the profile records no combine launch)
     per_decode = 2 + (1 if fused else 2) + (1 if int(launches[0][7]) > 0 else 0)
-    launches_per_step = ((7 if fused else 8) if peer else 12) if ep else (per_decode if B <= 8 else 11)
+    launches_per_step = ((7 if fused else 8) if peer else 17) if ep else (per_decode if B <= 8 else 11)
     res = {
         "metric": f"MoE-layer tok/s ({workload})", "value": tok / (ms * 1e-3), "unit": "tok/s",
         "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,

@@ -97,6 +97,32 @@ int mimo_moe_dispatch(const int32_t* idx, int32_t T, int32_t topk, int32_t E, in
                       int32_t* status, void* stream);
 
 /*
+ * Expert-parallel prefill exchange plan (no reference counterpart: the reference keeps every expert
+ * on one device; this moves each pair of model.py:235-244 to the rank owning its expert).  Rank d owns
+ * experts [d*per_rank, (d+1)*per_rank); routes p = t*topk + j are stable-sorted by destination rank:
+ *   counts   int64 [world][2]  (routes, token rows) sent to each rank
+ *   order    int32 [P]         route at send position s;   inv [P] = send position of route p
+ *                              (-1 and MIMO_ERANGE for an expert id outside [0, world*per_rank))
+ *   send_tok int32 [P]         token of send row r, the rows of rank 0 first (sum counts[:,1] used):
+ *                              each token row travels once to each rank owning any of its experts
+ *   send_tag int32 [P][2]      (row within the destination's rows, local expert id) per send position
+ * topk <= 16, world <= 8.  Workspace: mimo_moe_ep_plan_workspace_bytes(T, world).
+ * mimo_moe_gather_rows: out[r] = x[rows[r]] for r < n (bf16 rows of H; a row outside [0, x_rows) sets
+ * MIMO_ERANGE and gives zeros).  mimo_moe_ep_recv_gather, on the receiving rank: route i of the
+ * received routes (recv_counts = the senders' counts rows, device int64 [world][2]) names row tag[i][0]
+ * of the rows received from its sender; X[i] = that row of recv_rows, eid[i] = tag[i][1].
+ */
+size_t mimo_moe_ep_plan_workspace_bytes(int32_t T, int32_t world);
+int mimo_moe_ep_plan(const int32_t* idx, int32_t T, int32_t topk, int32_t per_rank, int32_t world,
+                     int64_t* counts, int32_t* order, int32_t* inv, int32_t* send_tok, int32_t* send_tag,
+                     void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+int mimo_moe_gather_rows(const uint16_t* x, int64_t x_rows, int32_t H, const int32_t* rows, int64_t n,
+                         uint16_t* out, int32_t* status, void* stream);
+int mimo_moe_ep_recv_gather(const uint16_t* recv_rows, const int32_t* recv_tag, const int64_t* recv_counts,
+                            int32_t world, int64_t n_recv, int32_t H, uint16_t* X, int32_t* eid,
+                            int32_t* status, void* stream);
+
+/*
  * Small-batch expert products over distinct experts — replaces moe_experts
  * (engine/mimo_stream/kernels.py:176-199: kernel A gate/up+SwiGLU, kernel B down*weight, combine).
  *   x [M,H] bf16; uslot/urows/ucnt/uw/gather_idx from mimo_moe_group_routes (uslot = pool slot per

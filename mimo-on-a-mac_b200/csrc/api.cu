@@ -679,6 +679,42 @@ int mimo_moe_dispatch(const int32_t* idx, int32_t T, int32_t topk, int32_t E, in
   return MIMO_OK;
 }
 
+size_t mimo_moe_ep_plan_workspace_bytes(int32_t T, int32_t world) {
+  if (T < 1 || world < 1 || world > 8) return 0;
+  return ep_plan_workspace_bytes(T, world);
+}
+
+int mimo_moe_ep_plan(const int32_t* idx, int32_t T, int32_t topk, int32_t per_rank, int32_t world,
+                     int64_t* counts, int32_t* order, int32_t* inv, int32_t* send_tok, int32_t* send_tag,
+                     void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!idx || !counts || !order || !inv || !send_tok || !send_tag || !workspace || T < 1 || topk < 1 ||
+      topk > 16 || world < 1 || world > 8 || per_rank < 1 || (int64_t)T * topk > (1 << 30))
+    return MIMO_EINVAL;
+  if (workspace_bytes < ep_plan_workspace_bytes(T, world)) return MIMO_EINVAL;
+  MIMO_TRY(launch_ep_plan(idx, T, topk, per_rank, world, counts, order, inv, send_tok, send_tag, workspace,
+                          status, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_gather_rows(const uint16_t* x, int64_t x_rows, int32_t H, const int32_t* rows, int64_t n,
+                         uint16_t* out, int32_t* status, void* stream) {
+  if ((n > 0 && (!x || !rows || !out)) || H < 8 || H % 8 || n < 0 || n > 0x7FFFFFFF || x_rows < 0)
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_gather_rows(x, x_rows, H, rows, n, out, status, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_ep_recv_gather(const uint16_t* recv_rows, const int32_t* recv_tag, const int64_t* recv_counts,
+                            int32_t world, int64_t n_recv, int32_t H, uint16_t* X, int32_t* eid, int32_t* status,
+                            void* stream) {
+  if ((n_recv > 0 && (!recv_rows || !recv_tag || !recv_counts || !X || !eid)) || world < 1 || world > 8 ||
+      H < 8 || H % 8 || n_recv < 0 || n_recv > 0x7FFFFFFF)
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_ep_recv_gather(recv_rows, recv_tag, recv_counts, world, n_recv, H, X, eid, status,
+                                 static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
 size_t mimo_moe_experts_workspace_bytes(int32_t M, int32_t U, int32_t R, int32_t H, int32_t I) {
   if (M < 1 || U < 1 || R < 1) return 0;
   Carver c(nullptr);

@@ -219,6 +219,16 @@ cudaError_t launch_group_routes(const int32_t* idx, const float* weight, int M, 
                                 int E, int32_t* uids, int32_t* urows, int32_t* ucnt, float* uw,
                                 int32_t* gidx, int32_t* num_unique, int32_t* status, cudaStream_t st);
 size_t dispatch_workspace_bytes(int P, int E);
+// Expert-parallel prefill exchange plan and row gathers (ep_plan.cu).
+size_t ep_plan_workspace_bytes(int T, int world);
+cudaError_t launch_ep_plan(const int32_t* idx, int T, int topk, int per_rank, int world, int64_t* counts,
+                           int32_t* order, int32_t* inv, int32_t* send_tok, int32_t* send_tag, void* ws,
+                           int32_t* status, cudaStream_t st);
+cudaError_t launch_gather_rows(const uint16_t* x, long long x_rows, int H, const int32_t* rows, long long n,
+                               uint16_t* out, int32_t* status, cudaStream_t st);
+cudaError_t launch_ep_recv_gather(const uint16_t* recv_rows, const int32_t* tag, const int64_t* recv_counts,
+                                  int world, long long n_recv, int H, uint16_t* X, int32_t* eid, int32_t* status,
+                                  cudaStream_t st);
 // Routes with expert id - id_base outside [0, E) are dropped (inv = -1); they set MIMO_ERANGE unless
 // skip_outside (expert parallelism: routes to other ranks' experts).
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* order,

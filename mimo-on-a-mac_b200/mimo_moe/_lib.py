@@ -5,7 +5,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_float, c_int32, c_size_t, c_uint64, c_void_p
+from ctypes import POINTER, c_float, c_int32, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(os.environ.get("MIMO_MOE_LIBRARY") or Path(__file__).resolve().with_name("libmimo_moe.so"))
@@ -35,6 +35,13 @@ SIGNATURES = {
     "mimo_moe_dispatch_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
     "mimo_moe_dispatch": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_ep_plan_workspace_bytes": (c_size_t, [c_int32, c_int32]),
+    "mimo_moe_ep_plan": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_gather_rows": (c_int32, [c_void_p, c_int64, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                                       c_void_p]),
+    "mimo_moe_ep_recv_gather": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_void_p,
+                                          c_void_p, c_void_p, c_void_p]),
     "mimo_moe_experts_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "mimo_moe_experts": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_int32,

@@ -10,7 +10,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 INCLUDE = PKG.parent.parent / "include"
 LIB = PKG / "libmimo_moe.so"
-SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "synth.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu", "norm.cu", "loader.cpp"]
+SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "synth.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu", "norm.cu", "ep_plan.cu", "loader.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -268,6 +268,9 @@ class PeerExpertParallelMoE:
 
 PairsFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
 CombinePairsFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, int, int], torch.Tensor]
+PlanFn = Callable[[torch.Tensor, int, int], "ops.EpPlan"]
+GatherFn = Callable[[torch.Tensor, torch.Tensor, int], torch.Tensor]
+RecvFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
 
 
 class ExpertParallelPrefill:
@@ -275,22 +278,26 @@ class ExpertParallelPrefill:
     every rank.  One step:
 
       1. route the rank's own T tokens (model.py:58-65);
-      2. dispatch: routes sorted by destination rank (stable); each token row travels once to every
-         rank that owns one of its experts, with a (row, local expert id) tag per route; the counts
-         of routes and rows per destination are exchanged first (they cross to the host once per
-         step, acceptable at prefill sizes), then one all-to-all of the rows and one of the tags;
-      3. expert side: the received routes' rows gathered from the received token rows, per-route bf16
-         products (`moe_prefill` with one route per row and weight 1, which returns each route's bf16
-         pair output unchanged, model.py:221-228);
+      2. plan (mimo_moe_ep_plan, on the device): routes ordered stably by destination rank; each token
+         row travels once to every rank that owns one of its experts, with a (row, local expert id) tag
+         per route; the counts of routes and rows per destination are exchanged first and cross to the
+         host once per step (all-to-all split sizes), then one all-to-all of the rows (gathered by
+         mimo_moe_gather_rows) and one of the tags;
+      3. expert side: the received routes' rows gathered from the received token rows
+         (mimo_moe_ep_recv_gather), per-route bf16 products (`moe_prefill` with one route per row and
+         weight 1, which returns each route's bf16 pair output unchanged, model.py:221-228);
       4. return: the inverse all-to-all;
       5. combine: y[t] = bf16(sum over k in order of fp32(out[t, k]) * w[t, k]) (model.py:266-271).
 
     Each route's bf16 output is computed by the same kernels as on one GPU, so the result equals the
-    single-GPU prefill path bit for bit.  Compute steps are pluggable for the CPU gloo tests."""
+    single-GPU prefill path bit for bit.  Compute, plan and gather steps are pluggable for the CPU gloo
+    tests (which pass torch restatements of the plan and gathers)."""
 
     def __init__(self, pools_local, router_w: torch.Tensor, bias: Optional[torch.Tensor], *,
                  num_experts: int = 256, topk: int = 8, group=None, router_fn: Optional[RouterFn] = None,
-                 pairs_fn: Optional[PairsFn] = None, combine_fn: Optional[CombinePairsFn] = None):
+                 pairs_fn: Optional[PairsFn] = None, combine_fn: Optional[CombinePairsFn] = None,
+                 plan_fn: Optional[PlanFn] = None, gather_fn: Optional[GatherFn] = None,
+                 recv_fn: Optional[RecvFn] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -303,49 +310,61 @@ class ExpertParallelPrefill:
         self.pairs_fn = pairs_fn or (lambda X, e: ops.moe_prefill(
             X, self.pools, e[:, None], torch.ones(e.shape[0], 1, device=X.device), E=self.per_rank))
         self.combine_fn = combine_fn or (lambda yp, inv, w, T, k: ops.combine_pairs(yp, inv, w, T, k))
+        self.plan_fn = plan_fn or (lambda idx, per_rank, world: ops.ep_plan(idx, per_rank, world))
+        self.gather_fn = gather_fn or (lambda x, rows, n: ops.gather_rows(x, rows, n))
+        self.recv_fn = recv_fn or (lambda rows, tag, counts: ops.ep_recv_gather(rows, tag, counts))
         self.routes_received = 0  # routes this rank's experts computed, summed over calls
+        self.trace: Optional[PhaseTrace] = None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         N, k, dev = self.world, self.topk, x.device
-        idx, w = self.router_fn(x)
-        idx = idx.to(torch.int32).reshape(-1)
-        w = w.to(torch.float32).contiguous()
-        P = idx.numel()
-        dest = (idx // self.per_rank).to(torch.int64)
-        order = torch.sort(dest, stable=True).indices            # send position -> route t*k + j
-        inv = torch.empty_like(order)
-        inv[order] = torch.arange(P, device=dev)                 # route -> send position
-        d_s, t_s = dest[order], order // k
-        # Within a destination, routes keep route order, so a token's routes there are adjacent: the
-        # first of them sends the token's row, every route carries that row's index in the segment.
-        new = torch.ones(P, dtype=torch.bool, device=dev)
-        if P > 1:
-            new[1:] = (d_s[1:] != d_s[:-1]) | (t_s[1:] != t_s[:-1])
-        send_counts = torch.bincount(dest, minlength=N).to(torch.int64)
-        row_counts = torch.bincount(d_s[new], minlength=N).to(torch.int64)
-        row_first = torch.cumsum(row_counts, 0) - row_counts
-        row_in_seg = (torch.cumsum(new.to(torch.int64), 0) - 1) - row_first[d_s]
-        counts = torch.stack([send_counts, row_counts], 1)      # [N, 2]: routes, rows per destination
-        recv_counts = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts, counts, group=self.group)
-        sc, rows_sc = send_counts.tolist(), row_counts.tolist()  # the step's one host crossing
-        rc, rows_rc = recv_counts[:, 0].tolist(), recv_counts[:, 1].tolist()
+        tr = self.trace
+        if tr:
+            tr.start()
+        if T:
+            idx, w = self.router_fn(x)
+            idx = idx.to(torch.int32).contiguous()
+            w = w.to(torch.float32).contiguous()
+            if tr:
+                tr.mark("route")
+            plan = self.plan_fn(idx, self.per_rank, N)
+        else:  # nothing to route; the exchange still runs (the other ranks wait for it)
+            w = torch.empty(0, k, dtype=torch.float32, device=dev)
+            z = torch.empty(0, dtype=torch.int32, device=dev)
+            plan = ops.EpPlan(torch.zeros(N, 2, dtype=torch.int64, device=dev), z, z, z, z.view(0, 2))
+        if tr:
+            tr.mark("plan")
+        recv_counts = torch.empty_like(plan.counts)
+        dist.all_to_all_single(recv_counts, plan.counts, group=self.group)
+        both = torch.cat([plan.counts, recv_counts]).tolist()  # the step's one host crossing
+        if tr:
+            tr.mark("counts_exchange")
+        sc, rows_sc = [c[0] for c in both[:N]], [c[1] for c in both[:N]]
+        rc, rows_rc = [c[0] for c in both[N:]], [c[1] for c in both[N:]]
         self.routes_received += sum(rc)
-        send_x = x[t_s[new]].contiguous()
-        send_tag = torch.stack([row_in_seg.to(torch.int32),
-                                idx[order] - d_s.to(torch.int32) * self.per_rank], 1).contiguous()
+        send_x = self.gather_fn(x, plan.send_tok, sum(rows_sc)) if T else x[:0]
+        send_tag = plan.send_tag[:sum(sc)].contiguous()
         recv_rows = torch.empty(sum(rows_rc), H, dtype=x.dtype, device=dev)
         recv_tag = torch.empty(sum(rc), 2, dtype=torch.int32, device=dev)
         dist.all_to_all_single(recv_rows, send_x, rows_rc, rows_sc, group=self.group)
         dist.all_to_all_single(recv_tag, send_tag, rc, sc, group=self.group)
+        if tr:
+            tr.mark("dispatch_rows")
         if recv_tag.shape[0]:
-            rrc = torch.tensor(rows_rc, dtype=torch.int64, device=dev)
-            src = torch.repeat_interleave(torch.arange(N, device=dev), torch.tensor(rc, device=dev))
-            rows = (torch.cumsum(rrc, 0) - rrc)[src] + recv_tag[:, 0].to(torch.int64)
-            out = self.pairs_fn(recv_rows[rows].contiguous(), recv_tag[:, 1].contiguous())
+            X, eid = self.recv_fn(recv_rows, recv_tag, recv_counts)
+            if tr:
+                tr.mark("recv_gather")
+            out = self.pairs_fn(X, eid)
         else:
             out = torch.empty(0, H, dtype=x.dtype, device=dev)
+        if tr:
+            tr.mark("experts")
         back = torch.empty(sum(sc), H, dtype=out.dtype, device=dev)
         dist.all_to_all_single(back, out.contiguous(), sc, rc, group=self.group)
-        return self.combine_fn(back, inv.to(torch.int32), w, T, k)
+        if tr:
+            tr.mark("return_rows")
+        y = self.combine_fn(back, plan.inv, w, T, k)
+        if tr:
+            tr.mark("combine")
+        return y

@@ -387,6 +387,72 @@ def combine_pairs(ypair: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, T: in
     return y
 
 
+# ------------------------------------------------------------------ expert-parallel prefill exchange
+@dataclass
+class EpPlan:
+    """The send side of one expert-parallel prefill step (mimo_moe_ep_plan): counts [world, 2] int64
+    (routes, token rows per destination rank); order / inv [P] (send position <-> route t*k + j);
+    send_tok [P] (token of each send row, rows of rank 0 first); send_tag [P, 2] (row within the
+    destination's rows, local expert id)."""
+    counts: torch.Tensor
+    order: torch.Tensor
+    inv: torch.Tensor
+    send_tok: torch.Tensor
+    send_tag: torch.Tensor
+
+
+def ep_plan(idx: torch.Tensor, per_rank: int, world: int, status: Optional[torch.Tensor] = None) -> EpPlan:
+    """Routes of idx [T, k] ordered stably by the rank owning their expert (rank d owns experts
+    [d * per_rank, (d + 1) * per_rank)), on the device."""
+    _need_cuda(idx, "idx")
+    idx = idx.to(torch.int32).contiguous()
+    T, k = idx.shape
+    P, dev = T * k, idx.device
+    counts = torch.empty(world, 2, dtype=torch.int64, device=dev)
+    order = torch.empty(P, dtype=torch.int32, device=dev)
+    inv = torch.empty(P, dtype=torch.int32, device=dev)
+    send_tok = torch.empty(P, dtype=torch.int32, device=dev)
+    send_tag = torch.empty(P, 2, dtype=torch.int32, device=dev)
+    ws = workspace(lib().mimo_moe_ep_plan_workspace_bytes(T, world), dev)
+    st = status if status is not None else _status(dev)
+    check(lib().mimo_moe_ep_plan(idx.data_ptr(), T, k, per_rank, world, counts.data_ptr(), order.data_ptr(),
+                                 inv.data_ptr(), send_tok.data_ptr(), send_tag.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 st.data_ptr(), _stream()), "ep_plan")
+    return EpPlan(counts, order, inv, send_tok, send_tag)
+
+
+def gather_rows(x: torch.Tensor, rows: torch.Tensor, n: int, status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[r] = x[rows[r]] for r < n (bf16 rows)."""
+    _need_cuda(x, "x")
+    x = x.to(torch.bfloat16).contiguous()
+    rows = rows.to(device=x.device, dtype=torch.int32).contiguous()
+    out = torch.empty(n, x.shape[1], dtype=torch.bfloat16, device=x.device)
+    st = status if status is not None else _status(x.device)
+    check(lib().mimo_moe_gather_rows(x.data_ptr(), x.shape[0], x.shape[1], rows.data_ptr(), n, out.data_ptr(),
+                                     st.data_ptr(), _stream()), "gather_rows")
+    return out
+
+
+def ep_recv_gather(recv_rows: torch.Tensor, recv_tag: torch.Tensor, recv_counts: torch.Tensor,
+                   status: Optional[torch.Tensor] = None):
+    """Receiving rank: (X [n, H] bf16, eid [n] int32), X[i] = the received row route i names (its tag's
+    row within the rows from its sender, recv_counts [world, 2] = the senders' counts rows)."""
+    _need_cuda(recv_tag, "recv_tag")
+    dev = recv_tag.device
+    n = recv_tag.shape[0]
+    H = recv_rows.shape[1]
+    recv_rows = recv_rows.to(torch.bfloat16).contiguous()
+    recv_tag = recv_tag.to(torch.int32).contiguous()
+    recv_counts = recv_counts.to(device=dev, dtype=torch.int64).contiguous()
+    X = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+    eid = torch.empty(n, dtype=torch.int32, device=dev)
+    st = status if status is not None else _status(dev)
+    check(lib().mimo_moe_ep_recv_gather(recv_rows.data_ptr(), recv_tag.data_ptr(), recv_counts.data_ptr(),
+                                        recv_counts.shape[0], n, H, X.data_ptr(), eid.data_ptr(), st.data_ptr(),
+                                        _stream()), "ep_recv_gather")
+    return X, eid
+
+
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, bias: Optional[torch.Tensor], pools,
               topk: int = TOPK, status: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
               return_routes: bool = False):

@@ -5,7 +5,9 @@ normalised sigmoid weights; expert e: tanh(x @ M_e) * w; combine: float32 sum ov
 bf16), so the test checks what the multi-GPU path adds: expert ownership, the all-gather dispatch,
 zero partials for other ranks' experts, the exact reduce-scatter return and the fixed-order combine;
 for the prefill path, the all-to-all of each route to its expert's rank (variable and empty splits),
-the return and the weighted combine.  The EP output must equal the single-process output bit for bit."""
+the return and the weighted combine (with the torch restatement of the device plan, tests/ep_ref.py,
+which the GPU tests hold the plan kernels to).  The EP output must equal the single-process output
+bit for bit."""
 import os
 import socket
 
@@ -127,9 +129,11 @@ def _prefill_worker(rank, world, port, out, clustered=False):
     try:
         from mimo_moe.ep import ExpertParallelPrefill, expert_range
         lo, _ = expert_range(rank, world, E)
+        import ep_ref
         blk = ExpertParallelPrefill(None, None, None, num_experts=E, topk=K,
                                     router_fn=_clustered_router if clustered else _router,
-                                    pairs_fn=_pairs(lo), combine_fn=_combine_pairs)
+                                    pairs_fn=_pairs(lo), combine_fn=_combine_pairs, plan_fn=ep_ref.plan,
+                                    gather_fn=ep_ref.gather_rows, recv_fn=ep_ref.recv_gather)
         # rank 1 routes no tokens in the second call: empty splits both ways
         for n in (T, T if rank == 0 else 0):
             y = blk(_tokens(rank)[:n])
