@@ -108,9 +108,10 @@ int mimo_moe_dispatch(const int32_t* idx, int32_t T, int32_t topk, int32_t E, in
  *   send_tag int32 [P][2]      (row within the destination's rows, local expert id) per send position
  * topk <= 16, world <= 8.  Workspace: mimo_moe_ep_plan_workspace_bytes(T, world).
  * mimo_moe_gather_rows: out[r] = x[rows[r]] for r < n (bf16 rows of H; a row outside [0, x_rows) sets
- * MIMO_ERANGE and gives zeros).  mimo_moe_ep_recv_gather, on the receiving rank: route i of the
+ * MIMO_ERANGE and gives zeros).  mimo_moe_ep_recv_index, on the receiving rank: route i of the
  * received routes (recv_counts = the senders' counts rows, device int64 [world][2]) names row tag[i][0]
- * of the rows received from its sender; X[i] = that row of recv_rows, eid[i] = tag[i][1].
+ * of the rows received from its sender; route_row[i] = that row's index in the received rows (-1 and
+ * MIMO_ERANGE outside them), eid[i] = tag[i][1].  The routes then run through mimo_moe_prefill_routes.
  */
 size_t mimo_moe_ep_plan_workspace_bytes(int32_t T, int32_t world);
 int mimo_moe_ep_plan(const int32_t* idx, int32_t T, int32_t topk, int32_t per_rank, int32_t world,
@@ -118,9 +119,8 @@ int mimo_moe_ep_plan(const int32_t* idx, int32_t T, int32_t topk, int32_t per_ra
                      void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 int mimo_moe_gather_rows(const uint16_t* x, int64_t x_rows, int32_t H, const int32_t* rows, int64_t n,
                          uint16_t* out, int32_t* status, void* stream);
-int mimo_moe_ep_recv_gather(const uint16_t* recv_rows, const int32_t* recv_tag, const int64_t* recv_counts,
-                            int32_t world, int64_t n_recv, int32_t H, uint16_t* X, int32_t* eid,
-                            int32_t* status, void* stream);
+int mimo_moe_ep_recv_index(const int32_t* recv_tag, const int64_t* recv_counts, int32_t world, int64_t n_recv,
+                           int32_t* route_row, int32_t* eid, int32_t* status, void* stream);
 
 /*
  * Small-batch expert products over distinct experts — replaces moe_experts
@@ -152,6 +152,16 @@ size_t mimo_moe_prefill_workspace_bytes(int32_t T, int32_t topk, int32_t H, int3
 int mimo_moe_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* slot_of, int32_t E,
                      const int32_t* idx, const float* weight, int32_t T, int32_t topk, uint16_t* y,
                      void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+/*
+ * Per-route prefill products (the expert side of expert-parallel prefill): route p applies expert idx[p]
+ * to row route_row[p] of x [x_rows,H] (x_rows <= P); y[p] = the route's bf16 pair output
+ * (model.py:221-228), the same bits mimo_moe_prefill combines.  Workspace:
+ * mimo_moe_prefill_workspace_bytes(P, 1, H, I, E).
+ */
+int mimo_moe_prefill_routes(const uint16_t* x, int32_t x_rows, const mimo_moe_pools* pools,
+                            const int32_t* slot_of, int32_t E, const int32_t* route_row, const int32_t* idx,
+                            int32_t P, uint16_t* y, void* workspace, size_t workspace_bytes, int32_t* status,
+                            void* stream);
 
 /*
  * The whole block — replaces one MoE layer of Engine.forward (engine/mimo_stream/model.py:303-336)

@@ -570,9 +570,12 @@ int run_experts(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* u
   return MIMO_OK;
 }
 
+// x_rows rows of x (route_row null: x_rows = T and route p reads row p / topk; else row route_row[p],
+// with x_rows <= T so the f16 copy fits the workspace); weight null: 1.
 int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* slot_of,
                 const int32_t* idx, const float* weight, int T, int topk, int E, uint16_t* y,
-                const PrefillWs& w, int32_t* status, cudaStream_t st) {
+                const PrefillWs& w, int32_t* status, cudaStream_t st, int x_rows,
+                const int32_t* route_row = nullptr) {
   const int H = pools->hidden;
   const int P = T * topk;
   const int sms = num_sms_current();
@@ -580,19 +583,19 @@ int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* s
     MIMO_TRY(launch_dispatch(idx, P, E, w.offsets, w.order, w.inv, w.dws, status, st));
     MIMO_TRY(launch_build_units(w.offsets, slot_of, E, pools->num_slots, kTcPrefillRoutes, w.ucap,
                                 w.unit_slot, w.unit_p0, w.unit_cnt, w.unit_first, w.unit_nsub, w.num_units,
-                                w.order, weight, P, topk, w.rtok, w.rw, status, st));
+                                w.order, weight, P, topk, w.rtok, w.rw, status, st, route_row));
     const int rc = run_tc(x, pools, kTcPrefillRoutes, w.unit_slot, w.unit_cnt, w.unit_p0, 0, w.unit_first,
                           w.unit_nsub, w.rtok, nullptr, w.num_units, w.ucap, 0, w.t, nullptr, w.ypair, status, st,
-                          0, false, false, nullptr, 0, nullptr, 0, /*x_rows=*/T);
+                          0, false, false, nullptr, 0, nullptr, 0, x_rows);
     if (rc != MIMO_OK) return rc;
     MIMO_TRY(launch_combine_prefill(w.ypair, w.inv, weight, T, topk, H, y, st));
     return MIMO_OK;
   }
-  MIMO_TRY(launch_to_f16(x, w.x16, (size_t)T * H, status, st));
+  MIMO_TRY(launch_to_f16(x, w.x16, (size_t)x_rows * H, status, st));
   MIMO_TRY(launch_dispatch(idx, P, E, w.offsets, w.order, w.inv, w.dws, status, st));
   MIMO_TRY(launch_build_units(w.offsets, slot_of, E, pools->num_slots, kPrefillUnit, w.ucap,
                               w.unit_slot, w.unit_p0, w.unit_cnt, nullptr, nullptr, w.num_units, w.order,
-                              weight, P, topk, w.rtok, w.rw, status, st));
+                              weight, P, topk, w.rtok, w.rw, status, st, route_row));
   ExpertParams p = gateup_params(pools, status);
   p.unit_slot = w.unit_slot;
   p.unit_p0 = w.unit_p0;
@@ -601,7 +604,7 @@ int run_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32_t* s
   p.units_cap = w.ucap;
   p.rtok = w.rtok;
   p.bsrc = w.x16;
-  p.brows = T;
+  p.brows = x_rows;
   p.h_out = w.h16;
   MIMO_TRY(tiles(p, 2, sms, st));
   ExpertParams q = down_params(p, pools);
@@ -704,14 +707,13 @@ int mimo_moe_gather_rows(const uint16_t* x, int64_t x_rows, int32_t H, const int
   return MIMO_OK;
 }
 
-int mimo_moe_ep_recv_gather(const uint16_t* recv_rows, const int32_t* recv_tag, const int64_t* recv_counts,
-                            int32_t world, int64_t n_recv, int32_t H, uint16_t* X, int32_t* eid, int32_t* status,
-                            void* stream) {
-  if ((n_recv > 0 && (!recv_rows || !recv_tag || !recv_counts || !X || !eid)) || world < 1 || world > 8 ||
-      H < 8 || H % 8 || n_recv < 0 || n_recv > 0x7FFFFFFF)
+int mimo_moe_ep_recv_index(const int32_t* recv_tag, const int64_t* recv_counts, int32_t world, int64_t n_recv,
+                           int32_t* route_row, int32_t* eid, int32_t* status, void* stream) {
+  if ((n_recv > 0 && (!recv_tag || !recv_counts || !route_row || !eid)) || world < 1 || world > 8 || n_recv < 0 ||
+      n_recv > 0x7FFFFFFF)
     return MIMO_EINVAL;
-  MIMO_TRY(launch_ep_recv_gather(recv_rows, recv_tag, recv_counts, world, n_recv, H, X, eid, status,
-                                 static_cast<cudaStream_t>(stream)));
+  MIMO_TRY(launch_ep_recv_index(recv_tag, recv_counts, world, n_recv, route_row, eid, status,
+                                static_cast<cudaStream_t>(stream)));
   return MIMO_OK;
 }
 
@@ -754,7 +756,21 @@ int mimo_moe_prefill(const uint16_t* x, const mimo_moe_pools* pools, const int32
   const PrefillWs w = carve_prefill(c, T, topk, pools->hidden, pools->inter, E);
   if (c.off > workspace_bytes) return MIMO_EINVAL;
   return run_prefill(x, pools, slot_of, idx, weight, T, topk, E, y, w, status,
-                     static_cast<cudaStream_t>(stream));
+                     static_cast<cudaStream_t>(stream), T);
+}
+
+int mimo_moe_prefill_routes(const uint16_t* x, int32_t x_rows, const mimo_moe_pools* pools,
+                            const int32_t* slot_of, int32_t E, const int32_t* route_row, const int32_t* idx,
+                            int32_t P, uint16_t* y, void* workspace, size_t workspace_bytes, int32_t* status,
+                            void* stream) {
+  if (!x || !pools_ok(pools) || !route_row || !idx || !y || !workspace || P < 1 || P > (1 << 26) ||
+      x_rows < 1 || x_rows > P || E < 1 || E > 1024 || (!slot_of && E != pools->num_slots))
+    return MIMO_EINVAL;
+  Carver c(workspace);
+  const PrefillWs w = carve_prefill(c, P, 1, pools->hidden, pools->inter, E);
+  if (c.off > workspace_bytes) return MIMO_EINVAL;
+  return run_prefill(x, pools, slot_of, idx, nullptr, P, 1, E, y, w, status, static_cast<cudaStream_t>(stream),
+                     x_rows, route_row);
 }
 
 size_t mimo_moe_block_workspace_bytes(int32_t T, int32_t H, int32_t I, int32_t E, int32_t topk) {
@@ -809,7 +825,7 @@ int mimo_moe_block(const uint16_t* x, const uint16_t* router_w, const float* bia
   if (c.off > workspace_bytes) return MIMO_EINVAL;
   MIMO_TRY(launch_router_logits(x, router_w, logits, T, H, E, st, status));
   MIMO_TRY(launch_router_topk(logits, bias, T, E, topk, idx, wts, st));
-  return run_prefill(x, pools, nullptr, idx, wts, T, topk, E, y, pw, status, st);
+  return run_prefill(x, pools, nullptr, idx, wts, T, topk, E, y, pw, status, st, T);
 }
 
 size_t mimo_moe_experts_routes_workspace_bytes(int32_t rows, int32_t topk, int32_t H, int32_t I, int32_t S) {

@@ -200,15 +200,17 @@ __global__ void __launch_bounds__(1024) build_units_kernel(
   if (e == 1023) num_units[0] = min(nu[1023], ucap);
 }
 
-// Per sorted route position i: token row and router weight of the pair order[i].
+// Per sorted route position i: token row and router weight of the pair order[i] (route_row given:
+// the row is route_row[pair]; weight null: 1).
 __global__ void route_rows_kernel(const int32_t* __restrict__ order, const float* __restrict__ weight,
                                   const int32_t* __restrict__ offsets, int E, int P, int topk,
-                                  int32_t* __restrict__ rtok, float* __restrict__ rw) {
+                                  const int32_t* __restrict__ route_row, int32_t* __restrict__ rtok,
+                                  float* __restrict__ rw) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < P && i < offsets[E]) {  // positions past offsets[E] belong to dropped (invalid) routes
     const int p = order[i];
-    rtok[i] = p / topk;
-    rw[i] = weight[p];
+    rtok[i] = route_row ? route_row[p] : p / topk;
+    rw[i] = weight ? weight[p] : 1.f;
   }
 }
 
@@ -217,10 +219,10 @@ cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, i
                                int32_t* unit_cnt, int32_t* unit_first, int32_t* unit_nsub,
                                int32_t* num_units, const int32_t* order,
                                const float* weight, int P, int topk, int32_t* rtok, float* rw,
-                               int32_t* status, cudaStream_t st) {
+                               int32_t* status, cudaStream_t st, const int32_t* route_row) {
   build_units_kernel<<<1, 1024, 0, st>>>(offsets, slot_of, E, S, unit_max, ucap, unit_slot, unit_p0,
                                          unit_cnt, unit_first, unit_nsub, num_units, status);
-  route_rows_kernel<<<(P + 255) / 256, 256, 0, st>>>(order, weight, offsets, E, P, topk, rtok, rw);
+  route_rows_kernel<<<(P + 255) / 256, 256, 0, st>>>(order, weight, offsets, E, P, topk, route_row, rtok, rw);
   return cudaGetLastError();
 }
 

@@ -16,8 +16,8 @@
 //
 // Kernels: per 1024-token chunk, each thread counts its token's routes per destination (count), one
 // CTA scans the chunk totals into per-destination bases (scan), and each chunk writes its tokens'
-// positions from block-wide exclusive scans (scatter).  The receiving rank then gathers each received
-// route's row from the received rows (ep_recv_gather); send rows are gathered by gather_rows.
+// positions from block-wide exclusive scans (scatter).  The receiving rank then finds each received
+// route's row among the received rows (ep_recv_index); send rows are gathered by gather_rows.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -208,15 +208,15 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 }
 
 // Receiving side: received route i came from rank src (the segment of i in the per-rank route counts
-// recv_counts[:, 0]) and names row tag[i][0] of the rows received from src (recv_counts[:, 1]);
-// X[i] = that row, eid[i] = tag[i][1].  A tag outside the rows received from its rank sets MIMO_ERANGE
-// and gives a zero row.
-__global__ void __launch_bounds__(256) ep_recv_gather_kernel(const uint16_t* __restrict__ recv_rows,
-                                                             const int32_t* __restrict__ tag,
-                                                             const int64_t* __restrict__ recv_counts, int world,
-                                                             int H, uint16_t* __restrict__ X,
-                                                             int32_t* __restrict__ eid, int32_t* status) {
-  const long long i = blockIdx.x;
+// recv_counts[:, 0]) and names row tag[i][0] of the rows received from src (recv_counts[:, 1]):
+// route_row[i] = that row's index in the received rows, eid[i] = tag[i][1].  A tag outside the rows
+// received from its rank sets MIMO_ERANGE and gives row -1.
+__global__ void __launch_bounds__(256) ep_recv_index_kernel(const int32_t* __restrict__ tag,
+                                                            const int64_t* __restrict__ recv_counts, int world,
+                                                            long long n, int32_t* __restrict__ route_row,
+                                                            int32_t* __restrict__ eid, int32_t* status) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
   long long route_end = 0, row_base = 0, nrows = 0;
   int src = world;
   for (int s = 0; s < world; ++s) {
@@ -230,13 +230,9 @@ __global__ void __launch_bounds__(256) ep_recv_gather_kernel(const uint16_t* __r
   }
   const int t0 = __ldg(tag + 2 * i);
   const bool ok = src < world && t0 >= 0 && t0 < nrows;
-  if (threadIdx.x == 0) {
-    if (!ok) set_status(status, MIMO_ERANGE);
-    eid[i] = __ldg(tag + 2 * i + 1);
-  }
-  const uint4* s = reinterpret_cast<const uint4*>(recv_rows + (size_t)(ok ? row_base + t0 : 0) * H);
-  uint4* d = reinterpret_cast<uint4*>(X + (size_t)i * H);
-  for (int k = threadIdx.x; k < H / 8; k += blockDim.x) d[k] = ok ? __ldg(s + k) : make_uint4(0, 0, 0, 0);
+  if (!ok) set_status(status, MIMO_ERANGE);
+  route_row[i] = ok ? (int32_t)(row_base + t0) : -1;
+  eid[i] = __ldg(tag + 2 * i + 1);
 }
 
 cudaError_t launch_gather_rows(const uint16_t* x, long long x_rows, int H, const int32_t* rows, long long n,
@@ -247,13 +243,12 @@ cudaError_t launch_gather_rows(const uint16_t* x, long long x_rows, int H, const
   return cudaGetLastError();
 }
 
-cudaError_t launch_ep_recv_gather(const uint16_t* recv_rows, const int32_t* tag, const int64_t* recv_counts,
-                                  int world, long long n_recv, int H, uint16_t* X, int32_t* eid, int32_t* status,
-                                  cudaStream_t st) {
-  if (n_recv < 0 || n_recv > 0x7FFFFFFFLL || H % 8 || world < 1 || world > ep::kMaxWorld)
-    return cudaErrorInvalidValue;
+cudaError_t launch_ep_recv_index(const int32_t* tag, const int64_t* recv_counts, int world, long long n_recv,
+                                 int32_t* route_row, int32_t* eid, int32_t* status, cudaStream_t st) {
+  if (n_recv < 0 || n_recv > 0x7FFFFFFFLL || world < 1 || world > ep::kMaxWorld) return cudaErrorInvalidValue;
   if (n_recv == 0) return cudaSuccess;
-  ep_recv_gather_kernel<<<(unsigned)n_recv, 256, 0, st>>>(recv_rows, tag, recv_counts, world, H, X, eid, status);
+  ep_recv_index_kernel<<<(unsigned)((n_recv + 255) / 256), 256, 0, st>>>(tag, recv_counts, world, n_recv, route_row,
+                                                                         eid, status);
   return cudaGetLastError();
 }
 

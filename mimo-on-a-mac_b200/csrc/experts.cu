@@ -807,7 +807,7 @@ __global__ void combine_prefill_kernel(const uint16_t* __restrict__ ypair, const
   for (int k = 0; k < topk; ++k) {
     const int pos = inv[t * topk + k];
     if (pos < 0) continue;
-    const float wk = w[t * topk + k];
+    const float wk = w ? w[t * topk + k] : 1.f;
     const uint4 v = *reinterpret_cast<const uint4*>(ypair + (size_t)pos * H + m);
     const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll

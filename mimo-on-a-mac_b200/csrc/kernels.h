@@ -226,9 +226,8 @@ cudaError_t launch_ep_plan(const int32_t* idx, int T, int topk, int per_rank, in
                            int32_t* status, cudaStream_t st);
 cudaError_t launch_gather_rows(const uint16_t* x, long long x_rows, int H, const int32_t* rows, long long n,
                                uint16_t* out, int32_t* status, cudaStream_t st);
-cudaError_t launch_ep_recv_gather(const uint16_t* recv_rows, const int32_t* tag, const int64_t* recv_counts,
-                                  int world, long long n_recv, int H, uint16_t* X, int32_t* eid, int32_t* status,
-                                  cudaStream_t st);
+cudaError_t launch_ep_recv_index(const int32_t* tag, const int64_t* recv_counts, int world, long long n_recv,
+                                 int32_t* route_row, int32_t* eid, int32_t* status, cudaStream_t st);
 // Routes with expert id - id_base outside [0, E) are dropped (inv = -1); they set MIMO_ERANGE unless
 // skip_outside (expert parallelism: routes to other ranks' experts).
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* order,
@@ -239,7 +238,7 @@ cudaError_t launch_build_units(const int32_t* offsets, const int32_t* slot_of, i
                                int32_t* unit_cnt, int32_t* unit_first, int32_t* unit_nsub,
                                int32_t* num_units, const int32_t* order,
                                const float* weight, int P, int topk, int32_t* rtok, float* rw,
-                               int32_t* status, cudaStream_t st);
+                               int32_t* status, cudaStream_t st, const int32_t* route_row = nullptr);
 cudaError_t launch_to_f16(const uint16_t* x, __half* y, size_t n, int32_t* status, cudaStream_t st);
 // kind: 0 decode gate/up, 1 decode down, 2 prefill gate/up, 3 prefill down
 cudaError_t launch_expert_tiles(const ExpertParams& p, int kind, int num_sms, cudaStream_t st);

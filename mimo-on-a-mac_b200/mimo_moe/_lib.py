@@ -40,8 +40,10 @@ SIGNATURES = {
                                    c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "mimo_moe_gather_rows": (c_int32, [c_void_p, c_int64, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
                                        c_void_p]),
-    "mimo_moe_ep_recv_gather": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_void_p,
-                                          c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_ep_recv_index": (c_int32, [c_void_p, c_void_p, c_int32, c_int64, c_void_p, c_void_p, c_void_p,
+                                         c_void_p]),
+    "mimo_moe_prefill_routes": (c_int32, [c_void_p, c_int32, POINTER(Pools), c_void_p, c_int32, c_void_p,
+                                          c_void_p, c_int32, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "mimo_moe_experts_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32, c_int32]),
     "mimo_moe_experts": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_int32, c_int32, c_void_p, c_int32, c_int32, c_int32,

@@ -266,11 +266,11 @@ class PeerExpertParallelMoE:
         self.local = {}
 
 
-PairsFn = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+PairsFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 CombinePairsFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, int, int], torch.Tensor]
 PlanFn = Callable[[torch.Tensor, int, int], "ops.EpPlan"]
 GatherFn = Callable[[torch.Tensor, torch.Tensor, int], torch.Tensor]
-RecvFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
+RecvFn = Callable[[torch.Tensor, torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
 
 
 class ExpertParallelPrefill:
@@ -283,9 +283,9 @@ class ExpertParallelPrefill:
          per route; the counts of routes and rows per destination are exchanged first and cross to the
          host once per step (all-to-all split sizes), then one all-to-all of the rows (gathered by
          mimo_moe_gather_rows) and one of the tags;
-      3. expert side: the received routes' rows gathered from the received token rows
-         (mimo_moe_ep_recv_gather), per-route bf16 products (`moe_prefill` with one route per row and
-         weight 1, which returns each route's bf16 pair output unchanged, model.py:221-228);
+      3. expert side: each received route's row among the received token rows (mimo_moe_ep_recv_index),
+         then per-route bf16 products straight from those rows (mimo_moe_prefill_routes: each route's
+         bf16 pair output, model.py:221-228, the bits the one-GPU prefill combines);
       4. return: the inverse all-to-all;
       5. combine: y[t] = bf16(sum over k in order of fp32(out[t, k]) * w[t, k]) (model.py:266-271).
 
@@ -307,12 +307,12 @@ class ExpertParallelPrefill:
         self.pools = pools_local
         self.router_w, self.bias = router_w, bias
         self.router_fn = router_fn or (lambda x: ops.router(x, self.router_w, self.bias, topk=self.topk))
-        self.pairs_fn = pairs_fn or (lambda X, e: ops.moe_prefill(
-            X, self.pools, e[:, None], torch.ones(e.shape[0], 1, device=X.device), E=self.per_rank))
+        self.pairs_fn = pairs_fn or (lambda rows, rr, e: ops.moe_prefill_routes(rows, self.pools, rr, e,
+                                                                                E=self.per_rank))
         self.combine_fn = combine_fn or (lambda yp, inv, w, T, k: ops.combine_pairs(yp, inv, w, T, k))
         self.plan_fn = plan_fn or (lambda idx, per_rank, world: ops.ep_plan(idx, per_rank, world))
         self.gather_fn = gather_fn or (lambda x, rows, n: ops.gather_rows(x, rows, n))
-        self.recv_fn = recv_fn or (lambda rows, tag, counts: ops.ep_recv_gather(rows, tag, counts))
+        self.recv_fn = recv_fn or (lambda tag, counts: ops.ep_recv_index(tag, counts))
         self.routes_received = 0  # routes this rank's experts computed, summed over calls
         self.trace: Optional[PhaseTrace] = None
 
@@ -352,10 +352,8 @@ class ExpertParallelPrefill:
         if tr:
             tr.mark("dispatch_rows")
         if recv_tag.shape[0]:
-            X, eid = self.recv_fn(recv_rows, recv_tag, recv_counts)
-            if tr:
-                tr.mark("recv_gather")
-            out = self.pairs_fn(X, eid)
+            route_row, eid = self.recv_fn(recv_tag, recv_counts)
+            out = self.pairs_fn(recv_rows, route_row, eid)
         else:
             out = torch.empty(0, H, dtype=x.dtype, device=dev)
         if tr:

@@ -433,24 +433,47 @@ def gather_rows(x: torch.Tensor, rows: torch.Tensor, n: int, status: Optional[to
     return out
 
 
-def ep_recv_gather(recv_rows: torch.Tensor, recv_tag: torch.Tensor, recv_counts: torch.Tensor,
-                   status: Optional[torch.Tensor] = None):
-    """Receiving rank: (X [n, H] bf16, eid [n] int32), X[i] = the received row route i names (its tag's
-    row within the rows from its sender, recv_counts [world, 2] = the senders' counts rows)."""
+def ep_recv_index(recv_tag: torch.Tensor, recv_counts: torch.Tensor, status: Optional[torch.Tensor] = None):
+    """Receiving rank: (route_row [n] int32, eid [n] int32), route_row[i] = the index among the received
+    rows of the row route i names (its tag's row within the rows from its sender; recv_counts [world, 2]
+    = the senders' counts rows), eid[i] = its local expert id."""
     _need_cuda(recv_tag, "recv_tag")
     dev = recv_tag.device
     n = recv_tag.shape[0]
-    H = recv_rows.shape[1]
-    recv_rows = recv_rows.to(torch.bfloat16).contiguous()
     recv_tag = recv_tag.to(torch.int32).contiguous()
     recv_counts = recv_counts.to(device=dev, dtype=torch.int64).contiguous()
-    X = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+    route_row = torch.empty(n, dtype=torch.int32, device=dev)
     eid = torch.empty(n, dtype=torch.int32, device=dev)
     st = status if status is not None else _status(dev)
-    check(lib().mimo_moe_ep_recv_gather(recv_rows.data_ptr(), recv_tag.data_ptr(), recv_counts.data_ptr(),
-                                        recv_counts.shape[0], n, H, X.data_ptr(), eid.data_ptr(), st.data_ptr(),
-                                        _stream()), "ep_recv_gather")
-    return X, eid
+    check(lib().mimo_moe_ep_recv_index(recv_tag.data_ptr(), recv_counts.data_ptr(), recv_counts.shape[0], n,
+                                       route_row.data_ptr(), eid.data_ptr(), st.data_ptr(), _stream()),
+          "ep_recv_index")
+    return route_row, eid
+
+
+def moe_prefill_routes(x: torch.Tensor, pools, route_row: torch.Tensor, eid: torch.Tensor,
+                       slot_of: Optional[torch.Tensor] = None, E: Optional[int] = None,
+                       status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-route prefill products: y[p] = bf16 pair output of expert eid[p] on row route_row[p] of x
+    (model.py:221-228), [P, H] bf16."""
+    _need_cuda(x, "x")
+    if not isinstance(pools, ExpertPools):
+        pools = ExpertPools(pools)
+    x = x.to(torch.bfloat16).contiguous()
+    dev = x.device
+    route_row = route_row.to(device=dev, dtype=torch.int32).contiguous()
+    eid = eid.to(device=dev, dtype=torch.int32).contiguous()
+    P = eid.shape[0]
+    so = None if slot_of is None else slot_of.to(device=dev, dtype=torch.int32).contiguous()
+    if E is None:
+        E = pools.S if so is None else so.numel()
+    y = torch.empty(P, pools.hidden, dtype=torch.bfloat16, device=dev)
+    ws = workspace(lib().mimo_moe_prefill_workspace_bytes(P, 1, pools.hidden, pools.inter, E), dev)
+    st = _status(dev) if status is None else status
+    check(lib().mimo_moe_prefill_routes(x.data_ptr(), x.shape[0], pools.struct, _ptr(so), E, route_row.data_ptr(),
+                                        eid.data_ptr(), P, y.data_ptr(), ws.data_ptr(), ws.numel(), st.data_ptr(),
+                                        _stream()), "moe_prefill_routes")
+    return y
 
 
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, bias: Optional[torch.Tensor], pools,

@@ -36,8 +36,9 @@ def gather_rows(x: torch.Tensor, rows: torch.Tensor, n: int) -> torch.Tensor:
     return x[rows[:n].to(torch.int64)].contiguous()
 
 
-def recv_gather(recv_rows: torch.Tensor, recv_tag: torch.Tensor, recv_counts: torch.Tensor):
+def recv_index(recv_tag: torch.Tensor, recv_counts: torch.Tensor):
+    """(row of each received route among the received rows, its local expert id)."""
     rc, rrc = recv_counts[:, 0], recv_counts[:, 1]
     src = torch.repeat_interleave(torch.arange(rc.shape[0], device=rc.device), rc)
     rows = (torch.cumsum(rrc, 0) - rrc)[src] + recv_tag[:, 0].to(torch.int64)
-    return recv_rows[rows].contiguous(), recv_tag[:, 1].contiguous()
+    return rows.to(torch.int32), recv_tag[:, 1].contiguous()

@@ -100,9 +100,9 @@ def _pairs(lo: int):
     all-to-all prefill computes them."""
     mats = _expert_mats()
 
-    def fn(X, e):
-        return torch.stack([torch.tanh(X[r].float() @ mats[lo + int(e[r])]).to(torch.bfloat16)
-                            for r in range(X.shape[0])]) if X.shape[0] else torch.empty(0, H, dtype=torch.bfloat16)
+    def fn(rows, rr, e):
+        return torch.stack([torch.tanh(rows[int(rr[r])].float() @ mats[lo + int(e[r])]).to(torch.bfloat16)
+                            for r in range(e.shape[0])]) if e.shape[0] else torch.empty(0, H, dtype=torch.bfloat16)
     return fn
 
 
@@ -133,7 +133,7 @@ def _prefill_worker(rank, world, port, out, clustered=False):
         blk = ExpertParallelPrefill(None, None, None, num_experts=E, topk=K,
                                     router_fn=_clustered_router if clustered else _router,
                                     pairs_fn=_pairs(lo), combine_fn=_combine_pairs, plan_fn=ep_ref.plan,
-                                    gather_fn=ep_ref.gather_rows, recv_fn=ep_ref.recv_gather)
+                                    gather_fn=ep_ref.gather_rows, recv_fn=ep_ref.recv_index)
         # rank 1 routes no tokens in the second call: empty splits both ways
         for n in (T, T if rank == 0 else 0):
             y = blk(_tokens(rank)[:n])

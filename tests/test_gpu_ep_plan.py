@@ -1,7 +1,7 @@
-"""Expert-parallel prefill plan and row gathers on the device (mimo_moe_ep_plan, mimo_moe_gather_rows,
-mimo_moe_ep_recv_gather) against their torch restatement (tests/ep_ref.py), bit for bit, and an
-exchange between simulated ranks on one GPU: every received route must see its own token's row and
-its local expert id."""
+"""Expert-parallel prefill plan, row gather and receive index on the device (mimo_moe_ep_plan,
+mimo_moe_gather_rows, mimo_moe_ep_recv_index) against their torch restatement (tests/ep_ref.py), bit
+for bit; an exchange between simulated ranks on one GPU (every received route must see its own
+token's row and its local expert id); and mimo_moe_prefill_routes against mimo_moe_prefill."""
 import numpy as np
 import pytest
 import torch
@@ -76,11 +76,29 @@ def test_exchange_between_simulated_ranks(gpu, world):
             origin += [(s, int(q)) for q in p.order[p0:p0 + c[r][0]].tolist()]
         recv_rows, recv_tag = torch.cat(seg_rows), torch.cat(seg_tags)
         recv_counts = torch.tensor(counts, dtype=torch.int64, device=gpu)
-        X, eid = ops.ep_recv_gather(recv_rows, recv_tag, recv_counts)
-        Xr, eidr = ep_ref.recv_gather(recv_rows, recv_tag, recv_counts)
-        assert torch.equal(X, Xr) and torch.equal(eid, eidr)
+        rr, eid = ops.ep_recv_index(recv_tag, recv_counts)
+        rr_ref, eid_ref = ep_ref.recv_index(recv_tag, recv_counts)
+        assert torch.equal(rr, rr_ref) and torch.equal(eid, eid_ref)
+        got = recv_rows[rr.long()]
         want = torch.stack([xs[s][q // K] for s, q in origin])
-        assert torch.equal(X, want)
+        assert torch.equal(got, want)
         want_e = torch.tensor([int(idxs[s].view(-1)[q]) - r * per for s, q in origin], dtype=torch.int32,
                               device=gpu)
         assert torch.equal(eid, want_e)
+
+
+def test_prefill_routes_equal_the_pair_outputs(gpu):
+    """mimo_moe_prefill_routes on rows named per route gives each route's bf16 pair output: the same
+    bits as mimo_moe_prefill with one route per (gathered) row and weight 1."""
+    import mimo_moe
+    import mimo_moe.ops as ops
+    S = 32
+    pool = mimo_moe.ExpertPools.synthetic(S, seed=5, layer=1, device=gpu)
+    g = np.random.default_rng(9)
+    rows = torch.randn(300, H, device=gpu).to(torch.bfloat16)
+    P = 1000
+    rr = torch.from_numpy(g.integers(0, 300, P).astype(np.int32)).to(gpu)
+    e = torch.from_numpy(g.integers(0, S, P).astype(np.int32)).to(gpu)
+    y = ops.moe_prefill_routes(rows, pool, rr, e)
+    ref = ops.moe_prefill(rows[rr.long()], pool, e[:, None], torch.ones(P, 1, device=gpu))
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
