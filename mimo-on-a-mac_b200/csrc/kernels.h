@@ -90,7 +90,8 @@ struct TcParams {
   CUtensorMap bmap;      // activation terms [units * 2 * ntok][K] e4m3: box [128 B, 2 * ntok rows]
                          // (gate/up), or the 3-D view [chunk][row][128 B] with 2 chunks per box (down)
   CUtensorMap bsmap;     // their ue8m0 scales [units * 2 * ntok][K / 32], box [16 B, 2 * ntok rows]
-  int S, Nw, K, tiles;   // Nw: weight rows (output features) per expert; tiles = Nw / 128
+  int S, Nw, K, tiles;   // Nw: weight rows (output features) per expert; tiles = Nw / 128 (Nw / 256 when an
+                         // item takes two row tiles, decode down kind 1)
   const int32_t* unit_slot;
   const int32_t* unit_cnt;
   const int32_t* unit_p0;     // null: p0 = unit * p0_stride

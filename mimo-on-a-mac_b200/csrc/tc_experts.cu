@@ -228,6 +228,11 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
   static_assert(EPI % 4 == 0 && NTOK % (EPI / 4) == 0 && QH % QC == 0, "epilogue split");
   static_assert(NM * KPS == 2, "two slots per stage");
   static_assert(N % 16 == 0 && N <= 256 && QH % QC == 0, "MMA N");
+  static_assert(MODE != 3 || NM == 2, "paired row tiles take the two slots");
+  // MODE 3 (decode down, paired row tiles): an item is 256 output rows, slot m holding rows
+  // [128 m, 128 m + 128) of it with one K chunk per stage; the two accumulators are separate rows.
+  constexpr int TROWS = MODE == 3 ? 2 * kM : kM;  // weight rows per item
+  constexpr int MROW = MODE == 3 ? kM : 0;        // row offset of slot 1's tile (gate/up: same rows)
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NSTAGE] tiles landed + scale blocks written
   uint64_t* empty = full + NSTAGE;                     // [NSTAGE] both issuers' MMAs of the stage done
@@ -309,7 +314,7 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
           set_status(p.status, MIMO_ERANGE);
           slot = 0;
         }
-        const int row0 = slot * p.Nw + tile * kM;
+        const int row0 = slot * p.Nw + tile * TROWS;
         const int brow = p.btok ? 0 : unit * N;
         for (int ks = 0; ks < ns; ++ks) {
           if (*s_abort) {
@@ -327,7 +332,8 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
             }
             uint8_t* sc = scbox + e * SCB;
             mbar_arrive_expect_tx(&sc_full[e], NM * kM * 16 + N * 16);
-            for (int m = 0; m < NM; ++m) tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0, &sc_full[e], pol_b);
+            for (int m = 0; m < NM; ++m)
+              tma_load_2d(sc + m * kM * 16, &p.smap[m], kc * 4, row0 + m * MROW, &sc_full[e], pol_b);
             tma_load_2d(sc + NM * kM * 16, &p.bsmap, kc * 4, brow, &sc_full[e], pol_b);
             ++groups;
           }
@@ -341,7 +347,7 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
           mbar_arrive_expect_tx(&full[stage], 2 * kAGlobal + KPS * N * kKC);
           if constexpr (KPS == 1) {
             tma_load_2d(sb, &p.amap[0], kc * kKC, row0, &full[stage], pol_a);
-            tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0, &full[stage], pol_a);
+            tma_load_2d(sb + kATile, &p.amap[1], kc * kKC, row0 + MROW, &full[stage], pol_a);
             tma_load_2d(sb + 2 * kATile, &p.bmap, kc * kKC, brow, &full[stage], pol_b);
           } else {  // 3-D boxes [2 chunks][rows][128 B]: both chunks' tiles in one copy each
             tma_load_3d(sb, &p.amap[0], 0, row0, kc, &full[stage], pol_a);
@@ -497,7 +503,7 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
       }
       tc_fence_after();
       const bool live = !aborted && slot >= 0 && slot < p.S;
-      const int row = tile * kM + quad * 32 + lane;  // output feature of this lane
+      const int row = tile * TROWS + quad * 32 + lane;  // output feature of this lane (slot 0's row)
       if (MODE == 0 && live && p.btok) {
         // Columns are tokens: route q reads its token's hi/lo columns.
 #pragma unroll 1
@@ -547,6 +553,18 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
           if (lane == 0) {
             p.hs[rh * (p.Nw / 32) + row / 32] = (uint8_t)b1;
             p.hs[rl * (p.Nw / 32) + row / 32] = (uint8_t)b2;
+          }
+        } else if constexpr (MODE == 3) {
+          if (q < cnt) {  // two rows: slot 0's and slot 1's, each hi + lo
+            const int orow = p.out_row ? __ldg(p.out_row + p0 + q) : p0 + q;
+            const float w = __ldg(p.rw + p0 + q);
+            const float d0 = h0 + l0, d1 = h1 + l1;
+            const float v0 = (p.pairs_rounding ? bf16_round(d0) : d0) * w;
+            const float v1 = (p.pairs_rounding ? bf16_round(d1) : d1) * w;
+            float* dst = p.peer_part ? p.peer_part[orow / p.peer_rows] + (size_t)(orow % p.peer_rows) * p.Nw
+                                     : p.part + (size_t)orow * p.Nw;
+            dst[row] = v0;
+            dst[row + kM] = v1;
           }
         } else {
           if (q < cnt) {
@@ -2253,7 +2271,8 @@ static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   static_assert(smem <= 232448, "shared memory budget");
   static_assert(tmem_cols_needed<2 * NTOK, NSTAGE>() <= 512, "TMEM budget");
   static_assert((2 * NSTAGE + 4 + 4 + 1) * 8 + 8 <= kBarBytes, "barrier area");
-  if (p.K % (4 * kKC) != 0 || p.Nw % kM != 0 || p.tiles != p.Nw / kM) return cudaErrorInvalidValue;
+  constexpr int trows = MODE == 3 ? 2 * kM : kM;
+  if (p.K % (4 * kKC) != 0 || p.Nw % trows != 0 || p.tiles != p.Nw / trows) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   return launch_k(kfn, dim3(grid), dim3((4 + EPI) * 32), smem, st, p);
@@ -2526,6 +2545,7 @@ cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStre
   switch (kind) {
     case 0: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 0, 8>(p, num_sms, st);
     case 1: return tc::launch<1, kTcDecodeRoutes, tc::kStages[1], 1, 8>(p, num_sms, st);
+    case 5: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 3, 8>(p, num_sms, st);  // down, paired rows
     case 2: return tc::launch<2, kTcPrefillRoutes, tc::kStages[2], 0, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     case 3: return tc::launch<1, kTcPrefillRoutes, tc::kStages[3], 2, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     default: return cudaErrorInvalidValue;

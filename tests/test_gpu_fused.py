@@ -1,15 +1,19 @@
 """Decode expert kernels (MIMO_MOE_DECODE_KERNEL, read once per process, so each variant runs in a
 child process):
 
-  e4m3        (default) two launches over whole tiles, kind::mxf8f6f4, two e4m3 activation terms;
+  e4m3        (default) two launches over whole tiles, kind::mxf8f6f4, two e4m3 activation terms; its
+              down pass takes two 128-row tiles per item (MIMO_MOE_DECODE_DOWN=tiles: one tile, the
+              two K halves in the two accumulators, the form the one-launch kernels share);
   sk          one stream-K launch: equal K-group ranges per CTA, group partials added in a fixed
               order, kind::mxf8f6f4 with two e4m3 activation terms;
   fp4         one launch, kind::mxf4, packed weights, five e2m1 activation terms;
   e4m3-fused  the e4m3 arithmetic in one launch (down tiles wait on per-unit counters).
 
 The combine runs as its own launch by default; MIMO_MOE_DECODE_COMBINE=down runs it in the down
-kernel's epilogue, and the two must agree bit for bit.  e4m3-fused must equal
-e4m3 bit for bit; sk adds each 512-value K group's partial separately, so it
+kernel's epilogue (with the one-tile down items), and the two must agree bit for bit.  e4m3-fused
+must equal e4m3 with one-tile down items bit for bit; the paired down items sum each row's K chunks
+in one accumulator instead of two halves, so they agree with it within rel_err 1e-2 and on nearly
+all bf16 outputs; sk adds each 512-value K group's partial separately, so it
 agrees with e4m3 within rel_err 1e-2 and on nearly all bf16 outputs; fp4 differs from them only by the activation terms' residual
 (about 1e-6 of a dot product) and the sum of five accumulator columns instead of two, so its block
 output stays within rel_err 1e-2 of the e4m3 path's (the oracle bar, engine/tests/test_kernels.py:54-56)
@@ -47,9 +51,10 @@ np.savez({path!r}, *out)
 TS = [1, 2, 3, 8]
 
 
-def _run(tmp_path, S, kernel, combine="separate"):
-    path = str(tmp_path / f"{kernel}_{combine}_{S}.npz")
-    env = dict(os.environ, MIMO_MOE_DECODE_KERNEL=kernel, MIMO_MOE_DECODE_COMBINE=combine)
+def _run(tmp_path, S, kernel, combine="separate", down="pairs"):
+    path = str(tmp_path / f"{kernel}_{combine}_{down}_{S}.npz")
+    env = dict(os.environ, MIMO_MOE_DECODE_KERNEL=kernel, MIMO_MOE_DECODE_COMBINE=combine,
+               MIMO_MOE_DECODE_DOWN=down)
     code = CHILD.format(root=str(ROOT), pkg=str(PKG_DIR), S=S, Ts=TS, path=path)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
@@ -75,10 +80,17 @@ def _rel(a_bits, ref):
 
 @pytest.mark.parametrize("S", [32, 256])
 def test_decode_kernels_agree(gpu, tmp_path, S):
-    e4 = _run(tmp_path, S, "e4m3")
-    e4s = _run(tmp_path, S, "e4m3", combine="down")
+    e4p = _run(tmp_path, S, "e4m3")                   # default: paired down items
+    e4 = _run(tmp_path, S, "e4m3", down="tiles")
+    e4s = _run(tmp_path, S, "e4m3", combine="down", down="tiles")
     for (a, ia, wa), (b, ib, wb) in zip(e4, e4s):   # combine in the down kernel == its own launch
         assert np.array_equal(ia, ib) and np.array_equal(a, b)
+    for T, (a, ia, wa), (b, ib, wb), ref in zip(TS, e4, e4p, _oracle(gpu, S, e4)):
+        assert np.array_equal(ia, ib)
+        assert (a == b).mean() >= 0.95, (T, (a == b).mean())
+        rel = _rel(b, ref)
+        print(f"S={S} T={T} e4m3 paired down: rel_err vs oracle {rel:.2e}")
+        assert rel <= 1e-2, (T, rel)
     e4f = _run(tmp_path, S, "e4m3-fused")
     fp4 = _run(tmp_path, S, "fp4")
     sk = _run(tmp_path, S, "sk")
