@@ -292,15 +292,18 @@ bool prefill_pair() {
 }
 
 
-// Decode down kernel items (MIMO_MOE_DECODE_DOWN, a comparison knob): "pairs" (default) takes two
-// 128-row tiles per item with one K chunk per stage (slot m = row tile m, the gate/up kernel's shape);
-// "tiles" one 128-row tile per item with two K chunks per stage (the two slots hold the K halves, added
-// in the epilogue).  The two differ only in float32 summation order (within 1e-2 of each other).
-// Measured on B200 (graph-replayed steps): B = 8 161.2 against 163.2 us, B = 1 45.0 against 45.9; the
-// forced-overlap B = 8 case (~22 units, half as many items to deal) 85.4 against 84.6.
+// Down kernel items, decode and prefill alike (MIMO_MOE_DOWN, a comparison knob): "pairs" (default)
+// takes two 128-row tiles per item with one K chunk per stage (slot m = row tile m, the gate/up
+// kernel's shape); "tiles" one 128-row tile per item with two K chunks per stage (the two slots hold
+// the K halves, added in the epilogue).  The two differ in float32 summation order (within 1e-2 of
+// each other); decode and prefill must use the same form, because expert-parallel and single-GPU
+// paths compute a route's product through either.  Measured on B200 (graph-replayed decode steps):
+// B = 8 161.2 against 163.2 us, B = 1 45.0 against 45.9; the forced-overlap B = 8 case (~22 units,
+// half as many items to deal) 85.4 against 84.6.  Prefill: the paired form runs four 48 KiB stages
+// where the one-tile form runs three of 64 KiB.
 bool down_pairs() {
   static const bool on = [] {
-    const char* e = getenv("MIMO_MOE_DECODE_DOWN");
+    const char* e = getenv("MIMO_MOE_DOWN");
     return !(e && std::string(e) == "tiles");
   }();
   return on;
@@ -448,13 +451,14 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
     MIMO_TRY(profiled(4, st, [&] { return launch_tc_decode_fused(f, fp4, sms, st); }));
     return MIMO_OK;
   }
-  if (decode && down_pairs()) {  // two row tiles per item, one K chunk per stage (2-D boxes)
+  if (!pair && down_pairs()) {
+    // two row tiles per item, one K chunk per stage (2-D boxes)
     TcParams r = q;
     MIMO_TRY(fp4_weight_map(&r.amap[0], pools->down_w, (uint64_t)S * H, I));
     r.amap[1] = r.amap[0];
     MIMO_TRY(rows_map(&r.bmap, t.hq, (uint64_t)ucap * N, I, N));
     r.tiles = H / 256;
-    MIMO_TRY(profiled(1, st, [&] { return launch_tc_experts(r, 5, sms, st); }));
+    MIMO_TRY(profiled(decode ? 1 : 3, st, [&] { return launch_tc_experts(r, decode ? 5 : 6, sms, st); }));
     return MIMO_OK;
   }
   if (decode && comb && part && !peer_part && by_token_rows && combine_in_down()) {

@@ -228,11 +228,12 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
   static_assert(EPI % 4 == 0 && NTOK % (EPI / 4) == 0 && QH % QC == 0, "epilogue split");
   static_assert(NM * KPS == 2, "two slots per stage");
   static_assert(N % 16 == 0 && N <= 256 && QH % QC == 0, "MMA N");
-  static_assert(MODE != 3 || NM == 2, "paired row tiles take the two slots");
-  // MODE 3 (decode down, paired row tiles): an item is 256 output rows, slot m holding rows
-  // [128 m, 128 m + 128) of it with one K chunk per stage; the two accumulators are separate rows.
-  constexpr int TROWS = MODE == 3 ? 2 * kM : kM;  // weight rows per item
-  constexpr int MROW = MODE == 3 ? kM : 0;        // row offset of slot 1's tile (gate/up: same rows)
+  // MODE 3 / 4 (decode / prefill down, paired row tiles): an item is 256 output rows, slot m holding
+  // rows [128 m, 128 m + 128) of it with one K chunk per stage; the two accumulators are separate rows.
+  constexpr bool PAIRED = MODE == 3 || MODE == 4;
+  static_assert(!PAIRED || NM == 2, "paired row tiles take the two slots");
+  constexpr int TROWS = PAIRED ? 2 * kM : kM;  // weight rows per item
+  constexpr int MROW = PAIRED ? kM : 0;        // row offset of slot 1's tile (gate/up: same rows)
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NSTAGE] tiles landed + scale blocks written
   uint64_t* empty = full + NSTAGE;                     // [NSTAGE] both issuers' MMAs of the stage done
@@ -565,6 +566,12 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
                                      : p.part + (size_t)orow * p.Nw;
             dst[row] = v0;
             dst[row + kM] = v1;
+          }
+        } else if constexpr (MODE == 4) {
+          if (q < cnt) {  // bf16 pair outputs of the two rows (model.py:221-228)
+            uint16_t* dst = p.ypair + (size_t)(p0 + q) * p.Nw;
+            dst[row] = (uint16_t)f32_to_bf16(h0 + l0);
+            dst[row + kM] = (uint16_t)f32_to_bf16(h1 + l1);
           }
         } else {
           if (q < cnt) {
@@ -2271,7 +2278,7 @@ static cudaError_t launch(const TcParams& p, int grid, cudaStream_t st) {
   static_assert(smem <= 232448, "shared memory budget");
   static_assert(tmem_cols_needed<2 * NTOK, NSTAGE>() <= 512, "TMEM budget");
   static_assert((2 * NSTAGE + 4 + 4 + 1) * 8 + 8 <= kBarBytes, "barrier area");
-  constexpr int trows = MODE == 3 ? 2 * kM : kM;
+  constexpr int trows = (MODE == 3 || MODE == 4) ? 2 * kM : kM;
   if (p.K % (4 * kKC) != 0 || p.Nw % trows != 0 || p.tiles != p.Nw / trows) return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
@@ -2546,6 +2553,8 @@ cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStre
     case 0: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 0, 8>(p, num_sms, st);
     case 1: return tc::launch<1, kTcDecodeRoutes, tc::kStages[1], 1, 8>(p, num_sms, st);
     case 5: return tc::launch<2, kTcDecodeRoutes, tc::kStages[0], 3, 8>(p, num_sms, st);  // down, paired rows
+    case 6:  // prefill down, paired rows
+      return tc::launch<2, kTcPrefillRoutes, tc::kStages[2], 4, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     case 2: return tc::launch<2, kTcPrefillRoutes, tc::kStages[2], 0, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     case 3: return tc::launch<1, kTcPrefillRoutes, tc::kStages[3], 2, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     default: return cudaErrorInvalidValue;

@@ -2,7 +2,7 @@
 child process):
 
   e4m3        (default) two launches over whole tiles, kind::mxf8f6f4, two e4m3 activation terms; its
-              down pass takes two 128-row tiles per item (MIMO_MOE_DECODE_DOWN=tiles: one tile, the
+              down pass takes two 128-row tiles per item (MIMO_MOE_DOWN=tiles: one tile, the
               two K halves in the two accumulators, the form the one-launch kernels share);
   sk          one stream-K launch: equal K-group ranges per CTA, group partials added in a fixed
               order, kind::mxf8f6f4 with two e4m3 activation terms;
@@ -54,7 +54,7 @@ TS = [1, 2, 3, 8]
 def _run(tmp_path, S, kernel, combine="separate", down="pairs"):
     path = str(tmp_path / f"{kernel}_{combine}_{down}_{S}.npz")
     env = dict(os.environ, MIMO_MOE_DECODE_KERNEL=kernel, MIMO_MOE_DECODE_COMBINE=combine,
-               MIMO_MOE_DECODE_DOWN=down)
+               MIMO_MOE_DOWN=down)
     code = CHILD.format(root=str(ROOT), pkg=str(PKG_DIR), S=S, Ts=TS, path=path)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
