@@ -309,6 +309,17 @@ bool down_pairs() {
   return on;
 }
 
+// Decode down launch waiting per unit for the gate/up launch's h instead of for the whole gate/up grid
+// (MIMO_MOE_EARLY_DOWN=0 turns it off, a comparison knob; the outputs are the same either way): down
+// items of units whose gate/up tiles are done run on the SMs the gate/up launch has already left.
+bool early_down() {
+  static const bool on = [] {
+    const char* e = getenv("MIMO_MOE_EARLY_DOWN");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
 // Decode combine placement (MIMO_MOE_DECODE_COMBINE, a comparison knob; bit-identical outputs):
 //   separate (default)  its own launch, M x H/1024 CTAs;
 //   down                in the down kernel's epilogue, by the CTA completing each output row tile.  One
@@ -391,6 +402,14 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   p.status = status;
   const bool sk = decode && decode_kernel() == kDecodeSk;
   const bool fused = decode && (decode_kernel() == kDecodeE4m3Fused || decode_kernel() == kDecodeFp4);
+  // decode, two launches: the down launch waits per unit for the gate/up epilogue's h (ready counters,
+  // zeroed per call: by the route kernel when it made the terms, else here)
+  const bool early = decode && !fused && !sk && down_pairs() && early_down();
+  if (early) {
+    if (!ready_zeroed) MIMO_TRY(cudaMemsetAsync(t.ready, 0, (size_t)ucap * sizeof(int32_t), st));
+    p.ready = t.ready;
+    p.ready_need = p.tiles * kTcDecodeEpiWarps;
+  }
   if (pair) MIMO_TRY(profiled(2, st, [&] { return launch_tc_pair(p, 2, sms, st); }));
   else if (!fused && !sk)
     MIMO_TRY(profiled(decode ? 0 : 2, st, [&] { return launch_tc_experts(p, decode ? 0 : 2, sms, st); }));
@@ -453,7 +472,7 @@ int run_tc(const uint16_t* x, const mimo_moe_pools* pools, int routes, const int
   }
   if (!pair && down_pairs()) {
     // two row tiles per item, one K chunk per stage (2-D boxes)
-    TcParams r = q;
+    TcParams r = q;  // (q inherits ready / ready_need from p: set for the early decode down launch)
     MIMO_TRY(fp4_weight_map(&r.amap[0], pools->down_w, (uint64_t)S * H, I));
     r.amap[1] = r.amap[0];
     MIMO_TRY(rows_map(&r.bmap, t.hq, (uint64_t)ucap * N, I, N));

@@ -114,6 +114,12 @@ struct TcParams {
   int peer_rows;
   int pairs_rounding;
   int32_t* status;
+  // Decode, per-unit readiness instead of the grid dependency wait: the gate/up launch (kind 0) adds 1 to
+  // ready[unit] per epilogue warp and item after its h stores; the paired-tile down launch (kind 1,
+  // MODE 3) skips the wait for the whole gate/up grid and loads a unit's h once ready[unit] reaches
+  // ready_need, so down items of finished units run on SMs the gate/up launch has already left.
+  int32_t* ready;
+  int ready_need;
   // Down, decode, fused combine (cy non-null, partials in `part`): the CTA storing the last unit's
   // partials of output rows [128 r, 128 r + 128) (cdone[r] counts them, zeroed per call) forms
   // cy[m] = bf16(sum over k in order of part[cgidx[m * ctopk + k]]) for those rows (cgidx null: the
@@ -199,6 +205,7 @@ cudaError_t launch_routes_prep(const int32_t* idx, const float* w, int route_ld,
 cudaError_t launch_tc_split_tokens(const uint16_t* x, int T, int K, uint8_t* bq, uint8_t* bs, int32_t* status,
                                    cudaStream_t st);
 constexpr int kTcDecodeRoutes = 8;   // routes per decode unit on the tcgen05 path
+constexpr int kTcDecodeEpiWarps = 8;  // epilogue warps of the decode tcgen05 kernels
 constexpr int kTcFp4Terms = 5;  // e2m1 activation terms of the kind::mxf4 decode path
 constexpr int kTcPrefillRoutes = 64; // routes per prefill unit on the tcgen05 path
 

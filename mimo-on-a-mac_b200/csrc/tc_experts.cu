@@ -171,6 +171,17 @@ __device__ __forceinline__ int unit_routes(const TcParams& p, int unit, int cap)
   return max(c, 0);
 }
 
+namespace fz {
+__device__ __forceinline__ int ld_acquire(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
+}
+}  // namespace fz
+
 // Decode combine (kernels.py:194-199) of output rows [128 tile, 128 tile + 128), run by the epilogue
 // warps (ew = 0 .. nw - 1) of the CTA whose tile stores complete the count p.cdone[tile] (one per unit
 // and tile).  Before counting, every thread's partial stores are fenced; the winner fences again and
@@ -273,11 +284,16 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_wait();  // the unit tables and activation terms come from the preceding kernel
+  // Early down (MODE 3 with ready counters): no wait for the whole gate/up grid.  The unit tables were
+  // written before the gate/up launch started its work (each launch of the chain waits for its
+  // predecessor before it lets its successor start), and a unit's h terms are waited for per unit by
+  // the producer below; nothing else this kernel reads comes from the gate/up launch.
+  const bool early = MODE == 3 && p.ready != nullptr;
+  if (!early) pdl_wait();  // the unit tables and activation terms come from the preceding kernel
   pdl_launch_dependents();
   const uint32_t tbase = *tmem_slot;
   // after the wait: the unit count is written by the preceding kernel
-  const int units = p.num_units ? min(__ldg(p.num_units), p.units_cap) : p.units_cap;
+  const int units = p.num_units ? min(__ldcg(p.num_units), p.units_cap) : p.units_cap;
   const long long items = (long long)units * p.tiles;
   // Items are dealt round-robin: at any time the CTAs work on consecutive items (the tiles and units
   // of the same experts), so a weight tile shared by an expert's units and a unit's activation tile
@@ -317,6 +333,22 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
         }
         const int row0 = slot * p.Nw + tile * TROWS;
         const int brow = p.btok ? 0 : unit * N;
+        if (early) {  // the unit's h must be complete: every gate/up epilogue warp of its tiles signalled
+          bool ok = fz::ld_acquire(p.ready + unit) >= p.ready_need;
+          if (!ok) {
+            const uint64_t t0 = global_timer_ns();
+            while (!(ok = fz::ld_acquire(p.ready + unit) >= p.ready_need)) {
+              if (*s_abort || global_timer_ns() - t0 > 2000000000ull) break;
+              __nanosleep(64);
+            }
+          }
+          if (!ok) {
+            set_status(p.status, MIMO_ETIMEOUT);
+            *s_abort = 1;
+            break;
+          }
+          fz::fence_proxy_async_global();  // h was written by generic stores; TMA reads it
+        }
         for (int ks = 0; ks < ns; ++ks) {
           if (*s_abort) {
             stop = true;
@@ -640,6 +672,14 @@ __global__ void __launch_bounds__((4 + EPI) * 32, 1) tc_expert_kernel(const __gr
       if constexpr (MODE == 1) {
         if (p.cy) combine_tile(p, tile, units, warp - 4, lane, EPI, s_abort + 1);
       }
+      if constexpr (MODE == 0) {
+        if (p.ready) {  // publish this warp's share of the unit's h (every item, so no wait is left open)
+          __threadfence();
+          fz::fence_proxy_async_global();
+          __syncwarp();
+          if (lane == 0) atomicAdd(p.ready + unit, 1);
+        }
+      }
     }
     if constexpr (MODE == 1) {  // no units: no tile completes, and the sum over no routes is 0
       if (p.cy && units == 0 && blockIdx.x == 0)
@@ -726,14 +766,6 @@ __device__ __forceinline__ Sched schedule(const TcParams& gu, const TcParams& dn
   return s;
 }
 
-__device__ __forceinline__ int ld_acquire(const int32_t* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;\n" ::: "memory");
-}
 }  // namespace fz
 
 template <int NSTAGE, bool FP4>

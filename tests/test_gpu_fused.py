@@ -9,7 +9,8 @@ child process):
   fp4         one launch, kind::mxf4, packed weights, five e2m1 activation terms;
   e4m3-fused  the e4m3 arithmetic in one launch (down tiles wait on per-unit counters).
 
-The combine runs as its own launch by default; MIMO_MOE_DECODE_COMBINE=down runs it in the down
+By default the down launch waits per unit for the gate/up launch's h (MIMO_MOE_EARLY_DOWN=0: for the
+whole gate/up grid); both give the same bits.  The combine runs as its own launch by default; MIMO_MOE_DECODE_COMBINE=down runs it in the down
 kernel's epilogue (with the one-tile down items), and the two must agree bit for bit.  e4m3-fused
 must equal e4m3 with one-tile down items bit for bit; the paired down items sum each row's K chunks
 in one accumulator instead of two halves, so they agree with it within rel_err 1e-2 and on nearly
@@ -51,10 +52,10 @@ np.savez({path!r}, *out)
 TS = [1, 2, 3, 8]
 
 
-def _run(tmp_path, S, kernel, combine="separate", down="pairs"):
-    path = str(tmp_path / f"{kernel}_{combine}_{down}_{S}.npz")
+def _run(tmp_path, S, kernel, combine="separate", down="pairs", early="1"):
+    path = str(tmp_path / f"{kernel}_{combine}_{down}_{early}_{S}.npz")
     env = dict(os.environ, MIMO_MOE_DECODE_KERNEL=kernel, MIMO_MOE_DECODE_COMBINE=combine,
-               MIMO_MOE_DOWN=down)
+               MIMO_MOE_DOWN=down, MIMO_MOE_EARLY_DOWN=early)
     code = CHILD.format(root=str(ROOT), pkg=str(PKG_DIR), S=S, Ts=TS, path=path)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
@@ -80,7 +81,10 @@ def _rel(a_bits, ref):
 
 @pytest.mark.parametrize("S", [32, 256])
 def test_decode_kernels_agree(gpu, tmp_path, S):
-    e4p = _run(tmp_path, S, "e4m3")                   # default: paired down items
+    e4p = _run(tmp_path, S, "e4m3")                   # default: paired down items, per-unit waits
+    e4w = _run(tmp_path, S, "e4m3", early="0")        # the down launch waits for the whole gate/up grid
+    for (a, ia, wa), (b, ib, wb) in zip(e4p, e4w):
+        assert np.array_equal(ia, ib) and np.array_equal(a, b)
     e4 = _run(tmp_path, S, "e4m3", down="tiles")
     e4s = _run(tmp_path, S, "e4m3", combine="down", down="tiles")
     for (a, ia, wa), (b, ib, wb) in zip(e4, e4s):   # combine in the down kernel == its own launch
