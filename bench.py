@@ -59,12 +59,13 @@ def peaks():
 
 def tensor_peaks(dev) -> dict:
     """Dense block-scaled tensor peaks of this GPU measured by the library's own probe
-    (mimo_moe_tensor_peak): kind::mxf8f6f4 with e2m1 x e4m3 operands (the expert kernels' MMA form)
-    and kind::mxf4 (e2m1 x e2m1, the FP4 rate); best of three 4000-step launches after one warm-up."""
+    (mimo_moe_tensor_peak, in the test and benchmark kit): kind::mxf8f6f4 with e2m1 x e4m3 operands (the
+    expert kernels' MMA form) and kind::mxf4 (e2m1 x e2m1, the FP4 rate); best of three 4000-step
+    launches after one warm-up."""
     import ctypes
     import torch
-    import mimo_moe
-    L = mimo_moe.lib()
+    from mimo_moe import _lib as mlib
+    L = mlib.testkit()
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
     out = {}

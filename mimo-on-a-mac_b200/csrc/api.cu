@@ -996,17 +996,6 @@ int mimo_moe_rmsnorm(const uint16_t* x, const uint16_t* weight, int32_t T, int32
   return MIMO_OK;
 }
 
-int mimo_moe_fill_synthetic_pool(uint32_t* gate_w, uint8_t* gate_s, uint32_t* up_w, uint8_t* up_s,
-                                 uint32_t* down_w, uint8_t* down_s, int32_t S, int32_t H, int32_t I,
-                                 uint64_t seed, int32_t layer, int32_t first_expert, void* stream) {
-  if (!gate_w || !gate_s || !up_w || !up_s || !down_w || !down_s || S < 1 || H < 256 || I < 256 ||
-      H % 256 || I % 256 || layer < 0 || first_expert < 0)
-    return MIMO_EINVAL;
-  MIMO_TRY(launch_fill_synthetic(gate_w, gate_s, up_w, up_s, down_w, down_s, S, H, I, seed, layer,
-                                 first_expert, static_cast<cudaStream_t>(stream)));
-  return MIMO_OK;
-}
-
 int mimo_moe_profile_enable(int32_t capacity) {
   if (capacity < 0) return MIMO_EINVAL;
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -1021,25 +1010,6 @@ int mimo_moe_profile_enable(int32_t capacity) {
   return MIMO_OK;
 }
 
-int mimo_moe_tensor_peak(int32_t kind, int32_t iters, float* tflops, int32_t* status, void* stream) {
-  if ((kind != 0 && kind != 1) || iters < 1 || iters > (1 << 24) || !tflops || !status) return MIMO_EINVAL;
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int sms = num_sms_current();
-  cudaEvent_t a = nullptr, b = nullptr;
-  MIMO_TRY(cudaEventCreate(&a));
-  cudaError_t e = cudaEventCreate(&b);
-  if (e == cudaSuccess) e = cudaEventRecord(a, st);
-  if (e == cudaSuccess) e = launch_tc_peak(kind, iters, sms, status, st);
-  if (e == cudaSuccess) e = cudaEventRecord(b, st);
-  if (e == cudaSuccess) e = cudaEventSynchronize(b);
-  float ms = 0.f;
-  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
-  cudaEventDestroy(a);
-  if (b) cudaEventDestroy(b);
-  if (e != cudaSuccess) return MIMO_ECUDA;
-  *tflops = ms > 0.f ? (float)(2.0 * 128 * 256 * 128 * (double)iters * sms / (ms * 1e-3) / 1e12) : 0.f;
-  return MIMO_OK;
-}
 
 int mimo_moe_profile_read(int32_t* launches, float* milliseconds) {
   if (!launches || !milliseconds) return MIMO_EINVAL;

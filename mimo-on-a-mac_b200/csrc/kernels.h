@@ -175,7 +175,6 @@ cudaError_t launch_tc_decode_sk(const TcSkParams& f, cudaStream_t st);
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st);
 // Dense block-scaled tensor peak probe: num_sms CTAs, each iters x (M 128, N 256, K 128) MMAs of
 // kind::mxf8f6f4 (e2m1 x e4m3, fp4 = 0) or kind::mxf4 (e2m1 x e2m1, fp4 = 1).
-cudaError_t launch_tc_peak(int fp4, int iters, int num_sms, int32_t* status, cudaStream_t st);
 // Prefill kinds 2 / 3 on SM pairs (clusters of two CTAs, tcgen05 cta_group::2): 256-row weight tiles
 // (tiles = Nw / 256) and term maps whose boxes hold half a unit's term rows (64).
 cudaError_t launch_tc_pair(const TcParams& p, int kind, int num_sms, cudaStream_t st);

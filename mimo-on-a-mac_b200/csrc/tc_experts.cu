@@ -113,21 +113,6 @@ constexpr uint32_t tmem_cols() {
   return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
 }
 
-// Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (5), B e4m3 (0), ue8m0 scales,
-// both K-major, M = 128, N = n, dense K = 32; the sf ids pick the byte (K block) of each 32-bit
-// TMEM scale cell and equal the top two bits of the scale addresses.
-__device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t kb) {
-  uint32_t d = 0;
-  d |= (kb & 3u) << 4;   // B scale id
-  d |= 5u << 7;          // A format E2M1
-  d |= 0u << 10;         // B format E4M3
-  d |= (uint32_t)(n >> 3) << 17;
-  d |= 1u << 23;         // scale format UE8M0
-  d |= (uint32_t)(kM >> 4) << 24;
-  d |= (kb & 3u) << 29;  // A scale id
-  return d;
-}
-
 // Splits v into hi/lo e4m3 bytes and their block scale bytes; the 32 lanes form one block.
 __device__ __forceinline__ void split_warp_block(float v, uint32_t& hi, uint32_t& lo, uint32_t& b1, uint32_t& b2) {
   // Non-negative floats order like their bit patterns: one redux.sync gives the block maximum.
@@ -2400,75 +2385,6 @@ __global__ void __launch_bounds__(128) split_rows_fp4_kernel(const uint16_t* __r
                       bs + r0 * nb + blk, (size_t)NTOK * nb, status);
 }
 
-// --------------------------------------------------------------------- dense tensor peak probe
-// The block-scaled tensor-core peak of this GPU for the MMA forms the expert kernels use, measured
-// rather than taken from a data sheet:
-//   fp4 = 0  tcgen05.mma.kind::mxf8f6f4.block_scale, A e2m1 (padded layout), B e4m3, K = 32 a step;
-//   fp4 = 1  tcgen05.mma.kind::mxf4.block_scale,      A and B e2m1 (packed),      K = 64 a step;
-// both M = 128, N = 256 (the largest single-SM tile, long enough per instruction that one issuing
-// thread keeps the pipe busy).  One CTA per SM; thread 0 issues `iters` x K = 128 worth of MMAs back
-// to back on operands that stay in shared memory (no memory traffic in the loop) into one TMEM
-// accumulator, then commits and waits (bounded).  FLOPs per launch = CTAs x iters x 2 x 128 x 256 x 128.
-constexpr int kPeakN = 256;
-// 52 KB used; 120 KB requested so that no SM holds two CTAs (each allocates all 512 TMEM columns).
-constexpr int kPeakSmem = 120 * 1024;
-static_assert(1024 + 1024 + 16384 + 32768 + 1024 <= kPeakSmem, "probe shared memory");
-__global__ void __launch_bounds__(128, 1) tc_peak_kernel(int iters, int fp4, int32_t* status) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* done = reinterpret_cast<uint64_t*>(smem);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 8);
-  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + 1024) + 1023) & ~(uintptr_t)1023);
-  uint8_t* A = base;                  // 128 x 128 e2m1: 16 KB padded / 8 KB packed
-  uint8_t* B = base + 16384;          // 256 x 128 e4m3 (32 KB) or e2m1 packed (16 KB)
-  uint8_t* SF = base + 16384 + 32768; // two 512-byte scale blocks
-  const int warp = threadIdx.x >> 5;
-  // Small finite operands: e2m1 1.0 in every nibble, e4m3 1.0, scales 2^0.
-  for (int i = threadIdx.x; i < 16384 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(A)[i] = 0x22222222u;
-  for (int i = threadIdx.x; i < 32768 / 4; i += blockDim.x)
-    reinterpret_cast<uint32_t*>(B)[i] = fp4 ? 0x22222222u : 0x38383838u;
-  for (int i = threadIdx.x; i < 1024 / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(SF)[i] = 0x7F7F7F7Fu;
-  fence_proxy_async_smem();
-  if (threadIdx.x == 0) {
-    mbar_init(done, 1);
-    mbar_fence_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tslot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tslot;
-  if (threadIdx.x == 0) {
-    const uint32_t sfa = tbase + kPeakN, sfb = tbase + kPeakN + 4;
-    tc_cp_sf(sfa, desc_sf(smem_u32(SF)));
-    tc_cp_sf(sfb, desc_sf(smem_u32(SF + 512)));
-    tc_cp_sf(sfb + 4, desc_sf(smem_u32(SF + 512)));  // scale rows 128..255 of B, if read from there
-    const uint32_t a = smem_u32(A), b = smem_u32(B);
-    for (int i = 0; i < iters; ++i) {
-      if (fp4) {
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk)
-          tc_mma_mxf4(tbase, desc_sw64(a + kk * 32), desc_sw64(b + kk * 32), idesc_mxf4(kM, kPeakN, 2 * kk),
-                      sfa | ((uint32_t)(2 * kk) << 30), sfb | ((uint32_t)(2 * kk) << 30), (i | kk) != 0);
-      } else {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc_mma_mx(tbase, desc_sw128(a + kk * 32), desc_sw128(b + kk * 32), idesc_mx(kPeakN, kk),
-                    sfa | ((uint32_t)kk << 30), sfb | ((uint32_t)kk << 30), (i | kk) != 0);
-      }
-    }
-    tc_commit(done);
-    if (!mbar_wait(done, 0)) set_status(status, MIMO_ETIMEOUT);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tbase, 512);
-  }
-}
 
 }  // namespace tc
 
@@ -2570,14 +2486,6 @@ cudaError_t launch_tc_pair(const TcParams& p, int kind, int num_sms, cudaStream_
     case 3: return tc::launch_pair<1, MIMO_TC_PST3, 2, MIMO_TC_EPI_PREFILL>(p, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
-}
-
-cudaError_t launch_tc_peak(int fp4, int iters, int num_sms, int32_t* status, cudaStream_t st) {
-  if (iters < 1 || num_sms < 1) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(tc::tc_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kPeakSmem);
-  if (e != cudaSuccess) return e;
-  tc::tc_peak_kernel<<<num_sms, 128, tc::kPeakSmem, st>>>(iters, fp4, status);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_tc_experts(const TcParams& p, int kind, int num_sms, cudaStream_t st) {

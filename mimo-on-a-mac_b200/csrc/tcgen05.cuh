@@ -375,5 +375,20 @@ __device__ __forceinline__ void split_block32_fp4(const uint16_t* src, uint8_t* 
   }
 }
 
+// Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (5), B e4m3 (0), ue8m0 scales,
+// both K-major, M = 128, N = n, dense K = 32; the sf ids pick the byte (K block) of each 32-bit
+// TMEM scale cell and equal the top two bits of the scale addresses.
+__device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t kb) {
+  uint32_t d = 0;
+  d |= (kb & 3u) << 4;   // B scale id
+  d |= 5u << 7;          // A format E2M1
+  d |= 0u << 10;         // B format E4M3
+  d |= (uint32_t)(n >> 3) << 17;
+  d |= 1u << 23;         // scale format UE8M0
+  d |= (uint32_t)(128 >> 4) << 24;  // M = 128
+  d |= (kb & 3u) << 29;  // A scale id
+  return d;
+}
+
 }  // namespace tc
 }  // namespace mimo

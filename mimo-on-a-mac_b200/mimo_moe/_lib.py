@@ -1,4 +1,5 @@
-"""ctypes binding of libmimo_moe.so (the C ABI in include/mimo_moe.h).
+"""ctypes bindings of libmimo_moe.so (the C ABI in include/mimo_moe.h) and of the test and benchmark
+kit beside it, libmimo_moe_testkit.so (include/mimo_moe_testkit.h: synthetic pools, tensor-peak probe).
 
 There is no CPU fallback: if the library is missing or cannot be loaded, every op raises."""
 from __future__ import annotations
@@ -9,6 +10,7 @@ from ctypes import POINTER, c_float, c_int32, c_int64, c_size_t, c_uint64, c_voi
 from pathlib import Path
 
 LIB_PATH = Path(os.environ.get("MIMO_MOE_LIBRARY") or Path(__file__).resolve().with_name("libmimo_moe.so"))
+TESTKIT_PATH = Path(__file__).resolve().with_name("libmimo_moe_testkit.so")
 
 MIMO_OK, MIMO_EINVAL, MIMO_ERANGE, MIMO_ETIMEOUT, MIMO_ECUDA, MIMO_EIO = 0, 1, 2, 3, 4, 5
 
@@ -79,6 +81,8 @@ SIGNATURES = {
                                           c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "mimo_moe_profile_enable": (c_int32, [c_int32]),
     "mimo_moe_profile_read": (c_int32, [c_void_p, c_void_p]),
+}
+TESTKIT_SIGNATURES = {
     "mimo_moe_tensor_peak": (c_int32, [c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "mimo_moe_fill_synthetic_pool": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                                c_void_p, c_int32, c_int32, c_int32, c_uint64, c_int32,
@@ -86,22 +90,36 @@ SIGNATURES = {
 }
 
 _lib = None
+_testkit = None
+
+
+def _load(path: Path, signatures: dict) -> ctypes.CDLL:
+    if not path.exists():
+        raise RuntimeError(f"mimo_moe: CUDA library not built ({path}); run "
+                           "`python mimo-on-a-mac_b200/mimo_moe/build.py` or __graft_entry__.build()")
+    L = ctypes.CDLL(str(path))
+    for name, (res, args) in signatures.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    return L
 
 
 def lib() -> ctypes.CDLL:
     """Load the CUDA library (raises RuntimeError when it is absent: there is no fallback)."""
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
-            raise RuntimeError(f"mimo_moe: CUDA library not built ({LIB_PATH}); run "
-                               "`python mimo-on-a-mac_b200/mimo_moe/build.py` or __graft_entry__.build()")
-        L = ctypes.CDLL(str(LIB_PATH))
-        for name, (res, args) in SIGNATURES.items():
-            fn = getattr(L, name)
-            fn.restype = res
-            fn.argtypes = args
-        _lib = L
+        _lib = _load(LIB_PATH, SIGNATURES)
     return _lib
+
+
+def testkit() -> ctypes.CDLL:
+    """Load the test and benchmark kit (synthetic pools, tensor-peak probe)."""
+    global _testkit
+    if _testkit is None:
+        lib()  # the block library first: the kit shares its error codes
+        _testkit = _load(TESTKIT_PATH, TESTKIT_SIGNATURES)
+    return _testkit
 
 
 class MimoError(RuntimeError):

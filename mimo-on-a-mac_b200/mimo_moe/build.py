@@ -1,4 +1,6 @@
-"""Build the sm_100a shared library in-tree: mimo_moe/libmimo_moe.so (nvcc, no torch extension)."""
+"""Build the sm_100a shared libraries in-tree (nvcc, no torch extension): mimo_moe/libmimo_moe.so (the
+MoE block, include/mimo_moe.h) and mimo_moe/libmimo_moe_testkit.so (synthetic pools and the tensor-peak
+probe for tests and benchmarks, include/mimo_moe_testkit.h)."""
 from __future__ import annotations
 
 import os
@@ -10,7 +12,10 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 INCLUDE = PKG.parent.parent / "include"
 LIB = PKG / "libmimo_moe.so"
-SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "synth.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu", "norm.cu", "ep_plan.cu", "loader.cpp"]
+LIB_TESTKIT = PKG / "libmimo_moe_testkit.so"
+SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu",
+           "norm.cu", "ep_plan.cu", "loader.cpp"]
+TESTKIT_SOURCES = ["synth.cu", "testkit.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -22,19 +27,19 @@ def nvcc() -> str:
 
 
 def sources():
-    return [CSRC / s for s in SOURCES]
+    return [CSRC / s for s in SOURCES + TESTKIT_SOURCES]
 
 
 def _stale() -> bool:
-    if not LIB.exists():
+    if not LIB.exists() or not LIB_TESTKIT.exists():
         return True
-    t = LIB.stat().st_mtime
-    deps = sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [INCLUDE / "mimo_moe.h"]
+    t = min(LIB.stat().st_mtime, LIB_TESTKIT.stat().st_mtime)
+    deps = sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
     return any(d.stat().st_mtime > t for d in deps if d.exists())
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    """Compile every .cu for sm_100a (-lineinfo, -O3) and link libmimo_moe.so next to this file."""
+    """Compile every .cu for sm_100a (-lineinfo, -O3) and link both libraries next to this file."""
     if not force and not _stale():
         return LIB
     build_dir = PKG.parent / "_build"
@@ -59,9 +64,11 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
             sys.stderr.write(f"\nFAILED: {' '.join(cmd)}\n")
     if not ok:
         raise RuntimeError("nvcc failed")
-    tmp = LIB.with_suffix(".so.tmp")
-    subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ["-lpthread"], check=True)
-    os.replace(tmp, LIB)
+    for lib, names in ((LIB, SOURCES), (LIB_TESTKIT, TESTKIT_SOURCES)):
+        tmp = lib.with_suffix(".so.tmp")
+        mine = [str(build_dir / (Path(n).stem + ".o")) for n in names]
+        subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(tmp)] + mine + ["-lpthread"], check=True)
+        os.replace(tmp, lib)
     return LIB
 
 

@@ -139,7 +139,7 @@ class ExpertPools:
         2^-8): experts [first_expert, first_expert+S) of `layer` in slots [0, S)."""
         p = ExpertPools.empty(S, hidden, inter, device)
         t = p.t
-        check(lib().mimo_moe_fill_synthetic_pool(
+        check(_lib.testkit().mimo_moe_fill_synthetic_pool(
             t["gate_w"].data_ptr(), t["gate_s"].data_ptr(), t["up_w"].data_ptr(), t["up_s"].data_ptr(),
             t["down_w"].data_ptr(), t["down_s"].data_ptr(), S, hidden, inter, seed, layer, first_expert,
             _stream()), "fill_synthetic_pool")

@@ -1,5 +1,6 @@
-"""C-ABI library checks that need no GPU: it loads, exports every symbol include/mimo_moe.h declares,
-and its host-side argument checks reject bad calls before touching the device."""
+"""C-ABI library checks that need no GPU: the block library and the test kit load, export every symbol
+include/mimo_moe.h and include/mimo_moe_testkit.h declare, and their host-side argument checks reject
+bad calls before touching the device."""
 import ctypes
 import re
 
@@ -9,8 +10,8 @@ import torch
 from conftest import ROOT
 
 
-def declared_functions():
-    hdr = (ROOT / "include" / "mimo_moe.h").read_text()
+def declared_functions(header="mimo_moe.h"):
+    hdr = (ROOT / "include" / header).read_text()
     hdr = re.sub(r"/\*.*?\*/", "", hdr, flags=re.S)
     return sorted(set(re.findall(r"\b(mimo_moe_[a-z0-9_]+)\s*\(", hdr)))
 
@@ -22,8 +23,13 @@ def test_library_exports_every_declared_symbol():
     assert len(names) >= 15
     missing = [n for n in names if not hasattr(L, n)]
     assert not missing, missing
-    from mimo_moe._lib import SIGNATURES
+    from mimo_moe._lib import SIGNATURES, TESTKIT_SIGNATURES, testkit
     assert set(names) <= set(SIGNATURES), set(names) - set(SIGNATURES)
+    kit = declared_functions("mimo_moe_testkit.h")
+    K = testkit()
+    assert kit and not [n for n in kit if not hasattr(K, n)]
+    assert set(kit) == set(TESTKIT_SIGNATURES)
+    assert not set(kit) & set(names)            # the block library does not carry the kit
 
 
 def test_version_and_errors():
@@ -63,7 +69,8 @@ def test_bad_arguments_return_einval_without_a_device():
                               16, None, None) == EINVAL                        # workspace too small
     assert L.mimo_moe_prefill(1, ctypes.byref(pools), None, 100, 1, 1, 4, 8, 1, 1, 1 << 30, None,
                               None) == EINVAL                                  # E != S without slot_of
-    assert L.mimo_moe_fill_synthetic_pool(None, None, None, None, None, None, 1, 4096, 2048, 0, 0, 0,
+    K = mimo_moe._lib.testkit()
+    assert K.mimo_moe_fill_synthetic_pool(None, None, None, None, None, None, 1, 4096, 2048, 0, 0, 0,
                                           None) == EINVAL
     assert L.mimo_moe_rmsnorm(None, None, 1, 4096, 1e-6, None, None) == EINVAL
     assert L.mimo_moe_rmsnorm(256, None, 1, 12, 1e-6, 256, None) == EINVAL       # H % 8

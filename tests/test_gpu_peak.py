@@ -1,4 +1,4 @@
-"""The library's dense tensor peak probe (mimo_moe_tensor_peak): both MMA forms run to completion on
+"""The test kit's dense tensor peak probe (mimo_moe_tensor_peak): both MMA forms run to completion on
 every SM and report a rate between the bf16 rate and twice the nominal FP4 rate of a B200, with the
 FP4 form (kind::mxf4) at least as fast as the e2m1 x e4m3 form (kind::mxf8f6f4)."""
 import ctypes
@@ -10,8 +10,8 @@ pytestmark = pytest.mark.gpu
 
 
 def test_tensor_peak_probe(gpu):
-    import mimo_moe
-    L = mimo_moe.lib()
+    from mimo_moe import _lib
+    L = _lib.testkit()
     status = torch.zeros(1, dtype=torch.int32, device=gpu)
     stream = torch.cuda.current_stream(gpu).cuda_stream
     rates = {}
