@@ -1,11 +1,13 @@
 // C ABI of the MoE block (include/mimo_moe.h): argument checks, workspace carving, launches.
 // No allocation, no host synchronisation, no device selection: everything is stream-ordered.
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
 
+#include "../../include/mimo_moe_layer.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -1027,6 +1029,91 @@ int mimo_moe_profile_read(int32_t* launches, float* milliseconds) {
     milliseconds[r.kind] += ms;
   }
   g_prof_used = 0;
+  return MIMO_OK;
+}
+
+// ------------------------------------------------------------- decoder layer (include/mimo_moe_layer.h)
+namespace {
+bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+size_t attn_split_bytes(int32_t T, int32_t nq, int32_t dv) { return (size_t)T * nq * ((size_t)dv + 2) * 4; }
+}  // namespace
+
+int mimo_moe_layer_rope_store(const uint16_t* qkv, int32_t T, int32_t n_heads, int32_t n_kv_heads,
+                              int32_t head_dim, int32_t v_head_dim, int32_t rotary_dim, float rope_theta,
+                              float v_scale, int32_t pos0, int32_t cap, uint16_t* q, uint16_t* k_cache,
+                              uint16_t* v_cache, void* stream) {
+  if (!qkv || !q || !k_cache || !v_cache || T < 1 || n_heads < 1 || n_kv_heads < 1 || head_dim < 8 ||
+      v_head_dim < 8 || head_dim % 8 || v_head_dim % 8 || rotary_dim < 0 || rotary_dim % 2 || rotary_dim > head_dim ||
+      !(rope_theta > 0.f) || !(v_scale >= 0.f) || pos0 < 0 || cap < T || (int64_t)pos0 + T > INT32_MAX ||
+      !a16(qkv) || !a16(q) || !a16(k_cache) || !a16(v_cache))
+    return MIMO_EINVAL;
+  RopeParams p{};
+  p.qkv = qkv, p.q = q, p.kc = k_cache, p.vc = v_cache;
+  p.T = T, p.nq = n_heads, p.nkv = n_kv_heads, p.dqk = head_dim, p.dv = v_head_dim, p.rot = rotary_dim;
+  p.pos0 = pos0, p.cap = cap, p.has_vscale = v_scale > 0.f ? 1 : 0, p.v_scale = v_scale;
+  p.log_base = std::log((double)rope_theta);
+  MIMO_TRY(launch_rope_store(p, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+size_t mimo_moe_layer_attention_workspace_bytes(int32_t T, int32_t n_heads, int32_t v_head_dim, int32_t splits) {
+  if (T < 1 || n_heads < 1 || v_head_dim < 1 || splits <= 1) return 0;
+  return (size_t)splits * attn_split_bytes(T, n_heads, v_head_dim);
+}
+
+int mimo_moe_layer_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                             const float* sinks, int32_t T, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                             int32_t v_head_dim, float scale, int32_t window, int32_t pos0, int32_t cap,
+                             int32_t splits, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !out || T < 1 || n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads ||
+      !attn_dims_supported(head_dim, v_head_dim) || !(scale > 0.f) || window < 0 || pos0 < 0 || cap < 1 ||
+      (int64_t)pos0 + T > INT32_MAX || !a16(q) || !a16(k_cache) || !a16(v_cache) || !a16(out))
+    return MIMO_EINVAL;
+  const int last = pos0 + T - 1;
+  const int first_visible = window > 0 ? std::max(0, pos0 - window + 1) : 0;
+  if (last - first_visible + 1 > cap) return MIMO_EINVAL;  // a visible key would have been overwritten
+  const int G = n_heads / n_kv_heads;
+  const int tiles = (T * G + 63) / 64;
+  const int nkeys = last - first_visible + 1, nblocks = (nkeys + 63) / 64;
+  const size_t per_split = attn_split_bytes(T, n_heads, v_head_dim);
+  if (splits <= 0) {
+    const int want = (2 * num_sms_current() + tiles * n_kv_heads - 1) / (tiles * n_kv_heads);
+    splits = std::max(1, std::min({want, nblocks, 64}));
+    if (splits > 1 && (!workspace || workspace_bytes < (size_t)splits * per_split))
+      splits = workspace ? (int)std::min<size_t>(splits, workspace_bytes / per_split) : 1;
+    splits = std::max(splits, 1);
+  }
+  if (splits > 1 && (!workspace || !a16(workspace) || workspace_bytes < (size_t)splits * per_split))
+    return MIMO_EINVAL;
+  AttnParams p{};
+  p.q = q, p.k = k_cache, p.v = v_cache, p.sinks = sinks, p.out = out;
+  p.part_o = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  p.part_ml = splits > 1 ? static_cast<float*>(workspace) + (size_t)splits * T * n_heads * v_head_dim : nullptr;
+  p.T = T, p.nq = n_heads, p.nkv = n_kv_heads, p.G = G, p.dqk = head_dim, p.dv = v_head_dim, p.cap = cap;
+  p.window = window, p.pos0 = pos0, p.splits = splits;
+  p.scale_log2 = (float)((double)scale * 1.4426950408889634);
+  MIMO_TRY(launch_attention(p, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_layer_add_rmsnorm(const uint16_t* x, const uint16_t* delta, const uint16_t* weight, int32_t T,
+                               int32_t H, float eps, uint16_t* h, uint16_t* r, void* stream) {
+  if (!x || !delta || !h || !r || T < 1 || H < 8 || H % 8 || !(eps >= 0.f) || !a16(x) || !a16(delta) || !a16(h) ||
+      !a16(r) || (weight && !a16(weight)))
+    return MIMO_EINVAL;
+  MIMO_TRY(launch_add_rmsnorm(x, delta, weight, T, H, eps, h, r, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_layer_swiglu(const uint16_t* gate_up, int32_t T, int32_t I, uint16_t* out, void* stream) {
+  if (!gate_up || !out || T < 1 || I < 8 || I % 8 || !a16(gate_up) || !a16(out)) return MIMO_EINVAL;
+  MIMO_TRY(launch_swiglu(gate_up, T, I, out, static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
+int mimo_moe_layer_add(const uint16_t* a, const uint16_t* b, int64_t n, uint16_t* out, void* stream) {
+  if (!a || !b || !out || n < 8 || n % 8 || !a16(a) || !a16(b) || !a16(out)) return MIMO_EINVAL;
+  MIMO_TRY(launch_add(a, b, (size_t)n, out, static_cast<cudaStream_t>(stream)));
   return MIMO_OK;
 }
 

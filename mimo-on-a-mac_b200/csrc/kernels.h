@@ -265,4 +265,33 @@ cudaError_t launch_fill_synthetic(uint32_t* gw, uint8_t* gs, uint32_t* uw, uint8
 
 constexpr int kPrefillUnit = 64;  // routes per prefill work unit (8 token blocks of 8)
 
+// ---- decoder layer around the MoE block (layer.cu)
+struct AttnParams {
+  const uint16_t* q;   // [T][nq][dqk] bf16, RoPE applied
+  const uint16_t* k;   // [nkv][cap][dqk] bf16 cache, position p in slot p % cap
+  const uint16_t* v;   // [nkv][cap][dv]
+  const float* sinks;  // [nq] sink logits, or null
+  uint16_t* out;       // [T][nq][dv] bf16
+  float* part_o;       // splits > 1: [splits][T*nq][dv] unnormalised partial outputs
+  float* part_ml;      // splits > 1: [splits][T*nq] (running max in log2 units, row sum)
+  int T, nq, nkv, G, dqk, dv, cap, window, pos0, splits;
+  float scale_log2;    // head_dim^-0.5 * log2(e)
+};
+struct RopeParams {
+  const uint16_t* qkv;  // [T][nq*dqk + nkv*dqk + nkv*dv] projection rows
+  uint16_t* q;          // [T][nq][dqk]
+  uint16_t* kc;         // [nkv][cap][dqk]
+  uint16_t* vc;         // [nkv][cap][dv]
+  int T, nq, nkv, dqk, dv, rot, pos0, cap, has_vscale;
+  float v_scale;        // already a bf16 value
+  double log_base;      // ln(rope_theta)
+};
+bool attn_dims_supported(int dqk, int dv);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t st);
+cudaError_t launch_rope_store(const RopeParams& p, cudaStream_t st);
+cudaError_t launch_add_rmsnorm(const uint16_t* x, const uint16_t* d, const uint16_t* weight, int T, int H, float eps,
+                               uint16_t* h, uint16_t* r, cudaStream_t st);
+cudaError_t launch_swiglu(const uint16_t* gu, int T, int I, uint16_t* out, cudaStream_t st);
+cudaError_t launch_add(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out, cudaStream_t st);
+
 }  // namespace mimo

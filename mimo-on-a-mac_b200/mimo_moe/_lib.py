@@ -1,4 +1,4 @@
-"""ctypes bindings of libmimo_moe.so (the C ABI in include/mimo_moe.h) and of the test and benchmark
+"""ctypes bindings of libmimo_moe.so (the C ABI in include/mimo_moe.h and include/mimo_moe_layer.h) and of the test and benchmark
 kit beside it, libmimo_moe_testkit.so (include/mimo_moe_testkit.h: synthetic pools, tensor-peak probe).
 
 There is no CPU fallback: if the library is missing or cannot be loaded, every op raises."""
@@ -79,6 +79,16 @@ SIGNATURES = {
     "mimo_moe_experts_static": (c_int32, [c_void_p, POINTER(Pools), c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32,
                                           c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_layer_rope_store": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float,
+                                            c_float, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_layer_attention_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
+    "mimo_moe_layer_attention": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                           c_int32, c_int32, c_float, c_int32, c_int32, c_int32, c_int32, c_void_p,
+                                           c_void_p, c_size_t, c_void_p]),
+    "mimo_moe_layer_add_rmsnorm": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p,
+                                             c_void_p, c_void_p]),
+    "mimo_moe_layer_swiglu": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    "mimo_moe_layer_add": (c_int32, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "mimo_moe_profile_enable": (c_int32, [c_int32]),
     "mimo_moe_profile_read": (c_int32, [c_void_p, c_void_p]),
 }

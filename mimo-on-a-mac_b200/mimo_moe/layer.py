@@ -1,0 +1,254 @@
+"""The rest of the MiMo decoder layer around the MoE block: attention with sinks (full or sliding window),
+the dense MLP of the non-MoE layers, and the layer wrapper.
+
+Mirrors engine/mimo_stream/mimo_v2.py (`Attention` :66-148, `MLP` :151-160, `DecoderLayer` :242-262) and the
+engine's per-layer loop (engine/mimo_stream/model.py:294-300, caches from model.py:169-170):
+
+    h   = x + self_attn(input_layernorm(x), mask, cache)
+    out = h + mlp(post_attention_layernorm(h))          (mlp = the MoE block on MoE layers)
+
+RoPE, the cache append, attention, the residual add fused with the next RMSNorm and the SwiGLU run in this
+library's CUDA kernels (include/mimo_moe_layer.h); the q/k/v/o and dense-MLP projections are plain bf16 GEMMs
+(cuBLAS through torch.matmul).  There is no CPU path.
+
+The checkpoint's config.json is not available offline, so every dimension is a constructor argument;
+`mimo_full_attention()` / `mimo_sliding_attention()` give the MiMo-like defaults the tests and the benchmark use
+(hidden 4096, 64 query heads of 192 (q/k) and 128 (v) dims, 64 rotary dims, 4 kv heads on full-attention layers
+and 8 on the 128-token sliding-window layers, sinks on the sliding-window layers)."""
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+from typing import Optional, Union
+
+import torch
+
+from ._lib import check, lib
+from .ops import ExpertPools, _need_cuda, _ptr, _stream, moe_block, rmsnorm, workspace
+
+
+@dataclass(frozen=True)
+class AttentionConfig:
+    """mimo_v2.py:68-83: the full-attention or sliding-window (swa_*) fields of ModelArgs."""
+    n_heads: int = 64
+    n_kv_heads: int = 4
+    head_dim: int = 192
+    v_head_dim: int = 128
+    rotary_dim: int = 64            # int(partial_rotary_factor * head_dim)
+    rope_theta: float = 5_000_000.0
+    window: int = 0                 # sliding_window_size on SWA layers, 0 = full causal attention
+    sinks: bool = False             # add_{full,swa}_attention_sink_bias
+    v_scale: Optional[float] = None  # attention_value_scale
+
+    @property
+    def scale(self) -> float:
+        return self.head_dim ** -0.5   # mimo_v2.py:92
+
+    @property
+    def qkv_width(self) -> int:
+        return self.n_heads * self.head_dim + self.n_kv_heads * (self.head_dim + self.v_head_dim)
+
+
+def mimo_full_attention(**kw) -> AttentionConfig:
+    return replace(AttentionConfig(), **kw)
+
+
+def mimo_sliding_attention(**kw) -> AttentionConfig:
+    return replace(AttentionConfig(n_kv_heads=8, rope_theta=10_000.0, window=128, sinks=True), **kw)
+
+
+def bf16_value(v: float) -> float:
+    """The float a Python scalar becomes when MLX multiplies it into a bf16 array (cast to bf16)."""
+    return float(torch.tensor(v, dtype=torch.float32).to(torch.bfloat16).to(torch.float32))
+
+
+class KVCache:
+    """Device KV cache of one attention layer: k [n_kv, cap, head_dim], v [n_kv, cap, v_head_dim] bf16,
+    position p in slot p % cap.  Full attention: cap = the longest sequence (mlx_lm KVCache); sliding window:
+    a ring of window + max_chunk - 1 slots (RotatingKVCache(max_size=window) keeps the last `window` keys and
+    concatenates a multi-token chunk before trimming, which is what the extra max_chunk - 1 slots hold)."""
+
+    def __init__(self, cfg: AttentionConfig, cap: int, device=None):
+        dev = torch.device(device or "cuda")
+        self.cfg = cfg
+        self.cap = int(cap)
+        self.k = torch.zeros(cfg.n_kv_heads, self.cap, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+        self.v = torch.zeros(cfg.n_kv_heads, self.cap, cfg.v_head_dim, dtype=torch.bfloat16, device=dev)
+        self.offset = 0
+
+    @classmethod
+    def for_layer(cls, cfg: AttentionConfig, max_len: int, max_chunk: int = 4096, device=None) -> "KVCache":
+        cap = max_len if cfg.window == 0 else min(max_len, cfg.window + max_chunk - 1)
+        return cls(cfg, cap, device)
+
+
+def rope_store(qkv: torch.Tensor, cfg: AttentionConfig, cache: KVCache, pos0: int,
+               q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mimo_v2.py:130-139: RoPE on q and k at positions pos0.., v * attention_value_scale, k/v appended to the
+    cache.  Returns q bf16 [T, n_heads, head_dim]."""
+    _need_cuda(qkv, "qkv")
+    T = qkv.shape[0]
+    q = q_out if q_out is not None else torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=torch.bfloat16,
+                                                    device=qkv.device)
+    vs = 0.0 if cfg.v_scale is None else bf16_value(cfg.v_scale)
+    check(lib().mimo_moe_layer_rope_store(qkv.data_ptr(), T, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                                          cfg.v_head_dim, cfg.rotary_dim, float(cfg.rope_theta), vs, int(pos0),
+                                          cache.cap, q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(),
+                                          _stream()), "rope_store")
+    return q
+
+
+def attention(q: torch.Tensor, cache: KVCache, cfg: AttentionConfig, pos0: int, sinks: Optional[torch.Tensor] = None,
+              splits: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mlx fast.scaled_dot_product_attention(q, k, v, scale=head_dim^-0.5, mask, sinks) over the cache for the
+    T queries at positions pos0..pos0+T-1 (causal; sliding window when cfg.window > 0).
+    Returns bf16 [T, n_heads, v_head_dim]."""
+    _need_cuda(q, "q")
+    T = q.shape[0]
+    dev = q.device
+    o = out if out is not None else torch.empty(T, cfg.n_heads, cfg.v_head_dim, dtype=torch.bfloat16, device=dev)
+    L = lib()
+    max_splits = 64 if splits <= 0 else splits
+    nb = L.mimo_moe_layer_attention_workspace_bytes(T, cfg.n_heads, cfg.v_head_dim, max_splits)
+    ws = workspace(nb, dev)
+    if sinks is not None:
+        sinks = sinks.to(device=dev, dtype=torch.float32).contiguous()
+    check(L.mimo_moe_layer_attention(q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), _ptr(sinks), T,
+                                     cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.v_head_dim, float(cfg.scale),
+                                     cfg.window, int(pos0), cache.cap, int(splits), o.data_ptr(), ws.data_ptr(),
+                                     ws.numel(), _stream()), "attention")
+    return o
+
+
+def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: Optional[torch.Tensor], eps: float):
+    """h = bf16(x + delta), r = rmsnorm(h) * weight (one pass).  Returns (h, r)."""
+    T, H = x.shape
+    h = torch.empty_like(x)
+    r = torch.empty_like(x)
+    w = None if weight is None else weight.to(device=x.device, dtype=torch.bfloat16).contiguous()
+    check(lib().mimo_moe_layer_add_rmsnorm(x.data_ptr(), delta.data_ptr(), _ptr(w), T, H, float(eps), h.data_ptr(),
+                                           r.data_ptr(), _stream()), "add_rmsnorm")
+    return h, r
+
+
+def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
+    """mlx_lm swiglu(gate, up) = silu(gate) * up in bf16 steps; gate_up [T, 2I] = [gate | up]."""
+    T, I2 = gate_up.shape
+    out = torch.empty(T, I2 // 2, dtype=torch.bfloat16, device=gate_up.device)
+    check(lib().mimo_moe_layer_swiglu(gate_up.data_ptr(), T, I2 // 2, out.data_ptr(), _stream()), "swiglu")
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    out = torch.empty_like(a)
+    check(lib().mimo_moe_layer_add(a.data_ptr(), b.data_ptr(), a.numel(), out.data_ptr(), _stream()), "add")
+    return out
+
+
+def _bf16(t: torch.Tensor, dev) -> torch.Tensor:
+    return t.to(device=dev, dtype=torch.bfloat16).contiguous()
+
+
+class Attention:
+    """mimo_v2.py:66-148 (no attention bias).  Weights in nn.Linear layout [out, in]: wq [n_heads*head_dim, H],
+    wk [n_kv*head_dim, H], wv [n_kv*v_head_dim, H], wo [H, n_heads*v_head_dim]; sinks float32 [n_heads]."""
+
+    def __init__(self, cfg: AttentionConfig, wq, wk, wv, wo, sinks: Optional[torch.Tensor] = None, device=None):
+        dev = torch.device(device or wq.device)
+        if cfg.sinks and sinks is None:
+            raise ValueError("this attention config has sinks: pass the sink logits")
+        self.cfg = cfg
+        self.w_qkv = torch.cat([_bf16(wq, dev), _bf16(wk, dev), _bf16(wv, dev)], 0).contiguous()
+        self.w_o = _bf16(wo, dev)
+        self.sinks = None if sinks is None else sinks.to(device=dev, dtype=torch.float32).contiguous()
+        if self.w_qkv.shape[0] != cfg.qkv_width:
+            raise ValueError("q/k/v weights do not match the attention config")
+
+    def __call__(self, r: torch.Tensor, cache: KVCache) -> torch.Tensor:
+        T = r.shape[0]
+        qkv = torch.matmul(r, self.w_qkv.t())
+        q = rope_store(qkv, self.cfg, cache, cache.offset)
+        o = attention(q, cache, self.cfg, cache.offset, self.sinks)
+        cache.offset += T
+        return torch.matmul(o.view(T, -1), self.w_o.t())
+
+
+class DenseMLP:
+    """mimo_v2.py:151-160: down(swiglu(gate(x), up(x))); weights [I, H], [I, H], [H, I]."""
+
+    def __init__(self, w_gate, w_up, w_down, device=None):
+        dev = torch.device(device or w_gate.device)
+        self.w_gate_up = torch.cat([_bf16(w_gate, dev), _bf16(w_up, dev)], 0).contiguous()
+        self.w_down = _bf16(w_down, dev)
+
+    def __call__(self, r: torch.Tensor) -> torch.Tensor:
+        return torch.matmul(swiglu(torch.matmul(r, self.w_gate_up.t())), self.w_down.t())
+
+
+class MoEMLP:
+    """An MoE layer's MLP: the router + resident experts of this library's MoE block (model.py:302-336)."""
+
+    def __init__(self, router_weight: torch.Tensor, bias: Optional[torch.Tensor], pools: ExpertPools):
+        self.router_weight = router_weight.to(torch.bfloat16).contiguous()
+        self.bias = None if bias is None else bias.to(torch.float32).contiguous()
+        self.pools = pools
+
+    def __call__(self, r: torch.Tensor) -> torch.Tensor:
+        return moe_block(r, self.router_weight, self.bias, self.pools)
+
+
+class DecoderLayer:
+    """mimo_v2.py:242-262: h = x + attn(input_layernorm(x)); out = h + mlp(post_attention_layernorm(h)).
+    __call__(x bf16 [T, H], cache) -> bf16 [T, H]; the cache's offset advances by T."""
+
+    def __init__(self, attn: Attention, mlp: Union[DenseMLP, MoEMLP], input_norm: Optional[torch.Tensor],
+                 post_norm: Optional[torch.Tensor], eps: float = 1e-5):
+        self.attn = attn
+        self.mlp = mlp
+        dev = attn.w_o.device
+        self.input_norm = None if input_norm is None else _bf16(input_norm, dev)
+        self.post_norm = None if post_norm is None else _bf16(post_norm, dev)
+        self.eps = float(eps)
+        self.trace = None   # optional callable(dict of the layer's intermediate tensors), for tests
+
+    def new_cache(self, max_len: int, max_chunk: int = 4096) -> KVCache:
+        return KVCache.for_layer(self.attn.cfg, max_len, max_chunk, self.attn.w_o.device)
+
+    def __call__(self, x: torch.Tensor, cache: KVCache) -> torch.Tensor:
+        _need_cuda(x, "x")
+        x = x.to(torch.bfloat16).contiguous()
+        r = rmsnorm(x, self.input_norm, self.eps)
+        a = self.attn(r, cache)
+        h, r2 = add_rmsnorm(x, a, self.post_norm, self.eps)
+        y = self.mlp(r2)
+        out = add(h, y)
+        if self.trace is not None:
+            self.trace({"x": x, "r": r, "a": a, "h": h, "r2": r2, "y": y, "out": out})
+        return out
+
+
+def synthetic_attention(cfg: AttentionConfig, hidden: int = 4096, seed: int = 4, std: float = 0.02,
+                        device=None) -> Attention:
+    """Seeded random-init attention weights of this shape (no checkpoint offline): N(0, std) bf16, sinks
+    N(0, 1) float32 when the config has them."""
+    g = torch.Generator("cpu").manual_seed(seed)
+    def w(o, i):
+        return (torch.randn(o, i, generator=g) * std).to(torch.bfloat16)
+    wq = w(cfg.n_heads * cfg.head_dim, hidden)
+    wk = w(cfg.n_kv_heads * cfg.head_dim, hidden)
+    wv = w(cfg.n_kv_heads * cfg.v_head_dim, hidden)
+    wo = w(hidden, cfg.n_heads * cfg.v_head_dim)
+    sinks = torch.randn(cfg.n_heads, generator=g) if cfg.sinks else None
+    return Attention(cfg, wq, wk, wv, wo, sinks, device=device or "cuda")
+
+
+def synthetic_dense_mlp(hidden: int = 4096, inter: int = 16384, seed: int = 5, std: float = 0.02,
+                        device=None) -> DenseMLP:
+    g = torch.Generator("cpu").manual_seed(seed)
+    def w(o, i):
+        return (torch.randn(o, i, generator=g) * std).to(torch.bfloat16)
+    return DenseMLP(w(inter, hidden), w(inter, hidden), w(hidden, inter), device=device or "cuda")
+
+
+__all__ = ["AttentionConfig", "Attention", "DecoderLayer", "DenseMLP", "KVCache", "MoEMLP", "add", "add_rmsnorm",
+           "attention", "bf16_value", "mimo_full_attention", "mimo_sliding_attention", "rope_store", "swiglu",
+           "synthetic_attention", "synthetic_dense_mlp"]

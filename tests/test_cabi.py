@@ -1,5 +1,5 @@
 """C-ABI library checks that need no GPU: the block library and the test kit load, export every symbol
-include/mimo_moe.h and include/mimo_moe_testkit.h declare, and their host-side argument checks reject
+include/mimo_moe.h, include/mimo_moe_layer.h and include/mimo_moe_testkit.h declare, and their host-side argument checks reject
 bad calls before touching the device."""
 import ctypes
 import re
@@ -19,8 +19,8 @@ def declared_functions(header="mimo_moe.h"):
 def test_library_exports_every_declared_symbol():
     import mimo_moe
     L = mimo_moe.lib()
-    names = declared_functions()
-    assert len(names) >= 15
+    names = declared_functions() + declared_functions("mimo_moe_layer.h")
+    assert len(names) >= 21
     missing = [n for n in names if not hasattr(L, n)]
     assert not missing, missing
     from mimo_moe._lib import SIGNATURES, TESTKIT_SIGNATURES, testkit
