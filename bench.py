@@ -36,8 +36,13 @@ DOWN_BYTES = H * I // 2 + H * I // 32
 # workload -> (tokens per GPU, routing)
 WORKLOADS = {"decode1": (1, "free"), "decode2": (2, "free"), "decode4": (4, "free"), "decode8": (8, "free"),
              "decode8_overlap": (8, "overlap"), "prefill2048": (2048, "free"), "prefill16384z": (16384, "zipf"),
-             "stack48_decode1": (1, "free"), "stack48_decode8": (8, "free")}
+             "stack48_decode1": (1, "free"), "stack48_decode8": (8, "free"),
+             "layer_decode1": (1, "free"), "layer_decode8": (8, "free"), "layer_prefill2048": (2048, "free")}
 NESTED = ("decode1", "decode8_overlap", "prefill2048")   # measured beside the default headline on one GPU
+# the whole decoder layer around the MoE block (attention with a 4096-token context, then the MoE block),
+# measured beside the headline too
+LAYER_NESTED = ("layer_decode1", "layer_decode8", "layer_prefill2048")
+LAYER_CONTEXT = 4096
 STACK_LAYERS = 48  # config 3: 48 MoE layers (~164 GB of experts), RMSNorm (unit weight) between layers
 # config 4: Zipf(1.1)-biased routing, bias_e = c * log(p_e * E); c = 0.055 puts the most loaded
 # expert at ~10x the mean load on the seeded 16384-token batch (tuned once on the CPU router)
@@ -170,6 +175,10 @@ def workload_config(workload: str, world: int = 1, NE: int = E) -> dict:
                   if T <= 8 else f"inputs > L2: every step streams the whole {NE * EXPERT_BYTES / 1e9:.2f} GB pool")}
     if workload.startswith("stack"):
         cfg["layers"] = STACK_LAYERS
+    if workload.startswith("layer"):
+        cfg["layer"] = ("MoE decoder layer: RMSNorm, full-attention block (64 q heads x 192, 4 kv heads, v 128, "
+                        "64 rotary dims, value scale 0.707), residual + RMSNorm, MoE block, residual")
+        cfg["context"] = LAYER_CONTEXT if T <= 8 else 0
     return cfg
 
 
@@ -283,6 +292,54 @@ def cpu_baseline(workload: str, budget_s: float, device_pool=None, emulator: boo
                       + b["sample"], "variants": rates}
 
 
+def cpu_layer_attention_seconds(T: int, context: int, budget_s: float) -> tuple:
+    """The attention half of the decoder layer (q/k/v projections, RoPE, attention over the cache, o_proj) as a
+    torch-CPU float32 restatement on all host threads, weights converted outside the clock; a bounded sample
+    (a slice of the rows and of the heads, scaled up by the fractions timed).  Returns (seconds per step,
+    sample text)."""
+    import torch
+    from mimo_moe.layer import mimo_full_attention
+    torch.set_num_threads(_host_cores())
+    c = mimo_full_attention()
+    g = torch.Generator().manual_seed(7)
+    rows = min(T, 128)
+    heads = 4 if T > 8 else c.n_heads
+    wqkv = torch.randn(c.qkv_width, H, generator=g) * 0.02
+    wo = torch.randn(H, c.n_heads * c.v_head_dim, generator=g) * 0.02
+    r = torch.randn(rows, H, generator=g)
+    nk = context + T
+    k = torch.randn(c.n_kv_heads, nk, c.head_dim, generator=g)
+    v = torch.randn(c.n_kv_heads, nk, c.v_head_dim, generator=g)
+    q = torch.randn(T, heads, c.head_dim, generator=g)
+    G = c.n_heads // c.n_kv_heads
+    o = torch.randn(rows, c.n_heads * c.v_head_dim, generator=g)
+    qpos = torch.arange(context, context + T)
+    half = c.rotary_dim // 2
+    t_proj = t_attn = 0.0
+    n = 0
+    while True:
+        t0 = time.perf_counter()
+        qkv = r @ wqkv.T
+        ang = torch.arange(rows, dtype=torch.float32)[:, None] * torch.pow(c.rope_theta, -torch.arange(half) * 2.0 / c.rotary_dim)
+        _ = qkv[:, :half] * torch.cos(ang) - qkv[:, half:2 * half] * torch.sin(ang)
+        _ = o @ wo.T
+        t1 = time.perf_counter()
+        for h in range(heads):
+            s_ = (q[:, h] @ k[h // G].T) * c.scale
+            s_ = s_.masked_fill(torch.arange(nk)[None] > qpos[:, None], float("-inf"))
+            _ = torch.softmax(s_, -1) @ v[h // G]
+        t2 = time.perf_counter()
+        t_proj += t1 - t0
+        t_attn += t2 - t1
+        n += 1
+        if t_proj + t_attn >= budget_s / 4 or n >= 20:
+            break
+    # the projections scale with the rows, the attention with the heads
+    sec = t_proj / n * (T / rows) + t_attn / n * (c.n_heads / heads)
+    return sec, (f"torch-CPU float32 attention half: {rows} of {T} rows, {heads} of {c.n_heads} heads over "
+                 f"{nk} keys, {n} repetitions, scaled to the full step")
+
+
 def run_reference(args):
     """The reference arm: the reference path on the host cores for the same workload, config and metric.
     The reference's own implementation is MLX on Metal, which does not exist on Linux; its CPU forms here
@@ -325,6 +382,145 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------------ GPU arm
+def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float):
+    """The decoder layer around the MoE block (mimo_moe.layer.DecoderLayer, full attention, MoE MLP) at
+    decode (T tokens at position LAYER_CONTEXT of a 4096-token cache) or prefill (T tokens from an empty
+    cache): device-timed throughput, per-phase times, the step's HBM roofline (decode) and the attention
+    kernel's own roofline, end to end through the public API, and a CPU baseline."""
+    import numpy as np
+    import torch
+    import mimo_moe
+    from mimo_moe import _lib, synthetic
+    from mimo_moe.layer import (DecoderLayer, MoEMLP, add, add_rmsnorm, attention, mimo_full_attention, rope_store,
+                                synthetic_attention)
+    dev = ctx.dev
+    T = WORKLOADS[workload][0]
+    decode = T <= 8
+    pool = ctx.pool()
+    NE = ctx.NE
+    W = synthetic.router_weight().to(dev)[:NE].contiguous()
+    bias = routing_bias(workload, NE).to(dev)
+    cfg = mimo_full_attention(v_scale=0.707)
+    attn = synthetic_attention(cfg, seed=4, device=dev)
+    layer = DecoderLayer(attn, MoEMLP(W, bias, pool), None, None, eps=1e-5)
+    pos0 = LAYER_CONTEXT if decode else 0
+    cache = layer.new_cache(LAYER_CONTEXT + 16 if decode else T, max_chunk=T)
+    gk = torch.Generator(device=dev).manual_seed(9)
+    cache.k.normal_(generator=gk)
+    cache.v.normal_(generator=gk)
+    xs = [x.to(dev) for x in batches(workload)]
+    nb = len(xs)
+
+    def eager(x):
+        cache.offset = pos0     # every step is the step at the same position of the same context
+        return layer(x, cache)
+
+    gstep = BatchGraphs(eager, xs) if decode else None
+
+    def step(i):
+        if gstep is not None:
+            gstep(i % nb)
+        else:
+            eager(xs[i % nb])
+
+    for i in range(max(3, warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(ctx.local)
+    clocks.start()
+    time.sleep(0.3)
+    ms = _timed(ctx, steps, step)
+    clk = clocks.stop()
+
+    # per-phase device times from an eager pass (CUDA event pairs between the layer's launches)
+    names = ["input_norm", "qkv_gemm", "rope_store", "attention", "o_gemm", "add_norm", "moe_block", "add"]
+    acc = {n: 0.0 for n in names}
+    nprof = 20 if decode else 3
+    for i in range(nprof):
+        x = xs[i % nb]
+        cache.offset = pos0
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        ev[0].record()
+        r = mimo_moe.rmsnorm(x, None, 1e-5); ev[1].record()
+        qkv = torch.matmul(r, attn.w_qkv.t()); ev[2].record()
+        q = rope_store(qkv, cfg, cache, pos0); ev[3].record()
+        o = attention(q, cache, cfg, pos0, attn.sinks); ev[4].record()
+        a = torch.matmul(o.view(T, -1), attn.w_o.t()); ev[5].record()
+        h, r2 = add_rmsnorm(x, a, None, 1e-5); ev[6].record()
+        y = layer.mlp(r2); ev[7].record()
+        add(h, y); ev[8].record()
+        torch.cuda.synchronize()
+        for j, n in enumerate(names):
+            acc[n] += ev[j].elapsed_time(ev[j + 1]) / nprof
+    hbm, tflops_peak, peak_kind = peaks()
+    attn_w_bytes = (attn.w_qkv.numel() + attn.w_o.numel()) * 2
+    keys = pos0 + T
+    kv_bytes = cfg.n_kv_heads * keys * (cfg.head_dim + cfg.v_head_dim) * 2
+    U = []
+    for x in xs:
+        idx, _ = mimo_moe.router(x, W, bias)
+        U.append(int(torch.unique(idx).numel()))
+    Um = statistics.mean(U)
+    step_bytes = attn_w_bytes + kv_bytes + Um * EXPERT_BYTES + NE * H * 2
+    step_ms = ms / steps
+    if decode:
+        achieved = step_bytes / (step_ms * 1e-3) / 1e9
+        roofline = {"kernel": "whole decoder-layer step (attention weights, KV cache, router, distinct experts)",
+                    "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
+                    "algorithmic_bytes_per_step": step_bytes,
+                    "attention_kernel": {"kernel": "attn_kernel<192,128> + attn_merge_kernel (split keys)",
+                                         "bytes": kv_bytes, "ms": acc["attention"],
+                                         "achieved_gbs": kv_bytes / (acc["attention"] * 1e-3) / 1e9,
+                                         "frac": kv_bytes / (acc["attention"] * 1e-3) / 1e9 / hbm}}
+    else:
+        pairs = T * (T + 1) // 2
+        flops = 2 * pairs * cfg.n_heads * (cfg.head_dim + cfg.v_head_dim)
+        tf = flops / (acc["attention"] * 1e-3) / 1e12
+        roofline = {"kernel": "attn_kernel<192,128> (causal prefill attention, bf16 mma.sync, float32 softmax)",
+                    "bound": "tensor", "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s",
+                    "frac": tf / tflops_peak, "peak_kind": f"{peak_kind} bf16_tflops_sustained",
+                    "traffic": None, "algorithmic_flops_per_launch": flops}
+    roofline["phases_ms"] = acc
+
+    xh = [x.cpu().pin_memory() for x in xs]
+    yh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i):
+        xd.copy_(xh[i % nb], non_blocking=True)
+        yh.copy_(eager(xd), non_blocking=True)
+    for i in range(3):
+        e2e_step(i)
+    e2e_ms = _timed(ctx, steps, e2e_step)
+    # our launches per step: rmsnorm, rope_store, attention (+ merge when split), add_rmsnorm, add, and the
+    # MoE block's (decode: route logits, select, gate/up, down, combine; prefill: 11)
+    per_step = 5 + (1 if decode else 0) + (5 if decode else 11)
+    res = {
+        "metric": f"decoder-layer tok/s ({workload})", "value": T * steps / (ms * 1e-3), "unit": "tok/s",
+        "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 attention (mma.sync, f32 softmax) + e2m1 x e4m3 MoE (tcgen05)",
+        "data": "synthetic (random-init attention weights N(0,0.02), random bf16 KV cache, seeded MXFP4 pool)",
+        "config": workload_config(workload, 1, NE), "mean_distinct_experts": Um, "roofline": roofline, "clocks": clk,
+        "e2e": {"value": T * steps / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2,
+                "how": "eager mimo_moe.layer.DecoderLayer call per step, pinned host x copied in and y read back"},
+        "gpu_launches": per_step * steps,
+    }
+    if not args.no_cpu_baseline:
+        moe_rates = cpu_port_rates("decode8" if T == 8 else ("decode1" if T == 1 else "prefill2048"),
+                                   cpu_budget, device_pool=pool)
+        best = max(moe_rates, key=lambda k: moe_rates[k]["value"])
+        t_moe = T / moe_rates[best]["value"]
+        t_att, sample = cpu_layer_attention_seconds(T, pos0, cpu_budget)
+        res["cpu_baseline"] = {"value": T / (t_moe + t_att), "unit": "tok/s", "cores": _host_cores(), "kind": "port",
+                               "sample": f"{sample}; plus the MoE block's {best} ({moe_rates[best]['sample']})"}
+    del gstep
+    torch.cuda.synchronize()
+    return res
+
+
 class BatchGraphs:
     """One CUDA graph per resident input batch (decode steps are a few short kernels, so a replayed
     graph keeps host launch costs out of the step; capturing one graph per batch keeps the input copy
@@ -820,6 +1016,11 @@ def main():
         return bench_stack(args)
     import torch.distributed as dist
     ctx = Ctx(args)
+    if args.workload.startswith("layer"):
+        if ctx.world > 1:
+            raise SystemExit("the decoder-layer workloads run on one GPU")
+        print(json.dumps(measure_layer(args, ctx, args.workload, args.steps, args.warmup, args.cpu_budget)))
+        return
     head = measure(args, ctx, args.workload, args.steps, args.warmup, args.cpu_budget, emulator=True)
     nested = {}
     if ctx.world == 1 and not args.no_nested and args.workload == "decode8" and args.pool_experts == E:
@@ -827,6 +1028,10 @@ def main():
             T = WORKLOADS[wl][0]
             k = args.steps if T <= 8 else max(10, min(args.steps, 40))
             nested[wl] = measure(args, ctx, wl, k, args.warmup, args.cpu_budget, emulator=False)
+        for wl in LAYER_NESTED:
+            T = WORKLOADS[wl][0]
+            k = args.steps if T <= 8 else max(10, min(args.steps, 20))
+            nested[wl] = measure_layer(args, ctx, wl, k, args.warmup, args.cpu_budget)
         head["configs"] = nested
     if ctx.rank == 0:
         print(json.dumps(head))

@@ -37,7 +37,7 @@ extern "C" {
  * (pos * rope_theta^(-2i/rotary_dim)); the other dims pass through.  v is multiplied by v_scale (a value
  * representable in bf16, as MLX casts the Python scale to the array's type) when v_scale > 0, else copied.
  * Outputs: q bf16 [T][n_heads][head_dim]; k and v of each token written to slot (pos % cap) of each kv head.
- * Needs T <= cap. */
+ * Needs T <= cap and rotary_dim <= 256. */
 int mimo_moe_layer_rope_store(const uint16_t* qkv, int32_t T, int32_t n_heads, int32_t n_kv_heads,
                               int32_t head_dim, int32_t v_head_dim, int32_t rotary_dim, float rope_theta,
                               float v_scale, int32_t pos0, int32_t cap, uint16_t* q, uint16_t* k_cache,
@@ -53,13 +53,18 @@ size_t mimo_moe_layer_attention_workspace_bytes(int32_t T, int32_t n_heads, int3
  * key position j is visible when j <= p and, for window > 0, j > p - window.  q bf16 [T][n_heads][head_dim]
  * (after RoPE), out bf16 [T][n_heads][v_head_dim], sinks float32 [n_heads] or null.  (head_dim, v_head_dim)
  * in {(192,128), (128,128), (64,64)}.  splits: the number of key ranges each query tile is divided into
- * (decode: many keys, few queries); 0 picks a split count that fills the GPU within the workspace given;
+ * (decode: many keys, few queries; at most 64); 0 picks a split count that fills the GPU within the workspace given;
  * splits > 1 need mimo_moe_layer_attention_workspace_bytes(T, n_heads, v_head_dim, splits).  Needs every
- * visible position resident: (pos0 + T - 1) - first visible position + 1 <= cap. */
+ * visible position resident: (pos0 + T - 1) - first visible position + 1 <= cap.  Query tiles of 128 rows
+ * (T * n_heads / n_kv_heads >= 256, no key split) run on the tcgen05 tensor cores when cap is a multiple of
+ * 128 and 128 is a multiple of n_heads / n_kv_heads; cache slots a key block reads beyond the visible
+ * positions must then hold finite values (a zero-initialised cache does).  status: optional caller-zeroed
+ * device word, set to MIMO_ETIMEOUT if a bounded wait of that kernel expires. */
 int mimo_moe_layer_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                              const float* sinks, int32_t T, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                              int32_t v_head_dim, float scale, int32_t window, int32_t pos0, int32_t cap,
-                             int32_t splits, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
+                             int32_t splits, uint16_t* out, void* workspace, size_t workspace_bytes, int32_t* status,
+                             void* stream);
 
 /* Residual add and the next RMSNorm in one pass (mimo_v2.py:260 then post_attention_layernorm):
  * h = bf16(x + delta); r = RMSNorm(h) * weight exactly as mimo_moe_rmsnorm computes it.  [T, H] bf16,

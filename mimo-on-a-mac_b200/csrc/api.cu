@@ -1044,6 +1044,7 @@ int mimo_moe_layer_rope_store(const uint16_t* qkv, int32_t T, int32_t n_heads, i
                               uint16_t* v_cache, void* stream) {
   if (!qkv || !q || !k_cache || !v_cache || T < 1 || n_heads < 1 || n_kv_heads < 1 || head_dim < 8 ||
       v_head_dim < 8 || head_dim % 8 || v_head_dim % 8 || rotary_dim < 0 || rotary_dim % 2 || rotary_dim > head_dim ||
+      rotary_dim > 256 ||
       !(rope_theta > 0.f) || !(v_scale >= 0.f) || pos0 < 0 || cap < T || (int64_t)pos0 + T > INT32_MAX ||
       !a16(qkv) || !a16(q) || !a16(k_cache) || !a16(v_cache))
     return MIMO_EINVAL;
@@ -1064,7 +1065,8 @@ size_t mimo_moe_layer_attention_workspace_bytes(int32_t T, int32_t n_heads, int3
 int mimo_moe_layer_attention(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                              const float* sinks, int32_t T, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                              int32_t v_head_dim, float scale, int32_t window, int32_t pos0, int32_t cap,
-                             int32_t splits, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+                             int32_t splits, uint16_t* out, void* workspace, size_t workspace_bytes, int32_t* status,
+                             void* stream) {
   if (!q || !k_cache || !v_cache || !out || T < 1 || n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads ||
       !attn_dims_supported(head_dim, v_head_dim) || !(scale > 0.f) || window < 0 || pos0 < 0 || cap < 1 ||
       (int64_t)pos0 + T > INT32_MAX || !a16(q) || !a16(k_cache) || !a16(v_cache) || !a16(out))
@@ -1073,25 +1075,25 @@ int mimo_moe_layer_attention(const uint16_t* q, const uint16_t* k_cache, const u
   const int first_visible = window > 0 ? std::max(0, pos0 - window + 1) : 0;
   if (last - first_visible + 1 > cap) return MIMO_EINVAL;  // a visible key would have been overwritten
   const int G = n_heads / n_kv_heads;
-  const int tiles = (T * G + 63) / 64;
-  const int nkeys = last - first_visible + 1, nblocks = (nkeys + 63) / 64;
   const size_t per_split = attn_split_bytes(T, n_heads, v_head_dim);
+  AttnParams p{};
+  p.T = T, p.nq = n_heads, p.nkv = n_kv_heads, p.G = G, p.dqk = head_dim, p.dv = v_head_dim, p.cap = cap;
+  p.window = window, p.pos0 = pos0;
   if (splits <= 0) {
-    const int want = (2 * num_sms_current() + tiles * n_kv_heads - 1) / (tiles * n_kv_heads);
-    splits = std::max(1, std::min({want, nblocks, 64}));
+    splits = attn_auto_splits(p, num_sms_current());
     if (splits > 1 && (!workspace || workspace_bytes < (size_t)splits * per_split))
       splits = workspace ? (int)std::min<size_t>(splits, workspace_bytes / per_split) : 1;
     splits = std::max(splits, 1);
   }
-  if (splits > 1 && (!workspace || !a16(workspace) || workspace_bytes < (size_t)splits * per_split))
+  if (splits > 64 || (splits > 1 && (!workspace || !a16(workspace) || workspace_bytes < (size_t)splits * per_split)))
     return MIMO_EINVAL;
-  AttnParams p{};
   p.q = q, p.k = k_cache, p.v = v_cache, p.sinks = sinks, p.out = out;
   p.part_o = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.part_ml = splits > 1 ? static_cast<float*>(workspace) + (size_t)splits * T * n_heads * v_head_dim : nullptr;
   p.T = T, p.nq = n_heads, p.nkv = n_kv_heads, p.G = G, p.dqk = head_dim, p.dv = v_head_dim, p.cap = cap;
   p.window = window, p.pos0 = pos0, p.splits = splits;
   p.scale_log2 = (float)((double)scale * 1.4426950408889634);
+  p.status = status;
   MIMO_TRY(launch_attention(p, static_cast<cudaStream_t>(stream)));
   return MIMO_OK;
 }

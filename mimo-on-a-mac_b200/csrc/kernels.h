@@ -276,6 +276,19 @@ struct AttnParams {
   float* part_ml;      // splits > 1: [splits][T*nq] (running max in log2 units, row sum)
   int T, nq, nkv, G, dqk, dv, cap, window, pos0, splits;
   float scale_log2;    // head_dim^-0.5 * log2(e)
+  int32_t* status;     // optional device word: MIMO_ETIMEOUT when a bounded wait of the tcgen05 kernel expires
+};
+// Parameters of the tcgen05 attention kernel (attn_tc.cu): TMA maps of q [T][nq][dqk] (box 64 x G x 128/G),
+// the K cache [nkv][cap][dqk] and the V cache [nkv][cap][dv] (boxes 64 x 128 x 1), 128B swizzle.
+struct AttnTcParams {
+  CUtensorMap qmap, kmap, vmap;
+  const float* sinks;
+  uint16_t* out;
+  int32_t* status;
+  float* part_o;   // splits > 1: unnormalised partials (the AttnParams layout)
+  float* part_ml;
+  int T, nq, nkv, G, cap, window, pos0, ntiles, splits;
+  float scale_log2;
 };
 struct RopeParams {
   const uint16_t* qkv;  // [T][nq*dqk + nkv*dqk + nkv*dv] projection rows
@@ -288,6 +301,9 @@ struct RopeParams {
 };
 bool attn_dims_supported(int dqk, int dv);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t st);
+bool attn_tc_supported(const AttnParams& p);
+int attn_auto_splits(const AttnParams& p, int num_sms);  // split count for the kernel launch_attention picks
+cudaError_t launch_attention_tc(const AttnParams& p, int32_t* status, cudaStream_t st);
 cudaError_t launch_rope_store(const RopeParams& p, cudaStream_t st);
 cudaError_t launch_add_rmsnorm(const uint16_t* x, const uint16_t* d, const uint16_t* weight, int T, int H, float eps,
                                uint16_t* h, uint16_t* r, cudaStream_t st);

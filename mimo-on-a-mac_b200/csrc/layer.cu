@@ -31,9 +31,12 @@
 // attn_kernel is a flash-attention forward on the bf16 mma.sync tensor path (m16n8k16, float32 accumulate):
 // one CTA = 64 query rows of one kv head (the G = n_heads / n_kv_heads query heads of consecutive tokens,
 // token-major, so every K/V block loaded to shared memory serves all heads of the group), four warps of
-// 16 rows, K/V blocks of 64 keys double-buffered by cp.async, online softmax in float32 (exp2 domain),
-// P rounded to bf16 for the P.V product.  Decode (few rows, many keys) splits the keys over CTAs
+// 16 rows, K/V blocks of 64 keys double-buffered by cp.async, online softmax in float32 (exp2 domain, the
+// row sum from the float32 P), P rounded to bf16 for the P.V product.  Decode (few rows, many keys) splits the keys over CTAs
 // (grid z); attn_merge_kernel folds the splits and the sink in a fixed split order.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -67,8 +70,17 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
+// Two float32 values rounded to nearest-even bf16 in one conversion: lo in bits 0-15, hi in bits 16-31.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return f32_to_bf16(lo) | (f32_to_bf16(hi) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;\n" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32: 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Byte offset of 16-byte chunk c of row r in a tile whose rows hold CH chunks; the chunk index is XORed
@@ -210,8 +222,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float v = s[j][h * 2 + e];
-          // P enters the P.V product as bf16: the row sum uses the same rounded values
-          const float pv = (v == -INFINITY) ? 0.f : bf16_round(exp2f(v - m_new));
+          const float pv = ex2_approx(v - (m_new == -INFINITY ? 0.f : m_new));  // 2^-inf = 0
           s[j][h * 2 + e] = pv;
           rs += pv;
         }
@@ -293,30 +304,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
   }
 }
 
-// One warp per (token, query head): folds the splits' (m, l, O) in split order with the sink.
+// One warp per (token, query head): folds the splits' (m, l, O) with the sink.  The lanes read the splits'
+// (m, l) in parallel (split s on lane s % 32), the warp takes their maximum and the sum of l * 2^(m - M) by
+// butterflies (a fixed order), then each lane sums its DV / 32 output values over the splits in split order.
 template <int DV>
 __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= p.T * p.nq) return;
   const int qh = row % p.nq;
-  float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.part_ml[((size_t)s * p.T * p.nq + row) * 2]);
+  const size_t stride = (size_t)p.T * p.nq;
+  float2 ml[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int s = lane + 32 * k;
+    ml[k] = s < p.splits ? *reinterpret_cast<const float2*>(p.part_ml + ((size_t)s * stride + row) * 2)
+                         : make_float2(-INFINITY, 0.f);
+  }
+  float M = fmaxf(ml[0].x, ml[1].x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
   const float sk = p.sinks ? p.sinks[qh] * kLog2e : -INFINITY;
   M = fmaxf(M, sk);
+  float f[2], L = 0.f;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    f[k] = ml[k].x == -INFINITY ? 0.f : exp2f(ml[k].x - M);
+    L += ml[k].y * f[k];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+  if (p.sinks) L += exp2f(sk - M);
   constexpr int PER = DV / 32;
   float acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-  float L = p.sinks ? exp2f(sk - M) : 0.f;
+  const float* src = p.part_o + (size_t)row * DV + lane * PER;
+#pragma unroll 4
   for (int s = 0; s < p.splits; ++s) {
-    const size_t prow = (size_t)s * p.T * p.nq + row;
-    const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + prow * 2);
-    if (ml.x == -INFINITY) continue;
-    const float f = exp2f(ml.x - M);
-    L += ml.y * f;
-    const float* src = p.part_o + prow * DV + lane * PER;
+    const float fs = __shfl_sync(0xFFFFFFFFu, f[s >> 5], s & 31);
+    const float* v = src + (size_t)s * stride * DV;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] += src[i] * f;
+    for (int i = 0; i < PER; ++i) acc[i] = fmaf(v[i], fs, acc[i]);
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
   uint16_t* dst = p.out + (size_t)row * DV + lane * PER;
@@ -324,44 +352,53 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
   for (int i = 0; i < PER; i += 2) *reinterpret_cast<uint32_t*>(dst + i) = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
 }
 
-// One warp per (token, head) of the packed projection row [q heads | k heads | v heads]: RoPE on q and k
-// (float64 angle and rotation, rounded once to float32, then bf16), v * v_scale, k/v into the cache slot.
+// One CTA per (token, 8 heads): the token's cos/sin of every rotary pair once (float64: the angle
+// pos * theta^(-2i/rot) and its sine and cosine), then one warp per head of the packed projection row
+// [q heads | k heads | v heads]:
+// RoPE on q and k (float64 rotation, rounded once to float32, then to bf16), v * v_scale, k/v into the cache
+// slot.  (A float32 table moves near-cancelling rotations by a few bf16 ulps.)
 __global__ void __launch_bounds__(256) rope_store_kernel(RopeParams p) {
-  const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  const int heads = p.nq + p.nkv;
-  if (item >= p.T * heads) return;
-  const int t = item / heads, hd = item % heads;
+  __shared__ double2 cs_tab[128];
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head0 = blockIdx.y * (blockDim.x / 32);  // this CTA's heads: head0 + warp
   const int pos = p.pos0 + t;
-  const size_t rowlen = (size_t)p.nq * p.dqk + (size_t)p.nkv * (p.dqk + p.dv);
-  const uint16_t* row = p.qkv + (size_t)t * rowlen;
-  const uint16_t* src;
-  uint16_t* dst;
-  const int slot = pos % p.cap;
-  if (hd < p.nq) {
-    src = row + (size_t)hd * p.dqk;
-    dst = p.q + ((size_t)t * p.nq + hd) * p.dqk;
-  } else {
-    const int hk = hd - p.nq;
-    src = row + (size_t)p.nq * p.dqk + (size_t)hk * p.dqk;
-    dst = p.kc + ((size_t)hk * p.cap + slot) * p.dqk;
-    // v row: scale and store
-    const uint16_t* vs = row + (size_t)p.nq * p.dqk + (size_t)p.nkv * p.dqk + (size_t)hk * p.dv;
-    uint16_t* vd = p.vc + ((size_t)hk * p.cap + slot) * p.dv;
-    for (int i = lane; i < p.dv; i += 32) {
-      const float x = bf16_to_f32(vs[i]);
-      vd[i] = (uint16_t)(p.has_vscale ? f32_to_bf16(x * p.v_scale) : vs[i]);
-    }
-  }
   const int half = p.rot / 2;
-  for (int i = lane; i < half; i += 32) {
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
     const double inv_freq = exp(-(double)(2 * i) / (double)p.rot * p.log_base);
     double sn, cs;
     sincos((double)pos * inv_freq, &sn, &cs);
-    const double x1 = bf16_to_f32(src[i]), x2 = bf16_to_f32(src[i + half]);
-    dst[i] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * cs - x2 * sn));
-    dst[i + half] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * sn + x2 * cs));
+    cs_tab[i] = make_double2(cs, sn);
   }
-  for (int i = p.rot + lane; i < p.dqk; i += 32) dst[i] = src[i];
+  __syncthreads();
+  const int heads = p.nq + p.nkv;
+  const size_t rowlen = (size_t)p.nq * p.dqk + (size_t)p.nkv * (p.dqk + p.dv);
+  const uint16_t* row = p.qkv + (size_t)t * rowlen;
+  const int slot = pos % p.cap;
+  for (int hd = head0 + warp; hd < min(heads, head0 + (int)(blockDim.x / 32)); hd += blockDim.x / 32) {
+    const uint16_t* src;
+    uint16_t* dst;
+    if (hd < p.nq) {
+      src = row + (size_t)hd * p.dqk;
+      dst = p.q + ((size_t)t * p.nq + hd) * p.dqk;
+    } else {
+      const int hk = hd - p.nq;
+      src = row + (size_t)p.nq * p.dqk + (size_t)hk * p.dqk;
+      dst = p.kc + ((size_t)hk * p.cap + slot) * p.dqk;
+      const uint16_t* vs = row + (size_t)p.nq * p.dqk + (size_t)p.nkv * p.dqk + (size_t)hk * p.dv;
+      uint16_t* vd = p.vc + ((size_t)hk * p.cap + slot) * p.dv;
+      for (int i = lane; i < p.dv; i += 32) {
+        const float x = bf16_to_f32(vs[i]);
+        vd[i] = (uint16_t)(p.has_vscale ? f32_to_bf16(x * p.v_scale) : vs[i]);
+      }
+    }
+    for (int i = lane; i < half; i += 32) {
+      const double2 c = cs_tab[i];
+      const double x1 = bf16_to_f32(src[i]), x2 = bf16_to_f32(src[i + half]);
+      dst[i] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * c.x - x2 * c.y));
+      dst[i + half] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * c.y + x2 * c.x));
+    }
+    for (int i = p.rot + lane; i < p.dqk; i += 32) dst[i] = src[i];
+  }
 }
 
 constexpr int kNormThreads = 256;
@@ -492,7 +529,39 @@ bool attn_dims_supported(int dqk, int dv) {
   return (dqk == 192 && dv == 128) || (dqk == 128 && dv == 128) || (dqk == 64 && dv == 64);
 }
 
+// The tcgen05 kernel (attn_tc.cu) takes query tiles of 128 rows without a key split (prefill, chunked
+// prefill); MIMO_MOE_ATTN=mma keeps every call on the mma.sync kernel (a comparison knob).
+static bool attn_tc_enabled() {
+  static const int on = [] {
+    const char* v = std::getenv("MIMO_MOE_ATTN");
+    return (v && std::strcmp(v, "mma") == 0) ? 0 : 1;
+  }();
+  return on != 0;
+}
+
+int attn_auto_splits(const AttnParams& p, int num_sms) {
+  const bool tc = attn_tc_enabled() && attn_tc_supported(p);
+  const int rows_tile = tc ? 128 : kAttnRows, keys_block = tc ? 128 : kAttnKeys;
+  const int tiles = (p.T * p.G + rows_tile - 1) / rows_tile;
+  const int last = p.pos0 + p.T - 1;
+  const int first = p.window > 0 ? std::max(0, p.pos0 - p.window + 1) : 0;
+  const int nblocks = (last - (tc ? (first & ~127) : first)) / keys_block + 1;
+  // tcgen05: about one CTA per SM, at least two key blocks per split (fewer partials to merge);
+  // mma.sync: two CTAs per SM
+  const int want = tc ? (num_sms + tiles * p.nkv - 1) / (tiles * p.nkv)
+                      : (2 * num_sms + tiles * p.nkv - 1) / (tiles * p.nkv);
+  const int most = tc ? std::max(1, nblocks / 2) : nblocks;
+  return std::max(1, std::min({want, most, 64}));
+}
+
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
+  if (attn_tc_enabled() && attn_tc_supported(p)) {
+    const cudaError_t e = launch_attention_tc(p, p.status, st);
+    if (e != cudaSuccess || p.splits == 1) return e;
+    if (p.dv == 128) attn_merge_kernel<128><<<(p.T * p.nq + 7) / 8, 256, 0, st>>>(p);
+    else attn_merge_kernel<64><<<(p.T * p.nq + 7) / 8, 256, 0, st>>>(p);
+    return cudaGetLastError();
+  }
   if (p.dqk == 192 && p.dv == 128) return launch_attn_t<192, 128>(p, st);
   if (p.dqk == 128 && p.dv == 128) return launch_attn_t<128, 128>(p, st);
   if (p.dqk == 64 && p.dv == 64) return launch_attn_t<64, 64>(p, st);
@@ -500,8 +569,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
 }
 
 cudaError_t launch_rope_store(const RopeParams& p, cudaStream_t st) {
-  const int items = p.T * (p.nq + p.nkv);
-  rope_store_kernel<<<(items + 7) / 8, 256, 0, st>>>(p);
+  if (p.rot > 256) return cudaErrorInvalidValue;
+  rope_store_kernel<<<dim3(p.T, (p.nq + p.nkv + 7) / 8), 256, 0, st>>>(p);
   return cudaGetLastError();
 }
 

@@ -241,6 +241,27 @@ cudaError_t bf16_rows_map(CUtensorMap* out, const void* base, uint64_t rows, uin
   return cudaSuccess;
 }
 
+cudaError_t bf16_map3(CUtensorMap* out, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, int b1, int b2) {
+  const Key key{(uint64_t)base, d1 | (d2 << 32), d0, 9, b1 * 1024 + b2};
+  if (cached(key, out)) return cudaSuccess;
+  auto fn = encode_fn();
+  if (!fn || d0 % 64 != 0 || b1 < 1 || b1 > 256 || b2 < 1 || b2 > 256 || ((uint64_t)base & 15) != 0 ||
+      d1 >= (1ull << 32) || d2 >= (1ull << 31))
+    return cudaErrorInvalidValue;
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)b1, (cuuint32_t)b2};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  remember(key, m);
+  *out = m;
+  return cudaSuccess;
+}
+
 cudaError_t rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows) {
   const Key key{(uint64_t)base, rows, row_bytes, 3, box_rows};
   if (cached(key, out)) return cudaSuccess;

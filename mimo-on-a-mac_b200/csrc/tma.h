@@ -36,6 +36,9 @@ cudaError_t rows_map3(CUtensorMap* out, const void* base, uint64_t rows, uint64_
 cudaError_t sf_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
 // bf16 matrix map [rows][cols], box [64 values, box_rows], 128B swizzle; rows past the end read 0.
 cudaError_t bf16_rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t cols, int box_rows);
+// 3-D bf16 tensor [d2][d1][d0] (d0 contiguous), box [64 values, b1, b2], 128B swizzle: lands as b1 * b2
+// consecutive 128-byte rows (d1 fastest); coordinates past an extent read 0.
+cudaError_t bf16_map3(CUtensorMap* out, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, int b1, int b2);
 // Byte-matrix map [rows][row_bytes], box [128 bytes, box_rows], 128B swizzle.
 cudaError_t rows_map(CUtensorMap* out, const void* base, uint64_t rows, uint64_t row_bytes, int box_rows);
 // Packed rows (e2m1, two values per byte: pool weights [rows][K/2] or activation terms) read 64 bytes

@@ -14,7 +14,7 @@ INCLUDE = PKG.parent.parent / "include"
 LIB = PKG / "libmimo_moe.so"
 LIB_TESTKIT = PKG / "libmimo_moe_testkit.so"
 SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu",
-           "norm.cu", "ep_plan.cu", "layer.cu", "loader.cpp"]
+           "norm.cu", "ep_plan.cu", "layer.cu", "attn_tc.cu", "loader.cpp"]
 TESTKIT_SOURCES = ["synth.cu", "testkit.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -34,7 +34,7 @@ def _stale() -> bool:
     if not LIB.exists() or not LIB_TESTKIT.exists():
         return True
     t = min(LIB.stat().st_mtime, LIB_TESTKIT.stat().st_mtime)
-    deps = sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
+    deps = sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h")) + [Path(__file__)]
     return any(d.stat().st_mtime > t for d in deps if d.exists())
 
 

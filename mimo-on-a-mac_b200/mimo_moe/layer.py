@@ -77,8 +77,10 @@ class KVCache:
 
     @classmethod
     def for_layer(cls, cfg: AttentionConfig, max_len: int, max_chunk: int = 4096, device=None) -> "KVCache":
+        """Capacity rounded up to a multiple of 128 (the tcgen05 attention reads 128-key blocks that must not
+        wrap around the ring)."""
         cap = max_len if cfg.window == 0 else min(max_len, cfg.window + max_chunk - 1)
-        return cls(cfg, cap, device)
+        return cls(cfg, -(-cap // 128) * 128, device)
 
 
 def rope_store(qkv: torch.Tensor, cfg: AttentionConfig, cache: KVCache, pos0: int,
@@ -98,10 +100,12 @@ def rope_store(qkv: torch.Tensor, cfg: AttentionConfig, cache: KVCache, pos0: in
 
 
 def attention(q: torch.Tensor, cache: KVCache, cfg: AttentionConfig, pos0: int, sinks: Optional[torch.Tensor] = None,
-              splits: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              splits: int = 0, out: Optional[torch.Tensor] = None,
+              status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """mlx fast.scaled_dot_product_attention(q, k, v, scale=head_dim^-0.5, mask, sinks) over the cache for the
-    T queries at positions pos0..pos0+T-1 (causal; sliding window when cfg.window > 0).
-    Returns bf16 [T, n_heads, v_head_dim]."""
+    T queries at positions pos0..pos0+T-1 (causal; sliding window when cfg.window > 0).  Query tiles of 128
+    rows run on the tcgen05 kernel (cache capacity a multiple of 128), decode-sized calls on the split-key
+    mma.sync kernel.  Returns bf16 [T, n_heads, v_head_dim]."""
     _need_cuda(q, "q")
     T = q.shape[0]
     dev = q.device
@@ -115,7 +119,7 @@ def attention(q: torch.Tensor, cache: KVCache, cfg: AttentionConfig, pos0: int, 
     check(L.mimo_moe_layer_attention(q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), _ptr(sinks), T,
                                      cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.v_head_dim, float(cfg.scale),
                                      cfg.window, int(pos0), cache.cap, int(splits), o.data_ptr(), ws.data_ptr(),
-                                     ws.numel(), _stream()), "attention")
+                                     ws.numel(), _ptr(status), _stream()), "attention")
     return o
 
 

@@ -66,6 +66,13 @@ CASES = [
     ("swa", {}, 8, 5000, 135, 0),
     ("swa", {}, 8, 77, 135, 1),
     ("full", {"head_dim": 128, "v_head_dim": 128, "n_kv_heads": 8, "rotary_dim": 128}, 40, 90, 256, 0),
+    # query tiles of 128 rows, no key split, cache capacity a multiple of 128: the tcgen05 kernel
+    ("full", {}, 2048, 0, 2048, 1),
+    ("full", {}, 37, 500, 640, 1),
+    ("swa", {}, 300, 0, 512, 1),
+    ("swa", {}, 200, 1000, 384, 1),
+    ("full", {"head_dim": 128, "v_head_dim": 128, "n_kv_heads": 8, "rotary_dim": 128}, 40, 90, 256, 1),
+    ("full", {"head_dim": 128, "v_head_dim": 128, "n_heads": 16, "n_kv_heads": 16, "rotary_dim": 128}, 300, 7, 512, 1),
     ("full", {"head_dim": 64, "v_head_dim": 64, "n_heads": 8, "n_kv_heads": 8, "rotary_dim": 32}, 5, 700, 1024, 0),
 ]
 
@@ -88,6 +95,24 @@ def test_attention_matches_oracle(gpu, kind, over, T, pos0, cap, splits):
     assert np.isfinite(got).all()
     assert rel(got, ref) <= 1e-2
     assert np.abs(got - ref).mean() <= 3e-3 * np.abs(ref).mean()
+
+
+def test_tensor_core_attention_status_stays_clear(gpu):
+    """The tcgen05 kernel's bounded waits complete on an ordinary prefill call (status word still 0) and the
+    output matches the split-key mma.sync kernel's on the same inputs (rel_err <= 1e-2)."""
+    from mimo_moe.layer import attention
+    cfg = _cfg("swa")
+    g = torch.Generator().manual_seed(5)
+    T, cap = 512, 768
+    k_all, v_all = rnd(g, 8, T, 192), rnd(g, 8, T, 128)
+    cache = _cache_from_positions(cfg, k_all, v_all, cap, gpu)
+    q = rnd(g, T, 64, 192).to(gpu)
+    sinks = torch.randn(64, generator=g)
+    status = torch.zeros(1, dtype=torch.int32, device=gpu)
+    tc = f(attention(q, cache, cfg, 0, sinks, splits=1, status=status))
+    mma = f(attention(q, cache, cfg, 0, sinks, splits=2))
+    assert int(status.item()) == 0
+    assert rel(tc, mma) <= 1e-2
 
 
 def test_attention_split_counts_agree(gpu):

@@ -98,20 +98,20 @@ def test_layer_entry_points_reject_bad_arguments_without_a_device():
     EINVAL = 1
     p = 1 << 20  # never dereferenced: every call below fails its host-side checks first
     # unsupported head dims
-    assert L.mimo_moe_layer_attention(p, p, p, None, 1, 64, 4, 96, 128, 0.1, 0, 0, 16, 1, p, None, 0, None) == EINVAL
+    assert L.mimo_moe_layer_attention(p, p, p, None, 1, 64, 4, 96, 128, 0.1, 0, 0, 16, 1, p, None, 0, None, None) == EINVAL
     # heads not a multiple of the kv heads
-    assert L.mimo_moe_layer_attention(p, p, p, None, 1, 63, 4, 192, 128, 0.1, 0, 0, 16, 1, p, None, 0, None) == EINVAL
+    assert L.mimo_moe_layer_attention(p, p, p, None, 1, 63, 4, 192, 128, 0.1, 0, 0, 16, 1, p, None, 0, None, None) == EINVAL
     # full attention: pos0 + T beyond the cache
-    assert L.mimo_moe_layer_attention(p, p, p, None, 4, 64, 4, 192, 128, 0.1, 0, 14, 16, 1, p, None, 0, None) == EINVAL
+    assert L.mimo_moe_layer_attention(p, p, p, None, 4, 64, 4, 192, 128, 0.1, 0, 14, 16, 1, p, None, 0, None, None) == EINVAL
     # sliding window: window + T - 1 > cap
     assert L.mimo_moe_layer_attention(p, p, p, None, 8, 64, 8, 192, 128, 0.1, 128, 500, 130, 1, p, None, 0,
-                                      None) == EINVAL
+                                      None, None) == EINVAL
     # explicit splits without a workspace
     assert L.mimo_moe_layer_attention(p, p, p, None, 1, 64, 4, 192, 128, 0.1, 0, 100, 4096, 4, p, None, 0,
-                                      None) == EINVAL
+                                      None, None) == EINVAL
     # unaligned pointer
     assert L.mimo_moe_layer_attention(p + 2, p, p, None, 1, 64, 4, 192, 128, 0.1, 0, 0, 16, 1, p, None, 0,
-                                      None) == EINVAL
+                                      None, None) == EINVAL
     assert L.mimo_moe_layer_rope_store(p, 8, 64, 4, 192, 128, 65, 1e4, 0.0, 0, 16, p, p, p, None) == EINVAL  # odd rot
     assert L.mimo_moe_layer_rope_store(p, 32, 64, 4, 192, 128, 64, 1e4, 0.0, 0, 16, p, p, p, None) == EINVAL  # T>cap
     assert L.mimo_moe_layer_swiglu(p, 1, 12, p, None) == EINVAL
