@@ -469,7 +469,7 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                     "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
                     "algorithmic_bytes_per_step": step_bytes,
-                    "attention_kernel": {"kernel": "attn_kernel<192,128> + attn_merge_kernel (split keys)",
+                    "attention_kernel": {"kernel": "attn_tc_kernel<192,128> with key splits + attn_merge_kernel",
                                          "bytes": kv_bytes, "ms": acc["attention"],
                                          "achieved_gbs": kv_bytes / (acc["attention"] * 1e-3) / 1e9,
                                          "frac": kv_bytes / (acc["attention"] * 1e-3) / 1e9 / hbm}}
@@ -477,7 +477,8 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
         pairs = T * (T + 1) // 2
         flops = 2 * pairs * cfg.n_heads * (cfg.head_dim + cfg.v_head_dim)
         tf = flops / (acc["attention"] * 1e-3) / 1e12
-        roofline = {"kernel": "attn_kernel<192,128> (causal prefill attention, bf16 mma.sync, float32 softmax)",
+        roofline = {"kernel": "attn_tc_kernel<192,128> (causal prefill attention, tcgen05 kind::f16, TMEM "
+                              "accumulators, float32 softmax)",
                     "bound": "tensor", "achieved": tf, "peak": tflops_peak, "unit": "TFLOP/s",
                     "frac": tf / tflops_peak, "peak_kind": f"{peak_kind} bf16_tflops_sustained",
                     "traffic": None, "algorithmic_flops_per_launch": flops}
@@ -500,7 +501,7 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
         "metric": f"decoder-layer tok/s ({workload})", "value": T * steps / (ms * 1e-3), "unit": "tok/s",
         "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": step_ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 attention (mma.sync, f32 softmax) + e2m1 x e4m3 MoE (tcgen05)",
+        "dtype": "bf16 attention (tcgen05, f32 softmax) + e2m1 x e4m3 MoE (tcgen05)",
         "data": "synthetic (random-init attention weights N(0,0.02), random bf16 KV cache, seeded MXFP4 pool)",
         "config": workload_config(workload, 1, NE), "mean_distinct_experts": Um, "roofline": roofline, "clocks": clk,
         "e2e": {"value": T * steps / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,

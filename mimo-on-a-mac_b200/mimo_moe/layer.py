@@ -23,7 +23,7 @@ from typing import Optional, Union
 import torch
 
 from ._lib import check, lib
-from .ops import ExpertPools, _need_cuda, _ptr, _stream, moe_block, rmsnorm, workspace
+from .ops import ExpertPools, _need_cuda, _ptr, _stream, moe_block, read_status, rmsnorm, workspace
 
 
 @dataclass(frozen=True)
@@ -189,15 +189,25 @@ class DenseMLP:
 
 
 class MoEMLP:
-    """An MoE layer's MLP: the router + resident experts of this library's MoE block (model.py:302-336)."""
+    """An MoE layer's MLP: the router + resident experts of this library's MoE block (model.py:302-336).
+    The block's device status word lives with the layer (zeroed once; the first error stays until
+    check_status() reads and clears it), so a step launches no per-call fill."""
 
     def __init__(self, router_weight: torch.Tensor, bias: Optional[torch.Tensor], pools: ExpertPools):
         self.router_weight = router_weight.to(torch.bfloat16).contiguous()
         self.bias = None if bias is None else bias.to(torch.float32).contiguous()
         self.pools = pools
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.router_weight.device)
 
     def __call__(self, r: torch.Tensor) -> torch.Tensor:
-        return moe_block(r, self.router_weight, self.bias, self.pools)
+        return moe_block(r, self.router_weight, self.bias, self.pools, status=self.status)
+
+    def check_status(self) -> None:
+        """Synchronise on the status word; raise like the reference for a bad route, then clear it."""
+        try:
+            read_status(self.status, "MoE layer")
+        finally:
+            self.status.zero_()
 
 
 class DecoderLayer:

@@ -235,6 +235,7 @@ def test_moe_decoder_layer_composition_and_oracle(gpu):
         y_ref = O.moe_layer(f(s["r2"]), opool, idx.cpu().numpy(), w.cpu().numpy())
         assert O.rel_err(f(y), y_ref) <= 1e-2
         assert torch.equal(s["out"].view(torch.int16), add(s["h"], s["y"]).view(torch.int16))
+    layer.mlp.check_status()   # no route error was recorded
 
 
 def test_decode_equals_prefill_two_layers(gpu):
