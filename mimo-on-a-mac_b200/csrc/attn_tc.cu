@@ -5,13 +5,15 @@
 // writes unnormalised partials that layer.cu's merge kernel folds with the sink.
 //
 // One CTA = 128 query rows of one kv head (the G = n_heads / n_kv_heads heads of 128 / G consecutive tokens,
-// token-major, so one K/V block serves the whole GQA group), key blocks of 128, 6 warps:
-//   warp 4 (one thread)  TMA producer: the Q tile once (head_dim / 64 boxes of [64 dims x G heads x 128/G
+// token-major, so one K/V block serves the whole GQA group), key blocks of 128, 10 warps:
+//   warp 8 (one thread)  TMA producer: the Q tile once (head_dim / 64 boxes of [64 dims x G heads x 128/G
 //                        tokens]), then K_j and V_j of every block through a ring of 3 shared-memory slots;
-//   warp 5 (one thread)  MMA issuer: S_j = Q K_j^T (M 128, N 128, K 16 per instruction, kind::f16, f32
+//   warp 9 (one thread)  MMA issuer: S_j = Q K_j^T (M 128, N 128, K 16 per instruction, kind::f16, f32
 //                        accumulate) into one of two TMEM buffers; O += P_j V_j (V read as an MN-major
 //                        operand) into the TMEM output; commits release ring slots and signal the softmax;
-//   warps 0-3            softmax, one thread per query row (TMEM lane = row): S_j from TMEM, mask, running
+//   warps 0-7            softmax, two threads per query row (TMEM lane = row; warps 0-3 take columns 0-63,
+//                        warps 4-7 columns 64-127, the row maximum exchanged through shared memory behind
+//                        named barriers): S_j from TMEM, mask, running
 //                        max in the exp2 domain, P_j = bf16(exp2(s - m)) into shared memory (128B-swizzled
 //                        K-major rows, the layout the MMA reads), the row sum from the float32 P; the TMEM
 //                        output is rescaled only when a row's maximum grows by more than 2^8 (the stale
@@ -31,7 +33,7 @@ namespace mimo {
 
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // warps 0-7 softmax (row, column half), 8 TMA producer, 9 MMA issuer
 constexpr int kRing = 3;
 
 __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -82,7 +84,8 @@ struct TcShape {
   static constexpr uint32_t QB = 128u * DQK * 2, KB = 128u * DQK * 2, VB = 128u * DV * 2;
   static constexpr uint32_t SLOT = KB > VB ? KB : VB;
   static constexpr uint32_t PB = 128u * 128 * 2;
-  static constexpr uint32_t SMEM = 2048 + QB + kRing * SLOT + PB;  // barriers + alignment slack + tiles
+  // barriers (1 KB), the row-maximum exchange (1 KB), alignment slack (1 KB), tiles
+  static constexpr uint32_t SMEM = 3072 + QB + kRing * SLOT + PB;
 };
 
 template <int DQK, int DV>
@@ -99,7 +102,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
   uint64_t* pv_done = p_full + 1;
   uint64_t* drain = pv_done + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 32);
-  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + 1024) + 1023) & ~(uintptr_t)1023);
+  float* xchg = reinterpret_cast<float*>(smem + 1024);  // [2 halves][128 rows]
+  uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)(smem + 2048) + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = base;
   uint8_t* sRing = base + S::QB;
   uint8_t* sP = sRing + kRing * S::SLOT;
@@ -127,14 +131,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
+      mbar_init(&s_free[i], 256);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 256);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     mbar_fence_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(tslot, 512);
     tc::tmem_relinquish();
   }
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
   const uint32_t tO = tbase + 256;
   bool ok = true;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {  // ---------------------------------------------------------------- TMA producer
       tma_prefetch_map(&p.qmap);
       tma_prefetch_map(&p.kmap);
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
         if (!mbar_wait(&ring_full[li % kRing], (uint32_t)((li / kRing) & 1))) ok = false;
       if (!mbar_wait(q_full, 0)) ok = false;
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {  // ----------------------------------------------------------------- MMA issuer
       const uint32_t idesc_s = tc::idesc_bf16(128, 128);
       const uint32_t idesc_o = tc::idesc_bf16(128, DV) | (1u << 16);  // B = V, MN-major
@@ -232,55 +236,62 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
       tc::tc_commit(drain);  // every MMA issued above has completed once this arrives
       if (!mbar_wait(drain, 0)) ok = false;
     }
-  } else {  // ------------------------------------------------------------------- softmax, one row each
-    const int r = threadIdx.x;
+  } else {  // ---------------------------------------- softmax: thread = (row, column half), warpgroup = half
+    const int h = warp >> 2;                 // columns [64 h, 64 h + 64) of S, P and O
+    const int r = threadIdx.x & 127;         // query row = TMEM lane
     const int gr = r0 + r;
     const bool row_ok = gr < rows;
     const int t = row_ok ? gr / G : t_last;
     const int qpos = p.pos0 + t;
     const int lo = p.window > 0 ? qpos - p.window + 1 : 0;  // first visible key position (may be negative)
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float sl2 = p.scale_log2;
-    float m_ref = -INFINITY, l = 0.f;
-    const uint32_t prow = smem_u32(sP) + (uint32_t)r * 128u;
+    float m_ref = -INFINITY, l = 0.f;        // l: this half's share of the row sum
+    const uint32_t prow = smem_u32(sP) + (uint32_t)h * 16384u + (uint32_t)r * 128u;
+    // Both halves of a row must use one maximum: each writes its half's maximum, a named barrier over
+    // the 256 softmax threads, each reads the other's.  A second barrier before the next write keeps
+    // the single buffer free of races.  No thread leaves the loop early (the barriers count on all
+    // 256); after a timed-out wait the loop runs on without waiting and the status records it.
+    auto exchange = [&](float mine) -> float {
+      asm volatile("bar.sync 1, 256;\n" ::: "memory");
+      xchg[h * 128 + r] = mine;
+      asm volatile("bar.sync 2, 256;\n" ::: "memory");
+      return xchg[(h ^ 1) * 128 + r];
+    };
     for (int j = 0; j < nblocks; ++j) {
       const int sb = j & 1;
-      ok = mbar_wait(&s_full[sb], (uint32_t)((j >> 1) & 1));
-      if (!__all_sync(0xFFFFFFFFu, ok)) {
-        ok = false;
-        break;
-      }
+      if (ok) ok = mbar_wait(&s_full[sb], (uint32_t)((j >> 1) & 1));
+      ok = __all_sync(0xFFFFFFFFu, ok);
       tc::tc_fence_after();
-      float s[8][16];
+      float s[4][16];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) tc::tmem_ld<16>(tS[sb] + lane_off + c * 16, s[c]);
+      for (int c = 0; c < 4; ++c) tc::tmem_ld<16>(tS[sb] + lane_off + h * 64 + c * 16, s[c]);
       tc::tmem_wait_ld();
       tc::tc_fence_before();
       mbar_arrive(&s_free[sb]);
       // The raw-score maximum (the scale is positive, so it orders the scaled scores alike); only blocks
       // that reach past a row's visible range mask by column.
-      const int kp0 = kbase + (b_begin + j) * 128;
-      const int c_lo = lo - kp0, c_hi = qpos - kp0;  // visible columns [c_lo, c_hi]
-      if (c_lo > 0 || c_hi < 127) {
+      const int kp0 = kbase + (b_begin + j) * 128 + h * 64;
+      const int c_lo = lo - kp0, c_hi = qpos - kp0;  // visible columns [c_lo, c_hi] of this half
+      if (c_lo > 0 || c_hi < 63) {
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int col = c * 16 + e;
             if (col < c_lo || col > c_hi) s[c][e] = -INFINITY;
           }
       }
-      float mxa[8];
+      float mxa[4];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float a = fmaxf(s[c][0], s[c][1]);
 #pragma unroll
         for (int e = 2; e < 16; ++e) a = fmaxf(a, s[c][e]);
         mxa[c] = a;
       }
-      const float mraw = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                               fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      const float mx = mraw * sl2;
+      const float mine = fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3]));
+      const float mx = fmaxf(mine, exchange(mine)) * sl2;
       float alpha = 1.f;
       bool rescale = false;
       if (mx > -INFINITY) {
@@ -293,64 +304,59 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
         }
       }
       // P = bf16(2^(s * scale * log2e - m)): one FFMA and one ex2 per score (2^-inf = 0 for masked
-      // scores; a row with nothing visible yet uses m = 0), one conversion per pair; the row sum
-      // takes the float32 values in eight independent partial sums
+      // scores; a row with nothing visible yet uses m = 0), one conversion per pair; the half's row sum
+      // takes the float32 values in four independent partial sums
       const float nm = (m_ref == -INFINITY) ? 0.f : -m_ref;
-      uint32_t pk[64];
-      float rsa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];
+      float rsa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float p0 = ex2_approx(fmaf(s[(2 * i) >> 4][(2 * i) & 15], sl2, nm));
         const float p1 = ex2_approx(fmaf(s[(2 * i + 1) >> 4][(2 * i + 1) & 15], sl2, nm));
-        rsa[i & 7] += p0 + p1;
+        rsa[i & 3] += p0 + p1;
         pk[i] = pack_bf16x2_rn(p0, p1);
       }
-      const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
-      l = l * alpha + rs;
+      l = l * alpha + ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3]));
       if (j > 0) {  // P_{j-1} V_{j-1} has completed: the P buffer is free and O is stable
-        ok = mbar_wait(pv_done, (uint32_t)((j - 1) & 1));
-        if (!__all_sync(0xFFFFFFFFu, ok)) {
-          ok = false;
-          break;
-        }
+        if (ok) ok = mbar_wait(pv_done, (uint32_t)((j - 1) & 1));
+        ok = __all_sync(0xFFFFFFFFu, ok);
         tc::tc_fence_after();
       }
       if (__any_sync(0xFFFFFFFFu, rescale)) {  // warp-collective TMEM access; alpha = 1 for the other rows
 #pragma unroll
-        for (int c = 0; c < DV; c += 16) {
+        for (int c = 0; c < DV / 2; c += 16) {
           float o[16];
-          tc::tmem_ld<16>(tO + lane_off + c, o);
+          tc::tmem_ld<16>(tO + lane_off + h * (DV / 2) + c, o);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 16; ++e) o[e] *= alpha;
-          tmem_st16(tO + lane_off + c, o);
+          tmem_st16(tO + lane_off + h * (DV / 2) + c, o);
         }
         tmem_wait_st();
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t addr = prow + c * 16384u + (uint32_t)((u ^ (r & 7)) << 4);
-          st_shared_v4(addr, pk[c * 32 + u * 4], pk[c * 32 + u * 4 + 1], pk[c * 32 + u * 4 + 2], pk[c * 32 + u * 4 + 3]);
-        }
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t addr = prow + (uint32_t)((u ^ (r & 7)) << 4);
+        st_shared_v4(addr, pk[u * 4], pk[u * 4 + 1], pk[u * 4 + 2], pk[u * 4 + 3]);
+      }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && nblocks > 0) {
-      ok = mbar_wait(pv_done, (uint32_t)((nblocks - 1) & 1));
+    if (nblocks > 0) {
+      if (ok) ok = mbar_wait(pv_done, (uint32_t)((nblocks - 1) & 1));
       ok = __all_sync(0xFFFFFFFFu, ok);
     }
+    const float l_row = l + exchange(l);  // both halves' sums (every softmax thread takes part)
+    const int qh = hk * G + (row_ok ? gr % G : 0);
+    tc::tc_fence_after();
     if (ok && p.splits > 1) {  // unnormalised partial (m in log2 units, l, O) for the merge kernel
-      tc::tc_fence_after();
-      const int qh = hk * G + (row_ok ? gr % G : 0);
-      const size_t prow = (size_t)blockIdx.z * p.T * p.nq + (size_t)t * p.nq + qh;
-      float* dst = p.part_o + prow * DV;
+      const size_t prow_g = (size_t)blockIdx.z * p.T * p.nq + (size_t)t * p.nq + qh;
+      float* dst = p.part_o + prow_g * DV + h * (DV / 2);
 #pragma unroll
-      for (int c = 0; c < DV; c += 16) {
+      for (int c = 0; c < DV / 2; c += 16) {
         float o[16];
-        tc::tmem_ld<16>(tO + lane_off + c, o);
+        tc::tmem_ld<16>(tO + lane_off + h * (DV / 2) + c, o);
         tc::tmem_wait_ld();
         if (row_ok) {
           float4* d4 = reinterpret_cast<float4*>(dst + c);
@@ -360,28 +366,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      if (row_ok) *reinterpret_cast<float2*>(p.part_ml + prow * 2) = make_float2(m_ref, l);
+      if (row_ok && h == 0) *reinterpret_cast<float2*>(p.part_ml + prow_g * 2) = make_float2(m_ref, l_row);
     } else if (ok) {
-      tc::tc_fence_after();
-      const int qh = hk * G + (row_ok ? gr % G : 0);
       float f;
       if (p.sinks) {
         const float sk = p.sinks[qh] * 1.4426950408889634f;
         const float Mn = fmaxf(m_ref, sk);
         const float sc = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - Mn);
-        f = sc / (l * sc + exp2f(sk - Mn));
+        f = sc / (l_row * sc + exp2f(sk - Mn));
       } else {
-        f = l > 0.f ? 1.f / l : 0.f;
+        f = l_row > 0.f ? 1.f / l_row : 0.f;
       }
-      uint16_t* dst = p.out + ((size_t)t * p.nq + qh) * DV;
+      uint16_t* dst = p.out + ((size_t)t * p.nq + qh) * DV + h * (DV / 2);
 #pragma unroll
-      for (int c = 0; c < DV; c += 16) {
+      for (int c = 0; c < DV / 2; c += 16) {
         float o[16];
-        tc::tmem_ld<16>(tO + lane_off + c, o);
+        tc::tmem_ld<16>(tO + lane_off + h * (DV / 2) + c, o);
         tc::tmem_wait_ld();
         uint32_t w[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) w[e] = f32_to_bf16(o[2 * e] * f) | (f32_to_bf16(o[2 * e + 1] * f) << 16);
+        for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2_rn(o[2 * e] * f, o[2 * e + 1] * f);
         if (row_ok) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c);
           d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -393,7 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
   if (!ok && p.status) set_status(p.status, MIMO_ETIMEOUT);
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 512);
   }
