@@ -37,7 +37,8 @@ DOWN_BYTES = H * I // 2 + H * I // 32
 WORKLOADS = {"decode1": (1, "free"), "decode2": (2, "free"), "decode4": (4, "free"), "decode8": (8, "free"),
              "decode8_overlap": (8, "overlap"), "prefill2048": (2048, "free"), "prefill16384z": (16384, "zipf"),
              "stack48_decode1": (1, "free"), "stack48_decode8": (8, "free"),
-             "layer_decode1": (1, "free"), "layer_decode8": (8, "free"), "layer_prefill2048": (2048, "free")}
+             "layer_decode1": (1, "free"), "layer_decode8": (8, "free"), "layer_prefill2048": (2048, "free"),
+             "model48_decode1": (1, "free"), "model48_decode8": (8, "free")}
 NESTED = ("decode1", "decode8_overlap", "prefill2048")   # measured beside the default headline on one GPU
 # the whole decoder layer around the MoE block (attention with a 4096-token context, then the MoE block),
 # measured beside the headline too
@@ -175,6 +176,12 @@ def workload_config(workload: str, world: int = 1, NE: int = E) -> dict:
                   if T <= 8 else f"inputs > L2: every step streams the whole {NE * EXPERT_BYTES / 1e9:.2f} GB pool")}
     if workload.startswith("stack"):
         cfg["layers"] = STACK_LAYERS
+    if workload.startswith("model"):
+        cfg["layers"] = STACK_LAYERS
+        cfg["model"] = ("48 decoder layers (embedding, final norm and lm_head excluded): layer 0 dense MLP "
+                        "(16384), layers 1-47 MoE; full attention (4 kv heads) on every sixth layer from 0, "
+                        "128-token sliding window with sinks (8 kv heads) elsewhere; 64 q heads x 192, v 128")
+        cfg["context"] = LAYER_CONTEXT
     if workload.startswith("layer"):
         cfg["layer"] = ("MoE decoder layer: RMSNorm, full-attention block (64 q heads x 192, 4 kv heads, v 128, "
                         "64 rotary dims, value scale 0.707), residual + RMSNorm, MoE block, residual")
@@ -827,6 +834,139 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, cpu_budget: float
     return res
 
 
+def bench_model(args):
+    """The decoder stack of a whole MiMo-like model on one GPU: one decode step = B tokens at position 4096
+    through 48 decoder layers (attention over each layer's cache, then the dense MLP or the MoE block), the
+    step replayed as one CUDA graph.  Random-init bf16 attention and dense weights drawn on the device, the
+    MoE layers' pools and routers seeded per layer like the stack workloads, random bf16 KV caches."""
+    import torch
+    import mimo_moe
+    from mimo_moe import synthetic
+    from mimo_moe.ep import GraphedStep
+    from mimo_moe.layer import (DecoderLayer, DecoderStack, MoEMLP, mimo_full_attention, mimo_sliding_attention,
+                                synthetic_attention, synthetic_dense_mlp)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("the model workloads run on one GPU")
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    B, L = WORKLOADS[args.workload][0], args.layers
+    layers, routers = [], []
+    for l in range(L):
+        cfg = mimo_full_attention(v_scale=0.707) if l % 6 == 0 else mimo_sliding_attention(v_scale=0.707)
+        attn = synthetic_attention(cfg, seed=100 + l, device=dev, on_device=True)
+        if l == 0:
+            mlp = synthetic_dense_mlp(inter=16384, seed=99, device=dev, on_device=True)
+            routers.append(None)
+        else:
+            W = synthetic.router_weight(seed=1 + 1000 * l).to(dev)
+            mlp = MoEMLP(W, None, mimo_moe.ExpertPools.synthetic(E, seed=0, layer=l, device=dev))
+            routers.append(W)
+        layers.append(DecoderLayer(attn, mlp, None, None, eps=1e-5))
+    stack = DecoderStack(layers, max_len=LAYER_CONTEXT + 16, max_chunk=B)
+    g = torch.Generator(device=dev).manual_seed(9)
+    for c in stack.caches:
+        c.k.normal_(generator=g)
+        c.v.normal_(generator=g)
+    torch.cuda.synchronize()
+    xs = [synthetic.hidden(B, seed=2 + 1000 * i).to(dev) for i in range(NBATCH)]
+
+    def block(x):
+        return stack.at(LAYER_CONTEXT)(x)
+
+    gstep = GraphedStep(block, B, H, dev)
+    for i in range(max(3, args.warmup)):
+        gstep(xs[i % NBATCH])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        gstep(xs[i % NBATCH])
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    # one eager pass per batch: every MoE layer's routes -> distinct experts per step (summed over layers)
+    U = []
+
+    def tracer(l):
+        def f(d):
+            idx, _ = mimo_moe.router(d["r2"], routers[l], None)
+            U.append(int(torch.unique(idx).numel()))
+        return f
+    for l, layer in enumerate(layers):
+        layer.trace = tracer(l) if routers[l] is not None else None
+    for i in range(NBATCH):
+        block(xs[i])
+    for layer in layers:
+        layer.trace = None
+    for layer in layers[1:]:
+        layer.mlp.check_status()
+    torch.cuda.synchronize()
+    hbm, _, peak_kind = peaks()
+    attn_bytes = sum((l.attn.w_qkv.numel() + l.attn.w_o.numel()) * 2 for l in layers)
+    kv_bytes = sum(c.n_kv_heads * ((min(LAYER_CONTEXT + B, c.window + B - 1) if c.window else LAYER_CONTEXT + B)
+                                   * (c.head_dim + c.v_head_dim) * 2) for c in (l.attn.cfg for l in layers))
+    dense_bytes = (layers[0].mlp.w_gate_up.numel() + layers[0].mlp.w_down.numel()) * 2
+    step_U = sum(U) / NBATCH
+    step_bytes = attn_bytes + kv_bytes + dense_bytes + step_U * EXPERT_BYTES + (L - 1) * E * H * 2
+    step_ms = ms / args.steps
+    achieved = step_bytes / (step_ms * 1e-3) / 1e9
+
+    xh = [x.cpu().pin_memory() for x in xs]
+    yh = torch.empty(B, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+    e2e_steps = max(3, min(args.steps, 40))
+
+    def e2e_step(i):
+        xd.copy_(xh[i % NBATCH], non_blocking=True)
+        yh.copy_(block(xd), non_blocking=True)
+    e2e_step(0)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1)
+
+    def g_step(i):
+        xd.copy_(xh[i % NBATCH], non_blocking=True)
+        yh.copy_(gstep(xd), non_blocking=True)
+    t0.record()
+    for i in range(args.steps):
+        g_step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    g_ms = t0.elapsed_time(t1)
+    res = {
+        "metric": f"decoder-stack tok/s ({args.workload})", "value": B * args.steps / (ms * 1e-3), "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 attention (tcgen05, f32 softmax) + e2m1 x e4m3 MoE (tcgen05)",
+        "data": "synthetic (random-init attention / dense weights, random bf16 KV caches, seeded MXFP4 pools)",
+        "config": workload_config(args.workload),
+        "distinct_experts_per_step": step_U,
+        "roofline": {"kernel": "whole decode step (attention weights, KV caches, dense MLP, routers, distinct experts)",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None, "algorithmic_bytes_per_step": step_bytes},
+        "clocks": clk,
+        "e2e": {"value": B * e2e_steps / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": B * H * 2,
+                "d2h_bytes_per_step": B * H * 2,
+                "how": "eager DecoderStack call per step (host launches of every layer), pinned host x in, y out",
+                "value_graph_replay": B * args.steps / (g_ms * 1e-3)},
+        # per layer: rmsnorm, RoPE + cache, attention + split merge, add + RMSNorm, add; per MoE layer the
+        # block's five (route logits, select, gate/up, down, combine); the dense layer's SwiGLU
+        "gpu_launches": (L * 6 + (L - 1) * 5 + 1) * args.steps,
+        "cpu_baseline": None,
+    }
+    print(json.dumps(res))
+
+
 def bench_stack(args):
     """one decode step = B tokens per GPU through L MoE layers (RMSNorm, unit weight,
     between layers), experts sharded 256/N per GPU for every layer, the peer-memory exchange per layer
@@ -1015,6 +1155,8 @@ def main():
         return run_reference(args)
     if args.workload.startswith("stack"):
         return bench_stack(args)
+    if args.workload.startswith("model"):
+        return bench_model(args)
     import torch.distributed as dist
     ctx = Ctx(args)
     if args.workload.startswith("layer"):

@@ -352,52 +352,62 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
   for (int i = 0; i < PER; i += 2) *reinterpret_cast<uint32_t*>(dst + i) = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
 }
 
-// One CTA per (token, 8 heads): the token's cos/sin of every rotary pair once (float64: the angle
-// pos * theta^(-2i/rot) and its sine and cosine), then one warp per head of the packed projection row
-// [q heads | k heads | v heads]:
-// RoPE on q and k (float64 rotation, rounded once to float32, then to bf16), v * v_scale, k/v into the cache
-// slot.  (A float32 table moves near-cancelling rotations by a few bf16 ulps.)
-__global__ void __launch_bounds__(256) rope_store_kernel(RopeParams p) {
+// A grid of up to 4 CTAs per SM walks the tokens: per token the CTA computes the cos/sin of every rotary pair
+// once (float64: the angle pos * theta^(-2i/rot) and its sine and cosine), then its 16 warps take the heads of
+// the packed projection row [q heads | k heads | v heads]: RoPE on q and k (float64 rotation, rounded once to
+// float32, then to bf16), v * v_scale, k/v into the cache slot; the value rows and the dims past the rotary
+// ones move as bf16 pairs (every row offset is an even number of values).  (A float32 table moves
+// near-cancelling rotations by a few bf16 ulps.)
+__global__ void __launch_bounds__(512) rope_store_kernel(RopeParams p) {
   __shared__ double2 cs_tab[128];
-  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head0 = blockIdx.y * (blockDim.x / 32);  // this CTA's heads: head0 + warp
-  const int pos = p.pos0 + t;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = p.rot / 2;
-  for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const double inv_freq = exp(-(double)(2 * i) / (double)p.rot * p.log_base);
-    double sn, cs;
-    sincos((double)pos * inv_freq, &sn, &cs);
-    cs_tab[i] = make_double2(cs, sn);
-  }
-  __syncthreads();
   const int heads = p.nq + p.nkv;
   const size_t rowlen = (size_t)p.nq * p.dqk + (size_t)p.nkv * (p.dqk + p.dv);
-  const uint16_t* row = p.qkv + (size_t)t * rowlen;
-  const int slot = pos % p.cap;
-  for (int hd = head0 + warp; hd < min(heads, head0 + (int)(blockDim.x / 32)); hd += blockDim.x / 32) {
-    const uint16_t* src;
-    uint16_t* dst;
-    if (hd < p.nq) {
-      src = row + (size_t)hd * p.dqk;
-      dst = p.q + ((size_t)t * p.nq + hd) * p.dqk;
-    } else {
-      const int hk = hd - p.nq;
-      src = row + (size_t)p.nq * p.dqk + (size_t)hk * p.dqk;
-      dst = p.kc + ((size_t)hk * p.cap + slot) * p.dqk;
-      const uint16_t* vs = row + (size_t)p.nq * p.dqk + (size_t)p.nkv * p.dqk + (size_t)hk * p.dv;
-      uint16_t* vd = p.vc + ((size_t)hk * p.cap + slot) * p.dv;
-      for (int i = lane; i < p.dv; i += 32) {
-        const float x = bf16_to_f32(vs[i]);
-        vd[i] = (uint16_t)(p.has_vscale ? f32_to_bf16(x * p.v_scale) : vs[i]);
+  for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
+    const int pos = p.pos0 + t;
+    __syncthreads();  // the previous token's table is no longer read
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const double inv_freq = exp(-(double)(2 * i) / (double)p.rot * p.log_base);
+      double sn, cs;
+      sincos((double)pos * inv_freq, &sn, &cs);
+      cs_tab[i] = make_double2(cs, sn);
+    }
+    __syncthreads();
+    const uint16_t* row = p.qkv + (size_t)t * rowlen;
+    const int slot = pos % p.cap;
+    for (int hd = warp; hd < heads; hd += blockDim.x / 32) {
+      const uint16_t* src;
+      uint16_t* dst;
+      if (hd < p.nq) {
+        src = row + (size_t)hd * p.dqk;
+        dst = p.q + ((size_t)t * p.nq + hd) * p.dqk;
+      } else {
+        const int hk = hd - p.nq;
+        src = row + (size_t)p.nq * p.dqk + (size_t)hk * p.dqk;
+        dst = p.kc + ((size_t)hk * p.cap + slot) * p.dqk;
+        const uint32_t* vs = reinterpret_cast<const uint32_t*>(row + (size_t)p.nq * p.dqk +
+                                                               (size_t)p.nkv * p.dqk + (size_t)hk * p.dv);
+        uint32_t* vd = reinterpret_cast<uint32_t*>(p.vc + ((size_t)hk * p.cap + slot) * p.dv);
+#pragma unroll 4
+        for (int i = lane; i < p.dv / 2; i += 32) {
+          const uint32_t w = vs[i];
+          vd[i] = p.has_vscale ? (f32_to_bf16(bf16_to_f32(w & 0xFFFFu) * p.v_scale) |
+                                  (f32_to_bf16(bf16_to_f32(w >> 16) * p.v_scale) << 16))
+                               : w;
+        }
       }
+      for (int i = lane; i < half; i += 32) {
+        const double2 c = cs_tab[i];
+        const double x1 = bf16_to_f32(src[i]), x2 = bf16_to_f32(src[i + half]);
+        dst[i] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * c.x - x2 * c.y));
+        dst[i + half] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * c.y + x2 * c.x));
+      }
+      const uint32_t* s2 = reinterpret_cast<const uint32_t*>(src + p.rot);
+      uint32_t* d2 = reinterpret_cast<uint32_t*>(dst + p.rot);
+#pragma unroll 4
+      for (int i = lane; i < (p.dqk - p.rot) / 2; i += 32) d2[i] = s2[i];
     }
-    for (int i = lane; i < half; i += 32) {
-      const double2 c = cs_tab[i];
-      const double x1 = bf16_to_f32(src[i]), x2 = bf16_to_f32(src[i + half]);
-      dst[i] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * c.x - x2 * c.y));
-      dst[i + half] = (uint16_t)f32_to_bf16(__double2float_rn(x1 * c.y + x2 * c.x));
-    }
-    for (int i = p.rot + lane; i < p.dqk; i += 32) dst[i] = src[i];
   }
 }
 
@@ -570,7 +580,7 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
 
 cudaError_t launch_rope_store(const RopeParams& p, cudaStream_t st) {
   if (p.rot > 256) return cudaErrorInvalidValue;
-  rope_store_kernel<<<dim3(p.T, (p.nq + p.nkv + 7) / 8), 256, 0, st>>>(p);
+  rope_store_kernel<<<std::min(p.T, 148 * 4), 512, 0, st>>>(p);
   return cudaGetLastError();
 }
 

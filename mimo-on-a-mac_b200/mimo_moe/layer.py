@@ -240,29 +240,68 @@ class DecoderLayer:
         return out
 
 
+class DecoderStack:
+    """Decoder layers run in order over one residual stream (the engine's layer loop, model.py:294-336, without
+    the embedding, final norm and lm_head): each layer's KV cache lives here, every layer of a call works at
+    the same position, and the output is a fixed buffer per shape, so a decode step replays as one CUDA
+    graph (the graph keeps the position it was captured at; `at(pos)` sets it for eager calls and captures)."""
+
+    def __init__(self, layers, max_len: int, max_chunk: int = 4096):
+        if not layers:
+            raise ValueError("empty stack")
+        self.layers = list(layers)
+        self.caches = [l.new_cache(max_len, max_chunk) for l in self.layers]
+        self._out = {}
+
+    def at(self, pos: int) -> "DecoderStack":
+        for c in self.caches:
+            c.offset = int(pos)
+        return self
+
+    @property
+    def offset(self) -> int:
+        return self.caches[0].offset
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        h = x
+        for layer, cache in zip(self.layers, self.caches):
+            h = layer(h, cache)
+        key = (tuple(h.shape), h.device)
+        if key not in self._out:
+            self._out[key] = torch.empty_like(h)
+        out = self._out[key]
+        out.copy_(h)
+        return out
+
+
 def synthetic_attention(cfg: AttentionConfig, hidden: int = 4096, seed: int = 4, std: float = 0.02,
-                        device=None) -> Attention:
+                        device=None, on_device: bool = False) -> Attention:
     """Seeded random-init attention weights of this shape (no checkpoint offline): N(0, std) bf16, sinks
-    N(0, 1) float32 when the config has them."""
-    g = torch.Generator("cpu").manual_seed(seed)
+    N(0, 1) float32 when the config has them.  on_device draws them with a CUDA generator (fast, for
+    benchmark-sized stacks) instead of the CPU generator the tests use."""
+    dev = torch.device(device or "cuda")
+    gdev = dev if on_device else torch.device("cpu")
+    g = torch.Generator(gdev).manual_seed(seed)
     def w(o, i):
-        return (torch.randn(o, i, generator=g) * std).to(torch.bfloat16)
+        return (torch.randn(o, i, generator=g, device=gdev) * std).to(torch.bfloat16)
     wq = w(cfg.n_heads * cfg.head_dim, hidden)
     wk = w(cfg.n_kv_heads * cfg.head_dim, hidden)
     wv = w(cfg.n_kv_heads * cfg.v_head_dim, hidden)
     wo = w(hidden, cfg.n_heads * cfg.v_head_dim)
-    sinks = torch.randn(cfg.n_heads, generator=g) if cfg.sinks else None
-    return Attention(cfg, wq, wk, wv, wo, sinks, device=device or "cuda")
+    sinks = torch.randn(cfg.n_heads, generator=g, device=gdev) if cfg.sinks else None
+    return Attention(cfg, wq, wk, wv, wo, sinks, device=dev)
 
 
 def synthetic_dense_mlp(hidden: int = 4096, inter: int = 16384, seed: int = 5, std: float = 0.02,
-                        device=None) -> DenseMLP:
-    g = torch.Generator("cpu").manual_seed(seed)
+                        device=None, on_device: bool = False) -> DenseMLP:
+    dev = torch.device(device or "cuda")
+    gdev = dev if on_device else torch.device("cpu")
+    g = torch.Generator(gdev).manual_seed(seed)
     def w(o, i):
-        return (torch.randn(o, i, generator=g) * std).to(torch.bfloat16)
-    return DenseMLP(w(inter, hidden), w(inter, hidden), w(hidden, inter), device=device or "cuda")
+        return (torch.randn(o, i, generator=g, device=gdev) * std).to(torch.bfloat16)
+    return DenseMLP(w(inter, hidden), w(inter, hidden), w(hidden, inter), device=dev)
 
 
-__all__ = ["AttentionConfig", "Attention", "DecoderLayer", "DenseMLP", "KVCache", "MoEMLP", "add", "add_rmsnorm",
-           "attention", "bf16_value", "mimo_full_attention", "mimo_sliding_attention", "rope_store", "swiglu",
+__all__ = ["AttentionConfig", "Attention", "DecoderLayer", "DecoderStack", "DenseMLP", "KVCache", "MoEMLP", "add",
+           "add_rmsnorm", "attention", "bf16_value", "mimo_full_attention", "mimo_sliding_attention", "rope_store", "swiglu",
            "synthetic_attention", "synthetic_dense_mlp"]

@@ -262,3 +262,38 @@ def test_decode_equals_prefill_two_layers(gpu):
     ref = f(run([(0, P + D)]))[P:]
     dec = f(run([(0, P)] + [(P + i, P + i + 1) for i in range(D)]))[P:]
     assert rel(dec, ref) <= 1e-2
+
+
+def test_decoder_stack_matches_its_layers_and_replays_as_a_graph(gpu):
+    """DecoderStack = its layers run one after another (bit for bit) over a prefill chunk and a decode step,
+    and a decode step captured as a CUDA graph replays the eager step at the same position bit for bit."""
+    import mimo_moe
+    from mimo_moe.ep import GraphedStep
+    from mimo_moe.layer import DecoderLayer, DecoderStack, MoEMLP, synthetic_attention, synthetic_dense_mlp
+    S = 32
+    W = synth.router_weight(E=S, seed=71).to(gpu)
+    pool = mimo_moe.ExpertPools.synthetic(S, seed=0, layer=1, device=gpu)
+
+    def build():
+        return [DecoderLayer(synthetic_attention(_cfg("full", v_scale=0.707), seed=72, device=gpu),
+                             synthetic_dense_mlp(inter=1024, seed=73, device=gpu), None, None),
+                DecoderLayer(synthetic_attention(_cfg("swa", v_scale=0.707), seed=74, device=gpu),
+                             MoEMLP(W, None, pool), None, None)]
+    stack = DecoderStack(build(), max_len=512, max_chunk=64)
+    ref_layers = build()
+    ref_caches = [l.new_cache(512, 64) for l in ref_layers]
+    for T, seed in ((50, 80), (8, 81)):
+        x = synth.hidden(T, seed=seed).to(gpu)
+        y = stack(x).clone()
+        h = x
+        for l, c in zip(ref_layers, ref_caches):
+            h = l(h, c)
+        assert torch.equal(y.view(torch.int16), h.view(torch.int16)), T
+    pos = stack.offset
+    x = synth.hidden(8, seed=82).to(gpu)
+    eager = stack.at(pos)(x).clone()
+    g = GraphedStep(lambda inp: stack.at(pos)(inp), 8, 4096, gpu)
+    replay = g(x).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(replay.view(torch.int16), eager.view(torch.int16))
+    stack.layers[1].mlp.check_status()
