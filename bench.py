@@ -398,8 +398,8 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
     import torch
     import mimo_moe
     from mimo_moe import _lib, synthetic
-    from mimo_moe.layer import (DecoderLayer, MoEMLP, add, add_rmsnorm, attention, mimo_full_attention, rope_store,
-                                synthetic_attention)
+    from mimo_moe.layer import (DecoderLayer, MoEMLP, add, add_rmsnorm, attention, linear, mimo_full_attention,
+                                rope_store, synthetic_attention)
     dev = ctx.dev
     T = WORKLOADS[workload][0]
     decode = T <= 8
@@ -449,10 +449,10 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
         ev[0].record()
         r = mimo_moe.rmsnorm(x, None, 1e-5); ev[1].record()
-        qkv = torch.matmul(r, attn.w_qkv.t()); ev[2].record()
+        qkv = linear(r, attn.w_qkv); ev[2].record()
         q = rope_store(qkv, cfg, cache, pos0); ev[3].record()
         o = attention(q, cache, cfg, pos0, attn.sinks); ev[4].record()
-        a = torch.matmul(o.view(T, -1), attn.w_o.t()); ev[5].record()
+        a = linear(o.view(T, -1), attn.w_o); ev[5].record()
         h, r2 = add_rmsnorm(x, a, None, 1e-5); ev[6].record()
         y = layer.mlp(r2); ev[7].record()
         add(h, y); ev[8].record()
@@ -501,9 +501,10 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
     for i in range(3):
         e2e_step(i)
     e2e_ms = _timed(ctx, steps, e2e_step)
-    # our launches per step: rmsnorm, rope_store, attention (+ merge when split), add_rmsnorm, add, and the
-    # MoE block's (decode: route logits, select, gate/up, down, combine; prefill: 11)
-    per_step = 5 + (1 if decode else 0) + (5 if decode else 11)
+    # our launches per step: rmsnorm, rope_store, attention (+ merge when split), add_rmsnorm, add, the two
+    # decode projections with their segment sums (prefill projections are cuBLAS), and the MoE block's
+    # (decode: route logits, select, gate/up, down, combine; prefill: 11)
+    per_step = 5 + (1 + 4 if decode else 0) + (5 if decode else 11)
     res = {
         "metric": f"decoder-layer tok/s ({workload})", "value": T * steps / (ms * 1e-3), "unit": "tok/s",
         "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": step_ms, "higher_is_better": True,
@@ -959,9 +960,10 @@ def bench_model(args):
                 "d2h_bytes_per_step": B * H * 2,
                 "how": "eager DecoderStack call per step (host launches of every layer), pinned host x in, y out",
                 "value_graph_replay": B * args.steps / (g_ms * 1e-3)},
-        # per layer: rmsnorm, RoPE + cache, attention + split merge, add + RMSNorm, add; per MoE layer the
-        # block's five (route logits, select, gate/up, down, combine); the dense layer's SwiGLU
-        "gpu_launches": (L * 6 + (L - 1) * 5 + 1) * args.steps,
+        # per layer: rmsnorm, RoPE + cache, attention + split merge, add + RMSNorm, add, the q|k|v and o
+        # projections with their segment sums; per MoE layer the block's five (route logits, select, gate/up,
+        # down, combine); the dense layer's SwiGLU and its two projections
+        "gpu_launches": (L * 10 + (L - 1) * 5 + 5) * args.steps,
         "cpu_baseline": None,
     }
     print(json.dumps(res))

@@ -4,7 +4,7 @@
  *
  * The decoder layer (engine/mimo_stream/mimo_v2.py:242-262, the engine's loop engine/mimo_stream/model.py:294-300):
  *   r   = input_layernorm(x)                          mimo_moe_rmsnorm (mimo_moe.h)
- *   qkv = r @ [Wq | Wk | Wv]^T                        caller's GEMM (cuBLAS)          mimo_v2.py:117-128
+ *   qkv = r @ [Wq | Wk | Wv]^T                        mimo_moe_layer_linear (decode) / caller's GEMM     :117-128
  *   q,k = RoPE, v *= value scale, k/v -> cache        mimo_moe_layer_rope_store       mimo_v2.py:130-139
  *   o   = attention with sinks over the cache         mimo_moe_layer_attention        mimo_v2.py:141-148
  *   h   = x + o @ Wo^T; r2 = post_attention_layernorm(h)
@@ -65,6 +65,18 @@ int mimo_moe_layer_attention(const uint16_t* q, const uint16_t* k_cache, const u
                              int32_t v_head_dim, float scale, int32_t window, int32_t pos0, int32_t cap,
                              int32_t splits, uint16_t* out, void* workspace, size_t workspace_bytes, int32_t* status,
                              void* stream);
+
+/* Decode-size projection (nn.Linear without bias on a few token rows: the q|k|v and o projections,
+ * mimo_v2.py:117-149, and the dense MLP's, :151-160): y[T, N] = bf16(x[T, K] . W[N, K]^T), float32
+ * accumulation.  x bf16 [T][K] with 1 <= T <= 16, W bf16 [N][K] (nn.Linear layout), y bf16 [T][N]; N a
+ * multiple of 8, K a multiple of 64 and at least 256.  The weights stream once through the tcgen05 tensor
+ * cores; the K dimension may be split over CTAs for balance, with float32 partials in the workspace
+ * (mimo_moe_layer_linear_workspace_bytes; a smaller or null workspace splits less) added in a fixed order.
+ * status: optional caller-zeroed device word (MIMO_ETIMEOUT if a bounded wait expires).  Prefill-sized
+ * projections are plain GEMMs the caller runs on its library (cuBLAS). */
+size_t mimo_moe_layer_linear_workspace_bytes(int32_t T, int32_t N, int32_t K);
+int mimo_moe_layer_linear(const uint16_t* x, const uint16_t* w, int32_t T, int32_t N, int32_t K, uint16_t* y,
+                          void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
 /* Residual add and the next RMSNorm in one pass (mimo_v2.py:260 then post_attention_layernorm):
  * h = bf16(x + delta); r = RMSNorm(h) * weight exactly as mimo_moe_rmsnorm computes it.  [T, H] bf16,

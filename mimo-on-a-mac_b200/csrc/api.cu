@@ -1098,6 +1098,25 @@ int mimo_moe_layer_attention(const uint16_t* q, const uint16_t* k_cache, const u
   return MIMO_OK;
 }
 
+size_t mimo_moe_layer_linear_workspace_bytes(int32_t T, int32_t N, int32_t K) {
+  if (T < 1 || T > 16 || N < 8 || N % 8 || K < 256 || K % 64) return 0;
+  const int S = linear_decode_splits(N, K, num_sms_current());
+  return S > 1 ? (size_t)S * T * N * 4 : 0;
+}
+
+int mimo_moe_layer_linear(const uint16_t* x, const uint16_t* w, int32_t T, int32_t N, int32_t K, uint16_t* y,
+                          void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!x || !w || !y || T < 1 || T > 16 || N < 8 || N % 8 || K < 256 || K % 64 || !a16(x) || !a16(w) || !a16(y) ||
+      (workspace && !a16(workspace)))
+    return MIMO_EINVAL;
+  const int sms = num_sms_current();
+  int S = linear_decode_splits(N, K, sms);
+  while (S > 1 && (!workspace || workspace_bytes < (size_t)S * T * N * 4)) S /= 2;  // what the workspace holds
+  MIMO_TRY(launch_linear_decode(x, w, T, N, K, S, y, S > 1 ? static_cast<float*>(workspace) : nullptr, status, sms,
+                                static_cast<cudaStream_t>(stream)));
+  return MIMO_OK;
+}
+
 int mimo_moe_layer_add_rmsnorm(const uint16_t* x, const uint16_t* delta, const uint16_t* weight, int32_t T,
                                int32_t H, float eps, uint16_t* h, uint16_t* r, void* stream) {
   if (!x || !delta || !h || !r || T < 1 || H < 8 || H % 8 || !(eps >= 0.f) || !a16(x) || !a16(delta) || !a16(h) ||

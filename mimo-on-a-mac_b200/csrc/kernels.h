@@ -299,6 +299,18 @@ struct RopeParams {
   float v_scale;        // already a bf16 value
   double log_base;      // ln(rope_theta)
 };
+// Decode-size projection y[T, N] = bf16(x[T, K] . W[N, K]^T) on tcgen05 (linear.cu): TMA maps of W (box
+// 64 x 128 rows) and x (box 64 x 16 rows), S K segments (partials [S][T][N] float32 when S > 1).
+struct LinearParams {
+  CUtensorMap wmap, xmap;
+  uint16_t* y;
+  float* part;
+  int32_t* status;
+  int T, N, K, S, tiles;
+};
+int linear_decode_splits(int N, int K, int num_sms);
+cudaError_t launch_linear_decode(const uint16_t* x, const uint16_t* w, int T, int N, int K, int S, uint16_t* y,
+                                 float* part, int32_t* status, int num_sms, cudaStream_t st);
 bool attn_dims_supported(int dqk, int dv);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t st);
 bool attn_tc_supported(const AttnParams& p);

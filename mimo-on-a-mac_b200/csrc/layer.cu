@@ -352,9 +352,10 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
   for (int i = 0; i < PER; i += 2) *reinterpret_cast<uint32_t*>(dst + i) = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
 }
 
-// A grid of up to 4 CTAs per SM walks the tokens: per token the CTA computes the cos/sin of every rotary pair
-// once (float64: the angle pos * theta^(-2i/rot) and its sine and cosine), then its 16 warps take the heads of
-// the packed projection row [q heads | k heads | v heads]: RoPE on q and k (float64 rotation, rounded once to
+// Grid (token slices, head groups): a CTA walks its tokens; per token it computes the cos/sin of every rotary
+// pair once (float64: the angle pos * theta^(-2i/rot) and its sine and cosine), then its 16 warps take the
+// heads (all of them, or the CTA's group of 16 when the grid has several) of the packed projection row
+// [q heads | k heads | v heads]: RoPE on q and k (float64 rotation, rounded once to
 // float32, then to bf16), v * v_scale, k/v into the cache slot; the value rows and the dims past the rotary
 // ones move as bf16 pairs (every row offset is an even number of values).  (A float32 table moves
 // near-cancelling rotations by a few bf16 ulps.)
@@ -376,7 +377,8 @@ __global__ void __launch_bounds__(512) rope_store_kernel(RopeParams p) {
     __syncthreads();
     const uint16_t* row = p.qkv + (size_t)t * rowlen;
     const int slot = pos % p.cap;
-    for (int hd = warp; hd < heads; hd += blockDim.x / 32) {
+    const int h_lo = gridDim.y > 1 ? blockIdx.y * 16 : 0, h_hi = gridDim.y > 1 ? min(heads, h_lo + 16) : heads;
+    for (int hd = h_lo + warp; hd < h_hi; hd += blockDim.x / 32) {
       const uint16_t* src;
       uint16_t* dst;
       if (hd < p.nq) {
@@ -580,7 +582,10 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
 
 cudaError_t launch_rope_store(const RopeParams& p, cudaStream_t st) {
   if (p.rot > 256) return cudaErrorInvalidValue;
-  rope_store_kernel<<<std::min(p.T, 148 * 4), 512, 0, st>>>(p);
+  // decode-sized calls: one CTA per (token, 16 heads); prefill: up to 4 CTAs per SM walk the tokens, each
+  // taking every head of its token
+  const int groups = p.T <= 148 ? (p.nq + p.nkv + 15) / 16 : 1;
+  rope_store_kernel<<<dim3(std::min(p.T, 148 * 4), groups), 512, 0, st>>>(p);
   return cudaGetLastError();
 }
 

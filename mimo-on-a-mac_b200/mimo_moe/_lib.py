@@ -85,6 +85,9 @@ SIGNATURES = {
     "mimo_moe_layer_attention": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                            c_int32, c_int32, c_float, c_int32, c_int32, c_int32, c_int32, c_void_p,
                                            c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_layer_linear_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "mimo_moe_layer_linear": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_size_t,
+                                        c_void_p, c_void_p]),
     "mimo_moe_layer_add_rmsnorm": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p,
                                              c_void_p, c_void_p]),
     "mimo_moe_layer_swiglu": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),

@@ -7,9 +7,9 @@ engine's per-layer loop (engine/mimo_stream/model.py:294-300, caches from model.
     h   = x + self_attn(input_layernorm(x), mask, cache)
     out = h + mlp(post_attention_layernorm(h))          (mlp = the MoE block on MoE layers)
 
-RoPE, the cache append, attention, the residual add fused with the next RMSNorm and the SwiGLU run in this
-library's CUDA kernels (include/mimo_moe_layer.h); the q/k/v/o and dense-MLP projections are plain bf16 GEMMs
-(cuBLAS through torch.matmul).  There is no CPU path.
+RoPE, the cache append, attention, the residual add fused with the next RMSNorm, the SwiGLU and the decode-size
+projections (T <= 16 token rows) run in this library's CUDA kernels (include/mimo_moe_layer.h); prefill-sized
+projections are plain bf16 GEMMs (cuBLAS through torch.matmul).  There is no CPU path.
 
 The checkpoint's config.json is not available offline, so every dimension is a constructor argument;
 `mimo_full_attention()` / `mimo_sliding_attention()` give the MiMo-like defaults the tests and the benchmark use
@@ -123,6 +123,26 @@ def attention(q: torch.Tensor, cache: KVCache, cfg: AttentionConfig, pos0: int, 
     return o
 
 
+DECODE_ROWS = 16  # projections of at most this many token rows run on the library's decode kernel
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, workspace_ok: bool = True) -> torch.Tensor:
+    """nn.Linear without bias: x bf16 [T, K] . weight bf16 [N, K]^T -> bf16 [T, N].  Decode sizes (T <= 16) run
+    on the library's tcgen05 stream kernel (mimo_moe_layer_linear, the weights read once); larger T are plain
+    GEMMs on cuBLAS."""
+    T, K = x.shape
+    N = weight.shape[0]
+    if T > DECODE_ROWS or N % 8 or K % 64 or K < 256:
+        return torch.matmul(x, weight.t())
+    y = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
+    L = lib()
+    nb = L.mimo_moe_layer_linear_workspace_bytes(T, N, K) if workspace_ok else 0
+    ws = workspace(nb, x.device) if nb else None
+    check(L.mimo_moe_layer_linear(x.data_ptr(), weight.data_ptr(), T, N, K, y.data_ptr(), _ptr(ws),
+                                  ws.numel() if ws is not None else 0, None, _stream()), "linear")
+    return y
+
+
 def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: Optional[torch.Tensor], eps: float):
     """h = bf16(x + delta), r = rmsnorm(h) * weight (one pass).  Returns (h, r)."""
     T, H = x.shape
@@ -169,11 +189,11 @@ class Attention:
 
     def __call__(self, r: torch.Tensor, cache: KVCache) -> torch.Tensor:
         T = r.shape[0]
-        qkv = torch.matmul(r, self.w_qkv.t())
+        qkv = linear(r, self.w_qkv)
         q = rope_store(qkv, self.cfg, cache, cache.offset)
         o = attention(q, cache, self.cfg, cache.offset, self.sinks)
         cache.offset += T
-        return torch.matmul(o.view(T, -1), self.w_o.t())
+        return linear(o.view(T, -1), self.w_o)
 
 
 class DenseMLP:
@@ -185,7 +205,7 @@ class DenseMLP:
         self.w_down = _bf16(w_down, dev)
 
     def __call__(self, r: torch.Tensor) -> torch.Tensor:
-        return torch.matmul(swiglu(torch.matmul(r, self.w_gate_up.t())), self.w_down.t())
+        return linear(swiglu(linear(r, self.w_gate_up)), self.w_down)
 
 
 class MoEMLP:
@@ -303,5 +323,5 @@ def synthetic_dense_mlp(hidden: int = 4096, inter: int = 16384, seed: int = 5, s
 
 
 __all__ = ["AttentionConfig", "Attention", "DecoderLayer", "DecoderStack", "DenseMLP", "KVCache", "MoEMLP", "add",
-           "add_rmsnorm", "attention", "bf16_value", "mimo_full_attention", "mimo_sliding_attention", "rope_store", "swiglu",
+           "add_rmsnorm", "attention", "linear", "bf16_value", "mimo_full_attention", "mimo_sliding_attention", "rope_store", "swiglu",
            "synthetic_attention", "synthetic_dense_mlp"]

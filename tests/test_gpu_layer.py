@@ -297,3 +297,26 @@ def test_decoder_stack_matches_its_layers_and_replays_as_a_graph(gpu):
     torch.cuda.synchronize()
     assert torch.equal(replay.view(torch.int16), eager.view(torch.int16))
     stack.layers[1].mlp.check_status()
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 13568, 4096), (8, 13568, 4096), (3, 4096, 8192), (8, 4096, 8192),
+                                   (16, 1024, 256), (5, 520, 4096)])
+def test_decode_linear_matches_oracle(gpu, T, N, K):
+    """The decode projection kernel against the float64 oracle (nn.Linear: exact dot products rounded once
+    to float32, then bf16): >= 99% of outputs identical, rel_err <= 4e-3, and outputs of at least 1% of the
+    largest within two bf16 ulps (a float32 sum of thousands of products moves a near-cancelling output by an
+    ulp or two; near zero an ulp count says nothing); with and without the workspace (one K segment vs the
+    balanced split, summed in a fixed order); and within 1e-2 of cuBLAS."""
+    from mimo_moe.layer import linear
+    g = torch.Generator().manual_seed(T * 131 + N)
+    x = rnd(g, T, K)
+    W = rnd(g, N, K, std=0.02)
+    ref = torch.from_numpy(LO.linear(f(x), f(W))).to(torch.bfloat16)
+    xg, Wg = x.to(gpu), W.to(gpu)
+    for ws in (True, False):
+        y = linear(xg, Wg, workspace_ok=ws)
+        d = np.abs(bits(y) - bits(ref))
+        big = np.abs(f(ref)) >= 1e-2 * np.abs(f(ref)).max()
+        assert (d == 0).mean() >= 0.99 and d[big].max() <= 2, (ws, d[big].max(), (d == 0).mean())
+        assert rel(f(y), f(ref)) <= 4e-3
+    assert rel(f(y), f(torch.matmul(xg, Wg.t()))) <= 1e-2
