@@ -304,52 +304,47 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
   }
 }
 
-// One warp per (token, query head): folds the splits' (m, l, O) with the sink.  The lanes read the splits'
-// (m, l) in parallel (split s on lane s % 32), the warp takes their maximum and the sum of l * 2^(m - M) by
-// butterflies (a fixed order), then each lane sums its DV / 32 output values over the splits in split order.
+// One CTA of DV threads per (token, query head): folds the splits' (m, l, O) with the sink.  Warp 0 reads the
+// splits' (m, l) in parallel (split s on lane s % 32) and takes their maximum and the sum of l * 2^(m - M) by
+// butterflies (a fixed order); then every thread sums its output value over the splits in split order, the
+// partial rows of consecutive threads contiguous (coalesced), several splits' loads in flight.
 template <int DV>
-__global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (row >= p.T * p.nq) return;
-  const int qh = row % p.nq;
+__global__ void __launch_bounds__(DV) attn_merge_kernel(AttnParams p) {
+  __shared__ float fs[64];
+  __shared__ float inv_l;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
   const size_t stride = (size_t)p.T * p.nq;
-  float2 ml[2];
+  if (tid < 32) {
+    float2 ml[2];
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int s = lane + 32 * k;
-    ml[k] = s < p.splits ? *reinterpret_cast<const float2*>(p.part_ml + ((size_t)s * stride + row) * 2)
-                         : make_float2(-INFINITY, 0.f);
+    for (int k = 0; k < 2; ++k) {
+      const int s = lane + 32 * k;
+      ml[k] = s < p.splits ? *reinterpret_cast<const float2*>(p.part_ml + ((size_t)s * stride + row) * 2)
+                           : make_float2(-INFINITY, 0.f);
+    }
+    float M = fmaxf(ml[0].x, ml[1].x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    const float sk = p.sinks ? p.sinks[row % p.nq] * kLog2e : -INFINITY;
+    M = fmaxf(M, sk);
+    float L = 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float f = ml[k].x == -INFINITY ? 0.f : exp2f(ml[k].x - M);
+      fs[lane + 32 * k] = f;
+      L += ml[k].y * f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+    if (p.sinks) L += exp2f(sk - M);
+    if (lane == 0) inv_l = L > 0.f ? 1.f / L : 0.f;
   }
-  float M = fmaxf(ml[0].x, ml[1].x);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
-  const float sk = p.sinks ? p.sinks[qh] * kLog2e : -INFINITY;
-  M = fmaxf(M, sk);
-  float f[2], L = 0.f;
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    f[k] = ml[k].x == -INFINITY ? 0.f : exp2f(ml[k].x - M);
-    L += ml[k].y * f[k];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
-  if (p.sinks) L += exp2f(sk - M);
-  constexpr int PER = DV / 32;
-  float acc[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-  const float* src = p.part_o + (size_t)row * DV + lane * PER;
-#pragma unroll 4
-  for (int s = 0; s < p.splits; ++s) {
-    const float fs = __shfl_sync(0xFFFFFFFFu, f[s >> 5], s & 31);
-    const float* v = src + (size_t)s * stride * DV;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] = fmaf(v[i], fs, acc[i]);
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  uint16_t* dst = p.out + (size_t)row * DV + lane * PER;
-#pragma unroll
-  for (int i = 0; i < PER; i += 2) *reinterpret_cast<uint32_t*>(dst + i) = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
+  __syncthreads();
+  const float* src = p.part_o + (size_t)row * DV + tid;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int s = 0; s < p.splits; ++s) acc = fmaf(src[(size_t)s * stride * DV], fs[s], acc);
+  p.out[(size_t)row * DV + tid] = (uint16_t)f32_to_bf16(acc * inv_l);
 }
 
 // Grid (token slices, head groups): a CTA walks its tokens; per token it computes the cos/sin of every rotary
@@ -531,7 +526,7 @@ cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st) {
   attn_kernel<DQK, DV><<<grid, kAttnThreads, smem, st>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.splits == 1) return e;
-  attn_merge_kernel<DV><<<(p.T * p.nq + 7) / 8, 256, 0, st>>>(p);
+  attn_merge_kernel<DV><<<p.T * p.nq, DV, 0, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -570,8 +565,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
   if (attn_tc_enabled() && attn_tc_supported(p)) {
     const cudaError_t e = launch_attention_tc(p, p.status, st);
     if (e != cudaSuccess || p.splits == 1) return e;
-    if (p.dv == 128) attn_merge_kernel<128><<<(p.T * p.nq + 7) / 8, 256, 0, st>>>(p);
-    else attn_merge_kernel<64><<<(p.T * p.nq + 7) / 8, 256, 0, st>>>(p);
+    if (p.dv == 128) attn_merge_kernel<128><<<p.T * p.nq, 128, 0, st>>>(p);
+    else attn_merge_kernel<64><<<p.T * p.nq, 64, 0, st>>>(p);
     return cudaGetLastError();
   }
   if (p.dqk == 192 && p.dv == 128) return launch_attn_t<192, 128>(p, st);
