@@ -119,3 +119,24 @@ def test_layer_entry_points_reject_bad_arguments_without_a_device():
     assert L.mimo_moe_layer_add_rmsnorm(p, p, None, 1, 4, 1e-5, p, p, None) == EINVAL
     assert L.mimo_moe_layer_attention_workspace_bytes(8, 64, 128, 1) == 0
     assert L.mimo_moe_layer_attention_workspace_bytes(8, 64, 128, 16) == 16 * 8 * 64 * (128 + 2) * 4
+
+
+def test_decode_linear_host_checks_and_workspace_without_a_device():
+    """mimo_moe_layer_linear's host side: argument checks before any launch, and the workspace its K split needs
+    (one float32 partial row per token and output per segment; none when the weights split into one segment)."""
+    import mimo_moe
+    L = mimo_moe.lib()
+    EINVAL = 1
+    p = 1 << 20
+    assert L.mimo_moe_layer_linear(p, p, 17, 4096, 4096, p, None, 0, None, None) == EINVAL   # T > 16
+    assert L.mimo_moe_layer_linear(p, p, 8, 4100, 4096, p, None, 0, None, None) == EINVAL   # N % 8
+    assert L.mimo_moe_layer_linear(p, p, 8, 4096, 4000, p, None, 0, None, None) == EINVAL   # K % 64
+    assert L.mimo_moe_layer_linear(p, p, 8, 4096, 192, p, None, 0, None, None) == EINVAL    # K < 256
+    assert L.mimo_moe_layer_linear(p + 2, p, 8, 4096, 4096, p, None, 0, None, None) == EINVAL
+    assert L.mimo_moe_layer_linear_workspace_bytes(17, 4096, 4096) == 0
+    for T, N, K in ((8, 13568, 4096), (1, 4096, 8192), (8, 32768, 4096), (8, 4096, 16384)):
+        nb = L.mimo_moe_layer_linear_workspace_bytes(T, N, K)
+        row = T * N * 4
+        assert nb % row == 0 and nb // row in (0, 2, 4, 8, 16, 32)
+        S = max(1, nb // row)
+        assert K % (64 * S) == 0 and K // S >= 256
