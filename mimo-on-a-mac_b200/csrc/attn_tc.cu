@@ -146,6 +146,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tslot;
+  pdl_wait();  // q and the cache come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   const uint32_t tS[2] = {tbase, tbase + 128};
   const uint32_t tO = tbase + 256;
   bool ok = true;
@@ -415,8 +417,7 @@ cudaError_t launch_tc(AttnTcParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  attn_tc_kernel<DQK, DV><<<dim3(p.ntiles, p.nkv, p.splits), kTcThreads, S::SMEM, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(attn_tc_kernel<DQK, DV>, dim3(p.ntiles, p.nkv, p.splits), dim3(kTcThreads), S::SMEM, st, p);
 }
 
 }  // namespace

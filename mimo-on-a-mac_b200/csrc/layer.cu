@@ -100,6 +100,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
   uint8_t* sQ = smem;
   uint8_t* sK[2] = {smem + kAttnRows * DQK * 2, smem + kAttnRows * DQK * 2 + kAttnKeys * (DQK + DV) * 2};
   uint8_t* sV[2] = {sK[0] + kAttnKeys * DQK * 2, sK[1] + kAttnKeys * DQK * 2};
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hk = blockIdx.y, split = blockIdx.z;
@@ -312,6 +314,8 @@ template <int DV>
 __global__ void __launch_bounds__(DV) attn_merge_kernel(AttnParams p) {
   __shared__ float fs[64];
   __shared__ float inv_l;
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
   const size_t stride = (size_t)p.T * p.nq;
   if (tid < 32) {
@@ -356,6 +360,8 @@ __global__ void __launch_bounds__(DV) attn_merge_kernel(AttnParams p) {
 // near-cancelling rotations by a few bf16 ulps.)
 __global__ void __launch_bounds__(512) rope_store_kernel(RopeParams p) {
   __shared__ double2 cs_tab[128];
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = p.rot / 2;
   const int heads = p.nq + p.nkv;
@@ -418,6 +424,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const uint16_
                                                                    float eps, uint16_t* __restrict__ hout,
                                                                    uint16_t* __restrict__ rout) {
   __shared__ float warp_ss[kNormThreads / 32];
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   const size_t row = (size_t)blockIdx.x * H;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row);
   const uint4* dr = reinterpret_cast<const uint4*>(d + row);
@@ -476,6 +484,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(const uint16_
 // out = bf16(bf16(g * bf16(sigmoid(g))) * u); gate_up rows are [gate (I) | up (I)].
 __global__ void __launch_bounds__(256) swiglu_kernel(const uint16_t* __restrict__ gu, int T, int I,
                                                      uint16_t* __restrict__ out) {
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   const size_t n8 = (size_t)T * I / 8;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
     const size_t e = i * 8, t = e / I, c = e % I;
@@ -496,6 +506,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const uint16_t* __restrict_
 // out = bf16(a + b) (the decoder layer's residual adds, mimo_v2.py:260-261).
 __global__ void __launch_bounds__(256) add_kernel(const uint16_t* __restrict__ a, const uint16_t* __restrict__ b,
                                                   size_t n8, uint16_t* __restrict__ out) {
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
     const uint4 x = __ldg(reinterpret_cast<const uint4*>(a) + i), y = __ldg(reinterpret_cast<const uint4*>(b) + i);
     const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
@@ -523,11 +535,9 @@ cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st) {
     attr_set[dev] = true;
   }
   const dim3 grid((p.T * p.G + kAttnRows - 1) / kAttnRows, p.nkv, p.splits);
-  attn_kernel<DQK, DV><<<grid, kAttnThreads, smem, st>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(attn_kernel<DQK, DV>, grid, dim3(kAttnThreads), smem, st, p);
   if (e != cudaSuccess || p.splits == 1) return e;
-  attn_merge_kernel<DV><<<p.T * p.nq, DV, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(attn_merge_kernel<DV>, dim3(p.T * p.nq), dim3(DV), 0, st, p);
 }
 
 }  // namespace
@@ -565,9 +575,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t st) {
   if (attn_tc_enabled() && attn_tc_supported(p)) {
     const cudaError_t e = launch_attention_tc(p, p.status, st);
     if (e != cudaSuccess || p.splits == 1) return e;
-    if (p.dv == 128) attn_merge_kernel<128><<<p.T * p.nq, 128, 0, st>>>(p);
-    else attn_merge_kernel<64><<<p.T * p.nq, 64, 0, st>>>(p);
-    return cudaGetLastError();
+    if (p.dv == 128) return launch_k(attn_merge_kernel<128>, dim3(p.T * p.nq), dim3(128), 0, st, p);
+    return launch_k(attn_merge_kernel<64>, dim3(p.T * p.nq), dim3(64), 0, st, p);
   }
   if (p.dqk == 192 && p.dv == 128) return launch_attn_t<192, 128>(p, st);
   if (p.dqk == 128 && p.dv == 128) return launch_attn_t<128, 128>(p, st);
@@ -580,28 +589,24 @@ cudaError_t launch_rope_store(const RopeParams& p, cudaStream_t st) {
   // decode-sized calls: one CTA per (token, 16 heads); prefill: up to 4 CTAs per SM walk the tokens, each
   // taking every head of its token
   const int groups = p.T <= 148 ? (p.nq + p.nkv + 15) / 16 : 1;
-  rope_store_kernel<<<dim3(std::min(p.T, 148 * 4), groups), 512, 0, st>>>(p);
-  return cudaGetLastError();
+  return launch_k(rope_store_kernel, dim3(std::min(p.T, 148 * 4), groups), dim3(512), 0, st, p);
 }
 
 cudaError_t launch_add_rmsnorm(const uint16_t* x, const uint16_t* d, const uint16_t* weight, int T, int H, float eps,
                                uint16_t* h, uint16_t* r, cudaStream_t st) {
-  add_rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(x, d, weight, H, eps, h, r);
-  return cudaGetLastError();
+  return launch_k(add_rmsnorm_kernel, dim3(T), dim3(kNormThreads), 0, st, x, d, weight, H, eps, h, r);
 }
 
 cudaError_t launch_swiglu(const uint16_t* gu, int T, int I, uint16_t* out, cudaStream_t st) {
   const size_t n8 = (size_t)T * I / 8;
   const int blocks = (int)std::min<size_t>((n8 + 255) / 256, 148 * 8);
-  swiglu_kernel<<<blocks, 256, 0, st>>>(gu, T, I, out);
-  return cudaGetLastError();
+  return launch_k(swiglu_kernel, dim3(blocks), dim3(256), 0, st, gu, T, I, out);
 }
 
 cudaError_t launch_add(const uint16_t* a, const uint16_t* b, size_t n, uint16_t* out, cudaStream_t st) {
   const size_t n8 = n / 8;
   const int blocks = (int)std::min<size_t>((n8 + 255) / 256, 148 * 8);
-  add_kernel<<<blocks, 256, 0, st>>>(a, b, n8, out);
-  return cudaGetLastError();
+  return launch_k(add_kernel, dim3(blocks), dim3(256), 0, st, a, b, n8, out);
 }
 
 }  // namespace mimo

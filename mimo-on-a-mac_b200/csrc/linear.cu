@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(kLinThreads, 1) linear_decode_kernel(const __g
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tacc = *tslot;
+  pdl_wait();  // x comes from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   bool ok = true;
 
   if (warp == 0) {
@@ -164,6 +166,8 @@ __global__ void __launch_bounds__(kLinThreads, 1) linear_decode_kernel(const __g
 // y = bf16(sum over segments, in order, of the float32 partials); four values per thread.
 __global__ void __launch_bounds__(256) linear_reduce_kernel(const float* __restrict__ part, int S, size_t n4,
                                                             uint16_t* __restrict__ y) {
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     float4 a = reinterpret_cast<const float4*>(part)[i];
     for (int s = 1; s < S; ++s) {
@@ -213,12 +217,11 @@ cudaError_t launch_linear_decode(const uint16_t* x, const uint16_t* w, int T, in
     attr_set[dev] = true;
   }
   const int items = p.tiles * S;
-  linear_decode_kernel<<<std::min(items, num_sms), kLinThreads, kLinSmem, st>>>(p);
-  e = cudaGetLastError();
+  e = launch_k(linear_decode_kernel, dim3(std::min(items, num_sms)), dim3(kLinThreads), kLinSmem, st, p);
   if (e != cudaSuccess || S == 1) return e;
   const size_t n4 = (size_t)T * N / 4;
-  linear_reduce_kernel<<<(int)std::min<size_t>((n4 + 255) / 256, (size_t)num_sms * 8), 256, 0, st>>>(part, S, n4, y);
-  return cudaGetLastError();
+  return launch_k(linear_reduce_kernel, dim3((unsigned)std::min<size_t>((n4 + 255) / 256, (size_t)num_sms * 8)),
+                  dim3(256), 0, st, (const float*)part, S, n4, y);
 }
 
 }  // namespace mimo

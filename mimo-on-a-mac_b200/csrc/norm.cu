@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t* _
                                                                const uint16_t* __restrict__ weight, int H,
                                                                float eps, uint16_t* __restrict__ y) {
   __shared__ float warp_ss[kNormThreads / 32];
+  pdl_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  pdl_launch_dependents();
   const size_t row = (size_t)blockIdx.x * H;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row);
   const int chunks = H / 8;
@@ -73,8 +75,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t* _
 
 cudaError_t launch_rmsnorm(const uint16_t* x, const uint16_t* weight, int T, int H, float eps, uint16_t* y,
                            cudaStream_t st) {
-  rmsnorm_kernel<<<T, kNormThreads, 0, st>>>(x, weight, H, eps, y);
-  return cudaGetLastError();
+  return launch_k(rmsnorm_kernel, dim3(T), dim3(kNormThreads), 0, st, x, weight, H, eps, y);
 }
 
 }  // namespace mimo
