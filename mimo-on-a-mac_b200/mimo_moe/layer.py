@@ -111,15 +111,22 @@ def attention(q: torch.Tensor, cache: KVCache, cfg: AttentionConfig, pos0: int, 
     dev = q.device
     o = out if out is not None else torch.empty(T, cfg.n_heads, cfg.v_head_dim, dtype=torch.bfloat16, device=dev)
     L = lib()
-    max_splits = 64 if splits <= 0 else splits
+    if splits <= 0:
+        # the library's own choice never exceeds two CTAs per SM over the call's 64-row query tiles (prefill:
+        # one split, no workspace)
+        G = cfg.n_heads // cfg.n_kv_heads
+        tiles = -(-T * G // 64)
+        max_splits = min(64, -(-2 * 148 // (tiles * cfg.n_kv_heads)))
+    else:
+        max_splits = splits
     nb = L.mimo_moe_layer_attention_workspace_bytes(T, cfg.n_heads, cfg.v_head_dim, max_splits)
-    ws = workspace(nb, dev)
+    ws = workspace(nb, dev) if nb else None
     if sinks is not None:
         sinks = sinks.to(device=dev, dtype=torch.float32).contiguous()
     check(L.mimo_moe_layer_attention(q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), _ptr(sinks), T,
                                      cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.v_head_dim, float(cfg.scale),
-                                     cfg.window, int(pos0), cache.cap, int(splits), o.data_ptr(), ws.data_ptr(),
-                                     ws.numel(), _ptr(status), _stream()), "attention")
+                                     cfg.window, int(pos0), cache.cap, int(splits), o.data_ptr(), _ptr(ws),
+                                     ws.numel() if ws is not None else 0, _ptr(status), _stream()), "attention")
     return o
 
 
