@@ -254,24 +254,32 @@ class DecoderLayer:
     def new_cache(self, max_len: int, max_chunk: int = 4096) -> KVCache:
         return KVCache.for_layer(self.attn.cfg, max_len, max_chunk, self.attn.w_o.device)
 
-    def __call__(self, x: torch.Tensor, cache: KVCache) -> torch.Tensor:
-        _need_cuda(x, "x")
-        x = x.to(torch.bfloat16).contiguous()
-        r = rmsnorm(x, self.input_norm, self.eps)
+    def parts(self, x: torch.Tensor, cache: KVCache, r: Optional[torch.Tensor] = None):
+        """The layer up to its last residual add: returns (h, y) with out = bf16(h + y).  r, when given, is
+        input_layernorm(x) already computed (a stack folds it into the previous layer's last add)."""
+        if r is None:
+            r = rmsnorm(x, self.input_norm, self.eps)
         a = self.attn(r, cache)
         h, r2 = add_rmsnorm(x, a, self.post_norm, self.eps)
         y = self.mlp(r2)
-        out = add(h, y)
         if self.trace is not None:
-            self.trace({"x": x, "r": r, "a": a, "h": h, "r2": r2, "y": y, "out": out})
-        return out
+            self.trace({"x": x, "r": r, "a": a, "h": h, "r2": r2, "y": y})
+        return h, y
+
+    def __call__(self, x: torch.Tensor, cache: KVCache) -> torch.Tensor:
+        _need_cuda(x, "x")
+        x = x.to(torch.bfloat16).contiguous()
+        h, y = self.parts(x, cache)
+        return add(h, y)
 
 
 class DecoderStack:
     """Decoder layers run in order over one residual stream (the engine's layer loop, model.py:294-336, without
     the embedding, final norm and lm_head): each layer's KV cache lives here, every layer of a call works at
-    the same position, and the output is a fixed buffer per shape, so a decode step replays as one CUDA
-    graph (the graph keeps the position it was captured at; `at(pos)` sets it for eager calls and captures)."""
+    the same position, each layer's last residual add runs together with the next layer's input norm (one
+    add + RMSNorm pass, bit-identical to the two), and the output is a fixed buffer per shape, so a decode
+    step replays as one CUDA graph (the graph keeps the position it was captured at; `at(pos)` sets it for
+    eager calls and captures)."""
 
     def __init__(self, layers, max_len: int, max_chunk: int = 4096):
         if not layers:
@@ -290,9 +298,17 @@ class DecoderStack:
         return self.caches[0].offset
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        h = x
-        for layer, cache in zip(self.layers, self.caches):
-            h = layer(h, cache)
+        _need_cuda(x, "x")
+        h = x.to(torch.bfloat16).contiguous()
+        r = None
+        n = len(self.layers)
+        for i, (layer, cache) in enumerate(zip(self.layers, self.caches)):
+            hh, y = layer.parts(h, cache, r)
+            if i + 1 < n:   # this layer's residual add and the next layer's input norm in one pass
+                nxt = self.layers[i + 1]
+                h, r = add_rmsnorm(hh, y, nxt.input_norm, nxt.eps)
+            else:
+                h = add(hh, y)
         key = (tuple(h.shape), h.device)
         if key not in self._out:
             self._out[key] = torch.empty_like(h)
