@@ -22,7 +22,6 @@
 // Key blocks start at multiples of 128 positions and the cache capacity is a multiple of 128, so a block
 // never wraps in the ring; keys outside a row's window are masked (P = 0).  Every wait is bounded and sets
 // MIMO_ETIMEOUT in the status word; the producer drains its copies and the issuer its MMAs before exit.
-#include <climits>
 #include <cstring>
 
 #include "common.cuh"
