@@ -88,6 +88,7 @@ def rope_store(qkv: torch.Tensor, cfg: AttentionConfig, cache: KVCache, pos0: in
     """mimo_v2.py:130-139: RoPE on q and k at positions pos0.., v * attention_value_scale, k/v appended to the
     cache.  Returns q bf16 [T, n_heads, head_dim]."""
     _need_cuda(qkv, "qkv")
+    qkv = qkv.to(torch.bfloat16).contiguous()
     T = qkv.shape[0]
     q = q_out if q_out is not None else torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=torch.bfloat16,
                                                     device=qkv.device)
@@ -107,6 +108,7 @@ def attention(q: torch.Tensor, cache: KVCache, cfg: AttentionConfig, pos0: int, 
     rows run on the tcgen05 kernel (cache capacity a multiple of 128), decode-sized calls on the split-key
     mma.sync kernel.  Returns bf16 [T, n_heads, v_head_dim]."""
     _need_cuda(q, "q")
+    q = q.to(torch.bfloat16).contiguous()
     T = q.shape[0]
     dev = q.device
     o = out if out is not None else torch.empty(T, cfg.n_heads, cfg.v_head_dim, dtype=torch.bfloat16, device=dev)
@@ -137,8 +139,13 @@ def linear(x: torch.Tensor, weight: torch.Tensor, workspace_ok: bool = True) -> 
     """nn.Linear without bias: x bf16 [T, K] . weight bf16 [N, K]^T -> bf16 [T, N].  Decode sizes (T <= 16) run
     on the library's tcgen05 stream kernel (mimo_moe_layer_linear, the weights read once); larger T are plain
     GEMMs on cuBLAS."""
+    _need_cuda(x, "x")
+    x = x.to(torch.bfloat16).contiguous()
+    weight = weight.to(torch.bfloat16).contiguous()
     T, K = x.shape
     N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise ValueError(f"linear: x has {K} features, weight expects {weight.shape[1]}")
     if T > DECODE_ROWS or N % 8 or K % 64 or K < 256:
         return torch.matmul(x, weight.t())
     y = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
@@ -152,6 +159,11 @@ def linear(x: torch.Tensor, weight: torch.Tensor, workspace_ok: bool = True) -> 
 
 def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: Optional[torch.Tensor], eps: float):
     """h = bf16(x + delta), r = rmsnorm(h) * weight (one pass).  Returns (h, r)."""
+    _need_cuda(x, "x")
+    x = x.to(torch.bfloat16).contiguous()
+    delta = delta.to(torch.bfloat16).contiguous()
+    if delta.shape != x.shape:
+        raise ValueError(f"add_rmsnorm: shapes {tuple(x.shape)} and {tuple(delta.shape)} differ")
     T, H = x.shape
     h = torch.empty_like(x)
     r = torch.empty_like(x)
@@ -163,6 +175,8 @@ def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, weight: Optional[torch.Ten
 
 def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
     """mlx_lm swiglu(gate, up) = silu(gate) * up in bf16 steps; gate_up [T, 2I] = [gate | up]."""
+    _need_cuda(gate_up, "gate_up")
+    gate_up = gate_up.to(torch.bfloat16).contiguous()
     T, I2 = gate_up.shape
     out = torch.empty(T, I2 // 2, dtype=torch.bfloat16, device=gate_up.device)
     check(lib().mimo_moe_layer_swiglu(gate_up.data_ptr(), T, I2 // 2, out.data_ptr(), _stream()), "swiglu")
@@ -170,6 +184,12 @@ def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
 
 
 def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """bf16(a + b), elementwise (the decoder layer's residual add)."""
+    _need_cuda(a, "a")
+    a = a.to(torch.bfloat16).contiguous()
+    b = b.to(torch.bfloat16).contiguous()
+    if a.shape != b.shape:
+        raise ValueError(f"add: shapes {tuple(a.shape)} and {tuple(b.shape)} differ")
     out = torch.empty_like(a)
     check(lib().mimo_moe_layer_add(a.data_ptr(), b.data_ptr(), a.numel(), out.data_ptr(), _stream()), "add")
     return out
