@@ -441,8 +441,8 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
 
     # per-phase device times from an eager pass (CUDA event pairs between the layer's launches)
     names = ["input_norm", "qkv_gemm", "rope_store", "attention", "o_gemm", "add_norm", "moe_block", "add"]
-    acc = {n: 0.0 for n in names}
-    nprof = 20 if decode else 3
+    samples = {n: [] for n in names}
+    nprof = 21 if decode else 7
     for i in range(nprof):
         x = xs[i % nb]
         cache.offset = pos0
@@ -458,7 +458,9 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
         add(h, y); ev[8].record()
         torch.cuda.synchronize()
         for j, n in enumerate(names):
-            acc[n] += ev[j].elapsed_time(ev[j + 1]) / nprof
+            samples[n].append(ev[j].elapsed_time(ev[j + 1]))
+    # the median per phase: an eager pass can catch a host stall between two launches in one iteration
+    acc = {n: statistics.median(v) for n, v in samples.items()}
     hbm, tflops_peak, peak_kind = peaks()
     attn_w_bytes = (attn.w_qkv.numel() + attn.w_o.numel()) * 2
     keys = pos0 + T

@@ -129,10 +129,19 @@ def test_attention_split_counts_agree(gpu):
         assert rel(o, outs[0]) <= 1e-2
 
 
-@pytest.mark.parametrize("kind,T,pos0,cap", [("full", 37, 0, 64), ("swa", 8, 300, 135), ("swa", 130, 10, 257)])
-def test_rope_store_matches_oracle(gpu, kind, T, pos0, cap):
+@pytest.mark.parametrize("kind,dims,T,pos0,cap", [
+    # T <= 16: the warp-per-(token, head) decode kernel
+    ("swa", {}, 8, 300, 135), ("full", {}, 1, 4000, 4096),
+    ("swa", {"rotary_dim": 34}, 12, 0, 256),     # pass-through dims not 16-byte aligned: bf16-pair copies
+    ("full", {"rotary_dim": 100}, 9, 7, 64),      # two rotary pairs per lane
+    ("full", {"rotary_dim": 160}, 16, 3, 128),    # up to four rotary pairs per lane
+    # larger T: one CTA per (token, 16 heads) up to 148 tokens, then CTAs walking the tokens
+    ("full", {}, 37, 0, 64), ("swa", {}, 130, 10, 257), ("full", {}, 300, 5, 320),
+    ("swa", {"rotary_dim": 34}, 24, 0, 256),
+])
+def test_rope_store_matches_oracle(gpu, kind, dims, T, pos0, cap):
     from mimo_moe.layer import KVCache, bf16_value, rope_store
-    cfg = _cfg(kind, v_scale=0.707)
+    cfg = _cfg(kind, v_scale=0.707, **dims)
     g = torch.Generator().manual_seed(T)
     qkv = rnd(g, T, cfg.qkv_width)
     cache = KVCache(cfg, cap, gpu)
