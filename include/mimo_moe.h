@@ -273,6 +273,35 @@ int mimo_moe_experts_static(const uint16_t* x, const mimo_moe_pools* pools, cons
                             void* stream);
 
 /*
+ * Expert residency table (host) — replaces engine/mimo_stream/cache.py:13-65 (SlotCache): which experts
+ * of one layer occupy its S device slots, with the reference's decayed-LFU eviction.  For a model or a
+ * device where a layer's experts do not all fit in HBM; the caller copies each returned (expert, slot)
+ * load into the slot and hands the kernels the slot map (mimo_moe_prefill's slot_of, or per-slot ids
+ * to mimo_moe_group_routes / mimo_moe_experts).
+ *   create(S, E): S slots (1 <= S <= E) for experts [0, E); NULL on bad sizes.  destroy frees it.
+ *   preload(experts, n): experts[i] into slot i for i < min(n, S) (cache.py:24-28); loads written to
+ *     load_expert/load_slot, *n_loads = min(n, S).
+ *   resolve(needed, n, count, stats): one tick; needed = the step's distinct expert ids; counts them
+ *     (count != 0), stamps their last use, assigns the missing ones the lowest-scoring slots
+ *     (count * 1e12 + last use; empty slots -1; slots of needed experts never taken; ties and victim
+ *     order by ascending slot), and adds to the hit / miss counters (stats != 0) (cache.py:30-62).
+ *     The loads are written in `needed` order.  MIMO_ERANGE, with nothing changed, when n > S;
+ *     MIMO_EINVAL for repeated or out-of-range ids.
+ *   decay(): halves every count (cache.py:64-65; the engine calls it every 16 decode tokens).
+ *   state(): copies slot_of [E] (expert -> slot or -1), expert_in [S] (slot -> expert or -1) and the
+ *     hit / miss counters (any pointer may be NULL).
+ * Host-only calls (no CUDA); one table per layer, not thread-safe.
+ */
+void* mimo_moe_slot_cache_create(int32_t n_slots, int32_t n_experts);
+void mimo_moe_slot_cache_destroy(void* cache);
+int mimo_moe_slot_cache_preload(void* cache, const int32_t* experts, int32_t n, int32_t* load_expert,
+                                int32_t* load_slot, int32_t* n_loads);
+int mimo_moe_slot_cache_resolve(void* cache, const int32_t* needed, int32_t n, int32_t count, int32_t stats,
+                                int32_t* load_expert, int32_t* load_slot, int32_t* n_loads);
+int mimo_moe_slot_cache_decay(void* cache);
+int mimo_moe_slot_cache_state(void* cache, int32_t* slot_of, int32_t* expert_in, int64_t* hits, int64_t* misses);
+
+/*
  * Benchmark support (no counterpart in the reference).  mimo_moe_profile_enable(n) with n > 0 makes
  * the library record a CUDA event pair around each of the next n expert-path kernel launches on the
  * launching stream (the events are created here, once); n = 0 turns it off.  mimo_moe_profile_read()

@@ -55,6 +55,13 @@ SIGNATURES = {
     "mimo_moe_experts_routes": (c_int32, [c_void_p, c_int32, c_int32, POINTER(Pools), c_int32, c_void_p,
                                           c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32,
                                           c_void_p, c_size_t, c_void_p, c_void_p]),
+    "mimo_moe_slot_cache_create": (c_void_p, [c_int32, c_int32]),
+    "mimo_moe_slot_cache_destroy": (None, [c_void_p]),
+    "mimo_moe_slot_cache_preload": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
+    "mimo_moe_slot_cache_resolve": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                              c_void_p]),
+    "mimo_moe_slot_cache_decay": (c_int32, [c_void_p]),
+    "mimo_moe_slot_cache_state": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "mimo_moe_peer_alloc": (c_int32, [c_size_t, c_void_p, c_void_p]),
     "mimo_moe_peer_open": (c_int32, [c_void_p, c_void_p]),
     "mimo_moe_peer_close": (c_int32, [c_void_p]),

@@ -14,7 +14,7 @@ INCLUDE = PKG.parent.parent / "include"
 LIB = PKG / "libmimo_moe.so"
 LIB_TESTKIT = PKG / "libmimo_moe_testkit.so"
 SOURCES = ["api.cu", "router.cu", "dispatch.cu", "experts.cu", "noalloc.cu", "tma.cu", "tc_experts.cu", "peer.cu",
-           "norm.cu", "ep_plan.cu", "layer.cu", "attn_tc.cu", "linear.cu", "loader.cpp"]
+           "norm.cu", "ep_plan.cu", "layer.cu", "attn_tc.cu", "linear.cu", "loader.cpp", "slot_cache.cpp"]
 TESTKIT_SOURCES = ["synth.cu", "testkit.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
