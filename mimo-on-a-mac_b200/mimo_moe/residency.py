@@ -46,8 +46,11 @@ class SlotCache:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
-            lib().mimo_moe_slot_cache_destroy(h)
             self._h = None
+            try:
+                lib().mimo_moe_slot_cache_destroy(h)
+            except Exception:   # interpreter shutdown: the library may already be gone
+                pass
 
     @staticmethod
     def _ids(ids) -> np.ndarray:
