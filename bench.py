@@ -6,7 +6,7 @@
   python bench.py --impl reference ...     # the reference path on the host cores (no GPU)
 
 One step = one MoE layer (router -> dispatch -> MXFP4 experts -> combine) over one batch of synthetic
-tokens, inputs resident in HBM.  The default run prints ONE JSON line: the headline workload (BASELINE
+tokens, inputs resident in HBM.  The default run prints ONE JSON line: the headline workload (BASELINE.json
 config 1 at B = 8 rows, decode / MTP verify, free routing, 256 experts of 13,369,344 B) and, on one GPU,
 nested results under "configs" for the other configurations the metric names: decode1 (config 0),
 decode8_overlap (config 1's forced-overlap variant: rows share experts) and prefill2048 (config 2), each
@@ -984,7 +984,7 @@ def bench_model(args):
 
 
 def bench_stack(args):
-    """BASELINE config 3: one decode step = B tokens per GPU through L MoE layers (RMSNorm, unit weight,
+    """BASELINE.json config 3: one decode step = B tokens per GPU through L MoE layers (RMSNorm, unit weight,
     between layers), experts sharded 256/N per GPU for every layer, the peer-memory exchange per layer
     on N > 1; the whole step replays as one CUDA graph.  Every layer's experts are seeded independently
     (pool layer index l, router W seed 1 + 1000 l, bias 0)."""

@@ -1,4 +1,4 @@
-"""Batched CPU restatement of the pair path, for parity checks at the BASELINE sizes.
+"""Batched CPU restatement of the pair path, for parity checks at the BASELINE.json sizes.
 
 TEST INFRASTRUCTURE ONLY (imported by `tests/` and the CPU legs of `bench.py`, never by the library).
 

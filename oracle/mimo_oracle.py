@@ -371,7 +371,7 @@ def rmsnorm(x, weight=None, eps: float = 1e-6) -> np.ndarray:
 
 
 def moe_stack(x, layers, eps: float = 1e-6, R: int = R):
-    """BASELINE config 3's decode stack: x_{l+1} = rmsnorm(moe_block_l(x_l)) between layers, unit weight;
+    """BASELINE.json config 3's decode stack: x_{l+1} = rmsnorm(moe_block_l(x_l)) between layers, unit weight;
     returns the last layer's MoE output and every layer's routes.  layers: [(W, bias, Pool), ...]."""
     routes = []
     y = None

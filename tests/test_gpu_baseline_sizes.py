@@ -1,4 +1,4 @@
-"""Parity at the BASELINE sizes (full 256-expert MiMo layer), through the C ABI, against the batched CPU
+"""Parity at the BASELINE.json sizes (full 256-expert MiMo layer), through the C ABI, against the batched CPU
 restatement of the reference's pair path (oracle/batched.py, pinned bit for bit to oracle/mimo_oracle.py
 by tests/test_oracle.py).
 

@@ -353,7 +353,7 @@ def test_downstream_logit_kl_through_a_random_head(gpu):
 
 
 def test_prefill_at_full_size_agrees_with_the_per_route_path(gpu):
-    """Size-independent check at BASELINE scale (T = 2048, 256 experts): the prefill path (64-route
+    """Size-independent check at BASELINE.json scale (T = 2048, 256 experts): the prefill path (64-route
     units, bf16 pair outputs, weighted fixed-order combine) against the per-route partials of the
     expert-parallel building block with bf16 rounding (the stream-K decode kernel: 8-route units, each
     512-value K group accumulated on its own and the groups added in order) followed by the route-order

@@ -1,4 +1,4 @@
-"""RMSNorm and the multi-layer decode stack (BASELINE config 3) on the GPU, through the C ABI.
+"""RMSNorm and the multi-layer decode stack (BASELINE.json config 3) on the GPU, through the C ABI.
 
 Bars: RMSNorm within one bf16 ulp of the oracle everywhere and bit-identical on >= 99.9% of elements
 (the oracle's float64 sum of squares versus the kernel's fixed float32 order); the stack equals the

@@ -171,7 +171,7 @@ def test_rmsnorm_oracle_properties():
 
 
 def test_batched_pair_path_equals_the_oracle_bit_for_bit():
-    """oracle/batched.py (torch, one float64 product per expert, used for the BASELINE-size GPU checks)
+    """oracle/batched.py (torch, one float64 product per expert, used for the GPU checks at the BASELINE.json sizes)
     against mimo_oracle.moe_pairs on full-size experts: every output bit equal, with a slot map, shared
     experts across rows and the M = 1 case."""
     import torch
@@ -204,7 +204,7 @@ def test_batched_pair_path_equals_the_oracle_bit_for_bit():
 
 
 def test_overlap_bias_gives_the_config1_expert_sharing():
-    """BASELINE config 1's forced-overlap variant: consecutive rows of the seeded 8-row decode batches share
+    """BASELINE.json config 1's forced-overlap variant: consecutive rows of the seeded 8-row decode batches share
     2.6 +- 0.1 of their 8 experts under synth.overlap_bias() (free routing shares ~0.25)."""
     W = synth.router_weight().float().numpy()
     b = synth.overlap_bias().numpy()
