@@ -108,9 +108,11 @@ class ExpertCache:
     """One MoE layer whose E experts live in host memory (the reference layout, `host` = {gate,up,down}_{w,s}
     CPU tensors with E experts each; pinned here if they are not) with `n_slots` of them resident on
     `device`.  __call__(x, router_w, bias) -> y bf16 [T, H], the reference's per-layer step
-    (model.py:184-222 decode / verify, the prefill path with every routed expert made resident); the step
-    raises ValueError when it routes to more distinct experts than there are slots.  Every
-    DECODE_DECAY_EVERY single-token calls the counts decay (model.py:348-354)."""
+    (model.py:184-222 decode / verify); a prefill step (T > 8) also makes every routed expert resident
+    through the table, where the reference's _moe_prefill (model.py:230-285) leaves the table alone and
+    streams the non-resident experts through staging banks.  A step raises ValueError when it routes to
+    more distinct experts than there are slots.  Every DECODE_DECAY_EVERY single-token calls the counts
+    decay (model.py:348-354)."""
 
     def __init__(self, host: Dict[str, torch.Tensor], n_slots: int, device=None, topk: int = TOPK):
         self.host = {}
