@@ -19,8 +19,15 @@ import numpy as np
 OUT = Path(__file__).resolve().with_name("slot_cache.json")
 
 
-def _reference_slot_cache():
-    root = os.environ.get("MIMO_REFERENCE_ROOT")
+# (seed, slots, experts, decode steps, preload, most tokens per step)
+RUNS = [(1, 64, 256, 240, True, 1),      # decode B=1, a quarter of the experts resident
+        (2, 96, 256, 160, True, 4),      # small verify batches
+        (3, 48, 256, 120, False, 2),     # starting empty: ties among empty slots
+        (4, 16, 64, 200, True, 1)]       # a small table: many evictions
+
+
+def reference_slot_cache(root=None):
+    root = root or os.environ.get("MIMO_REFERENCE_ROOT")
     if not root:
         sys.exit("set MIMO_REFERENCE_ROOT to the reference checkout (the directory holding engine/mimo_stream)")
     path = Path(root) / "engine" / "mimo_stream" / "cache.py"
@@ -66,14 +73,13 @@ def _run(SlotCache, seed: int, S: int, E: int, steps: int, preload: bool, max_to
     return {"seed": seed, "S": S, "E": E, "preload": preload, "log": log}
 
 
+def runs(SlotCache):
+    return [_run(SlotCache, *r) for r in RUNS]
+
+
 def main():
-    SlotCache = _reference_slot_cache()
-    runs = [_run(SlotCache, 1, 64, 256, 240, True, 1),      # decode B=1, a quarter of the experts resident
-            _run(SlotCache, 2, 96, 256, 160, True, 4),      # small verify batches
-            _run(SlotCache, 3, 48, 256, 120, False, 2),     # starting empty: ties among empty slots
-            _run(SlotCache, 4, 16, 64, 200, True, 1)]       # a small table: many evictions
     OUT.write_text(json.dumps({"source": "engine/mimo_stream/cache.py (SlotCache), run unchanged",
-                               "runs": runs}, separators=(",", ":")))
+                               "runs": runs(reference_slot_cache())}, separators=(",", ":")))
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes)")
 
 

@@ -121,3 +121,16 @@ def test_preload_on_a_filled_table_stays_consistent():
     assert list(ei) == [4, 9, 3, -1]
     assert so[4] == 0 and so[9] == 1 and so[3] == 2 and so[1] == -1 and so[2] == -1
     assert all(so[e] == s for s, e in enumerate(ei) if e >= 0)
+
+
+def test_fixture_regenerates_from_the_reference():
+    """Where the reference checkout is present (the build's reference root), its own SlotCache, loaded by path
+    and run unchanged, reproduces the committed runs exactly."""
+    import importlib.util
+    from __graft_entry__ import REFERENCE_ROOT
+    if not (REFERENCE_ROOT / "engine" / "mimo_stream" / "cache.py").exists():
+        pytest.skip("reference checkout not present")
+    spec = importlib.util.spec_from_file_location("make_slot_cache_golden", GOLDEN.with_name("make_slot_cache_golden.py"))
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    assert json.loads(json.dumps(gen.runs(gen.reference_slot_cache(str(REFERENCE_ROOT))))) == _runs()
