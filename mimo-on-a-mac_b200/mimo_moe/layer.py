@@ -216,6 +216,14 @@ class Attention:
 
     def __call__(self, r: torch.Tensor, cache: KVCache) -> torch.Tensor:
         T = r.shape[0]
+        cfg = self.cfg
+        # the attention call's own check (every key visible to the chunk still in the ring), made before the
+        # cache append so a refused chunk leaves the cache as it was
+        first = max(0, cache.offset - cfg.window + 1) if cfg.window > 0 else 0
+        need = cache.offset + T - first
+        if need > cache.cap:
+            raise ValueError(f"attention: {T} tokens at position {cache.offset} need {need} cache slots; the cache "
+                             f"has {cache.cap}")
         qkv = linear(r, self.w_qkv)
         q = rope_store(qkv, self.cfg, cache, cache.offset)
         o = attention(q, cache, self.cfg, cache.offset, self.sinks)

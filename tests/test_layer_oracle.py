@@ -140,3 +140,35 @@ def test_decode_linear_host_checks_and_workspace_without_a_device():
         assert nb % row == 0 and nb // row in (0, 2, 4, 8, 16, 32)
         S = max(1, nb // row)
         assert K % (64 * S) == 0 and K // S >= 256
+
+
+def test_attention_refuses_a_chunk_the_cache_cannot_hold_before_touching_it():
+    """A chunk whose visible keys would not all fit the cache (full attention: past its end; sliding window:
+    more than the ring holds) raises before the cache append, so the cache and its position are unchanged
+    (host-side check, no device needed); the bound is the attention entry point's own."""
+    import torch
+    from mimo_moe.layer import Attention, KVCache, mimo_full_attention, mimo_sliding_attention
+    for cfg, cap, offset, T in ((mimo_full_attention(), 256, 250, 8), (mimo_sliding_attention(), 256, 1000, 130)):
+        H = 256
+        wq = torch.zeros(cfg.n_heads * cfg.head_dim, H)
+        wk = torch.zeros(cfg.n_kv_heads * cfg.head_dim, H)
+        wv = torch.zeros(cfg.n_kv_heads * cfg.v_head_dim, H)
+        wo = torch.zeros(H, cfg.n_heads * cfg.v_head_dim)
+        attn = Attention(cfg, wq, wk, wv, wo, torch.zeros(cfg.n_heads) if cfg.sinks else None, device="cpu")
+        cache = KVCache(cfg, cap, "cpu")
+        cache.offset = offset
+        with pytest.raises(ValueError, match="cache slots"):
+            attn(torch.zeros(T, H, dtype=torch.bfloat16), cache)
+        assert cache.offset == offset and not cache.k.any() and not cache.v.any()
+    # the same bound as mimo_moe_layer_attention's (a ring shorter than window + T - 1 still takes a chunk
+    # whose earliest visible key is position 0)
+    import mimo_moe
+    L = mimo_moe.lib()
+    p = 1 << 20
+    for window, pos0, T, cap, ok in ((128, 0, 8, 128, True), (128, 0, 129, 128, False), (128, 1000, 129, 256, True),
+                                     (128, 1000, 130, 256, False), (0, 250, 6, 256, True), (0, 250, 7, 256, False)):
+        first = max(0, pos0 - window + 1) if window > 0 else 0
+        assert (pos0 + T - first <= cap) == ok
+        if not ok:   # refused on the host, before any launch
+            assert L.mimo_moe_layer_attention(p, p, p, None, T, 64, 8, 192, 128, 0.1, window, pos0, cap, 1, p, None,
+                                              0, None, None) == 1
