@@ -164,6 +164,8 @@ class ExpertCache:
 
     def __call__(self, x: torch.Tensor, router_w: torch.Tensor, bias: Optional[torch.Tensor] = None,
                  status: Optional[torch.Tensor] = None, return_routes: bool = False):
+        if router_w.shape[0] != self.E:
+            raise ValueError(f"router has {router_w.shape[0]} experts, the cache {self.E}")
         x = x.to(device=self.device, dtype=torch.bfloat16).contiguous()
         T = x.shape[0]
         idx, w = router(x, router_w, bias, self.topk)
