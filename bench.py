@@ -218,27 +218,33 @@ def expert_source(device_pool=None, seed: int = 0, layer: int = 0):
 
 
 def cpu_port_rates(workload: str, budget_s: float, device_pool=None, samples: int = 1):
-    """The vectorised torch-CPU restatement of the path (oracle/cpu_path.py) on all host threads, in its
-    two variants (float32 dequant cached outside the clock; dequant on the fly): tok/s of each, median
-    over `samples` batches, each a bounded sample of one step (experts until `budget_s`, extrapolated)."""
+    """The CPU restatement of the path (oracle/cpu_path.py) on all host threads, in its variants: float32
+    torch matrix products with the dequantised experts cached outside the clock or dequantised on the fly,
+    and the compiled kernel on the packed MXFP4 bytes (when oracle/libmimo_cpu_port.so was built): tok/s of
+    each, median over `samples` batches, each a bounded sample of one step (experts until `budget_s`,
+    extrapolated)."""
     import torch
     from mimo_moe import synthetic
-    from oracle.cpu_path import CpuLayer
+    from oracle.cpu_path import CpuLayer, native
     torch.set_num_threads(_host_cores())
     T = WORKLOADS[workload][0]
     layer = CpuLayer(synthetic.router_weight(), routing_bias(workload), expert_source(device_pool))
     xs = batches(workload)
     out = {}
-    for cached in (True, False):
+    variants = [("port_fp32_cached", True, False), ("port_on_the_fly", False, False)]
+    if native() is not None:
+        variants.append(("port_mxfp4_native", False, True))
+    for name, cached, packed in variants:
         rates, info = [], None
         for s in range(samples):
-            sec, done, U = layer.step_time(xs[s % len(xs)], cached, budget_s, wall_s=2 * budget_s)
+            sec, done, U = layer.step_time(xs[s % len(xs)], cached, budget_s, wall_s=2 * budget_s, packed=packed)
             rates.append(T / sec)
             info = (done, U)
-        name = "port_fp32_cached" if cached else "port_on_the_fly"
         out[name] = {"value": statistics.median(rates), "unit": "tok/s", "cores": torch.get_num_threads(),
                      "sample": f"{info[0]} of {info[1]} distinct experts of one {workload} batch, extrapolated "
                                f"by U/done; median of {samples} batch(es)"}
+        if packed:
+            out[name]["isa"] = "avx2+fma" if native().mimo_cpu_port_isa() == 2 else "scalar"
     return out
 
 

@@ -9,22 +9,67 @@ pair path (model.py:173-182, 221-228; bf16 expert outputs), with the fixed route
 threads, i.e. at the speed a CPU implementation of the path would have, not exactly rounded like
 mimo_oracle (which is the checker).
 
-Two variants of the expert weights:
+Three variants of the expert weights:
   cached     every needed expert dequantised to float32 before the clock starts (memory permitting:
              13.4 MB of MXFP4 become 100 MB of float32 per expert);
-  on the fly the MXFP4 bytes are dequantised inside the timed region, per expert and call.
+  on the fly the MXFP4 bytes are dequantised inside the timed region, per expert and call;
+  native     the packed MXFP4 bytes read directly by a compiled CPU kernel (oracle/cpu_mxfp4.c, built by
+             oracle/cpu_port_build.py; AVX2 + FMA where the host has them, OpenMP over output rows).
 Time per step = router + sum over the batch's distinct experts + combine; a bounded sample processes
 the first experts until the budget is spent and extrapolates by U / done (experts are alike in size).
 """
 from __future__ import annotations
 
+import ctypes
 import time
+from pathlib import Path
 from typing import Callable, Dict, Optional
 
 import numpy as np
 import torch
 
 from . import batched as B
+
+_NATIVE_LIB = Path(__file__).resolve().with_name("libmimo_cpu_port.so")
+_native = None
+
+
+def native():
+    """The compiled CPU kernel (oracle/libmimo_cpu_port.so), or None when it was not built."""
+    global _native
+    if _native is None and _NATIVE_LIB.exists():
+        try:
+            L = ctypes.CDLL(str(_NATIVE_LIB))
+        except OSError:   # built for another host: the variant is left out
+            return None
+        p = ctypes.c_void_p
+        L.mimo_cpu_port_expert.argtypes = [p, ctypes.c_int, ctypes.c_int, ctypes.c_int, p, p, p, p, p, p,
+                                           ctypes.c_int, p, p]
+        L.mimo_cpu_port_expert.restype = ctypes.c_int
+        L.mimo_cpu_port_isa.restype = ctypes.c_int
+        L.mimo_cpu_port_force_scalar.argtypes = [ctypes.c_int]
+        _native = L
+    return _native
+
+
+def native_expert(raw: Dict[str, torch.Tensor], X: torch.Tensor, pairs: bool) -> torch.Tensor:
+    """Expert `raw` (its MXFP4 tensors) on the rows X [R, H] (bf16 values) through the compiled kernel, eight
+    rows per call: float32 [R, H] down products (bf16-rounded when pairs)."""
+    L = native()
+    x = np.ascontiguousarray(X.float().numpy())
+    R_all, H = x.shape
+    a = {k: np.ascontiguousarray(v.numpy()) for k, v in raw.items()}
+    I = a["gate_w"].shape[0]
+    out = np.empty((R_all, H), np.float32)
+    hbuf = np.empty((8, I), np.float32)
+    for r0 in range(0, R_all, 8):
+        R = min(8, R_all - r0)
+        rc = L.mimo_cpu_port_expert(x[r0:].ctypes.data, R, H, I, a["gate_w"].ctypes.data, a["gate_s"].ctypes.data,
+                                    a["up_w"].ctypes.data, a["up_s"].ctypes.data, a["down_w"].ctypes.data,
+                                    a["down_s"].ctypes.data, int(pairs), hbuf.ctypes.data, out[r0:].ctypes.data)
+        if rc != 0:
+            raise ValueError(f"mimo_cpu_port_expert: bad sizes (R={R}, H={H}, I={I})")
+    return torch.from_numpy(out)
 
 
 def _bf16(a: torch.Tensor) -> torch.Tensor:
@@ -55,9 +100,10 @@ class CpuLayer:
         self.expert = expert
 
     def step_time(self, x: torch.Tensor, cached: bool, budget_s: float, wall_s: Optional[float] = None,
-                  min_experts: int = 2):
+                  min_experts: int = 2, packed: bool = False):
         """Seconds of one layer step for the token rows x [T, H] (bf16 values), measured on a bounded
-        sample.  Returns (seconds, experts done, distinct experts U)."""
+        sample (packed: the compiled kernel on the MXFP4 bytes; else float32 weights, cached or dequantised
+        on the fly).  Returns (seconds, experts done, distinct experts U)."""
         xf = x.float()
         T = xf.shape[0]
         t0 = time.perf_counter()
@@ -74,14 +120,18 @@ class CpuLayer:
             raw = self.expert(int(e))                    # bytes generated / loaded outside the clock
             ps = torch.from_numpy(np.nonzero(flat == e)[0])
             X = xf[ps // inds.shape[1]]
-            if cached:
-                Wg, Wu, Wd = (B.dequant(raw[f"{n}_w"], raw[f"{n}_s"]) for n in ("gate", "up", "down"))
+            if packed:
                 t1 = time.perf_counter()
+                d = native_expert(raw, X, pairs)
             else:
-                t1 = time.perf_counter()
-                Wg, Wu, Wd = (B.dequant(raw[f"{n}_w"], raw[f"{n}_s"]) for n in ("gate", "up", "down"))
-            h = _swiglu(X @ Wg.T, X @ Wu.T)
-            d = h @ Wd.T
+                if cached:
+                    Wg, Wu, Wd = (B.dequant(raw[f"{n}_w"], raw[f"{n}_s"]) for n in ("gate", "up", "down"))
+                    t1 = time.perf_counter()
+                else:
+                    t1 = time.perf_counter()
+                    Wg, Wu, Wd = (B.dequant(raw[f"{n}_w"], raw[f"{n}_s"]) for n in ("gate", "up", "down"))
+                h = _swiglu(X @ Wg.T, X @ Wu.T)
+                d = h @ Wd.T
             out[ps] = (_bf16(d) if pairs else d) * wf[ps].unsqueeze(1)
             t_exp += time.perf_counter() - t1
             done += 1
