@@ -233,6 +233,7 @@ def cpu_port_rates(workload: str, budget_s: float, device_pool=None, samples: in
     out = {}
     variants = [("port_fp32_cached", True, False), ("port_on_the_fly", False, False)]
     if native() is not None:
+        native().mimo_cpu_port_set_threads(torch.get_num_threads())   # the same threads as the torch forms
         variants.append(("port_mxfp4_native", False, True))
     for name, cached, packed in variants:
         rates, info = [], None
@@ -245,6 +246,7 @@ def cpu_port_rates(workload: str, budget_s: float, device_pool=None, samples: in
                                f"by U/done; median of {samples} batch(es)"}
         if packed:
             out[name]["isa"] = "avx2+fma" if native().mimo_cpu_port_isa() == 2 else "scalar"
+            out[name]["cores"] = native().mimo_cpu_port_threads()
     return out
 
 

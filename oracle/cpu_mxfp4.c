@@ -21,6 +21,7 @@
  * are bit-identical.  The summation order differs from the Metal kernel's lane sums, so results match the
  * checker within its tolerance, not bit for bit. */
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -144,6 +145,12 @@ int mimo_cpu_port_isa(void) { return pick() == rows_dot_scalar ? 1 : 2; }
 
 /* force != 0: the scalar path even where AVX2 is present (tests compare the two). */
 void mimo_cpu_port_force_scalar(int force) { g_force_scalar = force; }
+
+/* Threads of the calls made from this thread (the timed baseline reports the count it used). */
+void mimo_cpu_port_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
+int mimo_cpu_port_threads(void) { return omp_get_max_threads(); }
 
 /* One expert on R token rows: x [R][H] float32 (bf16 values); gate/up words [I][H/8], scales [I][H/32];
  * down words [H][I/8], scales [H][I/32]; hbuf [R][I] scratch (receives h); out [R][H] = the expert's

@@ -48,6 +48,8 @@ def native():
         L.mimo_cpu_port_expert.restype = ctypes.c_int
         L.mimo_cpu_port_isa.restype = ctypes.c_int
         L.mimo_cpu_port_force_scalar.argtypes = [ctypes.c_int]
+        L.mimo_cpu_port_set_threads.argtypes = [ctypes.c_int]
+        L.mimo_cpu_port_threads.restype = ctypes.c_int
         _native = L
     return _native
 
