@@ -102,10 +102,11 @@ class CpuLayer:
         self.expert = expert
 
     def step_time(self, x: torch.Tensor, cached: bool, budget_s: float, wall_s: Optional[float] = None,
-                  min_experts: int = 2, packed: bool = False):
+                  min_experts: int = 2, packed: bool = False, outputs: Optional[list] = None):
         """Seconds of one layer step for the token rows x [T, H] (bf16 values), measured on a bounded
         sample (packed: the compiled kernel on the MXFP4 bytes; else float32 weights, cached or dequantised
-        on the fly).  Returns (seconds, experts done, distinct experts U)."""
+        on the fly).  Returns (seconds, experts done, distinct experts U); with `outputs`, appends
+        (y, inds, w) of the step it timed (y complete when every expert was done)."""
         xf = x.float()
         T = xf.shape[0]
         t0 = time.perf_counter()
@@ -144,6 +145,8 @@ class CpuLayer:
         acc = torch.zeros(T, xf.shape[1])
         for j in range(inds.shape[1]):
             acc = acc + Y[:, j]
-        _bf16(acc)
+        y = _bf16(acc)
         t_comb = time.perf_counter() - t2
+        if outputs is not None:
+            outputs.append((y, inds, w))
         return t_route + t_exp / done * len(uids) + t_comb, done, len(uids)

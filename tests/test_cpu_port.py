@@ -60,3 +60,40 @@ def test_avx2_and_scalar_paths_agree_bit_for_bit(lib):
     finally:
         lib.mimo_cpu_port_force_scalar(0)
     assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32))
+
+
+class _LazyPool:
+    """pool[key][expert] -> that expert's tensor, generated on demand (the batched oracle's pool access)."""
+
+    def __init__(self, get):
+        self.get = get
+
+    def __getitem__(self, key):
+        get = self.get
+
+        class _Proj:
+            def __getitem__(self, e):
+                return get(int(e))[key]
+        return _Proj()
+
+
+@pytest.mark.parametrize("T,cached,packed", [(1, True, False), (3, True, False), (1, False, False),
+                                             (1, False, True), (3, False, True)])
+def test_timed_cpu_layer_computes_the_moe_layer(lib, T, cached, packed):
+    """The timed CPU step itself (router, every distinct expert, the fixed-order combine) against the batched
+    oracle on the same routes (the reference's dispatch rule: pair path at T = 1, kernels A/B at 2..8)."""
+    cache = {}
+
+    def get(e):
+        if e not in cache:
+            cache[e] = _expert(e)
+        return cache[e]
+    W = synth.router_weight()
+    layer = cpu_path.CpuLayer(W, torch.zeros(W.shape[0]), get)
+    x = synth.hidden(T, seed=60 + T)
+    outs = []
+    _, done, U = layer.step_time(x, cached, budget_s=1e9, packed=packed, outputs=outs)
+    assert done == U
+    y, inds, w = outs[0]
+    want = B.moe_layer(x.float().numpy(), _LazyPool(get), inds.numpy(), w.numpy())
+    assert O.rel_err(y.numpy(), want) <= 1e-2
