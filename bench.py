@@ -335,8 +335,14 @@ def cpu_layer_attention_seconds(T: int, context: int, budget_s: float) -> tuple:
     while True:
         t0 = time.perf_counter()
         qkv = r @ wqkv.T
-        ang = torch.arange(rows, dtype=torch.float32)[:, None] * torch.pow(c.rope_theta, -torch.arange(half) * 2.0 / c.rotary_dim)
-        _ = qkv[:, :half] * torch.cos(ang) - qkv[:, half:2 * half] * torch.sin(ang)
+        # RoPE on every q and k head's rotary dims (both halves of each pair), the value scale on v
+        ang = (torch.arange(rows, dtype=torch.float32)[:, None]
+               * torch.pow(c.rope_theta, -torch.arange(half) * 2.0 / c.rotary_dim))[:, None, :]
+        cs, sn = torch.cos(ang), torch.sin(ang)
+        qk = qkv[:, :(c.n_heads + c.n_kv_heads) * c.head_dim].reshape(rows, -1, c.head_dim)
+        x1, x2 = qk[..., :half], qk[..., half:2 * half]
+        _ = torch.cat([x1 * cs - x2 * sn, x1 * sn + x2 * cs], -1)
+        _ = qkv[:, (c.n_heads + c.n_kv_heads) * c.head_dim:] * 0.707
         _ = o @ wo.T
         t1 = time.perf_counter()
         for h in range(heads):
