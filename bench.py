@@ -190,6 +190,18 @@ def workload_config(workload: str, world: int = 1, NE: int = E) -> dict:
 
 
 # ------------------------------------------------------------------------------------ CPU legs
+def _cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def _host_cores() -> int:
     return int(os.environ.get("OMP_NUM_THREADS", 0)) or (os.cpu_count() or 1)
 
@@ -300,11 +312,11 @@ def cpu_baseline(workload: str, budget_s: float, device_pool=None, emulator: boo
         em = cpu_emulator_rate(T, budget_s)
         if em is not None:
             rates["reference_kernels_emulated"] = em
-    best = max(("port_fp32_cached", "port_on_the_fly"), key=lambda k: rates[k]["value"])
+    best = max((k for k in rates if k.startswith("port_")), key=lambda k: rates[k]["value"])
     b = rates[best]
-    return {"value": b["value"], "unit": "tok/s", "cores": b["cores"], "kind": "port",
-            "sample": f"{best}: vectorised torch-CPU restatement of the reference path (oracle/cpu_path.py); "
-                      + b["sample"], "variants": rates}
+    return {"value": b["value"], "unit": "tok/s", "cores": b["cores"], "kind": "port", "cpu_model": _cpu_model(),
+            "sample": f"{best}: the reference path restated for the CPU (oracle/cpu_path.py); " + b["sample"],
+            "variants": rates}
 
 
 def cpu_layer_attention_seconds(T: int, context: int, budget_s: float) -> tuple:
@@ -407,7 +419,7 @@ def run_reference(args):
            "warmup": args.warmup, "ms_per_step": T * world / v * 1e3, "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None,
            "dtype": "f32 (the reference path on the CPU)", "data": "synthetic", "config": cfg,
-           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": rates[best]["cores"],
+           "cpu_baseline": {"value": v, "unit": "tok/s", "cores": rates[best]["cores"], "cpu_model": _cpu_model(),
                             "kind": "reference" if best == "reference_kernels_emulated" and not layer else "port",
                             "sample": sample if layer else f"{best}: {sample}", "variants": rates},
            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -552,6 +564,7 @@ def measure_layer(args, ctx, workload: str, steps: int, warmup: int, cpu_budget:
         t_moe = T / moe_rates[best]["value"]
         t_att, sample = cpu_layer_attention_seconds(T, pos0, cpu_budget)
         res["cpu_baseline"] = {"value": T / (t_moe + t_att), "unit": "tok/s", "cores": _host_cores(), "kind": "port",
+                               "cpu_model": _cpu_model(),
                                "sample": f"{sample}; plus the MoE block's {best} ({moe_rates[best]['sample']})"}
     del gstep
     torch.cuda.synchronize()
